@@ -1,0 +1,244 @@
+"""B200-native INT4 Llama-2-7B batch-1 decode (drop-in for the 4PE_U250 path).
+
+Python/ctypes shim over ``libi4d.so`` (C ABI in include/i4d.h).  Mirrors the
+reference host's operator surface: load the four bank images and the RoPE
+LUT (decode_host.cpp:1236-1294), then one ``decode_token(position,
+residual)`` per step returning the 32256 padded logits
+(decode_host.cpp:1340-1556), plus the per-stage services used by parity
+tests (linear stage, RMSNorm+quant, attention, SwiGLU+quant).
+
+Errors raise I4DError carrying the C status and message; there is no CPU
+fallback: without the CUDA library every call fails.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+from . import formats
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libi4d.so")
+
+OK, ERR_ARG, ERR_SIZE, ERR_CUDA, ERR_TIMEOUT, ERR_STATE, ERR_NOMEM = range(7)
+FLAG_NO_GRAPH = 1
+FLAG_NO_PDL = 2
+
+# Every symbol include/i4d.h declares.
+EXPORTS = [
+    "i4d_create", "i4d_destroy", "i4d_last_error", "i4d_load_bank", "i4d_load_rope",
+    "i4d_load_embeddings", "i4d_decode_token", "i4d_kv_reset", "i4d_kv_read", "i4d_kv_write",
+    "i4d_sync", "i4d_linear_bank", "i4d_gemv", "i4d_quantize_g32", "i4d_rms_quant",
+    "i4d_attention", "i4d_swiglu_quant", "i4d_expf", "i4d_decode_token_async", "i4d_stream",
+    "i4d_profile_token",
+]
+
+KERNEL_CLASSES = ["qkv_gemv", "attention", "o_gemv", "gate_up_gemv", "down_gemv", "logits_gemv", "rms"]
+
+
+class I4DError(RuntimeError):
+    def __init__(self, status, message):
+        super().__init__(f"i4d status {status}: {message}")
+        self.status = status
+
+
+class _Config(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("num_layers", ctypes.c_int),
+                ("kv_capacity", ctypes.c_int), ("flags", ctypes.c_uint)]
+
+
+_lib = None
+
+
+def load_library():
+    """Loads libi4d.so (raises if it was not built; no fallback exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: run __graft_entry__.build()")
+    L = ctypes.CDLL(LIB_PATH)
+    P = ctypes.c_void_p
+    sig = {
+        "i4d_create": [ctypes.POINTER(_Config), ctypes.POINTER(P)],
+        "i4d_destroy": [P],
+        "i4d_last_error": [P],
+        "i4d_load_bank": [P, ctypes.c_int, P, ctypes.c_size_t],
+        "i4d_load_rope": [P, P, ctypes.c_size_t],
+        "i4d_load_embeddings": [P, P, ctypes.c_size_t],
+        "i4d_decode_token": [P, ctypes.c_uint32, P, P, P],
+        "i4d_kv_reset": [P],
+        "i4d_kv_read": [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P],
+        "i4d_kv_write": [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P],
+        "i4d_sync": [P],
+        "i4d_linear_bank": [P, P, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, P, P, ctypes.c_int, P],
+        "i4d_gemv": [P, ctypes.c_int, ctypes.c_int, P, P, P, P],
+        "i4d_quantize_g32": [P, P, ctypes.c_int, P, P],
+        "i4d_rms_quant": [P, P, P, P, P],
+        "i4d_attention": [P, ctypes.c_int, ctypes.c_uint32, P, P, P, P, P],
+        "i4d_swiglu_quant": [P, P, P, P, P],
+        "i4d_expf": [P, P, P, ctypes.c_size_t],
+        "i4d_decode_token_async": [P, ctypes.c_uint32, P, P],
+        "i4d_stream": [P],
+        "i4d_profile_token": [P, ctypes.c_uint32, P, P, P],
+    }
+    for name, args in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = ctypes.c_int
+    L.i4d_destroy.restype = None
+    L.i4d_last_error.restype = ctypes.c_char_p
+    L.i4d_stream.restype = ctypes.c_void_p
+    _lib = L
+    return L
+
+
+def _ptr(a):
+    return a.ctypes.data if a is not None else None
+
+
+class Context:
+    """One decode context on one GPU (i4d_ctx)."""
+
+    def __init__(self, device=0, num_layers=32, kv_capacity=4096, flags=0):
+        self._L = load_library()
+        cfg = _Config(device, num_layers, kv_capacity, flags)
+        h = ctypes.c_void_p()
+        st = self._L.i4d_create(ctypes.byref(cfg), ctypes.byref(h))
+        if st != OK:
+            raise I4DError(st, "i4d_create failed (see stderr)")
+        self._h = h
+        self.num_layers = num_layers
+        self.kv_capacity = kv_capacity
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._L.i4d_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def _check(self, st):
+        if st != OK:
+            raise I4DError(st, self._L.i4d_last_error(self._h).decode())
+
+    # -- loading ----------------------------------------------------------
+    def load_bank(self, bank, image):
+        image = np.ascontiguousarray(image, dtype=np.uint8)
+        self._check(self._L.i4d_load_bank(self._h, bank, image.ctypes.data, image.nbytes))
+
+    def load_banks(self, images):
+        for p, img in enumerate(images):
+            self.load_bank(p, img)
+
+    def load_rope(self, lut=None):
+        lut = formats.generate_rope_lut() if lut is None else lut
+        buf = np.frombuffer(lut, dtype=np.uint8)
+        self._check(self._L.i4d_load_rope(self._h, buf.ctypes.data, buf.nbytes))
+
+    def load_embeddings(self, emb):
+        emb = np.ascontiguousarray(emb, dtype=np.float32)
+        self._check(self._L.i4d_load_embeddings(self._h, emb.ctypes.data, emb.size))
+
+    # -- decode -----------------------------------------------------------
+    def decode_token(self, position, residual_in, want_residual=False):
+        x = np.ascontiguousarray(residual_in, dtype=np.float32)
+        assert x.size == formats.DIM
+        logits = np.empty(formats.PADDED_VOCAB, dtype=np.float32)
+        res = np.empty(formats.DIM, dtype=np.float32) if want_residual else None
+        self._check(self._L.i4d_decode_token(self._h, position, x.ctypes.data, logits.ctypes.data, _ptr(res)))
+        return (logits, res) if want_residual else logits
+
+    def decode_token_async(self, position, residual_in_dev_ptr, logits_out_dev_ptr):
+        """Enqueue one step on device pointers (e.g. torch tensor data_ptr())."""
+        self._check(self._L.i4d_decode_token_async(self._h, position, residual_in_dev_ptr, logits_out_dev_ptr))
+
+    def stream_handle(self):
+        return self._L.i4d_stream(self._h)
+
+    def profile_token(self, position, residual_in_dev_ptr):
+        ms = np.zeros(7, np.float32)
+        n = np.zeros(7, np.uint32)
+        self._check(self._L.i4d_profile_token(self._h, position, residual_in_dev_ptr, ms.ctypes.data, n.ctypes.data))
+        return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(KERNEL_CLASSES)}
+
+    def kv_reset(self):
+        self._check(self._L.i4d_kv_reset(self._h))
+
+    def kv_read(self, bank, layer, local_head, token):
+        out = np.empty(formats.KV_RECORD_BYTES, dtype=np.uint8)
+        self._check(self._L.i4d_kv_read(self._h, bank, layer, local_head, token, out.ctypes.data))
+        return out
+
+    def kv_write(self, bank, layer, local_head, token, record):
+        rec = np.ascontiguousarray(record, dtype=np.uint8)
+        assert rec.size == formats.KV_RECORD_BYTES
+        self._check(self._L.i4d_kv_write(self._h, bank, layer, local_head, token, rec.ctypes.data))
+
+    def sync(self):
+        self._check(self._L.i4d_sync(self._h))
+
+    # -- per-stage services -------------------------------------------------
+    def linear_bank(self, superblocks, local_in_tiles, out_tiles, act_q, act_e8m0, hls_zero_start=False):
+        sb = np.ascontiguousarray(superblocks, dtype=np.uint8)
+        q = np.ascontiguousarray(act_q, dtype=np.int16)
+        e = np.ascontiguousarray(act_e8m0, dtype=np.uint8)
+        out = np.empty(out_tiles * 128, dtype=np.float32)
+        self._check(self._L.i4d_linear_bank(self._h, sb.ctypes.data, sb.nbytes, local_in_tiles, out_tiles,
+                                            q.ctypes.data, e.ctypes.data, int(bool(hls_zero_start)),
+                                            out.ctypes.data))
+        return out
+
+    def gemv(self, layer, mode, act_q, act_e8m0, with_partials=False):
+        rows = formats.mode_rows(mode)
+        q = np.ascontiguousarray(act_q, dtype=np.int16)
+        e = np.ascontiguousarray(act_e8m0, dtype=np.uint8)
+        y = np.empty(rows, dtype=np.float32)
+        part = np.empty(4 * rows, dtype=np.float32) if with_partials else None
+        self._check(self._L.i4d_gemv(self._h, layer, mode, q.ctypes.data, e.ctypes.data, y.ctypes.data,
+                                     _ptr(part)))
+        return (y, part.reshape(4, rows)) if with_partials else y
+
+    def quantize_g32(self, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        q = np.empty(x.size, dtype=np.int16)
+        e = np.empty(x.size // 32, dtype=np.uint8)
+        self._check(self._L.i4d_quantize_g32(self._h, x.ctypes.data, x.size, q.ctypes.data, e.ctypes.data))
+        return q, e
+
+    def rms_quant(self, x, gamma):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        g = np.ascontiguousarray(gamma, dtype=np.float32)
+        q = np.empty(formats.DIM, dtype=np.int16)
+        e = np.empty(formats.DIM // 32, dtype=np.uint8)
+        self._check(self._L.i4d_rms_quant(self._h, x.ctypes.data, g.ctypes.data, q.ctypes.data, e.ctypes.data))
+        return q, e
+
+    def attention(self, layer, position, q, k, v):
+        arrs = [np.ascontiguousarray(a, dtype=np.int32) for a in (q, k, v)]
+        oq = np.empty(formats.DIM, dtype=np.int16)
+        oe = np.empty(formats.DIM // 32, dtype=np.uint8)
+        self._check(self._L.i4d_attention(self._h, layer, position, *[a.ctypes.data for a in arrs],
+                                          oq.ctypes.data, oe.ctypes.data))
+        return oq, oe
+
+    def swiglu_quant(self, gate, up):
+        g = np.ascontiguousarray(gate, dtype=np.float32)
+        u = np.ascontiguousarray(up, dtype=np.float32)
+        q = np.empty(formats.FFN, dtype=np.int16)
+        e = np.empty(formats.FFN // 32, dtype=np.uint8)
+        self._check(self._L.i4d_swiglu_quant(self._h, g.ctypes.data, u.ctypes.data, q.ctypes.data, e.ctypes.data))
+        return q, e
+
+    def expf(self, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.empty_like(x)
+        self._check(self._L.i4d_expf(self._h, x.ctypes.data, y.ctypes.data, x.size))
+        return y

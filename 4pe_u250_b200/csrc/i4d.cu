@@ -1,0 +1,898 @@
+// i4d.cu -- host runtime and C ABI of libi4d (see include/i4d.h).
+//
+// One context = one GPU, one CUDA stream.  The token schedule of
+// int4_decoder_controller.cpp:138-234 (RMS -> QKV -> attention -> O+residual
+// -> RMS -> GATE/UP -> SwiGLU -> DOWN+residual, 32 layers, final RMS ->
+// LOGITS) is 5 kernels per layer plus 2, launched with programmatic dependent
+// launch so every GEMV kernel streams its weights while the previous kernel
+// finishes, and captured once as a CUDA graph whose position lives in device
+// memory.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "i4d.h"
+#include "i4d_attention.cuh"
+#include "i4d_blocks.cuh"
+#include "i4d_linear.cuh"
+
+extern "C" {
+extern const unsigned int i4d_expf_fix_count;
+extern const unsigned int i4d_expf_fix[];
+extern const char i4d_expf_fix_libc[];
+}
+
+using namespace i4d;
+
+namespace {
+
+// Stage kinds of the GEMV layout.
+enum Stage { ST_QKV = 0, ST_O, ST_GU, ST_DOWN, ST_LOGITS, ST_COUNT };
+constexpr int kStageUnits[ST_COUNT] = {384, 128, 704, 128, 1008};
+constexpr int kStageChunks[ST_COUNT] = {4, 4, 4, 11, 4};
+constexpr size_t kSmemBudget = 115712;  // two CTAs per SM
+
+size_t stage_bank_bytes(int st) {
+    return static_cast<size_t>(kStageUnits[st]) * kStageChunks[st] * kChunkBytes;
+}
+
+// Reference geometry (emulator:786-797, autoround_pack_llama2_u250.py:59-99).
+int mode_rows(int m) { return (m <= 3 || m == 6) ? 4096 : (m <= 5 ? 11264 : 32256); }
+int mode_lit(int m) { return m == 6 ? 11 : 4; }
+uint64_t mode_words(int m) { return static_cast<uint64_t>(mode_rows(m) / 128) * mode_lit(m) / 16 * 4224; }
+uint64_t matrix_word_offset(int layer, int m) {
+    uint64_t stride = 0;
+    for (int i = 0; i < 7; ++i) stride += mode_words(i);
+    uint64_t off = 4160;
+    if (m == 7) return off + 32ull * stride;
+    off += static_cast<uint64_t>(layer) * stride;
+    for (int i = 0; i < m; ++i) off += mode_words(i);
+    return off;
+}
+int mode_stage(int m) { return m <= 2 ? ST_QKV : (m == 3 ? ST_O : (m <= 5 ? ST_GU : (m == 6 ? ST_DOWN : ST_LOGITS))); }
+int mode_unit_offset(int m) { return m <= 2 ? m * 128 : (m == 5 ? 352 : 0); }
+
+int32_t host_float_to_q17(float value) {
+    uint32_t bits;
+    std::memcpy(&bits, &value, 4);
+    const bool neg = (bits >> 31) != 0;
+    const uint32_t e = (bits >> 23) & 0xffu;
+    if (e < 109) return 0;
+    if (e >= 141) return neg ? INT32_MIN : INT32_MAX;
+    const uint32_t sig = (1u << 23) | (bits & 0x7fffffu);
+    uint64_t mag;
+    if (e >= 133) {
+        mag = static_cast<uint64_t>(sig) << (e - 133);
+    } else {
+        const unsigned sh = 133 - e;
+        uint32_t q = sig >> sh;
+        const uint32_t rem = sig & ((1u << sh) - 1u), half = 1u << (sh - 1);
+        if (rem > half || (rem == half && (q & 1u))) ++q;
+        mag = q;
+    }
+    if (!neg) return mag > 0x7fffffffull ? INT32_MAX : static_cast<int32_t>(mag);
+    return mag >= (1ull << 31) ? INT32_MIN : -static_cast<int32_t>(mag);
+}
+
+}  // namespace
+
+struct i4d_ctx {
+    int device = 0, layers = 32, stride = 4096, num_sms = 148, cpb = 37;
+    unsigned flags = 0;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    // weights (GEMV layout), norms, tables
+    uint8_t* d_w = nullptr;
+    size_t w_bytes = 0;
+    float* d_gamma = nullptr;  // [65][4096]: attn l at 2l, ffn l at 2l+1, final at 64
+    int32_t* d_rope_cos = nullptr;
+    int32_t* d_rope_sin = nullptr;
+    uint32_t* d_exp2 = nullptr;
+    uint32_t* d_expf_slots = nullptr;
+    ExpfFix expf{};
+    int log2e_q21 = 0;
+    int32_t score_scale = 0;
+    uint8_t* d_kv = nullptr;
+    size_t kv_bytes = 0;
+    float* d_emb = nullptr;
+    // workspace
+    float* d_resid = nullptr;
+    float* d_recip = nullptr;
+    float* d_partials = nullptr;
+    int16_t* d_ao_q = nullptr;
+    uint8_t* d_ao_e = nullptr;
+    int16_t* d_ad_q = nullptr;
+    uint8_t* d_ad_e = nullptr;
+    float* d_logits = nullptr;
+    unsigned* d_counters = nullptr;
+    unsigned* d_err = nullptr;
+    int* d_pos = nullptr;
+    float* d_scratch = nullptr;  // op-level staging, 3 x 32256 floats
+    // pinned staging for the decode contract
+    float* h_resid_in = nullptr;
+    float* h_resid_out = nullptr;
+    float* h_logits = nullptr;
+    int* h_pos = nullptr;
+    unsigned* h_err = nullptr;
+    bool bank_loaded[4] = {false, false, false, false};
+    bool rope_loaded = false;
+    cudaGraphExec_t graph = nullptr;       // H2D + token kernels + D2H
+    cudaGraphExec_t graph_dev = nullptr;   // token kernels only
+    // profiling: when set, enqueue_token brackets every kernel with events
+    cudaEvent_t prof_ev[2 * 256] = {};
+    int prof_class[256] = {};
+    int prof_n = 0;
+    bool profiling = false;
+};
+
+namespace {
+
+i4d_status fail(i4d_ctx* c, i4d_status st, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    if (c) c->err = buf;
+    return st;
+}
+
+#define CK(call)                                                                        \
+    do {                                                                                \
+        cudaError_t e_ = (call);                                                        \
+        if (e_ != cudaSuccess)                                                          \
+            return fail(c, I4D_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+size_t stage_offset(const i4d_ctx* c, int layer, int st) {
+    size_t per_layer = 0;
+    for (int s = 0; s < ST_LOGITS; ++s) per_layer += 4 * stage_bank_bytes(s);
+    if (st == ST_LOGITS) return static_cast<size_t>(c->layers) * per_layer;
+    size_t off = static_cast<size_t>(layer) * per_layer;
+    for (int s = 0; s < st; ++s) off += 4 * stage_bank_bytes(s);
+    return off;
+}
+
+int ring_slots(int chunks) {
+    const size_t fixed = linear_smem_bytes(0, chunks);
+    return static_cast<int>((kSmemBudget - fixed) / (kChunkBytes + 16));
+}
+
+template <typename Kern, typename... Args>
+cudaError_t launch(i4d_ctx* c, bool pdl, Kern kern, dim3 grid, dim3 block, size_t smem, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = c->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    if (pdl && !(c->flags & I4D_FLAG_NO_PDL)) {
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+    return e;
+}
+
+LinearArgs base_linear(i4d_ctx* c, int layer, int st) {
+    LinearArgs a = {};
+    a.w = c->d_w + stage_offset(c, layer, st);
+    a.bank_stride = stage_bank_bytes(st);
+    a.nbanks = 4;
+    a.cpb = c->cpb;
+    a.units = kStageUnits[st];
+    a.chunks = kStageChunks[st];
+    a.ns = ring_slots(a.chunks);
+    a.partials = c->d_partials;
+    a.counters = c->d_counters;
+    a.expf = c->expf;
+    a.err = c->d_err;
+    return a;
+}
+
+cudaError_t run_linear(i4d_ctx* c, const LinearArgs& a, bool pdl) {
+    const size_t smem = linear_smem_bytes(a.ns, a.chunks);
+    return launch(c, pdl, k_linear, dim3(a.nbanks * a.cpb), dim3(kLinearThreads), smem, a);
+}
+
+AttnArgs base_attn(i4d_ctx* c, int layer) {
+    AttnArgs a = {};
+    a.partials = c->d_partials;
+    a.pos_ptr = c->d_pos;
+    a.rope_cos = c->d_rope_cos;
+    a.rope_sin = c->d_rope_sin;
+    a.exp2_q30 = c->d_exp2;
+    a.log2e_q21 = c->log2e_q21;
+    a.score_scale = c->score_scale;
+    a.kv = c->d_kv;
+    a.layers = c->layers;
+    a.stride = c->stride;
+    a.layer = layer;
+    a.out_q = c->d_ao_q;
+    a.out_e = c->d_ao_e;
+    a.err = c->d_err;
+    return a;
+}
+
+enum KernelClass { KC_QKV = 0, KC_ATTN, KC_O, KC_GU, KC_DOWN, KC_LOGITS, KC_RMS, KC_COUNT };
+
+cudaError_t prof_begin(i4d_ctx* c, int cls) {
+    if (!c->profiling || c->prof_n >= 256) return cudaSuccess;
+    c->prof_class[c->prof_n] = cls;
+    return cudaEventRecord(c->prof_ev[2 * c->prof_n], c->stream);
+}
+
+cudaError_t prof_end(i4d_ctx* c) {
+    if (!c->profiling || c->prof_n >= 256) return cudaSuccess;
+    return cudaEventRecord(c->prof_ev[2 * c->prof_n++ + 1], c->stream);
+}
+
+#define TIMED(cls, call)        \
+    do {                        \
+        CK(prof_begin(c, cls)); \
+        CK(call);               \
+        CK(prof_end(c));        \
+    } while (0)
+
+// The kernels of one token (position and residual already in device memory).
+i4d_status enqueue_token(i4d_ctx* c) {
+    TIMED(KC_RMS, launch(c, false, k_rms_recip, dim3(1), dim3(32), 0, (const float*)c->d_resid, c->d_recip));
+    for (int l = 0; l < c->layers; ++l) {
+        LinearArgs q = base_linear(c, l, ST_QKV);
+        q.in_kind = IN_RMS;
+        q.resid = c->d_resid;
+        q.gamma = c->d_gamma + static_cast<size_t>(2 * l) * kDim;
+        q.recip = c->d_recip;
+        q.epi = EPI_PARTIAL;
+        TIMED(KC_QKV, run_linear(c, q, true));
+
+        TIMED(KC_ATTN, launch(c, true, k_attention, dim3(kHeads), dim3(kAttnThreads), 0, base_attn(c, l)));
+
+        LinearArgs o = base_linear(c, l, ST_O);
+        o.in_kind = IN_ACT;
+        o.act_q = c->d_ao_q;
+        o.act_e = c->d_ao_e;
+        o.act_bank_stride = 1024;
+        o.epi = EPI_RESID;
+        o.out = c->d_resid;
+        o.recip_out = c->d_recip;
+        TIMED(KC_O, run_linear(c, o, true));
+
+        LinearArgs gu = base_linear(c, l, ST_GU);
+        gu.in_kind = IN_RMS;
+        gu.resid = c->d_resid;
+        gu.gamma = c->d_gamma + static_cast<size_t>(2 * l + 1) * kDim;
+        gu.recip = c->d_recip;
+        gu.epi = EPI_SWIGLU;
+        gu.q_out = c->d_ad_q;
+        gu.e_out = c->d_ad_e;
+        TIMED(KC_GU, run_linear(c, gu, true));
+
+        LinearArgs dn = base_linear(c, l, ST_DOWN);
+        dn.in_kind = IN_ACT;
+        dn.act_q = c->d_ad_q;
+        dn.act_e = c->d_ad_e;
+        dn.act_bank_stride = 2816;
+        dn.epi = EPI_RESID;
+        dn.out = c->d_resid;
+        dn.recip_out = c->d_recip;
+        TIMED(KC_DOWN, run_linear(c, dn, true));
+    }
+    LinearArgs lg = base_linear(c, 0, ST_LOGITS);
+    lg.in_kind = IN_RMS;
+    lg.resid = c->d_resid;
+    lg.gamma = c->d_gamma + static_cast<size_t>(64) * kDim;
+    lg.recip = c->d_recip;
+    lg.epi = EPI_STORE;
+    lg.out = c->d_logits;
+    TIMED(KC_LOGITS, run_linear(c, lg, true));
+    return I4D_OK;
+}
+
+i4d_status enqueue_decode(i4d_ctx* c) {
+    CK(cudaMemcpyAsync(c->d_resid, c->h_resid_in, kDim * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->d_pos, c->h_pos, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    const i4d_status st = enqueue_token(c);
+    if (st != I4D_OK) return st;
+    CK(cudaMemcpyAsync(c->h_logits, c->d_logits, kPVocab * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(c->h_resid_out, c->d_resid, kDim * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream));
+    return I4D_OK;
+}
+
+i4d_status finish(i4d_ctx* c) {
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaGetLastError());
+    unsigned e = 0;
+    CK(cudaMemcpy(&e, c->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost));
+    if (e) {
+        CK(cudaMemset(c->d_err, 0, sizeof(unsigned)));
+        if (e & kErrArg) return fail(c, I4D_ERR_ARG, "device rejected an argument (error word 0x%x)", e);
+        return fail(c, I4D_ERR_TIMEOUT, "a bounded device wait gave up (error word 0x%x)", e);
+    }
+    return I4D_OK;
+}
+
+bool all_loaded(const i4d_ctx* c) {
+    return c->bank_loaded[0] && c->bank_loaded[1] && c->bank_loaded[2] && c->bank_loaded[3] && c->rope_loaded;
+}
+
+}  // namespace
+
+// ===================================================================== C ABI
+
+extern "C" {
+
+const char* i4d_last_error(const i4d_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+void i4d_destroy(i4d_ctx* c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->graph) cudaGraphExecDestroy(c->graph);
+    if (c->graph_dev) cudaGraphExecDestroy(c->graph_dev);
+    for (cudaEvent_t ev : c->prof_ev)
+        if (ev) cudaEventDestroy(ev);
+    void* dev[] = {c->d_w, c->d_gamma, c->d_rope_cos, c->d_rope_sin, c->d_exp2, c->d_expf_slots, c->d_kv,
+                   c->d_emb, c->d_resid, c->d_recip, c->d_partials, c->d_ao_q, c->d_ao_e, c->d_ad_q,
+                   c->d_ad_e, c->d_logits, c->d_counters, c->d_err, c->d_pos, c->d_scratch};
+    for (void* p : dev)
+        if (p) cudaFree(p);
+    void* host[] = {c->h_resid_in, c->h_resid_out, c->h_logits, c->h_pos, c->h_err};
+    for (void* p : host)
+        if (p) cudaFreeHost(p);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out) {
+    if (!cfg || !out) return I4D_ERR_ARG;
+    *out = nullptr;
+    i4d_ctx* c = new i4d_ctx();
+    c->device = cfg->device;
+    c->layers = cfg->num_layers;
+    c->stride = cfg->kv_capacity == 0 ? 4096 : cfg->kv_capacity;
+    c->flags = cfg->flags;
+    if (c->layers < 1 || c->layers > 32 || c->stride < 1 || c->stride > 4096) {
+        i4d_destroy(c);
+        return I4D_ERR_ARG;
+    }
+    auto bail = [&](i4d_status st) {
+        // keep the message readable by the caller through a temporary context
+        fprintf(stderr, "i4d_create: %s\n", c->err.c_str());
+        i4d_destroy(c);
+        return st;
+    };
+#define CKC(call)                                                                              \
+    do {                                                                                       \
+        cudaError_t e_ = (call);                                                               \
+        if (e_ != cudaSuccess) {                                                               \
+            fail(c, e_ == cudaErrorMemoryAllocation ? I4D_ERR_NOMEM : I4D_ERR_CUDA, "%s: %s", #call, \
+                 cudaGetErrorString(e_));                                                      \
+            return bail(e_ == cudaErrorMemoryAllocation ? I4D_ERR_NOMEM : I4D_ERR_CUDA);       \
+        }                                                                                      \
+    } while (0)
+    CKC(cudaSetDevice(c->device));
+    CKC(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, c->device));
+    c->cpb = c->num_sms / 4 > 0 ? c->num_sms / 4 : 1;
+    CKC(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    CKC(cudaFuncSetAttribute(k_linear, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBudget)));
+
+    c->w_bytes = stage_offset(c, 0, ST_LOGITS) + 4 * stage_bank_bytes(ST_LOGITS);
+    CKC(cudaMalloc(&c->d_w, c->w_bytes));
+    CKC(cudaMalloc(&c->d_gamma, 65ull * kDim * sizeof(float)));
+    CKC(cudaMalloc(&c->d_rope_cos, 4096ull * 64 * sizeof(int32_t)));
+    CKC(cudaMalloc(&c->d_rope_sin, 4096ull * 64 * sizeof(int32_t)));
+    c->kv_bytes = 4ull * c->layers * kLocalHeads * static_cast<size_t>(c->stride) * 320;
+    CKC(cudaMalloc(&c->d_kv, c->kv_bytes));
+    CKC(cudaMemset(c->d_kv, 0, c->kv_bytes));
+    CKC(cudaMalloc(&c->d_resid, kDim * sizeof(float)));
+    CKC(cudaMalloc(&c->d_recip, 16));
+    CKC(cudaMalloc(&c->d_partials, 4ull * kPVocab * sizeof(float)));
+    CKC(cudaMalloc(&c->d_ao_q, kDim * sizeof(int16_t)));
+    CKC(cudaMalloc(&c->d_ao_e, kDim / 32));
+    CKC(cudaMalloc(&c->d_ad_q, kFfn * sizeof(int16_t)));
+    CKC(cudaMalloc(&c->d_ad_e, kFfn / 32));
+    CKC(cudaMalloc(&c->d_logits, kPVocab * sizeof(float)));
+    CKC(cudaMalloc(&c->d_counters, kCounterSlots * sizeof(unsigned)));
+    CKC(cudaMemset(c->d_counters, 0, kCounterSlots * sizeof(unsigned)));
+    CKC(cudaMalloc(&c->d_err, sizeof(unsigned)));
+    CKC(cudaMemset(c->d_err, 0, sizeof(unsigned)));
+    CKC(cudaMalloc(&c->d_pos, sizeof(int)));
+    CKC(cudaMalloc(&c->d_scratch, 3ull * kPVocab * sizeof(float)));
+    CKC(cudaMallocHost(&c->h_resid_in, kDim * sizeof(float)));
+    CKC(cudaMallocHost(&c->h_resid_out, kDim * sizeof(float)));
+    CKC(cudaMallocHost(&c->h_logits, kPVocab * sizeof(float)));
+    CKC(cudaMallocHost(&c->h_pos, sizeof(int)));
+    CKC(cudaMallocHost(&c->h_err, sizeof(unsigned)));
+
+    // exp2 LUT of the online softmax: round(2^(30 + i/32)), and log2(e) in
+    // Q21 (emulator:566-579 define the same quantities).
+    uint32_t lut[33];
+    for (int i = 0; i <= 32; ++i) lut[i] = static_cast<uint32_t>(llroundl(exp2l(30.0L + i / 32.0L)));
+    CKC(cudaMalloc(&c->d_exp2, sizeof(lut)));
+    CKC(cudaMemcpy(c->d_exp2, lut, sizeof(lut), cudaMemcpyHostToDevice));
+    c->log2e_q21 = static_cast<int>(std::nearbyint(1.4426950408889634 * static_cast<double>(1 << 21)));
+    c->score_scale = host_float_to_q17(0.08838834764831845f);
+
+    // Hash table of the measured expf exceptions.
+    uint32_t cap = 1;
+    while (cap < 3u * i4d_expf_fix_count + 1u) cap <<= 1;
+    std::vector<uint32_t> slots(2ull * cap, 0xffffffffu);
+    int max_probe = 1;
+    for (uint32_t i = 0; i < i4d_expf_fix_count; ++i) {
+        const uint32_t key = i4d_expf_fix[2 * i], val = i4d_expf_fix[2 * i + 1];
+        uint32_t s = expf_hash(key) & (cap - 1);
+        int probe = 1;
+        while (slots[2 * s] != 0xffffffffu) {
+            s = (s + 1) & (cap - 1);
+            ++probe;
+        }
+        slots[2 * s] = key;
+        slots[2 * s + 1] = val;
+        if (probe > max_probe) max_probe = probe;
+    }
+    CKC(cudaMalloc(&c->d_expf_slots, slots.size() * sizeof(uint32_t)));
+    CKC(cudaMemcpy(c->d_expf_slots, slots.data(), slots.size() * sizeof(uint32_t), cudaMemcpyHostToDevice));
+    c->expf.slots = c->d_expf_slots;
+    c->expf.mask = cap - 1;
+    c->expf.max_probe = max_probe;
+#undef CKC
+    *out = c;
+    return I4D_OK;
+}
+
+i4d_status i4d_load_bank(i4d_ctx* c, int bank, const void* bytes, size_t n) {
+    if (!c || !bytes || bank < 0 || bank > 3) return c ? fail(c, I4D_ERR_ARG, "bad bank or pointer") : I4D_ERR_ARG;
+    if (n == I4D_LEGACY_BANK_BYTES)
+        return fail(c, I4D_ERR_SIZE, "legacy 891,277,312-byte bank layout is not supported; repack dense");
+    if (n != I4D_BANK_BYTES) return fail(c, I4D_ERR_SIZE, "bank image has %zu bytes; expected 865071104", n);
+    CK(cudaSetDevice(c->device));
+    if (c->graph) {
+        cudaGraphExecDestroy(c->graph);
+        c->graph = nullptr;
+    }
+    if (c->graph_dev) {
+        cudaGraphExecDestroy(c->graph_dev);
+        c->graph_dev = nullptr;
+    }
+    uint8_t* stage = nullptr;
+    CK(cudaMalloc(&stage, n));
+    cudaError_t e = cudaMemcpy(stage, bytes, n, cudaMemcpyHostToDevice);
+    for (int l = 0; e == cudaSuccess && l <= c->layers; ++l) {
+        for (int m = 0; m < 8; ++m) {
+            if ((l == c->layers) != (m == 7)) continue;
+            const int st = mode_stage(m);
+            RelayoutArgs r;
+            r.src = stage + matrix_word_offset(l, m) * 64;
+            r.dst = c->d_w + stage_offset(c, l, st) + static_cast<size_t>(bank) * stage_bank_bytes(st);
+            r.unit_offset = mode_unit_offset(m);
+            r.lit = mode_lit(m);
+            k_relayout<<<mode_rows(m) / 32 * r.lit, 256, 0, c->stream>>>(r);
+            e = cudaGetLastError();
+            if (e != cudaSuccess) break;
+        }
+    }
+    // Gammas: attention at word l*128, FFN at l*128+64, final at 4096.
+    for (int l = 0; e == cudaSuccess && l < 32; ++l)
+        for (int which = 0; which < 2 && e == cudaSuccess; ++which)
+            e = cudaMemcpyAsync(c->d_gamma + static_cast<size_t>(2 * l + which) * kDim + bank * 1024,
+                                stage + (static_cast<size_t>(l) * 128 + which * 64) * 64, 4096,
+                                cudaMemcpyDeviceToDevice, c->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(c->d_gamma + 64ull * kDim + bank * 1024, stage + 4096ull * 64, 4096,
+                            cudaMemcpyDeviceToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(stage);
+    if (e != cudaSuccess) return fail(c, I4D_ERR_CUDA, "bank load: %s", cudaGetErrorString(e));
+    c->bank_loaded[bank] = true;
+    return I4D_OK;
+}
+
+i4d_status i4d_load_rope(i4d_ctx* c, const void* bytes, size_t n) {
+    if (!c || !bytes) return c ? fail(c, I4D_ERR_ARG, "null rope pointer") : I4D_ERR_ARG;
+    if (n != I4D_ROPE_BYTES) return fail(c, I4D_ERR_SIZE, "rope LUT has %zu bytes; expected 2097152", n);
+    // Position p, pair i: 608-bit word p*4 + i/16 as two 64-byte words, lane
+    // i%16 at bit 38*lane, 19-bit cosine then sine, Q1.17 (generate_rope_lut.py:20-41).
+    const uint8_t* lut = static_cast<const uint8_t*>(bytes);
+    std::vector<int32_t> cs(4096 * 64), sn(4096 * 64);
+    for (int pos = 0; pos < 4096; ++pos)
+        for (int pair = 0; pair < 64; ++pair) {
+            const uint8_t* base = lut + (static_cast<size_t>(pos) * 4 + pair / 16) * 128;
+            const int lane = pair % 16;
+            for (int f = 0; f < 2; ++f) {
+                uint32_t v = 0;
+                for (int b = 0; b < 19; ++b) {
+                    const int bit = lane * 38 + f * 19 + b;
+                    v |= static_cast<uint32_t>((base[bit >> 3] >> (bit & 7)) & 1u) << b;
+                }
+                const int32_t sv = (v & (1u << 18)) ? static_cast<int32_t>(v | 0xfff80000u) : static_cast<int32_t>(v);
+                (f == 0 ? cs : sn)[static_cast<size_t>(pos) * 64 + pair] = sv;
+            }
+        }
+    CK(cudaSetDevice(c->device));
+    CK(cudaMemcpy(c->d_rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->d_rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    c->rope_loaded = true;
+    return I4D_OK;
+}
+
+i4d_status i4d_load_embeddings(i4d_ctx* c, const float* emb, size_t n_floats) {
+    if (!c || !emb) return c ? fail(c, I4D_ERR_ARG, "null embeddings") : I4D_ERR_ARG;
+    if (n_floats != 32000ull * kDim) return fail(c, I4D_ERR_SIZE, "embeddings have %zu floats; expected 131072000", n_floats);
+    CK(cudaSetDevice(c->device));
+    if (!c->d_emb) CK(cudaMalloc(&c->d_emb, n_floats * sizeof(float)));
+    CK(cudaMemcpy(c->d_emb, emb, n_floats * sizeof(float), cudaMemcpyHostToDevice));
+    return I4D_OK;
+}
+
+i4d_status i4d_decode_token(i4d_ctx* c, uint32_t position, const float* residual_in, float* logits_out,
+                            float* residual_out) {
+    if (!c || !residual_in || !logits_out) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    if (!all_loaded(c)) return fail(c, I4D_ERR_STATE, "banks and rope LUT must be loaded before decoding");
+    if (position >= static_cast<uint32_t>(c->stride))
+        return fail(c, I4D_ERR_ARG, "position %u out of range (KV capacity %d)", position, c->stride);
+    CK(cudaSetDevice(c->device));
+    std::memcpy(c->h_resid_in, residual_in, kDim * sizeof(float));
+    *c->h_pos = static_cast<int>(position);
+    *c->h_err = 0;
+    if (c->flags & I4D_FLAG_NO_GRAPH) {
+        const i4d_status st = enqueue_decode(c);
+        if (st != I4D_OK) return st;
+    } else {
+        if (!c->graph) {
+            cudaGraph_t g = nullptr;
+            CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+            const i4d_status st = enqueue_decode(c);
+            cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+            if (st != I4D_OK) {
+                if (g) cudaGraphDestroy(g);
+                return st;
+            }
+            if (e != cudaSuccess) return fail(c, I4D_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+            e = cudaGraphInstantiate(&c->graph, g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) {
+                c->graph = nullptr;
+                return fail(c, I4D_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+            }
+        }
+        CK(cudaGraphLaunch(c->graph, c->stream));
+    }
+    CK(cudaStreamSynchronize(c->stream));
+    if (*c->h_err) {
+        const unsigned e = *c->h_err;
+        CK(cudaMemset(c->d_err, 0, sizeof(unsigned)));
+        return fail(c, (e & kErrArg) ? I4D_ERR_ARG : I4D_ERR_TIMEOUT, "device error word 0x%x", e);
+    }
+    std::memcpy(logits_out, c->h_logits, kPVocab * sizeof(float));
+    if (residual_out) std::memcpy(residual_out, c->h_resid_out, kDim * sizeof(float));
+    return I4D_OK;
+}
+
+i4d_status i4d_kv_reset(i4d_ctx* c) {
+    if (!c) return I4D_ERR_ARG;
+    CK(cudaSetDevice(c->device));
+    CK(cudaMemsetAsync(c->d_kv, 0, c->kv_bytes, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return I4D_OK;
+}
+
+static i4d_status kv_addr(i4d_ctx* c, int bank, int layer, int lh, int token, size_t* off) {
+    if (bank < 0 || bank > 3 || layer < 0 || layer >= c->layers || lh < 0 || lh > 7 || token < 0 || token >= c->stride)
+        return fail(c, I4D_ERR_ARG, "KV record index out of range");
+    *off = ((((static_cast<size_t>(bank) * c->layers + layer) * kLocalHeads + lh) * c->stride) + token) * 320;
+    return I4D_OK;
+}
+
+i4d_status i4d_kv_read(i4d_ctx* c, int bank, int layer, int lh, int token, void* record) {
+    if (!c || !record) return c ? fail(c, I4D_ERR_ARG, "null record") : I4D_ERR_ARG;
+    size_t off;
+    const i4d_status st = kv_addr(c, bank, layer, lh, token, &off);
+    if (st != I4D_OK) return st;
+    CK(cudaSetDevice(c->device));
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaMemcpy(record, c->d_kv + off, 320, cudaMemcpyDeviceToHost));
+    return I4D_OK;
+}
+
+i4d_status i4d_kv_write(i4d_ctx* c, int bank, int layer, int lh, int token, const void* record) {
+    if (!c || !record) return c ? fail(c, I4D_ERR_ARG, "null record") : I4D_ERR_ARG;
+    size_t off;
+    const i4d_status st = kv_addr(c, bank, layer, lh, token, &off);
+    if (st != I4D_OK) return st;
+    CK(cudaSetDevice(c->device));
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaMemcpy(c->d_kv + off, record, 320, cudaMemcpyHostToDevice));
+    return I4D_OK;
+}
+
+i4d_status i4d_sync(i4d_ctx* c) {
+    if (!c) return I4D_ERR_ARG;
+    CK(cudaSetDevice(c->device));
+    return finish(c);
+}
+
+void* i4d_stream(i4d_ctx* c) { return c ? static_cast<void*>(c->stream) : nullptr; }
+
+static i4d_status capture(i4d_ctx* c, cudaGraphExec_t* out) {
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    const i4d_status st = enqueue_token(c);
+    cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+    if (st != I4D_OK) {
+        if (g) cudaGraphDestroy(g);
+        return st;
+    }
+    if (e != cudaSuccess) return fail(c, I4D_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+        *out = nullptr;
+        return fail(c, I4D_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    }
+    return I4D_OK;
+}
+
+i4d_status i4d_decode_token_async(i4d_ctx* c, uint32_t position, const float* residual_in_dev,
+                                  float* logits_out_dev) {
+    if (!c || !residual_in_dev || !logits_out_dev) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    if (!all_loaded(c)) return fail(c, I4D_ERR_STATE, "banks and rope LUT must be loaded before decoding");
+    if (position >= static_cast<uint32_t>(c->stride))
+        return fail(c, I4D_ERR_ARG, "position %u out of range (KV capacity %d)", position, c->stride);
+    CK(cudaSetDevice(c->device));
+    k_set_pos<<<1, 1, 0, c->stream>>>(c->d_pos, static_cast<int>(position));
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(c->d_resid, residual_in_dev, kDim * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
+    if (c->flags & I4D_FLAG_NO_GRAPH) {
+        const i4d_status st = enqueue_token(c);
+        if (st != I4D_OK) return st;
+    } else {
+        if (!c->graph_dev) {
+            const i4d_status st = capture(c, &c->graph_dev);
+            if (st != I4D_OK) return st;
+        }
+        CK(cudaGraphLaunch(c->graph_dev, c->stream));
+    }
+    CK(cudaMemcpyAsync(logits_out_dev, c->d_logits, kPVocab * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
+    return I4D_OK;
+}
+
+i4d_status i4d_profile_token(i4d_ctx* c, uint32_t position, const float* residual_in_dev, float* kernel_ms,
+                             uint32_t* launches) {
+    if (!c || !residual_in_dev || !kernel_ms || !launches) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    if (!all_loaded(c)) return fail(c, I4D_ERR_STATE, "banks and rope LUT must be loaded before decoding");
+    if (position >= static_cast<uint32_t>(c->stride)) return fail(c, I4D_ERR_ARG, "position out of range");
+    CK(cudaSetDevice(c->device));
+    for (cudaEvent_t& ev : c->prof_ev)
+        if (!ev) CK(cudaEventCreate(&ev));
+    k_set_pos<<<1, 1, 0, c->stream>>>(c->d_pos, static_cast<int>(position));
+    CK(cudaMemcpyAsync(c->d_resid, residual_in_dev, kDim * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
+    c->profiling = true;
+    c->prof_n = 0;
+    const i4d_status st = enqueue_token(c);
+    c->profiling = false;
+    if (st != I4D_OK) return st;
+    const i4d_status st2 = finish(c);
+    if (st2 != I4D_OK) return st2;
+    for (int k = 0; k < KC_COUNT; ++k) {
+        kernel_ms[k] = 0.0f;
+        launches[k] = 0;
+    }
+    for (int i = 0; i < c->prof_n; ++i) {
+        float ms = 0.0f;
+        CK(cudaEventElapsedTime(&ms, c->prof_ev[2 * i], c->prof_ev[2 * i + 1]));
+        kernel_ms[c->prof_class[i]] += ms;
+        launches[c->prof_class[i]] += 1;
+    }
+    return I4D_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------ op-level entry points
+
+namespace {
+struct DevBuf {
+    void* p = nullptr;
+    ~DevBuf() {
+        if (p) cudaFree(p);
+    }
+    template <typename T>
+    T* as() const { return static_cast<T*>(p); }
+};
+}  // namespace
+
+#define DEVBUF(name, bytes) \
+    DevBuf name;            \
+    CK(cudaMalloc(&name.p, (bytes)))
+
+extern "C" {
+
+i4d_status i4d_linear_bank(i4d_ctx* c, const void* superblocks, size_t n_bytes, int lit, int out_tiles,
+                           const int16_t* act_q, const uint8_t* act_e8m0, int hls_zero_start, float* partial_out) {
+    if (!c || !superblocks || !act_q || !act_e8m0 || !partial_out) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    if (lit < 1 || lit > 11 || out_tiles < 1 || out_tiles > 1008 || (out_tiles * lit) % 16 != 0)
+        return fail(c, I4D_ERR_ARG, "unsupported linear geometry: %d local input tiles, %d output tiles", lit, out_tiles);
+    const size_t need = static_cast<size_t>(out_tiles) * lit / 16 * 4224 * 64;
+    if (n_bytes != need) return fail(c, I4D_ERR_SIZE, "superblock stream has %zu bytes; expected %zu", n_bytes, need);
+    CK(cudaSetDevice(c->device));
+    DEVBUF(src, n_bytes);
+    DEVBUF(gem, n_bytes);
+    DEVBUF(aq, lit * 256 * sizeof(int16_t));
+    DEVBUF(ae, lit * 8);
+    CK(cudaMemcpy(src.p, superblocks, n_bytes, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(aq.p, act_q, lit * 256 * sizeof(int16_t), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(ae.p, act_e8m0, lit * 8, cudaMemcpyHostToDevice));
+    RelayoutArgs r;
+    r.src = src.as<uint8_t>();
+    r.dst = gem.as<uint8_t>();
+    r.unit_offset = 0;
+    r.lit = lit;
+    k_relayout<<<out_tiles * 4 * lit, 256, 0, c->stream>>>(r);
+    CK(cudaGetLastError());
+    LinearArgs a = {};
+    a.w = gem.as<uint8_t>();
+    a.bank_stride = 0;
+    a.nbanks = 1;
+    a.units = out_tiles * 4;
+    a.cpb = a.units < c->num_sms ? a.units : c->num_sms;
+    a.chunks = lit;
+    a.ns = ring_slots(lit);
+    a.in_kind = IN_ACT;
+    a.act_q = aq.as<int16_t>();
+    a.act_e = ae.as<uint8_t>();
+    a.act_bank_stride = 0;
+    a.hls_zero = hls_zero_start ? 1 : 0;
+    a.partials = c->d_partials;
+    a.epi = EPI_PARTIAL;
+    a.counters = c->d_counters;
+    a.expf = c->expf;
+    a.err = c->d_err;
+    CK(run_linear(c, a, false));
+    const i4d_status st = finish(c);
+    if (st != I4D_OK) return st;
+    CK(cudaMemcpy(partial_out, c->d_partials, static_cast<size_t>(out_tiles) * 128 * sizeof(float), cudaMemcpyDeviceToHost));
+    return I4D_OK;
+}
+
+i4d_status i4d_gemv(i4d_ctx* c, int layer, int mode, const int16_t* act_q, const uint8_t* act_e8m0, float* y_out,
+                    float* partials_out) {
+    if (!c || !act_q || !act_e8m0 || !y_out) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    if (mode < 0 || mode > 7 || (mode < 7 && (layer < 0 || layer >= c->layers)))
+        return fail(c, I4D_ERR_ARG, "bad layer %d / mode %d", layer, mode);
+    if (!c->bank_loaded[0] || !c->bank_loaded[1] || !c->bank_loaded[2] || !c->bank_loaded[3])
+        return fail(c, I4D_ERR_STATE, "all four banks must be loaded");
+    CK(cudaSetDevice(c->device));
+    const int rows = mode_rows(mode), cols = mode == 6 ? kFfn : kDim;
+    const int st = mode_stage(mode);
+    DEVBUF(aq, cols * sizeof(int16_t));
+    DEVBUF(ae, cols / 32);
+    DEVBUF(y, rows * sizeof(float));
+    CK(cudaMemcpy(aq.p, act_q, cols * sizeof(int16_t), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(ae.p, act_e8m0, cols / 32, cudaMemcpyHostToDevice));
+    LinearArgs a = base_linear(c, mode == 7 ? 0 : layer, st);
+    a.w += static_cast<size_t>(mode_unit_offset(mode)) * a.chunks * kChunkBytes;
+    a.units = rows / 32;
+    a.in_kind = IN_ACT;
+    a.act_q = aq.as<int16_t>();
+    a.act_e = ae.as<uint8_t>();
+    a.act_bank_stride = cols / 4;
+    a.epi = EPI_STORE;
+    a.out = y.as<float>();
+    CK(run_linear(c, a, false));
+    const i4d_status s2 = finish(c);
+    if (s2 != I4D_OK) return s2;
+    CK(cudaMemcpy(y_out, y.p, rows * sizeof(float), cudaMemcpyDeviceToHost));
+    if (partials_out)
+        CK(cudaMemcpy(partials_out, c->d_partials, 4ull * rows * sizeof(float), cudaMemcpyDeviceToHost));
+    return I4D_OK;
+}
+
+i4d_status i4d_quantize_g32(i4d_ctx* c, const float* x, int n, int16_t* q, uint8_t* e8m0) {
+    if (!c || !x || !q || !e8m0 || n <= 0 || n % 32) return c ? fail(c, I4D_ERR_ARG, "bad quantize arguments") : I4D_ERR_ARG;
+    CK(cudaSetDevice(c->device));
+    DEVBUF(dx, n * sizeof(float));
+    DEVBUF(dq, n * sizeof(int16_t));
+    DEVBUF(de, n / 32);
+    CK(cudaMemcpy(dx.p, x, n * sizeof(float), cudaMemcpyHostToDevice));
+    k_quant_g32<<<(n + 127) / 128, 128, 0, c->stream>>>(dx.as<float>(), n, dq.as<int16_t>(), de.as<uint8_t>());
+    CK(cudaGetLastError());
+    const i4d_status st = finish(c);
+    if (st != I4D_OK) return st;
+    CK(cudaMemcpy(q, dq.p, n * sizeof(int16_t), cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(e8m0, de.p, n / 32, cudaMemcpyDeviceToHost));
+    return I4D_OK;
+}
+
+i4d_status i4d_rms_quant(i4d_ctx* c, const float* x, const float* gamma, int16_t* q, uint8_t* e8m0) {
+    if (!c || !x || !gamma || !q || !e8m0) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    CK(cudaSetDevice(c->device));
+    DEVBUF(dx, kDim * sizeof(float));
+    DEVBUF(dg, kDim * sizeof(float));
+    DEVBUF(dr, 16);
+    DEVBUF(dq, kDim * sizeof(int16_t));
+    DEVBUF(de, kDim / 32);
+    CK(cudaMemcpy(dx.p, x, kDim * sizeof(float), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dg.p, gamma, kDim * sizeof(float), cudaMemcpyHostToDevice));
+    k_rms_recip<<<1, 32, 0, c->stream>>>(dx.as<float>(), dr.as<float>());
+    k_norm_quant<<<kDim / 128, 128, 0, c->stream>>>(dx.as<float>(), dg.as<float>(), dr.as<float>(), dq.as<int16_t>(),
+                                                    de.as<uint8_t>());
+    CK(cudaGetLastError());
+    const i4d_status st = finish(c);
+    if (st != I4D_OK) return st;
+    CK(cudaMemcpy(q, dq.p, kDim * sizeof(int16_t), cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(e8m0, de.p, kDim / 32, cudaMemcpyDeviceToHost));
+    return I4D_OK;
+}
+
+i4d_status i4d_attention(i4d_ctx* c, int layer, uint32_t position, const int32_t* q, const int32_t* k,
+                         const int32_t* v, int16_t* out_q, uint8_t* out_e8m0) {
+    if (!c || !q || !k || !v || !out_q || !out_e8m0) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    if (!c->rope_loaded) return fail(c, I4D_ERR_STATE, "rope LUT not loaded");
+    if (layer < 0 || layer >= c->layers || position >= static_cast<uint32_t>(c->stride))
+        return fail(c, I4D_ERR_ARG, "layer %d / position %u out of range", layer, position);
+    CK(cudaSetDevice(c->device));
+    DEVBUF(dqkv, 3ull * kDim * sizeof(int32_t));
+    DEVBUF(dq, kDim * sizeof(int16_t));
+    DEVBUF(de, kDim / 32);
+    CK(cudaMemcpy(dqkv.as<int32_t>(), q, kDim * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dqkv.as<int32_t>() + kDim, k, kDim * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dqkv.as<int32_t>() + 2 * kDim, v, kDim * 4, cudaMemcpyHostToDevice));
+    const int p = static_cast<int>(position);
+    CK(cudaMemcpy(c->d_pos, &p, sizeof(int), cudaMemcpyHostToDevice));
+    AttnArgs a = base_attn(c, layer);
+    a.partials = nullptr;
+    a.direct = dqkv.as<int32_t>();
+    a.out_q = dq.as<int16_t>();
+    a.out_e = de.as<uint8_t>();
+    k_attention<<<kHeads, kAttnThreads, 0, c->stream>>>(a);
+    CK(cudaGetLastError());
+    const i4d_status st = finish(c);
+    if (st != I4D_OK) return st;
+    CK(cudaMemcpy(out_q, dq.p, kDim * sizeof(int16_t), cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(out_e8m0, de.p, kDim / 32, cudaMemcpyDeviceToHost));
+    return I4D_OK;
+}
+
+i4d_status i4d_swiglu_quant(i4d_ctx* c, const float* gate, const float* up, int16_t* q, uint8_t* e8m0) {
+    if (!c || !gate || !up || !q || !e8m0) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    CK(cudaSetDevice(c->device));
+    DEVBUF(dg, kFfn * sizeof(float));
+    DEVBUF(du, kFfn * sizeof(float));
+    DEVBUF(dq, kFfn * sizeof(int16_t));
+    DEVBUF(de, kFfn / 32);
+    CK(cudaMemcpy(dg.p, gate, kFfn * sizeof(float), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(du.p, up, kFfn * sizeof(float), cudaMemcpyHostToDevice));
+    k_swiglu_quant<<<kFfn / 128, 128, 0, c->stream>>>(dg.as<float>(), du.as<float>(), kFfn, c->expf, dq.as<int16_t>(),
+                                                      de.as<uint8_t>());
+    CK(cudaGetLastError());
+    const i4d_status st = finish(c);
+    if (st != I4D_OK) return st;
+    CK(cudaMemcpy(q, dq.p, kFfn * sizeof(int16_t), cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(e8m0, de.p, kFfn / 32, cudaMemcpyDeviceToHost));
+    return I4D_OK;
+}
+
+i4d_status i4d_expf(i4d_ctx* c, const float* x, float* y, size_t n) {
+    if (!c || !x || !y) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    if (n == 0) return I4D_OK;
+    CK(cudaSetDevice(c->device));
+    DEVBUF(dx, n * sizeof(float));
+    DEVBUF(dy, n * sizeof(float));
+    CK(cudaMemcpy(dx.p, x, n * sizeof(float), cudaMemcpyHostToDevice));
+    k_expf<<<static_cast<unsigned>((n + 255) / 256), 256, 0, c->stream>>>(dx.as<float>(), dy.as<float>(), n, c->expf);
+    CK(cudaGetLastError());
+    const i4d_status st = finish(c);
+    if (st != I4D_OK) return st;
+    CK(cudaMemcpy(y, dy.p, n * sizeof(float), cudaMemcpyDeviceToHost));
+    return I4D_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,319 @@
+// i4d_linear.cuh -- fused dequant-GEMV stage kernel and the weight re-tiling.
+//
+// Replaces int4_linear_controller's reader / scale emitter / accumulator /
+// pair reducers (int4_linear_controller.cpp:253-951, 1339-1439).
+//
+// GEMV layout in HBM (written once at load by k_relayout from the unchanged
+// bank image): a "unit" is 32 output rows x one bank's local columns; it is
+// stored as chunks of 32 rows x 256 columns, 4224 bytes each:
+//   [  0,128): Q1.15 scales, int16 at (row*2 + g128)*2
+//   [128,4224): 8 groups x 32 rows x 16 bytes; the 16 bytes of (group, row)
+//               are its 32 INT4 weights: uint32 word j, byte b holds column
+//               4j+b in the low nibble as offset binary (w+8) and column
+//               16+4j+b in the high nibble as two's complement.
+// The units of one stage and bank are contiguous, so every CTA streams one
+// contiguous range with 1-D bulk copies.
+//
+// Arithmetic (bit-exact with emulator:216-264): per row and bank the G32
+// dot products are exact integers (dp4a on split activations a = 128*ah + al),
+// contrib = fl(float(dot) * fl(ws * as)), and the FP32 chain adds the
+// contributions in local-group order.  Rows are then combined as
+// (p0+p1)+(p2+p3) by whichever CTA completes a stripe last.
+#pragma once
+
+#include "i4d_device.cuh"
+#include "i4d_expf.cuh"
+
+namespace i4d {
+
+enum InKind : int { IN_ACT = 0, IN_RMS = 1 };
+enum EpiKind : int { EPI_PARTIAL = 0, EPI_STORE = 1, EPI_RESID = 2, EPI_SWIGLU = 3 };
+
+struct LinearArgs {
+    const uint8_t* w;      // unit 0 of bank 0 of this launch (GEMV layout)
+    size_t bank_stride;    // bytes from one bank's unit 0 to the next bank's
+    int nbanks;            // 1..4
+    int cpb;               // CTAs per bank; gridDim.x == nbanks * cpb
+    int units;             // units per bank
+    int chunks;            // chunks per unit: local columns / 256
+    int ns;                // ring slots
+    // input activation of this bank: IN_ACT reads act_q/act_e at
+    // bank*act_bank_stride; IN_RMS normalises resid with gamma and *recip.
+    int in_kind;
+    const int16_t* act_q;
+    const uint8_t* act_e;
+    int act_bank_stride;
+    const float* resid;
+    const float* gamma;
+    const float* recip;
+    int hls_zero;          // 1: chains start at the first contribution
+    float* partials;       // [bank][units*32]
+    int epi;
+    float* out;            // EPI_STORE: y; EPI_RESID: residual (updated in place)
+    float* recip_out;      // EPI_RESID: RMS reciprocal of the updated residual
+    int16_t* q_out;        // EPI_SWIGLU
+    uint8_t* e_out;
+    unsigned* counters;
+    ExpfFix expf;
+    unsigned* err;
+};
+
+struct LinearSmem {
+    uint8_t* ring;
+    uint64_t* full;
+    uint64_t* empty;
+    int8_t* act_hi;     // [groups][32]
+    uint8_t* act_lo;    // [groups][32]
+    int* corr;          // [groups]: 8 * sum of the group's first 16 values
+    float* act_scale;   // [groups]
+    float* contrib;     // [2][groups*32]
+};
+
+__host__ __device__ inline size_t linear_smem_bytes(int ns, int chunks) {
+    const size_t groups = static_cast<size_t>(chunks) * 8;
+    size_t b = static_cast<size_t>(ns) * kChunkBytes;
+    b += 2 * static_cast<size_t>(ns) * 8;
+    b += groups * 64 + groups * 8;
+    b += 2 * groups * 32 * 4;
+    return b;
+}
+
+__device__ __forceinline__ LinearSmem carve(uint8_t* base, int ns, int chunks) {
+    LinearSmem s;
+    const int groups = chunks * 8;
+    s.ring = base;
+    uint8_t* p = base + static_cast<size_t>(ns) * kChunkBytes;
+    s.full = reinterpret_cast<uint64_t*>(p);
+    s.empty = s.full + ns;
+    p += 2 * ns * 8;
+    s.act_hi = reinterpret_cast<int8_t*>(p);
+    s.act_lo = reinterpret_cast<uint8_t*>(p + groups * 32);
+    p += groups * 64;
+    s.corr = reinterpret_cast<int*>(p);
+    s.act_scale = reinterpret_cast<float*>(p + groups * 4);
+    p += groups * 8;
+    s.contrib = reinterpret_cast<float*>(p);
+    return s;
+}
+
+// Stores one lane's INT14 activation (value q of local group lg, column
+// `lane`) in split form, plus the group's scale and offset correction.
+__device__ __forceinline__ void put_act(const LinearSmem& s, int lg, int lane, int q, uint32_t e8m0) {
+    s.act_hi[lg * 32 + lane] = static_cast<int8_t>(q >> 7);
+    s.act_lo[lg * 32 + lane] = static_cast<uint8_t>(q & 127);
+    int lo16 = lane < 16 ? q : 0;
+    lo16 = __reduce_add_sync(0xffffffffu, lo16);
+    if (lane == 0) {
+        s.corr[lg] = 8 * lo16;
+        s.act_scale[lg] = e8m0_scale(e8m0);
+    }
+}
+
+// Exact G32 dot of one (row, group): weights w (16 bytes), split activations.
+__device__ __forceinline__ int group_dot(uint4 w, const int8_t* hi, const uint8_t* lo, int corr) {
+    const uint4 h0 = *reinterpret_cast<const uint4*>(hi);
+    const uint4 h1 = *reinterpret_cast<const uint4*>(hi + 16);
+    const uint4 l0 = *reinterpret_cast<const uint4*>(lo);
+    const uint4 l1 = *reinterpret_cast<const uint4*>(lo + 16);
+    int Lh = 0, Ll = 0, Hh = 0, Hl = 0;
+    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+    const uint32_t h0v[4] = {h0.x, h0.y, h0.z, h0.w};
+    const uint32_t h1v[4] = {h1.x, h1.y, h1.z, h1.w};
+    const uint32_t l0v[4] = {l0.x, l0.y, l0.z, l0.w};
+    const uint32_t l1v[4] = {l1.x, l1.y, l1.z, l1.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t u = wv[j] & 0x0F0F0F0Fu;  // (w + 8) of columns 4j..4j+3
+        const uint32_t h = wv[j] & 0xF0F0F0F0u;  // 16 * w of columns 16+4j..
+        Lh = dp4a_us(u, h0v[j], Lh);
+        Ll = dp4a_uu(u, l0v[j], Ll);
+        Hh = dp4a_ss(h, h1v[j], Hh);
+        Hl = dp4a_su(h, l1v[j], Hl);
+    }
+    return ((Lh + (Hh >> 4)) << 7) + Ll + (Hl >> 4) - corr;
+}
+
+// Epilogue of one finished unit, run by the warp that chained it.
+__device__ __noinline__ void linear_epilogue(const LinearArgs& a, int bank, int unit, float acc) {
+    const int lane = threadIdx.x & 31;
+    const int rows_total = a.units * 32;
+    a.partials[static_cast<size_t>(bank) * rows_total + unit * 32 + lane] = acc;
+    if (a.epi == EPI_PARTIAL) return;
+    __threadfence();
+    __syncwarp();
+    const int stripes = a.epi == EPI_SWIGLU ? a.units / 2 : a.units;
+    const int stripe = unit % stripes;
+    const unsigned need = static_cast<unsigned>(a.epi == EPI_SWIGLU ? 2 * a.nbanks : a.nbanks);
+    unsigned old = 0;
+    if (lane == 0) old = atomicAdd(&a.counters[stripe], 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old + 1 != need) return;
+    __threadfence();
+    if (lane == 0) a.counters[stripe] = 0;
+    const float* P = a.partials;
+    if (a.epi == EPI_STORE) {
+        const int row = stripe * 32 + lane;
+        a.out[row] = a.nbanks == 4 ? combine4(P, rows_total, row) : P[row];
+        return;
+    }
+    if (a.epi == EPI_SWIGLU) {
+        const int gr = stripe * 32 + lane, ur = (stripes + stripe) * 32 + lane;
+        const float g = combine4(P, rows_total, gr);
+        const float u = combine4(P, rows_total, ur);
+        uint32_t e8;
+        const int q = quantize_g32_lane(swiglu1(g, u, a.expf), &e8);
+        a.q_out[stripe * 32 + lane] = static_cast<int16_t>(q);
+        if (lane == 0) a.e_out[stripe] = static_cast<uint8_t>(e8);
+        return;
+    }
+    // EPI_RESID: residual += y, then the RMS reciprocal once every stripe is in.
+    const int row = stripe * 32 + lane;
+    a.out[row] = __fadd_rn(a.out[row], combine4(P, rows_total, row));
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) old = atomicAdd(&a.counters[kCounterLevel2], 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old + 1 != static_cast<unsigned>(stripes)) return;
+    __threadfence();
+    if (lane == 0) a.counters[kCounterLevel2] = 0;
+    const float r = rms_recip_warp(a.out);
+    if (lane == 0) *a.recip_out = r;
+}
+
+__global__ void __launch_bounds__(kLinearThreads, 2) k_linear(const LinearArgs a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    const int groups = a.chunks * 8;
+    LinearSmem s = carve(smem_raw, a.ns, a.chunks);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bank = blockIdx.x / a.cpb, c = blockIdx.x % a.cpb;
+    const int u0 = static_cast<int>((static_cast<long long>(c) * a.units) / a.cpb);
+    const int u1 = static_cast<int>((static_cast<long long>(c + 1) * a.units) / a.cpb);
+    const int nchunks = (u1 - u0) * a.chunks;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < a.ns; ++i) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.empty[i], kConsumerWarps);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+    pdl_trigger();
+
+    if (warp == 0) {
+        // Producer: weights never depend on the previous kernel, so streaming
+        // starts before griddepcontrol.wait.
+        if (lane == 0) {
+            const uint8_t* src = a.w + static_cast<size_t>(bank) * a.bank_stride +
+                                 static_cast<size_t>(u0) * a.chunks * kChunkBytes;
+            int slot = 0;
+            uint32_t phase = 0;
+            for (int i = 0; i < nchunks; ++i) {
+                if (i >= a.ns) mbar_wait(&s.empty[slot], phase ^ 1u, a.err, kErrWaitEmpty);
+                mbar_arrive_expect_tx(&s.full[slot], kChunkBytes);
+                bulk_g2s(s.ring + static_cast<size_t>(slot) * kChunkBytes,
+                         src + static_cast<size_t>(i) * kChunkBytes, kChunkBytes, &s.full[slot]);
+                if (++slot == a.ns) { slot = 0; phase ^= 1u; }
+            }
+        }
+        return;
+    }
+
+    // Consumers.
+    pdl_wait();
+    const int cw = warp - 1;
+    for (int lg = cw; lg < groups; lg += kConsumerWarps) {
+        uint32_t e8;
+        int q;
+        if (a.in_kind == IN_RMS) {
+            const int col = bank * groups * 32 + lg * 32 + lane;
+            const float v = __fmul_rn(__fmul_rn(a.resid[col], *a.recip), a.gamma[col]);
+            q = quantize_g32_lane(v, &e8);
+        } else {
+            const size_t base = static_cast<size_t>(bank) * a.act_bank_stride;
+            q = a.act_q[base + lg * 32 + lane];
+            e8 = a.act_e[base / 32 + lg];
+        }
+        put_act(s, lg, lane, q, e8);
+    }
+    consumer_bar();
+
+    int slot = 0;
+    uint32_t phase = 0;
+    for (int u = u0; u < u1; ++u) {
+        float* contrib = s.contrib + ((u - u0) & 1) * groups * 32;
+        for (int j = 0; j < a.chunks; ++j) {
+            mbar_wait(&s.full[slot], phase, a.err, kErrWaitFull);
+            const uint8_t* ch = s.ring + static_cast<size_t>(slot) * kChunkBytes;
+            const int lg = j * 8 + cw;
+            const uint4 wv = *reinterpret_cast<const uint4*>(ch + kChunkScaleBytes + (cw * 32 + lane) * 16);
+            const int16_t raw = reinterpret_cast<const int16_t*>(ch)[lane * 2 + (cw >> 2)];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.empty[slot]);
+            const int dot = group_dot(wv, s.act_hi + lg * 32, s.act_lo + lg * 32, s.corr[lg]);
+            const float ws = __fmul_rn(static_cast<float>(raw), 1.0f / 32768.0f);
+            contrib[lg * 32 + lane] = __fmul_rn(static_cast<float>(dot), __fmul_rn(ws, s.act_scale[lg]));
+            if (++slot == a.ns) { slot = 0; phase ^= 1u; }
+        }
+        consumer_bar();
+        if (cw == ((u - u0) & (kConsumerWarps - 1))) {
+            float acc = contrib[lane];
+            if (!a.hls_zero) acc = __fadd_rn(0.0f, acc);
+            for (int lg = 1; lg < groups; ++lg) acc = __fadd_rn(acc, contrib[lg * 32 + lane]);
+            linear_epilogue(a, bank, u, acc);
+        }
+    }
+}
+
+// ------------------------------------------------------------- re-tiling
+
+struct RelayoutArgs {
+    const uint8_t* src;    // the bank's superblock stream of one matrix
+    uint8_t* dst;          // this bank's unit 0 of the stage in the GEMV layout
+    int unit_offset;       // first unit of this matrix inside the stage
+    int lit;               // local input tiles (chunks per unit)
+};
+
+// One block per (stripe, chunk); thread = (group g, row).  Reads the
+// reference tile words (autoround_pack_llama2_u250.py:114-189,
+// emulator:840-888) and writes the GEMV layout above.
+__global__ void __launch_bounds__(256) k_relayout(const RelayoutArgs a) {
+    const int stripe = blockIdx.x / a.lit, j = blockIdx.x % a.lit;
+    const int g = threadIdx.x >> 5, row = threadIdx.x & 31;
+    const int ot = stripe >> 2, sub = stripe & 3;
+    const int t = ot * a.lit + j;
+    const uint8_t* blk = a.src + static_cast<size_t>(t / 16) * 4224 * 64;
+    const int tib = t % 16;
+    const int trow = sub * 32 + row;
+    uint8_t* chunk = a.dst + (static_cast<size_t>(a.unit_offset + stripe) * a.lit + j) * kChunkBytes;
+    if (threadIdx.x < 64) {
+        const int r = threadIdx.x >> 1, g128 = threadIdx.x & 1;
+        const int tr = sub * 32 + r;
+        const int16_t v = *reinterpret_cast<const int16_t*>(blk + (tib * 8 + tr / 16) * 64 + (2 * (tr % 16) + g128) * 2);
+        reinterpret_cast<int16_t*>(chunk)[r * 2 + g128] = v;
+    }
+    const uint8_t* word = blk + 128 * 64 + (static_cast<size_t>(tib) * 256 + g * 32 + trow / 4) * 64;
+    const int r4 = trow & 3;
+    int wv[32];
+#pragma unroll
+    for (int l = 0; l < 32; ++l) {
+        const uint8_t byte = word[2 * l + (r4 >> 1)];
+        const int nib = (r4 & 1) ? (byte & 15) : (byte >> 4);
+        wv[l] = nib >= 8 ? nib - 16 : nib;
+    }
+    uint32_t out[4];
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+        uint32_t v = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const uint32_t lo = static_cast<uint32_t>(wv[4 * jj + b] + 8) & 15u;
+            const uint32_t hi = static_cast<uint32_t>(wv[16 + 4 * jj + b]) & 15u;
+            v |= (lo | (hi << 4)) << (8 * b);
+        }
+        out[jj] = v;
+    }
+    *reinterpret_cast<uint4*>(chunk + kChunkScaleBytes + (g * 32 + row) * 16) = make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+}  // namespace i4d

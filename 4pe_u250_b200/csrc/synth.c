@@ -137,7 +137,9 @@ static void pack_tile(uint8_t* dst, int t, int lit, const int8_t* tw /*128x256*/
  * bank; M and K are the padded sizes.  Mirrors pack_matrix_to_super_blocks. */
 void i4s_pack_arrays(const int8_t* w, const int16_t* s, int M, int K, int bank,
                      int out_tiles, int lit, uint8_t* dst) {
-    const int tiles = out_tiles * lit;
+    /* Only whole superblocks are written, as block_count = tiles // 16 in the
+     * reference packer (autoround_pack_llama2_u250.py:119-120). */
+    const int tiles = out_tiles * lit / 16 * 16;
 #pragma omp parallel for schedule(static)
     for (int t = 0; t < tiles; ++t) {
         int8_t tw[128 * 256];

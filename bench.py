@@ -1,0 +1,334 @@
+#!/usr/bin/env python
+"""Benchmark: batch-1 INT4 Llama-2-7B decode.
+
+One step = one decode token through all 32 layers and the LM head
+(int4_decoder_controller.cpp:138-234) on seeded synthetic weights in the
+reference bank format: a 16-token prompt of ids uniform in [3, 31999], then
+greedy tokens, KV capacity 2048, seed 2.  Warm-up steps are the first W
+positions; the K timed steps are positions W..W+K-1 (defaults: the 16 prompt
+positions, then 128 decode steps).
+
+value  tokens/s over K steps with inputs resident in HBM (embedding rows
+       already on the device), CUDA events on the library's stream, max over
+       ranks.
+e2e    the same K steps through the public C ABI i4d_decode_token with host
+       buffers (residual in, logits out copied every step).
+Weights (3.46 GB per token) exceed the 126 MB L2, so no flush is needed.
+
+`--impl reference` times the reference's own CPU implementation (the
+emulator compiled from its source into oracle/_ref) on the host cores.
+"""
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "batch-1 INT4 Llama-2-7B decode tokens/s"
+UNIT = "tokens/s"
+PROMPT = 16
+# Algorithmic bytes of each GEMV launch (GEMV layout = bank data regions).
+GEMV_BYTES = {"qkv_gemv": 3 * 8_650_752, "o_gemv": 8_650_752, "gate_up_gemv": 2 * 23_789_568,
+              "down_gemv": 23_789_568, "logits_gemv": 68_124_672}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", default="i4d", choices=["i4d", "reference"])
+    ap.add_argument("--seed", type=int, default=2)
+    ap.add_argument("--kv-capacity", type=int, default=2048)
+    ap.add_argument("--cpu-layers", type=int, default=4, help="layers in the CPU baseline sample")
+    ap.add_argument("--cpu-steps", type=int, default=6)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--soak", type=int, default=400, help="untimed steps before timing (clock steady state)")
+    return ap.parse_args()
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="i4d_clocks_", suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = [r.split(",") for r in open(self.path).read().strip().splitlines() if r.strip()]
+        os.unlink(self.path)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for n, v in zip(names, r[5:9]):
+                    if v.strip() == "Active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peak():
+    try:
+        p = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def committed_traffic():
+    """DRAM bytes per GEMV launch from the committed ncu summary, if any."""
+    try:
+        return json.load(open(os.path.join(ROOT, "profiles", "k_linear_traffic.json")))
+    except (OSError, ValueError):
+        return None
+
+
+def write_model_dir(d, banks, emb, lut):
+    for p, b in enumerate(banks):
+        b.tofile(os.path.join(d, f"model_bank{p}.bin"))
+    emb.tofile(os.path.join(d, "embeddings.bin"))
+    with open(os.path.join(d, "rope_lut.bin"), "wb") as f:
+        f.write(lut)
+
+
+def cpu_sample(banks, emb, lut, tokens, layers, steps):
+    """Times the reference emulator (or, without it, the oracle port) on a
+    bounded sample: `layers` decoder layers + LM head per token, `steps`
+    tokens; the per-token time is scaled to 32 layers by MAC count."""
+    from oracle import RefEmulator, Oracle, ref_available
+    macs_layer = 4 * 4096 * 4096 + 3 * 11264 * 4096
+    macs_head = 32256 * 4096
+    scale = (32 * macs_layer + macs_head) / (layers * macs_layer + macs_head)
+    if ref_available():
+        tmp = "/dev/shm" if os.path.isdir("/dev/shm") else None
+        with tempfile.TemporaryDirectory(prefix="i4d_ref_", dir=tmp) as d:
+            write_model_dir(d, banks, emb, lut)
+            ref = RefEmulator()
+            ref.load(d, layers, 2048)
+            ref.forward(tokens[0], 0)
+            t0 = time.perf_counter()
+            for i in range(steps):
+                ref.forward(tokens[i + 1], i + 1)
+            dt = (time.perf_counter() - t0) / steps
+            cores = ref.threads()
+        kind = "reference"
+    else:
+        orc = Oracle()
+        tables = orc.rope_tables(lut)
+        kv = orc.kv_store(layers, 2048)
+        t0 = time.perf_counter()
+        for i in range(steps):
+            orc.forward(banks, tables, kv, layers, 2048, i, emb[tokens[i] * 4096:(tokens[i] + 1) * 4096])
+        dt = (time.perf_counter() - t0) / steps
+        cores = os.cpu_count()
+        kind = "port"
+    per_token = dt * scale
+    return {"value": 1.0 / per_token, "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"{steps} decode steps of {layers} layers + LM head on the same synthetic model, "
+                      f"per-token time scaled x{scale:.2f} to 32 layers by MAC count"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    syn = importlib.import_module("4pe_u250_b200.synth")
+    F = importlib.import_module("4pe_u250_b200.formats")
+    banks = syn.model_banks(args.cpu_layers, args.seed)
+    syn.fill_matrix(banks, 0, F.MODE_LOGITS, args.seed)
+    emb = syn.embeddings(args.seed)
+    lut = F.generate_rope_lut()
+    prompt = np.random.default_rng(args.seed).integers(3, 32000, size=PROMPT).tolist()
+    tokens = (prompt * ((args.steps + args.warmup) // PROMPT + 2))[: args.steps + args.warmup + 1]
+    r = cpu_sample(banks, emb, lut, tokens, args.cpu_layers, min(args.steps, args.cpu_steps))
+    line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / r["value"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4xint14/fp32",
+            "data": "synthetic", "config": workload_config(args, world),
+            "cpu_baseline": r, "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                                       "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args, world):
+    return {"workload": "config3: full 32-layer INT4 Llama-2-7B decode, 16-token prompt then greedy, "
+                        "KV capacity 2048, seed 2",
+            "layers": 32, "kv_capacity": args.kv_capacity, "positions": [args.warmup, args.warmup + args.steps - 1],
+            "parallelism": f"replicas{world}" if world > 1 else "1gpu",
+            "l2": "weights 3.46 GB/token exceed the 126 MB L2 (no flush needed)"}
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        if world > 1:
+            import torch.distributed as dist
+            dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=600))
+        run_reference(args, world, rank)
+        return
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    pkg = importlib.import_module("4pe_u250_b200")
+    syn = importlib.import_module("4pe_u250_b200.synth")
+    F = pkg.formats
+    total = args.warmup + args.steps
+    assert total <= args.kv_capacity
+
+    banks = syn.model_banks(32, args.seed)
+    emb = syn.embeddings(args.seed)
+    lut = F.generate_rope_lut()
+    ctx = pkg.Context(device=local, num_layers=32, kv_capacity=args.kv_capacity)
+    ctx.load_banks(banks)
+    ctx.load_rope(lut)
+    stream = torch.cuda.ExternalStream(ctx.stream_handle())
+    prompt = np.random.default_rng(args.seed).integers(3, 32000, size=PROMPT).tolist()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- e2e through the public C ABI (host buffers), greedy ----
+    tokens, nxt, last_logits = [], None, None
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for pos in range(total):
+        if pos == args.warmup:
+            barrier()
+            ev0.record(stream)
+        tok = prompt[pos] if pos < PROMPT else nxt
+        tokens.append(tok)
+        last_logits = ctx.decode_token(pos, emb[tok * 4096:(tok + 1) * 4096])
+        nxt = int(np.argmax(last_logits[:F.VOCAB]))
+    ev1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1))
+
+    # ---- device-resident replay of the same token sequence ----
+    d_emb = torch.from_numpy(emb).to("cuda")
+    d_logits = torch.empty(F.PADDED_VOCAB, dtype=torch.float32, device="cuda")
+    row = lambda t: d_emb.data_ptr() + t * 4096 * 4  # noqa: E731
+    for pos in range(args.warmup):
+        ctx.decode_token_async(pos, row(tokens[pos]), d_logits.data_ptr())
+    ctx.sync()
+    clocks = Clocks(local)
+    clocks.start()
+    for i in range(args.soak):  # untimed, same positions: brings clocks to steady state
+        pos = args.warmup + i % args.steps
+        ctx.decode_token_async(pos, row(tokens[pos]), d_logits.data_ptr())
+    ctx.sync()
+    barrier()
+    ev0.record(stream)
+    for pos in range(args.warmup, total):
+        ctx.decode_token_async(pos, row(tokens[pos]), d_logits.data_ptr())
+    ev1.record(stream)
+    ctx.sync()
+    barrier()
+    clk = clocks.stop()
+    dev_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    replay_ok = bool(np.array_equal(d_logits.cpu().numpy(), last_logits))
+
+    # ---- per-kernel device times (eager, events around every launch) ----
+    prof = None
+    for _ in range(3):
+        p = ctx.profile_token(args.warmup + args.steps // 2, row(tokens[args.warmup]))
+        if prof is None or sum(v[0] for v in p.values()) < sum(v[0] for v in prof.values()):
+            prof = p
+    gemv_ms = sum(prof[k][0] for k in GEMV_BYTES)
+    gemv_launches = sum(prof[k][1] for k in GEMV_BYTES)
+    gemv_bytes = sum(GEMV_BYTES[k] * prof[k][1] for k in GEMV_BYTES)
+    peak, peak_kind = measured_peak()
+    achieved = gemv_bytes / (gemv_ms * 1e-3) / 1e9
+    traffic = committed_traffic()
+
+    value = world * args.steps / (dev_ms * 1e-3)
+    e2e = world * args.steps / (e2e_ms * 1e-3)
+    launches_per_step = 2 + 5 * 32
+    mid = args.warmup + args.steps // 2
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int4xint14/fp32", "data": "synthetic",
+        "config": workload_config(args, world),
+        "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4096 * 4 + 4,
+                "d2h_bytes_per_step": F.PADDED_VOCAB * 4 + 4096 * 4 + 4, "ms_per_step": e2e_ms / args.steps},
+        "roofline": {"bound": "hbm", "kernel": "k_linear (fused dequant-GEMV)", "achieved": achieved,
+                     "peak": peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback", "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic["bytes_per_launch_avg"] if traffic else None,
+                     "algorithmic_bytes_per_token_gemv": gemv_bytes, "gemv_ms_per_token": gemv_ms,
+                     "gemv_launches_per_token": gemv_launches},
+        "token_roofline": {"bytes_per_token": F.token_bytes(mid), "achieved_gbs":
+                           F.token_bytes(mid) / (dev_ms / args.steps * 1e-3) / 1e9,
+                           "frac": F.token_bytes(mid) / (dev_ms / args.steps * 1e-3) / 1e9 / peak},
+        "kernel_ms_per_token": {k: v[0] for k, v in prof.items()},
+        "gpu_launches": launches_per_step * args.steps,
+        "replay_matches_e2e": replay_ok,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_sample(banks, emb, lut, tokens, args.cpu_layers, args.cpu_steps)
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

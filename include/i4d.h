@@ -1,0 +1,183 @@
+/*
+ * i4d.h -- C ABI of the B200-native INT4 Llama-2-7B batch-1 decode path.
+ *
+ * Drop-in for the per-token decode of the 4PE_U250 design: it consumes the
+ * reference's unchanged model images (model_bank{0..3}.bin, rope_lut.bin,
+ * embeddings.bin) and keeps its launch contract (scalar position in, logits
+ * shards out).  Plain C: pointers and sizes only, integer status codes, no
+ * exceptions cross this boundary.
+ *
+ * A context is not thread-safe; every call on it is serialised on the
+ * context's CUDA stream and returns once its host buffers may be reused.
+ * Reference interfaces replaced are cited as path:line inside the reference
+ * project.
+ */
+#ifndef I4D_H
+#define I4D_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int i4d_status;
+#define I4D_OK 0
+#define I4D_ERR_ARG 1     /* bad argument: range, null pointer, mode */
+#define I4D_ERR_SIZE 2    /* buffer size differs from the format's size */
+#define I4D_ERR_CUDA 3    /* a CUDA call failed (message in i4d_last_error) */
+#define I4D_ERR_TIMEOUT 4 /* a bounded device-side wait gave up */
+#define I4D_ERR_STATE 5   /* call out of order (e.g. decode before loading) */
+#define I4D_ERR_NOMEM 6   /* device or pinned host allocation failed */
+
+/* Geometry of the reference model (int4_types.hpp:33-56,
+ * int4_model_layout.hpp:151-173, decode_host.cpp:63-119). */
+#define I4D_DIM 4096
+#define I4D_FFN 11264          /* 11008 padded to 44 x 256 */
+#define I4D_VOCAB 32000
+#define I4D_PADDED_VOCAB 32256 /* 4 logits shards of 8064 */
+#define I4D_BANKS 4
+#define I4D_LAYERS 32
+#define I4D_MAX_POSITIONS 4096
+#define I4D_BANK_BYTES 865071104ULL        /* dense image, 13,516,736 words */
+#define I4D_LEGACY_BANK_BYTES 891277312ULL /* rejected, as decode_host does */
+#define I4D_ROPE_BYTES 2097152ULL
+#define I4D_KV_RECORD_BYTES 320            /* metadata, K0, K1, V0, V1 words */
+
+/* Linear modes (int4_types.hpp:152-177). */
+#define I4D_MODE_Q 0
+#define I4D_MODE_K 1
+#define I4D_MODE_V 2
+#define I4D_MODE_O 3
+#define I4D_MODE_GATE 4
+#define I4D_MODE_UP 5
+#define I4D_MODE_DOWN 6
+#define I4D_MODE_LOGITS 7
+
+/* Context flags. */
+#define I4D_FLAG_NO_GRAPH 1u /* launch the token schedule eagerly */
+#define I4D_FLAG_NO_PDL 2u   /* no programmatic dependent launch */
+
+typedef struct i4d_ctx i4d_ctx;
+
+typedef struct i4d_config {
+    int device;       /* CUDA device ordinal */
+    int num_layers;   /* decoder layers run per token, 1..32 (emulator g_num_layers) */
+    int kv_capacity;  /* token slots per (layer, head), 1..4096; 0 = 4096 as the HLS */
+    unsigned flags;   /* I4D_FLAG_* */
+} i4d_config;
+
+/* Creates a context on cfg->device and allocates its device memory (weights,
+ * KV cache, workspace).  Replaces decode_host.cpp:1161-1294 (device open,
+ * buffer allocation, KV zeroing). */
+i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out);
+void i4d_destroy(i4d_ctx* ctx);
+/* Message of the last failing call on ctx (never NULL). */
+const char* i4d_last_error(const i4d_ctx* ctx);
+
+/* Loads one unchanged bank image (n must be I4D_BANK_BYTES; the legacy
+ * 891,277,312-byte layout is rejected with I4D_ERR_SIZE as
+ * decode_host.cpp:1218-1227 detects it).  The image is re-tiled on the device
+ * into the GEMV layout; gammas are extracted from its norm words.
+ * Replaces load_bo_from_file(modelN, ...) decode_host.cpp:1261-1268. */
+i4d_status i4d_load_bank(i4d_ctx* ctx, int bank, const void* bytes, size_t n);
+
+/* Loads rope_lut.bin (n must be I4D_ROPE_BYTES).  Replaces
+ * load_bo_from_file(ropeN, ...) decode_host.cpp:1282-1289. */
+i4d_status i4d_load_rope(i4d_ctx* ctx, const void* bytes, size_t n);
+
+/* Loads embeddings.bin (n_floats must be 32000*4096) into device memory.
+ * Replaces load_embeddings, decode_host.cpp:1296. */
+i4d_status i4d_load_embeddings(i4d_ctx* ctx, const float* emb, size_t n_floats);
+
+/* One decode step: the reference launch contract of
+ * int4_decoder_pe{0..3}_kernel (int4_decoder_multikernel.hpp:11-65) as driven
+ * by run_one_token (decode_host.cpp:1340-1556).  residual_in is the
+ * embedding row (the four 1024-float residual shards concatenated,
+ * decode_host.cpp:666-676); logits_out receives the 32256 padded logits
+ * (four 8064-float shards concatenated, decode_host.cpp:690-701);
+ * residual_out (may be NULL) the final residual.  position must be below the
+ * KV capacity; every position < `position` must already hold this
+ * sequence's KV records. */
+i4d_status i4d_decode_token(i4d_ctx* ctx, uint32_t position, const float* residual_in,
+                            float* logits_out, float* residual_out);
+
+/* Device-resident form of i4d_decode_token for pipelines that keep their
+ * data on the GPU: residual_in_dev / logits_out_dev are device pointers
+ * (4096 / 32256 floats).  The step is only enqueued on the context stream;
+ * i4d_sync waits for it and reports device-side errors.  No reference
+ * counterpart (the XRT host always stages through host memory). */
+i4d_status i4d_decode_token_async(i4d_ctx* ctx, uint32_t position, const float* residual_in_dev,
+                                  float* logits_out_dev);
+
+/* The context's CUDA stream (a cudaStream_t), for callers that record their
+ * own events around i4d_decode_token_async.  No reference counterpart. */
+void* i4d_stream(i4d_ctx* ctx);
+
+/* Measurement hook: runs one step eagerly with a CUDA event pair around every
+ * kernel and returns the device time per kernel class in kernel_ms[7] and the
+ * launch counts in launches[7]: 0 QKV GEMV, 1 attention, 2 O GEMV,
+ * 3 GATE/UP GEMV, 4 DOWN GEMV, 5 LOGITS GEMV, 6 RMS.  No reference
+ * counterpart (decode_host's verbose timing, decode_host.cpp:1539-1553, is
+ * host-side only). */
+i4d_status i4d_profile_token(i4d_ctx* ctx, uint32_t position, const float* residual_in_dev,
+                             float* kernel_ms, uint32_t* launches);
+
+/* Clears the KV cache (decode_host.cpp:1291-1294 zero_bo). */
+i4d_status i4d_kv_reset(i4d_ctx* ctx);
+/* Reads / writes one 320-byte KV record in the HLS layout
+ * (swiftkv_attention.hpp:21-36): bank, layer, local head 0..7, token. */
+i4d_status i4d_kv_read(i4d_ctx* ctx, int bank, int layer, int local_head, int token, void* record);
+i4d_status i4d_kv_write(i4d_ctx* ctx, int bank, int layer, int local_head, int token, const void* record);
+/* Waits for all work on the context. */
+i4d_status i4d_sync(i4d_ctx* ctx);
+
+/* ---- Op-level entry points (the per-stage services of the reference) ---- */
+
+/* One bank's linear stage over a raw superblock stream (n_bytes =
+ * out_tiles*local_in_tiles/16 superblocks): FP32 partials of every output
+ * row, chained over the bank's G32 groups in order.  Replaces
+ * int4_linear_local_stage_peN (int4_linear_controller.hpp:50-62).
+ * act_q: local_in_tiles*256 INT14 values; act_e8m0: one E8M0 byte per G32
+ * group (scale 2^(byte-140)).  hls_zero_start != 0 starts each row chain
+ * from its first contribution as the HLS does; 0 starts from +0.0f as the
+ * software emulator does (they differ only in the sign of an all-zero sum). */
+i4d_status i4d_linear_bank(i4d_ctx* ctx, const void* superblocks, size_t n_bytes,
+                           int local_in_tiles, int out_tiles, const int16_t* act_q,
+                           const uint8_t* act_e8m0, int hls_zero_start, float* partial_out);
+
+/* Full 4-bank GEMV of a loaded matrix: y = (p0+p1)+(p2+p3) (pair reducers and
+ * finalizer, int4_linear_controller.hpp:64-93; emulator sharded_gemv_4pe).
+ * partials_out ([4][rows], may be NULL) receives the per-bank partials. */
+i4d_status i4d_gemv(i4d_ctx* ctx, int layer, int mode, const int16_t* act_q,
+                    const uint8_t* act_e8m0, float* y_out, float* partials_out);
+
+/* G32 E8M0/INT14 activation quantizer (int4_decoder_blocks.cpp:22-73); n % 32 == 0. */
+i4d_status i4d_quantize_g32(i4d_ctx* ctx, const float* x, int n, int16_t* q, uint8_t* e8m0);
+
+/* RMSNorm + quantize of a 4096 residual (int4_local_sumsq, pair schedule and
+ * int4_local_rms_normalize_quantize, int4_decoder_blocks.hpp:77-125). */
+i4d_status i4d_rms_quant(i4d_ctx* ctx, const float* x, const float* gamma, int16_t* q,
+                         uint8_t* e8m0);
+
+/* SwiftKV attention of one layer at `position` (int4_swiftkv_attention_pe0..3,
+ * swiftkv_attention.hpp:167-209): q, k, v are the Q15.17 projections before
+ * RoPE (4096 each); RoPE, the KV record write and the scan run on the device.
+ * Output: INT14[4096] + E8M0[128] for the O projection. */
+i4d_status i4d_attention(i4d_ctx* ctx, int layer, uint32_t position, const int32_t* q,
+                         const int32_t* k, const int32_t* v, int16_t* out_q, uint8_t* out_e8m0);
+
+/* SwiGLU + quantize over 11264 rows (int4_local_swiglu_quantize,
+ * int4_decoder_blocks.cpp:487-521). */
+i4d_status i4d_swiglu_quant(i4d_ctx* ctx, const float* gate, const float* up, int16_t* q,
+                            uint8_t* e8m0);
+
+/* The device expf used by SwiGLU, element-wise (test hook: its results must
+ * equal the host C library's expf, which the reference emulator calls). */
+i4d_status i4d_expf(i4d_ctx* ctx, const float* x, float* y, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,254 @@
+"""CPU parity checkers (TEST INFRASTRUCTURE ONLY).
+
+``Oracle`` wraps this repository's C restatement (oracle/i4d_oracle.c);
+``RefEmulator`` wraps the unmodified reference emulator compiled from its own
+source into oracle/_ref/ (present when the reference tree was available at
+build time).  Only tests/, __graft_entry__.smoke() and bench.py's CPU
+baseline use them; the product library never does.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "_build", "libi4d_oracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libref_emulator.so")
+
+P = ctypes.c_void_p
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data
+
+
+class Oracle:
+    def __init__(self):
+        if not os.path.exists(ORACLE_SO):
+            raise RuntimeError(f"{ORACLE_SO} missing: run `make -C oracle`")
+        L = ctypes.CDLL(ORACLE_SO)
+        sigs = {
+            "i4o_quantize_g32": [P, ctypes.c_int, P, P],
+            "i4o_rmsnorm_quantize": [P, P, P, P, P],
+            "i4o_linear_bank": [P, ctypes.c_int, ctypes.c_int, P, P, ctypes.c_int, P],
+            "i4o_gemv": [P, ctypes.c_int, ctypes.c_int, P, P, P, P],
+            "i4o_decode_rope_lut": [P, P, P],
+            "i4o_rope_q17": [P, P, P],
+            "i4o_kv_write_record": [P, P, P],
+            "i4o_attention": [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P, P, P],
+            "i4o_swiglu": [P, P, ctypes.c_int, P],
+            "i4o_read_gamma": [P, ctypes.c_int, ctypes.c_int, P],
+            "i4o_forward": [P, P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P],
+            "i4o_float_to_q17_array": [P, ctypes.c_int, P],
+            "i4o_expf_array": [P, P, ctypes.c_size_t],
+            "i4o_argmax": [P, ctypes.c_int],
+            "i4o_exp_negative_q17": [ctypes.c_int32],
+        }
+        for k, v in sigs.items():
+            getattr(L, k).argtypes = v
+        L.i4o_argmax.restype = ctypes.c_int
+        L.i4o_exp_negative_q17.restype = ctypes.c_uint32
+        self.L = L
+        self._rope = None
+
+    @staticmethod
+    def _banks(banks):
+        return (ctypes.c_void_p * 4)(*[b.ctypes.data for b in banks])
+
+    def quantize_g32(self, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        q = np.empty(x.size, np.int16)
+        e = np.empty(x.size // 32, np.uint8)
+        self.L.i4o_quantize_g32(x.ctypes.data, x.size, q.ctypes.data, e.ctypes.data)
+        return q, e
+
+    def rms_quant(self, x, gamma):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        g = np.ascontiguousarray(gamma, dtype=np.float32)
+        q = np.empty(4096, np.int16)
+        e = np.empty(128, np.uint8)
+        r = np.empty(1, np.float32)
+        self.L.i4o_rmsnorm_quantize(x.ctypes.data, g.ctypes.data, q.ctypes.data, e.ctypes.data, r.ctypes.data)
+        return q, e, r[0]
+
+    def linear_bank(self, superblocks, out_tiles, local_in_tiles, act_q, act_e, hls_zero_start=False):
+        sb = np.ascontiguousarray(superblocks, dtype=np.uint8)
+        q = np.ascontiguousarray(act_q, dtype=np.int16)
+        e = np.ascontiguousarray(act_e, dtype=np.uint8)
+        out = np.empty(out_tiles * 128, np.float32)
+        self.L.i4o_linear_bank(sb.ctypes.data, out_tiles, local_in_tiles, q.ctypes.data, e.ctypes.data,
+                               int(bool(hls_zero_start)), out.ctypes.data)
+        return out
+
+    def gemv(self, banks, layer, mode, act_q, act_e):
+        from importlib import import_module
+        F = import_module("4pe_u250_b200.formats")
+        rows = F.mode_rows(mode)
+        q = np.ascontiguousarray(act_q, dtype=np.int16)
+        e = np.ascontiguousarray(act_e, dtype=np.uint8)
+        y = np.empty(rows, np.float32)
+        part = np.empty(4 * rows, np.float32)
+        self.L.i4o_gemv(self._banks(banks), layer, mode, q.ctypes.data, e.ctypes.data, y.ctypes.data,
+                        part.ctypes.data)
+        return y, part.reshape(4, rows)
+
+    def rope_tables(self, lut):
+        buf = np.frombuffer(lut, dtype=np.uint8)
+        c = np.empty(4096 * 64, np.int32)
+        s = np.empty(4096 * 64, np.int32)
+        self.L.i4o_decode_rope_lut(buf.ctypes.data, c.ctypes.data, s.ctypes.data)
+        return c, s
+
+    def float_to_q17(self, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty(x.size, np.int32)
+        self.L.i4o_float_to_q17_array(x.ctypes.data, x.size, out.ctypes.data)
+        return out
+
+    def rope(self, vec, tables, pos):
+        c, s = tables
+        v = np.array(vec, dtype=np.int32, copy=True)
+        self.L.i4o_rope_q17(v.ctypes.data, c[pos * 64:].ctypes.data, s[pos * 64:].ctypes.data)
+        return v
+
+    def kv_store(self, layers, stride):
+        return np.zeros(4 * layers * 8 * stride * 320, np.uint8)
+
+    def kv_record(self, k, v):
+        rec = np.empty(320, np.uint8)
+        k = np.ascontiguousarray(k, dtype=np.int32)
+        v = np.ascontiguousarray(v, dtype=np.int32)
+        self.L.i4o_kv_write_record(rec.ctypes.data, k.ctypes.data, v.ctypes.data)
+        return rec
+
+    def attention(self, kv, layers, stride, layer, pos, q_rot, k_rot, v):
+        arrs = [np.ascontiguousarray(a, dtype=np.int32) for a in (q_rot, k_rot, v)]
+        oq = np.empty(4096, np.int16)
+        oe = np.empty(128, np.uint8)
+        self.L.i4o_attention(kv.ctypes.data, layers, stride, layer, pos, *[a.ctypes.data for a in arrs],
+                             oq.ctypes.data, oe.ctypes.data)
+        return oq, oe
+
+    def swiglu(self, gate, up):
+        g = np.ascontiguousarray(gate, dtype=np.float32)
+        u = np.ascontiguousarray(up, dtype=np.float32)
+        out = np.empty(g.size, np.float32)
+        self.L.i4o_swiglu(g.ctypes.data, u.ctypes.data, g.size, out.ctypes.data)
+        return out
+
+    def expf(self, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.empty_like(x)
+        self.L.i4o_expf_array(x.ctypes.data, y.ctypes.data, x.size)
+        return y
+
+    def gamma(self, banks, layer, which):
+        g = np.empty(4096, np.float32)
+        self.L.i4o_read_gamma(self._banks(banks), layer, which, g.ctypes.data)
+        return g
+
+    def forward(self, banks, tables, kv, layers, stride, pos, residual):
+        c, s = tables
+        res = np.array(residual, dtype=np.float32, copy=True)
+        logits = np.empty(32256, np.float32)
+        self.L.i4o_forward(self._banks(banks), c.ctypes.data, s.ctypes.data, kv.ctypes.data, layers, stride, pos,
+                           res.ctypes.data, logits.ctypes.data)
+        return logits, res
+
+    def argmax(self, logits, n=32000):
+        x = np.ascontiguousarray(logits, dtype=np.float32)
+        return self.L.i4o_argmax(x.ctypes.data, n)
+
+
+def ref_available():
+    return os.path.exists(REF_SO)
+
+
+class RefEmulator:
+    """The reference emulator itself (software_sim/llama2_decoder_sw_emulator.cpp).
+
+    It holds one model and one KV state per process (its globals).
+    """
+
+    def __init__(self):
+        if not ref_available():
+            raise RuntimeError(f"{REF_SO} missing: build with `make -C oracle ref` where the reference exists")
+        L = ctypes.CDLL(REF_SO)
+        sigs = {
+            "ref_load": [ctypes.c_char_p, ctypes.c_int, ctypes.c_int],
+            "ref_kv_reset": [],
+            "ref_threads": [],
+            "ref_forward": [ctypes.c_int, ctypes.c_int, P, P],
+            "ref_quantize_g32": [P, ctypes.c_int, P, P],
+            "ref_rmsnorm_quantize": [P, P, P, P],
+            "ref_gemv": [ctypes.c_int, ctypes.c_int, P, P, P],
+            "ref_float_to_q17": [ctypes.c_float],
+            "ref_rope_q17": [P, ctypes.c_int],
+            "ref_attention": [P, P, P, ctypes.c_int, ctypes.c_int, P, P],
+            "ref_swiglu": [P, P, ctypes.c_int, P],
+            "ref_kv_get": [ctypes.c_int] * 4 + [P, P, P, P],
+            "ref_argmax": [P, ctypes.c_int],
+        }
+        for k, v in sigs.items():
+            getattr(L, k).argtypes = v
+        L.ref_float_to_q17.restype = ctypes.c_int32
+        self.L = L
+
+    def load(self, directory, layers, stride):
+        if self.L.ref_load(directory.encode(), layers, stride) != 0:
+            raise RuntimeError(f"reference emulator could not load model from {directory}")
+
+    def forward(self, token, pos):
+        logits = np.empty(32000, np.float32)
+        res = np.empty(4096, np.float32)
+        self.L.ref_forward(token, pos, logits.ctypes.data, res.ctypes.data)
+        return logits, res
+
+    def gemv(self, layer, mode, q, e):
+        from importlib import import_module
+        F = import_module("4pe_u250_b200.formats")
+        y = np.empty(F.mode_rows(mode), np.float32)
+        q = np.ascontiguousarray(q, dtype=np.int16)
+        e = np.ascontiguousarray(e, dtype=np.uint8)
+        self.L.ref_gemv(layer, mode, q.ctypes.data, e.ctypes.data, y.ctypes.data)
+        return y
+
+    def rms_quant(self, x, gamma):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        g = np.ascontiguousarray(gamma, dtype=np.float32)
+        q = np.empty(4096, np.int16)
+        e = np.empty(128, np.uint8)
+        self.L.ref_rmsnorm_quantize(x.ctypes.data, g.ctypes.data, q.ctypes.data, e.ctypes.data)
+        return q, e
+
+    def quantize_g32(self, x):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        q = np.empty(x.size, np.int16)
+        e = np.empty(x.size // 32, np.uint8)
+        self.L.ref_quantize_g32(x.ctypes.data, x.size, q.ctypes.data, e.ctypes.data)
+        return q, e
+
+    def attention(self, q_rot, k_rot, v, layer, pos):
+        arrs = [np.ascontiguousarray(a, dtype=np.int32) for a in (q_rot, k_rot, v)]
+        oq = np.empty(4096, np.int16)
+        oe = np.empty(128, np.uint8)
+        self.L.ref_attention(*[a.ctypes.data for a in arrs], layer, pos, oq.ctypes.data, oe.ctypes.data)
+        return oq, oe
+
+    def swiglu(self, gate, up):
+        g = np.ascontiguousarray(gate, dtype=np.float32)
+        u = np.ascontiguousarray(up, dtype=np.float32)
+        out = np.empty(g.size, np.float32)
+        self.L.ref_swiglu(g.ctypes.data, u.ctypes.data, g.size, out.ctypes.data)
+        return out
+
+    def kv_get(self, bank, layer, lh, token):
+        k8 = np.empty(128, np.int8)
+        v8 = np.empty(128, np.int8)
+        ks = np.empty(4, np.uint8)
+        vs = np.empty(4, np.uint8)
+        self.L.ref_kv_get(bank, layer, lh, token, k8.ctypes.data, ks.ctypes.data, v8.ctypes.data, vs.ctypes.data)
+        return ks, vs, k8, v8
+
+    def threads(self):
+        return self.L.ref_threads()

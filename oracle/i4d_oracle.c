@@ -577,3 +577,12 @@ int i4o_argmax(const float* logits, int n) {
         if (logits[i] > bv) { best = i; bv = logits[i]; }
     return best;
 }
+
+void i4o_float_to_q17_array(const float* x, int n, int32_t* out) {
+    for (int i = 0; i < n; ++i) out[i] = i4o_float_to_q17(x[i]);
+}
+
+void i4o_expf_array(const float* x, float* y, size_t n) {
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < (long long)n; ++i) y[i] = expf(x[i]);
+}

@@ -130,6 +130,10 @@ void i4o_forward(const uint8_t* const banks[4], const int32_t* rope_cos,
                  const int32_t* rope_sin, uint8_t* kv, int layers, int stride,
                  int pos, float* residual, float* logits);
 
+/* Array helpers for the Python test harness. */
+void i4o_float_to_q17_array(const float* x, int n, int32_t* out);
+void i4o_expf_array(const float* x, float* y, size_t n); /* host C library expf */
+
 /* emulator:1428-1438: index of the first strict maximum over n. */
 int i4o_argmax(const float* logits, int n);
 
