@@ -2,6 +2,7 @@
 
   libi4d.so        the CUDA decode library (sm_100a) behind include/i4d.h
   libi4d_synth.so  seeded synthetic model images in the reference format
+  i4d_decode       C++ host program over libi4d (replaces decode_host)
   csrc/gen/*       build-time tables (expf constants and exceptions)
 
 Run as ``python -m`` or through ``__graft_entry__.build()``.  The expf
@@ -89,6 +90,16 @@ def build_i4d():
     return out
 
 
+def build_host():
+    src = os.path.join(CSRC, "host", "i4d_decode.cpp")
+    out = os.path.join(HERE, "i4d_decode")
+    lib = os.path.join(HERE, "libi4d.so")
+    if _newer(out, [src, lib, os.path.join(ROOT, "include", "i4d.h")]):
+        _run(["g++", "-O2", "-std=c++17", "-I", os.path.join(ROOT, "include"), src, "-o", out,
+              "-L" + HERE, "-l:libi4d.so", "-Wl,-rpath,$ORIGIN"])
+    return out
+
+
 def build_oracle():
     _run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "oracle"])
     if os.path.isdir(os.environ.get("I4D_REF_ROOT", "/root/reference")):
@@ -99,6 +110,7 @@ def build_oracle():
 def main():
     build_synth()
     build_i4d()
+    build_host()
     build_oracle()
 
 

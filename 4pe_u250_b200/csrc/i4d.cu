@@ -112,6 +112,7 @@ struct i4d_ctx {
     unsigned* d_counters = nullptr;
     unsigned* d_err = nullptr;
     int* d_pos = nullptr;
+    uint32_t* d_attn_coef = nullptr;  // [32][stride] attention coefficients
     float* d_scratch = nullptr;  // op-level staging, 3 x 32256 floats
     // pinned staging for the decode contract
     float* h_resid_in = nullptr;
@@ -158,8 +159,15 @@ size_t stage_offset(const i4d_ctx* c, int layer, int st) {
     return off;
 }
 
+// Units in flight per CTA (FP32 contribution buffers): about 24 KB of them.
+int contrib_slots(int chunks) {
+    const int per_unit = chunks * 8 * 32 * 4;
+    const int nu = 24576 / per_unit;
+    return nu < 2 ? 2 : nu;
+}
+
 int ring_slots(int chunks) {
-    const size_t fixed = linear_smem_bytes(0, chunks);
+    const size_t fixed = linear_smem_bytes(0, chunks, contrib_slots(chunks));
     return static_cast<int>((kSmemBudget - fixed) / (kChunkBytes + 16));
 }
 
@@ -190,6 +198,7 @@ LinearArgs base_linear(i4d_ctx* c, int layer, int st) {
     a.units = kStageUnits[st];
     a.chunks = kStageChunks[st];
     a.ns = ring_slots(a.chunks);
+    a.nu = contrib_slots(a.chunks);
     a.partials = c->d_partials;
     a.counters = c->d_counters;
     a.expf = c->expf;
@@ -198,7 +207,7 @@ LinearArgs base_linear(i4d_ctx* c, int layer, int st) {
 }
 
 cudaError_t run_linear(i4d_ctx* c, const LinearArgs& a, bool pdl) {
-    const size_t smem = linear_smem_bytes(a.ns, a.chunks);
+    const size_t smem = linear_smem_bytes(a.ns, a.chunks, a.nu);
     return launch(c, pdl, k_linear, dim3(a.nbanks * a.cpb), dim3(kLinearThreads), smem, a);
 }
 
@@ -215,6 +224,7 @@ AttnArgs base_attn(i4d_ctx* c, int layer) {
     a.layers = c->layers;
     a.stride = c->stride;
     a.layer = layer;
+    a.coef_scratch = c->d_attn_coef;
     a.out_q = c->d_ao_q;
     a.out_e = c->d_ao_e;
     a.err = c->d_err;
@@ -253,7 +263,7 @@ i4d_status enqueue_token(i4d_ctx* c) {
         q.epi = EPI_PARTIAL;
         TIMED(KC_QKV, run_linear(c, q, true));
 
-        TIMED(KC_ATTN, launch(c, true, k_attention, dim3(kHeads), dim3(kAttnThreads), 0, base_attn(c, l)));
+        TIMED(KC_ATTN, launch(c, true, k_attention, dim3(kHeads), dim3(kAttnThreads), attn_smem_bytes(), base_attn(c, l)));
 
         LinearArgs o = base_linear(c, l, ST_O);
         o.in_kind = IN_ACT;
@@ -341,7 +351,7 @@ void i4d_destroy(i4d_ctx* c) {
         if (ev) cudaEventDestroy(ev);
     void* dev[] = {c->d_w, c->d_gamma, c->d_rope_cos, c->d_rope_sin, c->d_exp2, c->d_expf_slots, c->d_kv,
                    c->d_emb, c->d_resid, c->d_recip, c->d_partials, c->d_ao_q, c->d_ao_e, c->d_ad_q,
-                   c->d_ad_e, c->d_logits, c->d_counters, c->d_err, c->d_pos, c->d_scratch};
+                   c->d_ad_e, c->d_logits, c->d_counters, c->d_err, c->d_pos, c->d_scratch, c->d_attn_coef};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* host[] = {c->h_resid_in, c->h_resid_out, c->h_logits, c->h_pos, c->h_err};
@@ -383,6 +393,8 @@ i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out) {
     c->cpb = c->num_sms / 4 > 0 ? c->num_sms / 4 : 1;
     CKC(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     CKC(cudaFuncSetAttribute(k_linear, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBudget)));
+    CKC(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(attn_smem_bytes())));
 
     c->w_bytes = stage_offset(c, 0, ST_LOGITS) + 4 * stage_bank_bytes(ST_LOGITS);
     CKC(cudaMalloc(&c->d_w, c->w_bytes));
@@ -405,6 +417,7 @@ i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out) {
     CKC(cudaMalloc(&c->d_err, sizeof(unsigned)));
     CKC(cudaMemset(c->d_err, 0, sizeof(unsigned)));
     CKC(cudaMalloc(&c->d_pos, sizeof(int)));
+    CKC(cudaMalloc(&c->d_attn_coef, 32ull * c->stride * sizeof(uint32_t)));
     CKC(cudaMalloc(&c->d_scratch, 3ull * kPVocab * sizeof(float)));
     CKC(cudaMallocHost(&c->h_resid_in, kDim * sizeof(float)));
     CKC(cudaMallocHost(&c->h_resid_out, kDim * sizeof(float)));
@@ -745,6 +758,7 @@ i4d_status i4d_linear_bank(i4d_ctx* c, const void* superblocks, size_t n_bytes, 
     a.cpb = a.units < c->num_sms ? a.units : c->num_sms;
     a.chunks = lit;
     a.ns = ring_slots(lit);
+    a.nu = contrib_slots(lit);
     a.in_kind = IN_ACT;
     a.act_q = aq.as<int16_t>();
     a.act_e = ae.as<uint8_t>();
@@ -852,7 +866,7 @@ i4d_status i4d_attention(i4d_ctx* c, int layer, uint32_t position, const int32_t
     a.direct = dqkv.as<int32_t>();
     a.out_q = dq.as<int16_t>();
     a.out_e = de.as<uint8_t>();
-    k_attention<<<kHeads, kAttnThreads, 0, c->stream>>>(a);
+    k_attention<<<kHeads, kAttnThreads, attn_smem_bytes(), c->stream>>>(a);
     CK(cudaGetLastError());
     const i4d_status st = finish(c);
     if (st != I4D_OK) return st;

@@ -8,11 +8,20 @@
 // quantised to INT14 + E8M0 for the O projection.  All arithmetic is integer
 // or single-rounding FP32 and bit-exact with emulator:602-714.
 //
-// Parallel form of the sequential recurrence: scores are exact integers and
-// computed for all tokens at once; the running maximum before each token is
-// a prefix maximum, so every softmax coefficient c_t is computed in
-// parallel; only the normaliser and the per-dimension state chains run
-// serially over tokens.
+// Parallel form of the sequential recurrence (one CTA per head, cached
+// records streamed through shared memory in tiles of 64 tokens):
+//  * scores are exact integers, computed for all tokens at once;
+//  * the running maximum before each token is a prefix maximum, so every
+//    softmax coefficient c_t is computed in parallel;
+//  * the tokens where the maximum grows ("events", plus token 0) split the
+//    sequence into segments; inside a segment the normaliser adds c_t modulo
+//    2^30 and each state dimension adds mulq17(v_t, c_t), so both are
+//    per-segment sums computed in parallel; only the events themselves are
+//    applied serially.  The state chain saturates at each step in the
+//    reference, so a segment sum is used only when |S| + sum|terms| < 2^31
+//    proves no step saturates; otherwise that segment (or, beyond 16 events,
+//    the whole head) is replayed sequentially.  The result is bit-exact in
+//    every case.
 #pragma once
 
 #include "i4d_device.cuh"
@@ -30,13 +39,15 @@ struct AttnArgs {
     int32_t score_scale;      // float_to_q17(1/sqrt(128))
     uint8_t* kv;              // [4][layers][8][stride][320]
     int layers, stride, layer;
+    uint32_t* coef_scratch;   // [32][stride]: c_t | rescale << 31 (fallback paths)
     int16_t* out_q;
     uint8_t* out_e;
     unsigned* err;
 };
 
-constexpr int kAttnThreads = 128;
-constexpr int kMaxCtx = 4096;
+constexpr int kAttnThreads = 256;
+constexpr int kTile = 64;       // tokens per shared-memory tile
+constexpr int kMaxSeg = 16;     // rescale events handled by the segmented path
 
 // Fixed-point exp of a non-positive Q15.17 value (emulator:575-595,
 // swiftkv_attention.cpp:199-260).
@@ -77,6 +88,27 @@ __device__ __forceinline__ int kv_quant(int32_t raw, uint32_t shift) {
     return w < 0 ? -static_cast<int>(mag) : static_cast<int>(mag);
 }
 
+__device__ __forceinline__ int dp2a_lo_ss(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp2a_hi_ss(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp2a_lo_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.lo.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp2a_hi_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.hi.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 __device__ __forceinline__ uint8_t* kv_record(const AttnArgs& a, int head, int token) {
     const int bank = head / kLocalHeads, lh = head % kLocalHeads;
     const size_t rec = ((static_cast<size_t>(bank) * a.layers + a.layer) * kLocalHeads + lh) *
@@ -84,183 +116,407 @@ __device__ __forceinline__ uint8_t* kv_record(const AttnArgs& a, int head, int t
     return a.kv + rec * 320;
 }
 
-__global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
-    __shared__ int32_t s_q[kHeadDim], s_k[kHeadDim];
-    __shared__ int8_t s_k8[kHeadDim], s_v8[kHeadDim];
-    __shared__ uint32_t s_shift[8];
-    __shared__ uint32_t s_lut[33];
-    __shared__ int32_t s_score[kMaxCtx];
-    __shared__ uint32_t s_coef[kMaxCtx];
-    __shared__ int32_t s_cmax[kAttnThreads];
-    __shared__ uint32_t s_norm;
+struct AttnSmem {
+    uint8_t* tile[2];
+    uint8_t* cur;        // current token's record
+    uint64_t* bar;       // [2]
+    uint32_t* lut;       // [33]
+    int32_t* score;      // [kTile]
+    uint32_t* coef;      // [kTile]: c | event << 31
+    int32_t* seg;        // [kTile]: rescale-segment index of each token
+    unsigned long long* zbin;  // [kMaxSeg]: sum of c over each segment's non-event tokens
+    long long* sbin;     // [kMaxSeg][128]: sum of mulq17(v, c) per segment and dimension
+    long long* abin;     // [kMaxSeg][128]: sum of |mulq17(v, c)|
+    int32_t* ev_v;       // [kMaxSeg][128]: v of each event token
+    uint32_t* ev_c;      // [kMaxSeg]
+    int32_t* ev_tok;     // [kMaxSeg]
+    int32_t* qrot;       // [128]
+    int* misc;           // [16]: carry max, events, warp-0 max, z, warp-0 events, shifts
+};
 
-    const int h = blockIdx.x, d = threadIdx.x, lane = d & 31, warp = d >> 5;
-    if (d < 33) s_lut[d] = a.exp2_q30[d];
+__host__ __device__ inline size_t attn_align16(size_t b) { return (b + 15) & ~static_cast<size_t>(15); }
+
+__host__ __device__ inline size_t attn_smem_bytes() {
+    size_t b = 2 * kTile * 320 + 320;
+    b = attn_align16(b) + 16;
+    b += attn_align16(33 * 4);
+    b += 3 * attn_align16(kTile * 4);
+    b += kMaxSeg * 8 + 2 * kMaxSeg * 128 * 8 + kMaxSeg * 128 * 4;
+    b += 2 * attn_align16(kMaxSeg * 4);
+    b += 128 * 4 + 16 * 4;
+    return b;
+}
+
+__device__ __forceinline__ AttnSmem attn_carve(uint8_t* p) {
+    AttnSmem s;
+    s.tile[0] = p;
+    s.tile[1] = p + kTile * 320;
+    s.cur = p + 2 * kTile * 320;
+    p += attn_align16(2 * kTile * 320 + 320);
+    s.bar = reinterpret_cast<uint64_t*>(p);
+    p += 16;
+    s.lut = reinterpret_cast<uint32_t*>(p);
+    p += attn_align16(33 * 4);
+    s.score = reinterpret_cast<int32_t*>(p);
+    p += attn_align16(kTile * 4);
+    s.coef = reinterpret_cast<uint32_t*>(p);
+    p += attn_align16(kTile * 4);
+    s.seg = reinterpret_cast<int32_t*>(p);
+    p += attn_align16(kTile * 4);
+    s.zbin = reinterpret_cast<unsigned long long*>(p);
+    p += kMaxSeg * 8;
+    s.sbin = reinterpret_cast<long long*>(p);
+    p += kMaxSeg * 128 * 8;
+    s.abin = reinterpret_cast<long long*>(p);
+    p += kMaxSeg * 128 * 8;
+    s.ev_v = reinterpret_cast<int32_t*>(p);
+    p += kMaxSeg * 128 * 4;
+    s.ev_c = reinterpret_cast<uint32_t*>(p);
+    p += attn_align16(kMaxSeg * 4);
+    s.ev_tok = reinterpret_cast<int32_t*>(p);
+    p += attn_align16(kMaxSeg * 4);
+    s.qrot = reinterpret_cast<int32_t*>(p);
+    p += 128 * 4;
+    s.misc = reinterpret_cast<int*>(p);
+    return s;
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Value of dimension d of token t (v << shift), from a record.
+__device__ __forceinline__ int32_t rec_v(const uint8_t* rec, int d) {
+    const unsigned long long meta = *reinterpret_cast<const unsigned long long*>(rec);
+    return static_cast<int32_t>(static_cast<int8_t>(rec[192 + d])) << ((meta >> (20 + 5 * (d >> 5))) & 31u);
+}
+
+__global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constant__ AttnArgs a) {
+    extern __shared__ __align__(128) uint8_t attn_smem[];
+    AttnSmem S = attn_carve(attn_smem);
+    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned FULL = 0xffffffffu;
+    const uint32_t M30 = (1u << 30) - 1u;
+    int* misc = S.misc;
+    if (tid < 33) S.lut[tid] = a.exp2_q30[tid];
+    if (tid == 0) {
+        mbar_init(&S.bar[0], 1);
+        mbar_init(&S.bar[1], 1);
+        mbar_fence_init();
+        misc[0] = INT32_MIN;  // running max of all earlier tiles
+        misc[1] = 0;          // events so far (token 0 counts)
+    }
+    if (tid < kMaxSeg) S.zbin[tid] = 0;
+    for (int i = tid; i < kMaxSeg * 128; i += kAttnThreads) {
+        S.sbin[i] = 0;
+        S.abin[i] = 0;
+    }
+    __syncthreads();
     pdl_trigger();
-    pdl_wait();
+    // The position is written before the token's first kernel, and cached
+    // records of earlier tokens never change during a token, so the first
+    // tile streams in while the QKV projection is still finishing.
     const int pos = *a.pos_ptr;
-    if (pos < 0 || pos >= a.stride) {
-        if (d == 0) atomicOr(a.err, kErrArg);
+    const bool bad = pos < 0 || pos >= a.stride;
+    const int n = pos + 1;
+    const int ntiles = (n + kTile - 1) / kTile;
+    const uint8_t* head_base = kv_record(a, h, 0);
+    if (!bad && tid == 0) {
+        const int cnt = min(kTile, n);
+        mbar_arrive_expect_tx(&S.bar[0], cnt * 320);
+        bulk_g2s(S.tile[0], head_base, cnt * 320, &S.bar[0]);
+    }
+    pdl_wait();
+    if (bad) {
+        if (tid == 0) atomicOr(a.err, kErrArg);
         return;
     }
 
-    // Q/K/V rows of this head (finalizer pair tree + float_to_q17).
-    int32_t qv, kv, vv;
+    // ---- current token: finish Q/K/V rows, RoPE, KV record ----
+    const int d = tid & 127;
+    int32_t* tq = S.qrot;
+    int32_t* tk = S.ev_v;  // scratch until the tile loop
+    int32_t qv = 0, kv = 0, vv = 0;
     const int row = h * kHeadDim + d;
-    if (a.direct) {
-        qv = a.direct[row];
-        kv = a.direct[kDim + row];
-        vv = a.direct[2 * kDim + row];
-    } else {
-        qv = float_to_q17(combine4(a.partials, 3 * kDim, row));
-        kv = float_to_q17(combine4(a.partials, 3 * kDim, kDim + row));
-        vv = float_to_q17(combine4(a.partials, 3 * kDim, 2 * kDim + row));
+    if (tid < 128) {
+        if (a.direct) {
+            qv = a.direct[row];
+            kv = a.direct[kDim + row];
+            vv = a.direct[2 * kDim + row];
+        } else {
+            qv = float_to_q17(combine4(a.partials, 3 * kDim, row));
+            kv = float_to_q17(combine4(a.partials, 3 * kDim, kDim + row));
+            vv = float_to_q17(combine4(a.partials, 3 * kDim, 2 * kDim + row));
+        }
+        tq[d] = qv;
+        tk[d] = kv;
     }
-    s_q[d] = qv;
-    s_k[d] = kv;
     __syncthreads();
-    // Adjacent-pair RoPE (emulator:526-541).
-    {
+    if (tid < 128) {  // adjacent-pair RoPE (emulator:526-541)
         const int pr = d >> 1;
         const long long c = a.rope_cos[pos * 64 + pr], sn = a.rope_sin[pos * 64 + pr];
-        const long long qa = s_q[2 * pr], qb = s_q[2 * pr + 1];
-        const long long ka = s_k[2 * pr], kb = s_k[2 * pr + 1];
+        const long long qa = tq[2 * pr], qb = tq[2 * pr + 1];
+        const long long ka = tk[2 * pr], kb = tk[2 * pr + 1];
         qv = (d & 1) ? sat32((qa * sn + qb * c) >> 17) : sat32((qa * c - qb * sn) >> 17);
         kv = (d & 1) ? sat32((ka * sn + kb * c) >> 17) : sat32((ka * c - kb * sn) >> 17);
     }
     __syncthreads();
-    s_q[d] = qv;
-
-    // Current token's KV record: warp = 32-value group.
-    {
+    uint8_t* grec = kv_record(a, h, pos);
+    if (tid < 128) {  // warp = 32-value group of the record
+        tq[d] = qv;
         const uint32_t kmag = static_cast<uint32_t>(kv < 0 ? -static_cast<long long>(kv) : kv);
         const uint32_t vmag = static_cast<uint32_t>(vv < 0 ? -static_cast<long long>(vv) : vv);
-        const uint32_t ks = kv_shift_of(__reduce_max_sync(0xffffffffu, kmag));
-        const uint32_t vs = kv_shift_of(__reduce_max_sync(0xffffffffu, vmag));
-        const int k8 = kv_quant(kv, ks), v8 = kv_quant(vv, vs);
-        s_k8[d] = static_cast<int8_t>(k8);
-        s_v8[d] = static_cast<int8_t>(v8);
+        const uint32_t ks = kv_shift_of(__reduce_max_sync(FULL, kmag));
+        const uint32_t vs = kv_shift_of(__reduce_max_sync(FULL, vmag));
+        const uint8_t k8 = static_cast<uint8_t>(kv_quant(kv, ks)), v8 = static_cast<uint8_t>(kv_quant(vv, vs));
+        S.cur[64 + d] = k8;
+        S.cur[192 + d] = v8;
+        grec[64 + d] = k8;
+        grec[192 + d] = v8;
         if (lane == 0) {
-            s_shift[warp] = ks;
-            s_shift[4 + warp] = vs;
+            misc[8 + warp] = static_cast<int>(ks);
+            misc[12 + warp] = static_cast<int>(vs);
         }
-        uint8_t* rec = kv_record(a, h, pos);
-        rec[64 + d] = static_cast<uint8_t>(k8);
-        rec[192 + d] = static_cast<uint8_t>(v8);
+    }
+    __syncthreads();
+    if (tid < 8) {
+        unsigned long long meta = 0;
+        if (tid == 0)
+            for (int g = 0; g < 4; ++g) {
+                meta |= static_cast<unsigned long long>(misc[8 + g]) << (5 * g);
+                meta |= static_cast<unsigned long long>(misc[12 + g]) << (20 + 5 * g);
+            }
+        reinterpret_cast<unsigned long long*>(S.cur)[tid] = meta;
+        reinterpret_cast<unsigned long long*>(grec)[tid] = meta;
+    }
+    // Q of this lane's half-group (16 values) split into 16-bit halves for dp2a.
+    const int hg = lane & 7;
+    uint32_t qh2[8], ql2[8];
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int32_t x0 = tq[hg * 16 + 2 * i], x1 = tq[hg * 16 + 2 * i + 1];
+        qh2[i] = (static_cast<uint32_t>(x0 >> 16) & 0xffffu) | (static_cast<uint32_t>(x1 >> 16) << 16);
+        ql2[i] = (static_cast<uint32_t>(x0) & 0xffffu) | (static_cast<uint32_t>(x1) << 16);
+    }
+
+    // ---- tiles of kTile cached records ----
+    for (int k = 0; k < ntiles; ++k) {
+        const int T0 = k * kTile, cnt = min(kTile, n - T0);
+        uint8_t* buf = S.tile[k & 1];
+        if (tid == 0 && k + 1 < ntiles) {
+            fence_proxy_async_smem();
+            const int c2 = min(kTile, n - T0 - kTile);
+            mbar_arrive_expect_tx(&S.bar[(k + 1) & 1], c2 * 320);
+            bulk_g2s(S.tile[(k + 1) & 1], head_base + static_cast<size_t>(T0 + kTile) * 320, c2 * 320,
+                     &S.bar[(k + 1) & 1]);
+        }
+        mbar_wait(&S.bar[k & 1], static_cast<uint32_t>((k >> 1) & 1), a.err, kErrWaitFull);
+        if (pos < T0 + cnt) {  // this tile holds the current token: use the fresh record
+            if (tid < 80)
+                reinterpret_cast<uint32_t*>(buf + (pos - T0) * 320)[tid] = reinterpret_cast<const uint32_t*>(S.cur)[tid];
+            __syncthreads();
+        }
+        // Scores (emulator:633-655): 8 lanes per token, one half-group each.
+        for (int r = 0; r < kTile / 32; ++r) {
+            const int tl = r * 32 + warp * 4 + (lane >> 3);
+            long long hv = 0;
+            if (tl < cnt) {
+                const uint8_t* rec = buf + tl * 320;
+                const uint4 kw = *reinterpret_cast<const uint4*>(rec + 64 + hg * 16);
+                const unsigned long long meta = *reinterpret_cast<const unsigned long long*>(rec);
+                const uint32_t sh = static_cast<uint32_t>((meta >> (5 * (hg >> 1))) & 31u);
+                int sh16 = 0, sl16 = 0;
+                sh16 = dp2a_lo_ss(qh2[0], kw.x, sh16);
+                sh16 = dp2a_hi_ss(qh2[1], kw.x, sh16);
+                sh16 = dp2a_lo_ss(qh2[2], kw.y, sh16);
+                sh16 = dp2a_hi_ss(qh2[3], kw.y, sh16);
+                sh16 = dp2a_lo_ss(qh2[4], kw.z, sh16);
+                sh16 = dp2a_hi_ss(qh2[5], kw.z, sh16);
+                sh16 = dp2a_lo_ss(qh2[6], kw.w, sh16);
+                sh16 = dp2a_hi_ss(qh2[7], kw.w, sh16);
+                sl16 = dp2a_lo_us(ql2[0], kw.x, sl16);
+                sl16 = dp2a_hi_us(ql2[1], kw.x, sl16);
+                sl16 = dp2a_lo_us(ql2[2], kw.y, sl16);
+                sl16 = dp2a_hi_us(ql2[3], kw.y, sl16);
+                sl16 = dp2a_lo_us(ql2[4], kw.z, sl16);
+                sl16 = dp2a_hi_us(ql2[5], kw.z, sl16);
+                sl16 = dp2a_lo_us(ql2[6], kw.w, sl16);
+                sl16 = dp2a_hi_us(ql2[7], kw.w, sl16);
+                const long long half = static_cast<long long>(sh16) * 65536 + sl16;
+                hv = wrap_bits(sh >= 10 ? static_cast<long long>(static_cast<unsigned long long>(half) << (sh - 10))
+                                        : (half >> (10 - sh)), 44);
+            }
+            hv += __shfl_xor_sync(FULL, hv, 1);
+            hv += __shfl_xor_sync(FULL, hv, 2);
+            hv += __shfl_xor_sync(FULL, hv, 4);
+            if ((lane & 7) == 0 && tl < cnt) S.score[tl] = sat32(rshift_even(wrap_bits(hv, 44) * a.score_scale, 24));
+        }
         __syncthreads();
-        if (d < 8) {
-            unsigned long long meta = 0;
-            if (d == 0) {
-                for (int g = 0; g < 4; ++g) {
-                    meta |= static_cast<unsigned long long>(s_shift[g]) << (5 * g);
-                    meta |= static_cast<unsigned long long>(s_shift[4 + g]) << (20 + 5 * g);
+
+        // Coefficients from the running maximum before each token
+        // (emulator:656-672); events = token 0 and every new maximum.
+        const int carry = misc[0], ev_before = misc[1];
+        int32_t m_incl = INT32_MIN, m_excl = INT32_MIN, sc = INT32_MIN;
+        if (tid < kTile) {
+            sc = tid < cnt ? S.score[tid] : INT32_MIN;
+            m_incl = sc;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int32_t y = __shfl_up_sync(FULL, m_incl, o);
+                if (lane >= o) m_incl = max(m_incl, y);
+            }
+            m_excl = __shfl_up_sync(FULL, m_incl, 1);
+            if (lane == 0) m_excl = INT32_MIN;
+            if (tid == 31) misc[2] = m_incl;
+        }
+        __syncthreads();
+        bool ev = false;
+        uint32_t c = 0;
+        if (tid < kTile) {
+            const int32_t prev = max(max(carry, m_excl), warp == 1 ? misc[2] : INT32_MIN);
+            const int t = T0 + tid;
+            if (tid < cnt) {
+                if (t == 0) {
+                    c = 1u << 17;
+                    ev = true;
+                } else if (sc <= prev) {
+                    c = exp_negative_q17(sat32(static_cast<long long>(sc) - prev), S.lut, a.log2e_q21);
+                } else {
+                    c = exp_negative_q17(sat32(static_cast<long long>(prev) - sc), S.lut, a.log2e_q21);
+                    ev = true;
                 }
             }
-            reinterpret_cast<unsigned long long*>(rec)[d] = meta;
+            const unsigned bal = __ballot_sync(FULL, ev);
+            if (tid == 0) misc[4] = __popc(bal);
+            S.coef[tid] = c | (ev ? 0x80000000u : 0u);
+            S.score[tid] = __popc(bal & ((1u << lane) - 1u)) + (ev ? 1 : 0);  // events up to t in this warp
         }
-    }
-
-    // Scores for every token (emulator:633-655).
-    {
-        long long qe[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) qe[i] = s_q[4 * lane + i];
-        const int grp = lane >> 3;
-        for (int t = warp; t <= pos; t += 4) {
-            uint32_t kw;
-            uint32_t sh;
-            if (t == pos) {
-                kw = *reinterpret_cast<const uint32_t*>(s_k8 + 4 * lane);
-                sh = s_shift[grp];
-            } else {
-                const uint8_t* rec = kv_record(a, h, t);
-                kw = *reinterpret_cast<const uint32_t*>(rec + 64 + 4 * lane);
-                const unsigned long long meta = *reinterpret_cast<const unsigned long long*>(rec);
-                sh = static_cast<uint32_t>((meta >> (5 * grp)) & 31u);
+        __syncthreads();
+        if (tid < kTile) {
+            const int e_incl = ev_before + S.score[tid] + (warp == 1 ? misc[4] : 0);
+            const int sg = e_incl - 1;
+            const int t = T0 + tid;
+            S.seg[tid] = sg;
+            if (tid < cnt) {
+                a.coef_scratch[static_cast<size_t>(h) * a.stride + t] = S.coef[tid];
+                if (ev && sg < kMaxSeg) {
+                    S.ev_c[sg] = c;
+                    S.ev_tok[sg] = t;
+                } else if (!ev && sg < kMaxSeg) {
+                    atomicAdd(&S.zbin[sg], static_cast<unsigned long long>(c));
+                }
             }
-            long long part = 0;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) part += qe[i] * static_cast<long long>(static_cast<int8_t>(kw >> (8 * i)));
-            part += __shfl_xor_sync(0xffffffffu, part, 1);
-            part += __shfl_xor_sync(0xffffffffu, part, 2);
-            long long hv = wrap_bits(sh >= 10 ? static_cast<long long>(static_cast<unsigned long long>(part) << (sh - 10))
-                                              : (part >> (10 - sh)), 44);
-            if (lane & 3) hv = 0;
-            hv += __shfl_xor_sync(0xffffffffu, hv, 4);
-            hv += __shfl_xor_sync(0xffffffffu, hv, 8);
-            hv += __shfl_xor_sync(0xffffffffu, hv, 16);
-            const long long dot = wrap_bits(hv, 44);
-            if (lane == 0) s_score[t] = sat32(rshift_even(dot * a.score_scale, 24));
-        }
-    }
-    __syncthreads();
-
-    // Coefficients from the prefix maximum (emulator:656-672).
-    const int n = pos + 1;
-    const int cs = (n + kAttnThreads - 1) / kAttnThreads;
-    const int t0 = d * cs, t1 = min(n, t0 + cs);
-    {
-        int32_t m = INT32_MIN;
-        for (int t = t0; t < t1; ++t) m = max(m, s_score[t]);
-        s_cmax[d] = m;
-    }
-    __syncthreads();
-    {
-        int32_t run = INT32_MIN;  // max of all tokens before t0
-        for (int i = 0; i < d; ++i) run = max(run, s_cmax[i]);
-        for (int t = t0; t < t1; ++t) {
-            const int32_t sc = s_score[t];
-            uint32_t cf;
-            if (t == 0) {
-                cf = 1u << 17;
-            } else if (sc <= run) {
-                cf = exp_negative_q17(sat32(static_cast<long long>(sc) - run), s_lut, a.log2e_q21);
-            } else {
-                cf = exp_negative_q17(sat32(static_cast<long long>(run) - sc), s_lut, a.log2e_q21) | 0x80000000u;
+            if (tid == kTile - 1) {
+                misc[1] = e_incl;
+                misc[0] = max(carry, max(m_incl, misc[2]));
             }
-            s_coef[t] = cf;
-            run = max(run, sc);
         }
-    }
-    __syncthreads();
+        __syncthreads();
 
-    // Normaliser chain (thread 0) and state chain (one dimension per thread).
-    if (d == 0) {
+        // Per-segment sums of the state updates: thread (d, half of the tile).
+        {
+            const int p = tid >> 7;
+            const int t_lo = p * (kTile / 2), t_hi = min(cnt, t_lo + kTile / 2);
+            long long acc = 0, aab = 0;
+            int cs = -1;
+            for (int tl = t_lo; tl < t_hi; ++tl) {
+                const int32_t v = rec_v(buf + tl * 320, d);
+                const uint32_t cf = S.coef[tl];
+                const int sg = S.seg[tl];
+                if (cf >> 31) {
+                    if (cs >= 0 && cs < kMaxSeg) {
+                        atomicAdd(reinterpret_cast<unsigned long long*>(&S.sbin[cs * 128 + d]), static_cast<unsigned long long>(acc));
+                        atomicAdd(reinterpret_cast<unsigned long long*>(&S.abin[cs * 128 + d]), static_cast<unsigned long long>(aab));
+                    }
+                    if (sg < kMaxSeg) S.ev_v[sg * 128 + d] = v;
+                    cs = sg;
+                    acc = 0;
+                    aab = 0;
+                } else {
+                    if (sg != cs) {
+                        if (cs >= 0 && cs < kMaxSeg) {
+                            atomicAdd(reinterpret_cast<unsigned long long*>(&S.sbin[cs * 128 + d]), static_cast<unsigned long long>(acc));
+                            atomicAdd(reinterpret_cast<unsigned long long*>(&S.abin[cs * 128 + d]), static_cast<unsigned long long>(aab));
+                        }
+                        cs = sg;
+                        acc = 0;
+                        aab = 0;
+                    }
+                    const int32_t tv = mulq17(v, cf);
+                    acc += tv;
+                    aab += tv < 0 ? -static_cast<long long>(tv) : tv;
+                }
+            }
+            if (cs >= 0 && cs < kMaxSeg) {
+                atomicAdd(reinterpret_cast<unsigned long long*>(&S.sbin[cs * 128 + d]), static_cast<unsigned long long>(acc));
+                atomicAdd(reinterpret_cast<unsigned long long*>(&S.abin[cs * 128 + d]), static_cast<unsigned long long>(aab));
+            }
+        }
+        __syncthreads();
+    }
+
+    // ---- compose the segments in order ----
+    const int m = misc[1];
+    const bool overflow = m > kMaxSeg;
+    if (tid == 0) {
         uint32_t z = 1u << 17;
-        const uint32_t m30 = (1u << 30) - 1u;
-        for (int t = 1; t < n; ++t) {
-            const uint32_t cf = s_coef[t];
-            const uint32_t c = cf & 0x7fffffffu;
-            if (cf >> 31) z = ((static_cast<uint32_t>(rshift_even(static_cast<long long>(z) * c, 17)) & m30) + (1u << 17)) & m30;
-            else z = (z + c) & m30;
-        }
-        s_norm = z;
-    }
-    const int grp = d >> 5;
-    int32_t st = 0;
-    for (int t = 0; t < n; ++t) {
-        int32_t val;
-        if (t == pos) {
-            val = static_cast<int32_t>(s_v8[d]) << s_shift[4 + grp];
+        if (!overflow) {
+            z = (z + static_cast<uint32_t>(S.zbin[0] & M30)) & M30;
+            for (int e = 1; e < m; ++e) {
+                z = ((static_cast<uint32_t>(rshift_even(static_cast<long long>(z) * S.ev_c[e], 17)) & M30) + (1u << 17)) & M30;
+                z = (z + static_cast<uint32_t>(S.zbin[e] & M30)) & M30;
+            }
         } else {
-            const uint8_t* rec = kv_record(a, h, t);
-            const unsigned long long meta = *reinterpret_cast<const unsigned long long*>(rec);
-            val = static_cast<int32_t>(static_cast<int8_t>(rec[192 + d])) << ((meta >> (20 + 5 * grp)) & 31u);
+            for (int t = 1; t < n; ++t) {
+                const uint32_t cf = a.coef_scratch[static_cast<size_t>(h) * a.stride + t];
+                const uint32_t cc = cf & 0x7fffffffu;
+                if (cf >> 31) z = ((static_cast<uint32_t>(rshift_even(static_cast<long long>(z) * cc, 17)) & M30) + (1u << 17)) & M30;
+                else z = (z + cc) & M30;
+            }
         }
-        const uint32_t cf = s_coef[t];
-        const uint32_t c = cf & 0x7fffffffu;
-        if (t == 0) st = val;
-        else if (cf >> 31) st = sat32(static_cast<long long>(mulq17(st, c)) + val);
-        else st = sat32(static_cast<long long>(st) + mulq17(val, c));
+        misc[3] = static_cast<int>(z);
+    }
+    int32_t st = 0;
+    if (tid < 128) {
+        auto vat = [&](int t) -> int32_t { return t == pos ? rec_v(S.cur, d) : rec_v(kv_record(a, h, t), d); };
+        auto seq = [&](int t0, int t1) {  // sequential chain over non-event tokens [t0, t1)
+            for (int t = t0; t < t1; ++t) {
+                const uint32_t cf = a.coef_scratch[static_cast<size_t>(h) * a.stride + t];
+                st = sat32(static_cast<long long>(st) + mulq17(vat(t), cf & 0x7fffffffu));
+            }
+        };
+        if (!overflow) {
+            st = S.ev_v[d];
+            for (int e = 0; e < m; ++e) {
+                if (e > 0) st = sat32(static_cast<long long>(mulq17(st, S.ev_c[e])) + S.ev_v[e * 128 + d]);
+                const long long mag = st < 0 ? -static_cast<long long>(st) : st;
+                if (mag + S.abin[e * 128 + d] <= INT32_MAX) {
+                    st = static_cast<int32_t>(st + S.sbin[e * 128 + d]);
+                } else {
+                    seq(S.ev_tok[e] + 1, e + 1 < m ? S.ev_tok[e + 1] : n);
+                }
+            }
+        } else {
+            st = vat(0);
+            for (int t = 1; t < n; ++t) {
+                const uint32_t cf = a.coef_scratch[static_cast<size_t>(h) * a.stride + t];
+                const uint32_t cc = cf & 0x7fffffffu;
+                const int32_t v = vat(t);
+                if (cf >> 31) st = sat32(static_cast<long long>(mulq17(st, cc)) + v);
+                else st = sat32(static_cast<long long>(st) + mulq17(v, cc));
+            }
+        }
     }
     __syncthreads();
+    if (tid >= 128) return;
 
-    // Normalise and quantise the head output (emulator:686-711).
-    const uint32_t z = s_norm;
+    // ---- normalise and quantise the head output (emulator:686-711) ----
+    const uint32_t z = static_cast<uint32_t>(misc[3]);
     const uint32_t inv = z == 0 ? 0u : static_cast<uint32_t>(((1ull << 34) + (z >> 1)) / z);
     const int32_t o = mulq17(st, inv);
     const int32_t mag = o == INT32_MIN ? INT32_MAX : abs(o);
-    const int32_t mx = __reduce_max_sync(0xffffffffu, mag);
+    const int32_t mx = __reduce_max_sync(FULL, mag);
     const float maxf = __fmul_rn(__int2float_rn(mx), 1.0f / 131072.0f);
     int maxe = -127;
     if (maxf != 0.0f) frexpf(maxf, &maxe);
@@ -271,5 +527,6 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
     a.out_q[row] = static_cast<int16_t>(__float2int_rz(r));
     if (lane == 0) a.out_e[h * 4 + warp] = maxf == 0.0f ? 0 : static_cast<uint8_t>(maxe + 127);
 }
+
 
 }  // namespace i4d

@@ -201,9 +201,11 @@ __device__ __forceinline__ int quantize_g32_lane(float v, uint32_t* e8m0) {
 
 // Pair tree of the four bank partials: (p0 + p1) + (p2 + p3)
 // (int4_linear_finalize_pair_schedule, int4_linear_controller.cpp:1384-1439).
+// Partials come from other CTAs of the same or the previous kernel, so they
+// are read at L2 (ld.global.cg), never from a possibly stale L1 line.
 __device__ __forceinline__ float combine4(const float* partials, int stride, int row) {
-    const float s01 = __fadd_rn(partials[row], partials[stride + row]);
-    const float s23 = __fadd_rn(partials[2 * stride + row], partials[3 * stride + row]);
+    const float s01 = __fadd_rn(__ldcg(partials + row), __ldcg(partials + stride + row));
+    const float s23 = __fadd_rn(__ldcg(partials + 2 * stride + row), __ldcg(partials + 3 * stride + row));
     return __fadd_rn(s01, s23);
 }
 

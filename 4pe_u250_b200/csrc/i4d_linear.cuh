@@ -37,6 +37,7 @@ struct LinearArgs {
     int units;             // units per bank
     int chunks;            // chunks per unit: local columns / 256
     int ns;                // ring slots
+    int nu;                // contribution slots (units in flight per CTA)
     // input activation of this bank: IN_ACT reads act_q/act_e at
     // bank*act_bank_stride; IN_RMS normalises resid with gamma and *recip.
     int in_kind;
@@ -58,6 +59,8 @@ struct LinearArgs {
     unsigned* err;
 };
 
+constexpr int kFinMax = 64;   // stripes one CTA may finalise (<= units per CTA)
+
 struct LinearSmem {
     uint8_t* ring;
     uint64_t* full;
@@ -66,33 +69,45 @@ struct LinearSmem {
     uint8_t* act_lo;    // [groups][32]
     int* corr;          // [groups]: 8 * sum of the group's first 16 values
     float* act_scale;   // [groups]
-    float* contrib;     // [2][groups*32]
+    float* contrib;     // [nu][groups*32]
+    int* unit_cnt;      // [nu]: chunks of the unit done
+    int* slot_ok;       // [nu]: first unit index allowed to use the slot
+    int* fin;           // [kFinMax + 2]: count, level-2 flag, stripe list
 };
 
-__host__ __device__ inline size_t linear_smem_bytes(int ns, int chunks) {
+__host__ __device__ inline size_t align16(size_t b) { return (b + 15) & ~static_cast<size_t>(15); }
+
+__host__ __device__ inline size_t linear_smem_bytes(int ns, int chunks, int nu) {
     const size_t groups = static_cast<size_t>(chunks) * 8;
     size_t b = static_cast<size_t>(ns) * kChunkBytes;
-    b += 2 * static_cast<size_t>(ns) * 8;
-    b += groups * 64 + groups * 8;
-    b += 2 * groups * 32 * 4;
+    b += align16(2 * static_cast<size_t>(ns) * 8);
+    b += align16(groups * 64) + align16(groups * 8);
+    b += static_cast<size_t>(nu) * groups * 32 * 4;
+    b += align16(2 * static_cast<size_t>(nu) * 4) + align16((kFinMax + 2) * 4);
     return b;
 }
 
-__device__ __forceinline__ LinearSmem carve(uint8_t* base, int ns, int chunks) {
+__device__ __forceinline__ LinearSmem carve(uint8_t* base, int ns, int chunks, int nu) {
     LinearSmem s;
-    const int groups = chunks * 8;
-    s.ring = base;
-    uint8_t* p = base + static_cast<size_t>(ns) * kChunkBytes;
+    const size_t groups = static_cast<size_t>(chunks) * 8;
+    uint8_t* p = base;
+    s.ring = p;
+    p += static_cast<size_t>(ns) * kChunkBytes;
     s.full = reinterpret_cast<uint64_t*>(p);
     s.empty = s.full + ns;
-    p += 2 * ns * 8;
+    p += align16(2 * static_cast<size_t>(ns) * 8);
     s.act_hi = reinterpret_cast<int8_t*>(p);
     s.act_lo = reinterpret_cast<uint8_t*>(p + groups * 32);
-    p += groups * 64;
+    p += align16(groups * 64);
     s.corr = reinterpret_cast<int*>(p);
     s.act_scale = reinterpret_cast<float*>(p + groups * 4);
-    p += groups * 8;
+    p += align16(groups * 8);
     s.contrib = reinterpret_cast<float*>(p);
+    p += static_cast<size_t>(nu) * groups * 32 * 4;
+    s.unit_cnt = reinterpret_cast<int*>(p);
+    s.slot_ok = s.unit_cnt + nu;
+    p += align16(2 * static_cast<size_t>(nu) * 4);
+    s.fin = reinterpret_cast<int*>(p);
     return s;
 }
 
@@ -133,30 +148,62 @@ __device__ __forceinline__ int group_dot(uint4 w, const int8_t* hi, const uint8_
     return ((Lh + (Hh >> 4)) << 7) + Ll + (Hl >> 4) - corr;
 }
 
-// Epilogue of one finished unit, run by the warp that chained it.
-__device__ __noinline__ void linear_epilogue(const LinearArgs& a, int bank, int unit, float acc) {
+// Builds this bank's split activations in shared memory (consumer warps).
+__device__ __forceinline__ void linear_prologue(const LinearArgs& a, const LinearSmem& s, int bank, int cw,
+                                                int lane, int groups) {
+    constexpr int kMaxPer = (kMaxLocalGroups + kConsumerWarps - 1) / kConsumerWarps;  // 11
+    float v[kMaxPer];
+    int qv[kMaxPer];
+    uint32_t ev[kMaxPer];
+    if (a.in_kind == IN_RMS) {
+        const float r = *a.recip;
+        float x[kMaxPer], g[kMaxPer];
+#pragma unroll
+        for (int k = 0; k < kMaxPer; ++k) {
+            const int lg = cw + k * kConsumerWarps;
+            if (lg < groups) {
+                const int col = bank * groups * 32 + lg * 32 + lane;
+                x[k] = a.resid[col];
+                g[k] = a.gamma[col];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kMaxPer; ++k) v[k] = __fmul_rn(__fmul_rn(x[k], r), g[k]);
+#pragma unroll
+        for (int k = 0; k < kMaxPer; ++k) {
+            const int lg = cw + k * kConsumerWarps;
+            if (lg < groups) qv[k] = quantize_g32_lane(v[k], &ev[k]);
+        }
+    } else {
+        const size_t base = static_cast<size_t>(bank) * a.act_bank_stride;
+#pragma unroll
+        for (int k = 0; k < kMaxPer; ++k) {
+            const int lg = cw + k * kConsumerWarps;
+            if (lg < groups) {
+                qv[k] = a.act_q[base + lg * 32 + lane];
+                ev[k] = a.act_e[base / 32 + lg];
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < kMaxPer; ++k) {
+        const int lg = cw + k * kConsumerWarps;
+        if (lg < groups) put_act(s, lg, lane, qv[k], ev[k]);
+    }
+}
+
+// Finalises one stripe once all its bank partials are in (one warp).
+__device__ __noinline__ void linear_finalize(const LinearArgs& a, int stripe, int* level2_last) {
     const int lane = threadIdx.x & 31;
     const int rows_total = a.units * 32;
-    a.partials[static_cast<size_t>(bank) * rows_total + unit * 32 + lane] = acc;
-    if (a.epi == EPI_PARTIAL) return;
-    __threadfence();
-    __syncwarp();
-    const int stripes = a.epi == EPI_SWIGLU ? a.units / 2 : a.units;
-    const int stripe = unit % stripes;
-    const unsigned need = static_cast<unsigned>(a.epi == EPI_SWIGLU ? 2 * a.nbanks : a.nbanks);
-    unsigned old = 0;
-    if (lane == 0) old = atomicAdd(&a.counters[stripe], 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old + 1 != need) return;
-    __threadfence();
-    if (lane == 0) a.counters[stripe] = 0;
     const float* P = a.partials;
     if (a.epi == EPI_STORE) {
         const int row = stripe * 32 + lane;
-        a.out[row] = a.nbanks == 4 ? combine4(P, rows_total, row) : P[row];
+        a.out[row] = a.nbanks == 4 ? combine4(P, rows_total, row) : __ldcg(P + row);
         return;
     }
     if (a.epi == EPI_SWIGLU) {
+        const int stripes = a.units / 2;
         const int gr = stripe * 32 + lane, ur = (stripes + stripe) * 32 + lane;
         const float g = combine4(P, rows_total, gr);
         const float u = combine4(P, rows_total, ur);
@@ -166,24 +213,26 @@ __device__ __noinline__ void linear_epilogue(const LinearArgs& a, int bank, int 
         if (lane == 0) a.e_out[stripe] = static_cast<uint8_t>(e8);
         return;
     }
-    // EPI_RESID: residual += y, then the RMS reciprocal once every stripe is in.
+    // EPI_RESID: residual += y; the last stripe overall triggers the RMS.
     const int row = stripe * 32 + lane;
-    a.out[row] = __fadd_rn(a.out[row], combine4(P, rows_total, row));
+    a.out[row] = __fadd_rn(__ldcg(a.out + row), combine4(P, rows_total, row));
     __threadfence();
     __syncwarp();
+    unsigned old = 0;
     if (lane == 0) old = atomicAdd(&a.counters[kCounterLevel2], 1u);
     old = __shfl_sync(0xffffffffu, old, 0);
-    if (old + 1 != static_cast<unsigned>(stripes)) return;
-    __threadfence();
-    if (lane == 0) a.counters[kCounterLevel2] = 0;
-    const float r = rms_recip_warp(a.out);
-    if (lane == 0) *a.recip_out = r;
+    if (old + 1 == static_cast<unsigned>(a.units)) {
+        if (lane == 0) {
+            a.counters[kCounterLevel2] = 0;
+            *level2_last = 1;
+        }
+    }
 }
 
-__global__ void __launch_bounds__(kLinearThreads, 2) k_linear(const LinearArgs a) {
+__global__ void __launch_bounds__(kLinearThreads, 2) k_linear(const __grid_constant__ LinearArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int groups = a.chunks * 8;
-    LinearSmem s = carve(smem_raw, a.ns, a.chunks);
+    LinearSmem s = carve(smem_raw, a.ns, a.chunks, a.nu);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bank = blockIdx.x / a.cpb, c = blockIdx.x % a.cpb;
     const int u0 = static_cast<int>((static_cast<long long>(c) * a.units) / a.cpb);
@@ -193,10 +242,15 @@ __global__ void __launch_bounds__(kLinearThreads, 2) k_linear(const LinearArgs a
     if (threadIdx.x == 0) {
         for (int i = 0; i < a.ns; ++i) {
             mbar_init(&s.full[i], 1);
-            mbar_init(&s.empty[i], kConsumerWarps);
+            mbar_init(&s.empty[i], 1);
         }
         mbar_fence_init();
     }
+    if (threadIdx.x < a.nu) {
+        s.unit_cnt[threadIdx.x] = 0;
+        s.slot_ok[threadIdx.x] = threadIdx.x;
+    }
+    if (threadIdx.x < 2) s.fin[threadIdx.x] = 0;
     __syncthreads();
     pdl_trigger();
 
@@ -219,49 +273,107 @@ __global__ void __launch_bounds__(kLinearThreads, 2) k_linear(const LinearArgs a
         return;
     }
 
-    // Consumers.
-    pdl_wait();
+    // Consumers: warp cw takes chunks cw, cw+8, ... whole (8 groups x 32 rows).
     const int cw = warp - 1;
-    for (int lg = cw; lg < groups; lg += kConsumerWarps) {
-        uint32_t e8;
-        int q;
-        if (a.in_kind == IN_RMS) {
-            const int col = bank * groups * 32 + lg * 32 + lane;
-            const float v = __fmul_rn(__fmul_rn(a.resid[col], *a.recip), a.gamma[col]);
-            q = quantize_g32_lane(v, &e8);
-        } else {
-            const size_t base = static_cast<size_t>(bank) * a.act_bank_stride;
-            q = a.act_q[base + lg * 32 + lane];
-            e8 = a.act_e[base / 32 + lg];
-        }
-        put_act(s, lg, lane, q, e8);
-    }
+    pdl_wait();
+    linear_prologue(a, s, bank, cw, lane, groups);
     consumer_bar();
 
-    int slot = 0;
-    uint32_t phase = 0;
-    for (int u = u0; u < u1; ++u) {
-        float* contrib = s.contrib + ((u - u0) & 1) * groups * 32;
-        for (int j = 0; j < a.chunks; ++j) {
-            mbar_wait(&s.full[slot], phase, a.err, kErrWaitFull);
-            const uint8_t* ch = s.ring + static_cast<size_t>(slot) * kChunkBytes;
-            const int lg = j * 8 + cw;
-            const uint4 wv = *reinterpret_cast<const uint4*>(ch + kChunkScaleBytes + (cw * 32 + lane) * 16);
-            const int16_t raw = reinterpret_cast<const int16_t*>(ch)[lane * 2 + (cw >> 2)];
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s.empty[slot]);
-            const int dot = group_dot(wv, s.act_hi + lg * 32, s.act_lo + lg * 32, s.corr[lg]);
-            const float ws = __fmul_rn(static_cast<float>(raw), 1.0f / 32768.0f);
-            contrib[lg * 32 + lane] = __fmul_rn(static_cast<float>(dot), __fmul_rn(ws, s.act_scale[lg]));
-            if (++slot == a.ns) { slot = 0; phase ^= 1u; }
+    const int rows_total = a.units * 32;
+    for (int i = cw; i < nchunks; i += kConsumerWarps) {
+        const int slot = i % a.ns;
+        mbar_wait(&s.full[slot], static_cast<uint32_t>((i / a.ns) & 1), a.err, kErrWaitFull);
+        const uint8_t* ch = s.ring + static_cast<size_t>(slot) * kChunkBytes;
+        uint4 wv[8];
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+            wv[g] = *reinterpret_cast<const uint4*>(ch + kChunkScaleBytes + (g * 32 + lane) * 16);
+        const int16_t raw0 = reinterpret_cast<const int16_t*>(ch)[lane * 2];
+        const int16_t raw1 = reinterpret_cast<const int16_t*>(ch)[lane * 2 + 1];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.empty[slot]);
+
+        const int uidx = i / a.chunks, j = i - uidx * a.chunks;
+        const int us = uidx % a.nu;
+        // Contribution slot `us` is free once unit uidx - nu has been chained.
+        if (*reinterpret_cast<volatile int*>(&s.slot_ok[us]) < uidx) {
+            uint32_t spins = 0;
+            while (*reinterpret_cast<volatile int*>(&s.slot_ok[us]) < uidx) {
+                __nanosleep(64);
+                if (++spins > (1u << 24)) { atomicOr(a.err, kErrWaitFull); break; }
+            }
         }
-        consumer_bar();
-        if (cw == ((u - u0) & (kConsumerWarps - 1))) {
-            float acc = contrib[lane];
+        float* cb = s.contrib + static_cast<size_t>(us) * groups * 32;
+        const float ws0 = __fmul_rn(static_cast<float>(raw0), 1.0f / 32768.0f);
+        const float ws1 = __fmul_rn(static_cast<float>(raw1), 1.0f / 32768.0f);
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const int lg = j * 8 + g;
+            const int dot = group_dot(wv[g], s.act_hi + lg * 32, s.act_lo + lg * 32, s.corr[lg]);
+            cb[lg * 32 + lane] = __fmul_rn(static_cast<float>(dot), __fmul_rn(g < 4 ? ws0 : ws1, s.act_scale[lg]));
+        }
+        __syncwarp();
+        __threadfence_block();
+        int old = 0;
+        if (lane == 0) old = atomicAdd(&s.unit_cnt[us], 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old == a.chunks - 1) {
+            // Last chunk of the unit: FP32 chain in local-group order.
+            __threadfence_block();
+            float acc = cb[lane];
             if (!a.hls_zero) acc = __fadd_rn(0.0f, acc);
-            for (int lg = 1; lg < groups; ++lg) acc = __fadd_rn(acc, contrib[lg * 32 + lane]);
-            linear_epilogue(a, bank, u, acc);
+            for (int lg = 1; lg < groups; ++lg) acc = __fadd_rn(acc, cb[lg * 32 + lane]);
+            a.partials[static_cast<size_t>(bank) * rows_total + static_cast<size_t>(u0 + uidx) * 32 + lane] = acc;
+            __syncwarp();
+            __threadfence_block();
+            if (lane == 0) {
+                s.unit_cnt[us] = 0;
+                *reinterpret_cast<volatile int*>(&s.slot_ok[us]) = uidx + a.nu;
+            }
         }
+    }
+    if (a.epi == EPI_PARTIAL) return;
+
+    // End of this CTA's stage: one counter add per stripe it touched; the CTA
+    // that completes a stripe (all banks) finalises it.
+    __threadfence();
+    consumer_bar();
+    const int stripes = a.epi == EPI_SWIGLU ? a.units / 2 : a.units;
+    const unsigned need = static_cast<unsigned>(a.epi == EPI_SWIGLU ? 2 * a.nbanks : a.nbanks);
+    if (cw == 0) {
+        for (int b = u0; b < u1; b += 32) {
+            const int u = b + lane;
+            if (u < u1) {
+                const int stripe = u % stripes;
+                const unsigned old = atomicAdd(&a.counters[stripe], 1u);
+                if (old + 1 == need) {
+                    a.counters[stripe] = 0;
+                    const int k = atomicAdd(&s.fin[0], 1);
+                    if (k < kFinMax) s.fin[2 + k] = stripe;
+                    else atomicOr(a.err, kErrArg);
+                }
+            }
+        }
+        __threadfence();
+    }
+    consumer_bar();
+    const int nfin = min(s.fin[0], kFinMax);
+    for (int k = cw; k < nfin; k += kConsumerWarps) linear_finalize(a, s.fin[2 + k], &s.fin[1]);
+    if (a.epi != EPI_RESID) return;
+    consumer_bar();
+    if (s.fin[1] == 0) return;
+    // Last stripe of the whole residual: RMS reciprocal for the next norm.
+    __threadfence();
+    float* xs = reinterpret_cast<float*>(s.ring);
+    const int t = threadIdx.x - 32;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        reinterpret_cast<float4*>(xs)[t + k * 256] =
+            __ldcg(reinterpret_cast<const float4*>(a.out) + t + k * 256);
+    consumer_bar();
+    if (cw == 0) {
+        const float r = rms_recip_warp(xs);
+        if (lane == 0) *a.recip_out = r;
     }
 }
 

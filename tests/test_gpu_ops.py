@@ -164,3 +164,61 @@ def test_attention_long_context(ctx, oracle, rope_tables, length):
     oq, oe = oracle.attention(kv, 2, 4096, 0, pos, oracle.rope(q, rope_tables, pos),
                               oracle.rope(k, rope_tables, pos), v)
     assert np.array_equal(gq, oq) and np.array_equal(ge, oe)
+
+
+def _write_records(ctx, kv, layer, records_by_head):
+    for head, recs in records_by_head.items():
+        bank, lh = divmod(head, 8)
+        base = (((bank * 2) + layer) * 8 + lh) * 4096 * 320
+        for t, rec in enumerate(recs):
+            kv[base + t * 320: base + (t + 1) * 320] = rec
+            ctx.kv_write(bank, layer, lh, t, rec)
+
+
+def _record(k8, ks, v8, vs):
+    rec = np.zeros(320, np.uint8)
+    meta = 0
+    for g in range(4):
+        meta |= (ks[g] & 31) << (5 * g)
+        meta |= (vs[g] & 31) << (20 + 5 * g)
+    rec[:5] = np.frombuffer(meta.to_bytes(8, "little")[:5], np.uint8)
+    rec[64:192] = np.asarray(k8, np.int8).view(np.uint8)
+    rec[192:320] = np.asarray(v8, np.int8).view(np.uint8)
+    return rec
+
+
+def test_attention_many_rescale_events(ctx, oracle, rope_tables):
+    """Scores that rise every other token: more than 16 rescale events, so the
+    kernel takes its fully sequential path."""
+    rng = np.random.default_rng(9)
+    pos = 40
+    q = rng.integers(-1024, 1024, 4096).astype(np.int32)
+    qr = oracle.rope(q, rope_tables, pos)
+    kv = oracle.kv_store(2, 4096)
+    recs = {}
+    for head in (0, 9, 31):
+        k8 = np.where(qr[head * 128:(head + 1) * 128] >= 0, 100, -100)
+        recs[head] = [_record(k8, [10 + t // 2] * 4, rng.integers(-127, 128, 128), [3] * 4) for t in range(pos)]
+    _write_records(ctx, kv, 1, recs)
+    k, v = (_rand_q17(rng, 4096, 0.01) for _ in range(2))
+    gq, ge = ctx.attention(1, pos, q, k, v)
+    oq, oe = oracle.attention(kv, 2, 4096, 1, pos, qr, oracle.rope(k, rope_tables, pos), v)
+    assert np.array_equal(gq, oq) and np.array_equal(ge, oe)
+
+
+def test_attention_saturating_state(ctx, oracle, rope_tables):
+    """Equal scores and large values: the per-step int32 saturation of the
+    state chain triggers, so the kernel replays the segment sequentially."""
+    rng = np.random.default_rng(10)
+    pos = 60
+    kv = oracle.kv_store(2, 4096)
+    recs = {}
+    for head in (1, 17):
+        k8 = rng.integers(-5, 6, 128)
+        recs[head] = [_record(k8, [2] * 4, [100] * 128, [24] * 4) for _ in range(pos)]
+    _write_records(ctx, kv, 0, recs)
+    q, k, v = (_rand_q17(rng, 4096, 0.01) for _ in range(3))
+    gq, ge = ctx.attention(0, pos, q, k, v)
+    oq, oe = oracle.attention(kv, 2, 4096, 0, pos, oracle.rope(q, rope_tables, pos),
+                              oracle.rope(k, rope_tables, pos), v)
+    assert np.array_equal(gq, oq) and np.array_equal(ge, oe)
