@@ -191,6 +191,7 @@ def test_attention_many_rescale_events(ctx, oracle, rope_tables):
     """Scores that rise every other token: more than 16 rescale events, so the
     kernel takes its fully sequential path."""
     rng = np.random.default_rng(9)
+    ctx.kv_reset()
     pos = 40
     q = rng.integers(-1024, 1024, 4096).astype(np.int32)
     qr = oracle.rope(q, rope_tables, pos)
@@ -210,6 +211,7 @@ def test_attention_saturating_state(ctx, oracle, rope_tables):
     """Equal scores and large values: the per-step int32 saturation of the
     state chain triggers, so the kernel replays the segment sequentially."""
     rng = np.random.default_rng(10)
+    ctx.kv_reset()
     pos = 60
     kv = oracle.kv_store(2, 4096)
     recs = {}
