@@ -23,6 +23,7 @@ LIB_PATH = os.path.join(_HERE, "libi4d.so")
 OK, ERR_ARG, ERR_SIZE, ERR_CUDA, ERR_TIMEOUT, ERR_STATE, ERR_NOMEM = range(7)
 FLAG_NO_GRAPH = 1
 FLAG_NO_PDL = 2
+FLAG_STAGED = 4
 
 # Every symbol include/i4d.h declares.
 EXPORTS = [
@@ -33,7 +34,7 @@ EXPORTS = [
     "i4d_profile_token",
 ]
 
-KERNEL_CLASSES = ["qkv_gemv", "attention", "o_gemv", "gate_up_gemv", "down_gemv", "logits_gemv", "rms"]
+KERNEL_CLASSES = ["qkv_gemv", "attention", "o_gemv", "gate_up_gemv", "down_gemv", "logits_gemv", "rms", "token"]
 
 
 class I4DError(RuntimeError):
@@ -164,8 +165,8 @@ class Context:
         return self._L.i4d_stream(self._h)
 
     def profile_token(self, position, residual_in_dev_ptr):
-        ms = np.zeros(7, np.float32)
-        n = np.zeros(7, np.uint32)
+        ms = np.zeros(8, np.float32)
+        n = np.zeros(8, np.uint32)
         self._check(self._L.i4d_profile_token(self._h, position, residual_in_dev_ptr, ms.ctypes.data, n.ctypes.data))
         return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(KERNEL_CLASSES)}
 

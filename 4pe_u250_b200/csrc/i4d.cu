@@ -20,6 +20,7 @@
 #include "i4d_attention.cuh"
 #include "i4d_blocks.cuh"
 #include "i4d_linear.cuh"
+#include "i4d_token.cuh"
 
 extern "C" {
 extern const unsigned int i4d_expf_fix_count;
@@ -112,7 +113,9 @@ struct i4d_ctx {
     unsigned* d_counters = nullptr;
     unsigned* d_err = nullptr;
     int* d_pos = nullptr;
-    uint32_t* d_attn_coef = nullptr;  // [32][stride] attention coefficients
+    uint32_t* d_attn_coef = nullptr;  // [128][stride] attention coefficients
+    unsigned* d_sync = nullptr;       // persistent-kernel synchronisation words
+    float* d_recips = nullptr;        // [65] RMS reciprocal of every norm of a token
     float* d_scratch = nullptr;  // op-level staging, 3 x 32256 floats
     // pinned staging for the decode contract
     float* h_resid_in = nullptr;
@@ -231,7 +234,7 @@ AttnArgs base_attn(i4d_ctx* c, int layer) {
     return a;
 }
 
-enum KernelClass { KC_QKV = 0, KC_ATTN, KC_O, KC_GU, KC_DOWN, KC_LOGITS, KC_RMS, KC_COUNT };
+enum KernelClass { KC_QKV = 0, KC_ATTN, KC_O, KC_GU, KC_DOWN, KC_LOGITS, KC_RMS, KC_TOKEN, KC_COUNT };
 
 cudaError_t prof_begin(i4d_ctx* c, int cls) {
     if (!c->profiling || c->prof_n >= 256) return cudaSuccess;
@@ -251,8 +254,54 @@ cudaError_t prof_end(i4d_ctx* c) {
         CK(prof_end(c));        \
     } while (0)
 
+TokenArgs token_args(i4d_ctx* c) {
+    TokenArgs t = {};
+    t.w = c->d_w;
+    t.layer_bytes = stage_offset(c, 1, ST_QKV);
+    for (int st = 0; st < ST_COUNT; ++st) {
+        t.stage_off[st] = st == ST_LOGITS ? stage_offset(c, 0, ST_LOGITS) : stage_offset(c, 0, st);
+        t.bank_bytes[st] = stage_bank_bytes(st);
+    }
+    t.layers = c->layers;
+    t.cpb = c->cpb;
+    t.resid = c->d_resid;
+    t.recip = c->d_recips;
+    t.gamma = c->d_gamma;
+    t.partials = c->d_partials;
+    t.ao_q = c->d_ao_q;
+    t.ao_e = c->d_ao_e;
+    t.ad_q = c->d_ad_q;
+    t.ad_e = c->d_ad_e;
+    t.logits = c->d_logits;
+    t.counters = c->d_counters;
+    t.sync = c->d_sync;
+    t.attn = base_attn(c, 0);
+    t.expf = c->expf;
+    t.err = c->d_err;
+    return t;
+}
+
+// One token as a single cooperative launch of the persistent kernel.
+cudaError_t launch_token(i4d_ctx* c) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(4 * c->cpb);
+    cfg.blockDim = dim3(kTokThreads);
+    cfg.dynamicSmemBytes = tok_smem_bytes();
+    cfg.stream = c->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_token, token_args(c));
+}
+
 // The kernels of one token (position and residual already in device memory).
 i4d_status enqueue_token(i4d_ctx* c) {
+    if (!(c->flags & I4D_FLAG_STAGED)) {
+        TIMED(KC_TOKEN, launch_token(c));
+        return I4D_OK;
+    }
     TIMED(KC_RMS, launch(c, false, k_rms_recip, dim3(1), dim3(32), 0, (const float*)c->d_resid, c->d_recip));
     for (int l = 0; l < c->layers; ++l) {
         LinearArgs q = base_linear(c, l, ST_QKV);
@@ -324,6 +373,7 @@ i4d_status finish(i4d_ctx* c) {
     CK(cudaMemcpy(&e, c->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost));
     if (e) {
         CK(cudaMemset(c->d_err, 0, sizeof(unsigned)));
+        CK(cudaMemset(c->d_sync, 0, kSyncWords * sizeof(unsigned)));
         if (e & kErrArg) return fail(c, I4D_ERR_ARG, "device rejected an argument (error word 0x%x)", e);
         return fail(c, I4D_ERR_TIMEOUT, "a bounded device wait gave up (error word 0x%x)", e);
     }
@@ -351,7 +401,7 @@ void i4d_destroy(i4d_ctx* c) {
         if (ev) cudaEventDestroy(ev);
     void* dev[] = {c->d_w, c->d_gamma, c->d_rope_cos, c->d_rope_sin, c->d_exp2, c->d_expf_slots, c->d_kv,
                    c->d_emb, c->d_resid, c->d_recip, c->d_partials, c->d_ao_q, c->d_ao_e, c->d_ad_q,
-                   c->d_ad_e, c->d_logits, c->d_counters, c->d_err, c->d_pos, c->d_scratch, c->d_attn_coef};
+                   c->d_ad_e, c->d_logits, c->d_counters, c->d_err, c->d_pos, c->d_scratch, c->d_attn_coef, c->d_sync, c->d_recips};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* host[] = {c->h_resid_in, c->h_resid_out, c->h_logits, c->h_pos, c->h_err};
@@ -395,6 +445,13 @@ i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out) {
     CKC(cudaFuncSetAttribute(k_linear, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBudget)));
     CKC(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(attn_smem_bytes())));
+    CKC(cudaFuncSetAttribute(k_token, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(tok_smem_bytes())));
+    {
+        int per_sm = 0;
+        CKC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_token, kTokThreads, tok_smem_bytes()));
+        if (per_sm < 1 || 4 * c->cpb > c->num_sms) c->flags |= I4D_FLAG_STAGED;
+    }
 
     c->w_bytes = stage_offset(c, 0, ST_LOGITS) + 4 * stage_bank_bytes(ST_LOGITS);
     CKC(cudaMalloc(&c->d_w, c->w_bytes));
@@ -417,7 +474,10 @@ i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out) {
     CKC(cudaMalloc(&c->d_err, sizeof(unsigned)));
     CKC(cudaMemset(c->d_err, 0, sizeof(unsigned)));
     CKC(cudaMalloc(&c->d_pos, sizeof(int)));
-    CKC(cudaMalloc(&c->d_attn_coef, 32ull * c->stride * sizeof(uint32_t)));
+    CKC(cudaMalloc(&c->d_attn_coef, 128ull * c->stride * sizeof(uint32_t)));
+    CKC(cudaMalloc(&c->d_sync, kSyncWords * sizeof(unsigned)));
+    CKC(cudaMemset(c->d_sync, 0, kSyncWords * sizeof(unsigned)));
+    CKC(cudaMalloc(&c->d_recips, 80 * sizeof(float)));
     CKC(cudaMalloc(&c->d_scratch, 3ull * kPVocab * sizeof(float)));
     CKC(cudaMallocHost(&c->h_resid_in, kDim * sizeof(float)));
     CKC(cudaMallocHost(&c->h_resid_out, kDim * sizeof(float)));
@@ -582,6 +642,7 @@ i4d_status i4d_decode_token(i4d_ctx* c, uint32_t position, const float* residual
     if (*c->h_err) {
         const unsigned e = *c->h_err;
         CK(cudaMemset(c->d_err, 0, sizeof(unsigned)));
+        CK(cudaMemset(c->d_sync, 0, kSyncWords * sizeof(unsigned)));
         return fail(c, (e & kErrArg) ? I4D_ERR_ARG : I4D_ERR_TIMEOUT, "device error word 0x%x", e);
     }
     std::memcpy(logits_out, c->h_logits, kPVocab * sizeof(float));

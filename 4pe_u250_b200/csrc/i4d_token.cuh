@@ -1,0 +1,895 @@
+// i4d_token.cuh -- the whole decode step as one persistent kernel.
+//
+// Replaces the 4-CU control plane and the per-PE token schedule of the
+// reference (int4_decoder_multikernel.cpp:70-424, int4_decoder_controller.cpp
+// :138-234): one cooperative launch per token, one CTA per SM.  In every CTA
+// a producer warp streams the CTA's share of ALL the token's weights (each
+// GEMV stage's unit range of the CTA's bank, layer after layer, then the LM
+// head) through a shared-memory ring with 1-D bulk copies; it never waits on
+// activations, so HBM keeps streaming across the dependency points.  Sixteen
+// consumer warps run the stages in order:
+//   QKV GEMV -> attention (128 items: head x 32-dim part) -> O GEMV
+//   (+ residual, RMS) -> GATE/UP GEMV (+ SwiGLU) -> DOWN GEMV (+ residual,
+//   RMS) ... -> LM head,
+// waiting between stages on readiness counters in global memory.  The
+// arithmetic is the per-stage kernels' (i4d_linear.cuh, i4d_attention.cuh),
+// bit-exact with the reference emulator.
+//
+// All CTAs are co-resident (cooperative launch), so the counter waits always
+// end; each wait is still bounded: on timeout it raises the error word and an
+// abort flag that makes every other wait return at once, so the kernel always
+// terminates.
+#pragma once
+
+#include "i4d_attention.cuh"
+#include "i4d_device.cuh"
+#include "i4d_expf.cuh"
+#include "i4d_linear.cuh"
+
+namespace i4d {
+
+constexpr int kTokWarps = 16;
+constexpr int kTokThreads = 32 * (1 + kTokWarps);
+constexpr int kTokRing = 40;               // ring slots of kChunkBytes
+constexpr int kTokUnion = 55296;           // GEMV activations + contributions, or attention scratch
+constexpr int kTokContribBytes = 32768;
+constexpr int kAttnParts = 4;              // 32-dimension parts per head
+constexpr int kAttnItems = kHeads * kAttnParts;
+
+// Global synchronisation words (zeroed by the last CTA at the end of a token).
+constexpr int kSyncAbort = 0;
+constexpr int kSyncExit = 1;
+constexpr int kSyncQkv = 2;        // + layer: CTAs that stored their QKV partials
+constexpr int kSyncAtt = 34;       // + layer: attention items finished
+constexpr int kSyncSwiglu = 66;    // + layer: SwiGLU stripes finalised
+constexpr int kSyncRms = 98;       // + norm index (2l, 2l+1, 2L): RMS reciprocal ready
+constexpr int kSyncWords = 164;
+
+enum TokStage : int { TS_QKV = 0, TS_O, TS_GU, TS_DOWN, TS_LOGITS };
+
+struct TokenArgs {
+    const uint8_t* w;          // GEMV layout
+    size_t layer_bytes;        // bytes of one layer's four stages (all banks)
+    size_t stage_off[5];       // offset of each stage inside its layer (LOGITS: absolute)
+    size_t bank_bytes[5];      // one bank's region of each stage
+    int layers;
+    int cpb;                   // CTAs per bank (gridDim.x == 4 * cpb)
+    float* resid;              // [4096], updated in place
+    float* recip;              // [65]: RMS reciprocal of each norm
+    const float* gamma;        // [65][4096]
+    float* partials;           // [4][32256]
+    int16_t* ao_q;             // attention output
+    uint8_t* ao_e;
+    int16_t* ad_q;             // SwiGLU output
+    uint8_t* ad_e;
+    float* logits;
+    unsigned* counters;        // stripe counters [kCounterSlots]
+    unsigned* sync;            // [kSyncWords]
+    AttnArgs attn;             // position, RoPE, KV, LUT, coefficient scratch
+    ExpfFix expf;
+    unsigned* err;
+};
+
+__host__ __device__ constexpr int stage_units(int st) {
+    return st == TS_QKV ? 384 : st == TS_O ? 128 : st == TS_GU ? 704 : st == TS_DOWN ? 128 : 1008;
+}
+__host__ __device__ constexpr int stage_chunks(int st) { return st == TS_DOWN ? 11 : 4; }
+
+struct TokSmem {
+    uint8_t* ring;
+    uint64_t* full;
+    uint64_t* empty;
+    uint64_t* abar;      // [2] attention tile barriers
+    uint8_t* uni;        // union region
+    int* next;           // dynamic chunk counter
+    int* unit_cnt;       // [8]
+    int* slot_ok;        // [8]
+    int* fin;            // [kFinMax + 2]
+    int* flag;           // [4] misc
+};
+
+__host__ __device__ inline size_t tok_smem_bytes() {
+    return static_cast<size_t>(kTokRing) * kChunkBytes + 2 * kTokRing * 8 + 16 + kTokUnion + 16 + 64 +
+           align16((kFinMax + 2) * 4) + 16;
+}
+
+__device__ __forceinline__ TokSmem tok_carve(uint8_t* p) {
+    TokSmem s;
+    s.ring = p;
+    p += static_cast<size_t>(kTokRing) * kChunkBytes;
+    s.full = reinterpret_cast<uint64_t*>(p);
+    s.empty = s.full + kTokRing;
+    s.abar = s.empty + kTokRing;
+    p += 2 * kTokRing * 8 + 16;
+    s.uni = p;
+    p += kTokUnion;
+    s.next = reinterpret_cast<int*>(p);
+    p += 16;
+    s.unit_cnt = reinterpret_cast<int*>(p);
+    s.slot_ok = s.unit_cnt + 8;
+    p += 64;
+    s.fin = reinterpret_cast<int*>(p);
+    p += align16((kFinMax + 2) * 4);
+    s.flag = reinterpret_cast<int*>(p);
+    return s;
+}
+
+__device__ __forceinline__ void tok_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+
+__device__ __forceinline__ bool aborted(const TokenArgs& a) {
+    return *reinterpret_cast<volatile unsigned*>(&a.sync[kSyncAbort]) != 0;
+}
+
+__device__ __forceinline__ void raise_abort(const TokenArgs& a, unsigned code) {
+    atomicOr(a.err, code);
+    atomicExch(&a.sync[kSyncAbort], 1u);
+}
+
+// Spins (bounded) until *word >= target; false on abort or timeout.
+__device__ bool wait_counter(const TokenArgs& a, const unsigned* word, unsigned target) {
+    for (uint32_t it = 0;; ++it) {
+        if (*reinterpret_cast<const volatile unsigned*>(word) >= target) {
+            __threadfence();
+            return true;
+        }
+        if (aborted(a)) return false;
+        if (it > (1u << 24)) {
+            raise_abort(a, kErrWaitFull);
+            return false;
+        }
+        __nanosleep(it < 64 ? 32 : 256);
+    }
+}
+
+// mbarrier wait that also gives up when the token was aborted.
+__device__ __forceinline__ bool tok_mbar_wait(const TokenArgs& a, uint64_t* bar, uint32_t parity, unsigned code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 15) == 0 && aborted(a)) return false;
+        if (it > (1u << 22)) {
+            raise_abort(a, code);
+            return false;
+        }
+        __nanosleep(64);
+    }
+}
+
+// ------------------------------------------------------------ GEMV stages
+
+struct StageDesc {
+    int st;               // TokStage
+    int layer;
+    int u0, u1;           // this CTA's units in its bank
+    int bank;
+    int gbase;            // global chunk sequence number of the stage's first chunk
+};
+
+__device__ __forceinline__ int stage_stripes(int st) { return st == TS_GU ? 352 : stage_units(st); }
+
+// Linear args view for the shared prologue / finalize helpers.
+__device__ __forceinline__ LinearArgs stage_view(const TokenArgs& a, int st, int layer) {
+    LinearArgs v = {};
+    v.nbanks = 4;
+    v.units = stage_units(st);
+    v.chunks = stage_chunks(st);
+    v.partials = a.partials;
+    v.counters = a.counters;
+    v.expf = a.expf;
+    v.err = a.err;
+    v.hls_zero = 0;
+    if (st == TS_QKV || st == TS_GU || st == TS_LOGITS) {
+        v.in_kind = IN_RMS;
+        v.resid = a.resid;
+        const int norm = st == TS_LOGITS ? 2 * a.layers : (st == TS_QKV ? 2 * layer : 2 * layer + 1);
+        v.gamma = a.gamma + static_cast<size_t>(st == TS_LOGITS ? 64 : (st == TS_QKV ? 2 * layer : 2 * layer + 1)) * kDim;
+        v.recip = a.recip + norm;
+    } else {
+        v.in_kind = IN_ACT;
+        v.act_q = st == TS_O ? a.ao_q : a.ad_q;
+        v.act_e = st == TS_O ? a.ao_e : a.ad_e;
+        v.act_bank_stride = st == TS_O ? 1024 : 2816;
+    }
+    v.epi = st == TS_QKV ? EPI_PARTIAL : st == TS_GU ? EPI_SWIGLU : st == TS_LOGITS ? EPI_STORE : EPI_RESID;
+    v.out = st == TS_LOGITS ? a.logits : a.resid;
+    v.q_out = a.ad_q;
+    v.e_out = a.ad_e;
+    return v;
+}
+
+// Activation prologue of the persistent kernel (cross-CTA data is read at L2).
+template <int C>
+__device__ __forceinline__ void tok_prologue(const LinearArgs& v, const LinearSmem& ls, int bank, int cw, int lane) {
+    constexpr int G = C * 8;
+    constexpr int kPer = (G + kTokWarps - 1) / kTokWarps;
+    int qv[kPer];
+    uint32_t ev[kPer];
+    if (v.in_kind == IN_RMS) {
+        const float r = __ldcg(v.recip);
+        float x[kPer], g[kPer];
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int lg = cw + k * kTokWarps;
+            if (lg < G) {
+                const int col = bank * G * 32 + lg * 32 + lane;
+                x[k] = __ldcg(v.resid + col);
+                g[k] = v.gamma[col];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int lg = cw + k * kTokWarps;
+            if (lg < G) qv[k] = quantize_g32_lane(__fmul_rn(__fmul_rn(x[k], r), g[k]), &ev[k]);
+        }
+    } else {
+        const size_t base = static_cast<size_t>(bank) * v.act_bank_stride;
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const int lg = cw + k * kTokWarps;
+            if (lg < G) {
+                qv[k] = __ldcg(v.act_q + base + lg * 32 + lane);
+                ev[k] = __ldcg(v.act_e + base / 32 + lg);
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const int lg = cw + k * kTokWarps;
+        if (lg < G) put_act(ls, lg, lane, qv[k], ev[k]);
+    }
+}
+
+// One GEMV stage of this CTA: wait for its input, build the split
+// activations, consume the stage's chunks from the ring (dynamic chunk
+// assignment across warps), chain units, then the last-arriver epilogue.
+template <int C>
+__device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s, const StageDesc& d, int cw,
+                                            int lane) {
+    constexpr int G = C * 8;
+    constexpr int NU = kTokContribBytes / (G * 128) > 8 ? 8 : kTokContribBytes / (G * 128);
+    static_assert(NU >= 2, "contribution slots");
+    const unsigned FULL = 0xffffffffu;
+    const LinearArgs v = stage_view(a, d.st, d.layer);
+    LinearSmem ls;
+    ls.act_hi = reinterpret_cast<int8_t*>(s.uni);
+    ls.act_lo = s.uni + G * 32;
+    ls.corr = reinterpret_cast<int*>(s.uni + G * 64);
+    ls.act_scale = reinterpret_cast<float*>(s.uni + G * 68);
+    float* contrib = reinterpret_cast<float*>(s.uni + align16(G * 72));
+    const int tid = cw * 32 + lane;
+
+    // Input readiness.
+    if (tid == 0) {
+        const unsigned* word;
+        unsigned target = 1;
+        if (d.st == TS_QKV) word = &a.sync[kSyncRms + 2 * d.layer];
+        else if (d.st == TS_O) { word = &a.sync[kSyncAtt + d.layer]; target = kAttnItems; }
+        else if (d.st == TS_GU) word = &a.sync[kSyncRms + 2 * d.layer + 1];
+        else if (d.st == TS_DOWN) { word = &a.sync[kSyncSwiglu + d.layer]; target = 352; }
+        else word = &a.sync[kSyncRms + 2 * a.layers];
+        wait_counter(a, word, target);
+        *s.next = 0;
+        s.fin[0] = 0;
+        s.fin[1] = 0;
+    }
+    if (tid < NU) {
+        s.unit_cnt[tid] = 0;
+        s.slot_ok[tid] = tid;
+    }
+    tok_bar();
+    tok_prologue<C>(v, ls, d.bank, cw, lane);
+    tok_bar();
+
+    const int nchunks = (d.u1 - d.u0) * C;
+    const int rows_total = stage_units(d.st) * 32;
+    for (;;) {
+        int i = 0;
+        if (lane == 0) i = atomicAdd(s.next, 1);
+        i = __shfl_sync(FULL, i, 0);
+        if (i >= nchunks) break;
+        const int gi = d.gbase + i;
+        const int slot = gi % kTokRing;
+        tok_mbar_wait(a, &s.full[slot], static_cast<uint32_t>((gi / kTokRing) & 1), kErrWaitFull);
+        const uint8_t* ch = s.ring + static_cast<size_t>(slot) * kChunkBytes;
+        uint4 wv[8];
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+            wv[g] = *reinterpret_cast<const uint4*>(ch + kChunkScaleBytes + (g * 32 + lane) * 16);
+        const int16_t raw0 = reinterpret_cast<const int16_t*>(ch)[lane * 2];
+        const int16_t raw1 = reinterpret_cast<const int16_t*>(ch)[lane * 2 + 1];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.empty[slot]);
+
+        const int uidx = i / C, j = i - uidx * C;
+        const int us = uidx % NU;
+        if (*reinterpret_cast<volatile int*>(&s.slot_ok[us]) < uidx) {
+            for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.slot_ok[us]) < uidx; ++it) {
+                __nanosleep(32);
+                if ((it & 63) == 0 && aborted(a)) break;
+                if (it > (1u << 24)) {
+                    raise_abort(a, kErrWaitFull);
+                    break;
+                }
+            }
+        }
+        float* cb = contrib + us * G * 32;
+        const float ws0 = __fmul_rn(static_cast<float>(raw0), 1.0f / 32768.0f);
+        const float ws1 = __fmul_rn(static_cast<float>(raw1), 1.0f / 32768.0f);
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const int lg = j * 8 + g;
+            const int dot = group_dot(wv[g], ls.act_hi + lg * 32, ls.act_lo + lg * 32, ls.corr[lg]);
+            cb[lg * 32 + lane] = __fmul_rn(static_cast<float>(dot), __fmul_rn(g < 4 ? ws0 : ws1, ls.act_scale[lg]));
+        }
+        __syncwarp();
+        __threadfence_block();
+        int old = 0;
+        if (lane == 0) old = atomicAdd(&s.unit_cnt[us], 1);
+        old = __shfl_sync(FULL, old, 0);
+        if (old == C - 1) {
+            __threadfence_block();
+            float acc = __fadd_rn(0.0f, cb[lane]);
+#pragma unroll 8
+            for (int lg = 1; lg < G; ++lg) acc = __fadd_rn(acc, cb[lg * 32 + lane]);
+            a.partials[static_cast<size_t>(d.bank) * rows_total + static_cast<size_t>(d.u0 + uidx) * 32 + lane] = acc;
+            __syncwarp();
+            __threadfence_block();
+            if (lane == 0) {
+                s.unit_cnt[us] = 0;
+                *reinterpret_cast<volatile int*>(&s.slot_ok[us]) = uidx + NU;
+            }
+        }
+    }
+    __threadfence();
+    tok_bar();
+
+    if (d.st == TS_QKV) {
+        if (tid == 0) atomicAdd(&a.sync[kSyncQkv + d.layer], 1u);
+        return;
+    }
+    // Last-arriver epilogue over the stripes this CTA touched.
+    const int stripes = stage_stripes(d.st);
+    const unsigned need = d.st == TS_GU ? 8u : 4u;
+    if (cw == 0) {
+        for (int b = d.u0; b < d.u1; b += 32) {
+            const int u = b + lane;
+            if (u < d.u1) {
+                const int stripe = u % stripes;
+                const unsigned old = atomicAdd(&a.counters[stripe], 1u);
+                if (old + 1 == need) {
+                    a.counters[stripe] = 0;
+                    const int k = atomicAdd(&s.fin[0], 1);
+                    if (k < kFinMax) s.fin[2 + k] = stripe;
+                    else atomicOr(a.err, kErrArg);
+                }
+            }
+        }
+        __threadfence();
+    }
+    tok_bar();
+    const int nfin = min(s.fin[0], kFinMax);
+    for (int k = cw; k < nfin; k += kTokWarps) {
+        linear_finalize(v, s.fin[2 + k], &s.fin[1]);
+        if (d.st == TS_GU) {
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) atomicAdd(&a.sync[kSyncSwiglu + d.layer], 1u);
+        }
+    }
+    if (d.st != TS_O && d.st != TS_DOWN) {
+        tok_bar();
+        return;
+    }
+    tok_bar();
+    if (s.fin[1] != 0) {
+        // This CTA finalised the last residual stripe: RMS reciprocal.
+        float* xs = reinterpret_cast<float*>(s.uni);
+        for (int k = tid; k < kDim / 4; k += 32 * kTokWarps)
+            reinterpret_cast<float4*>(xs)[k] = __ldcg(reinterpret_cast<const float4*>(a.resid) + k);
+        tok_bar();
+        if (cw == 0) {
+            const int norm = d.st == TS_O ? 2 * d.layer + 1 : 2 * d.layer + 2;
+            const float r = rms_recip_warp(xs);
+            if (lane == 0) {
+                a.recip[norm] = r;
+                __threadfence();
+                atomicExch(&a.sync[kSyncRms + norm], 1u);
+            }
+        }
+    }
+    tok_bar();
+}
+
+// ------------------------------------------------------------ attention item
+
+// Scratch of one attention item inside the union region.
+struct TokAttnSmem {
+    uint8_t* tile[2];     // kTile records each
+    uint8_t* cur;         // current token's record
+    int32_t* score;       // [kTile]
+    uint32_t* coef;       // [kTile]
+    int32_t* seg;         // [kTile]
+    unsigned long long* zbin;  // [kMaxSeg]
+    long long* sbin;      // [kMaxSeg][32]
+    long long* abin;      // [kMaxSeg][32]
+    int32_t* ev_v;        // [kMaxSeg][32]; the first 1 KB doubles as RoPE scratch
+    uint32_t* ev_c;       // [kMaxSeg]
+    int32_t* ev_tok;      // [kMaxSeg]
+    int32_t* qrot;        // [128]
+    int32_t* krot;        // [128]
+    int* misc;            // [16]
+};
+
+__device__ __forceinline__ TokAttnSmem tok_attn_carve(uint8_t* p) {
+    TokAttnSmem s;
+    s.tile[0] = p;
+    s.tile[1] = p + kTile * 320;
+    s.cur = p + 2 * kTile * 320;
+    p += 2 * kTile * 320 + 320;
+    s.score = reinterpret_cast<int32_t*>(p);
+    s.coef = reinterpret_cast<uint32_t*>(p + kTile * 4);
+    s.seg = reinterpret_cast<int32_t*>(p + kTile * 8);
+    p += kTile * 12;
+    s.zbin = reinterpret_cast<unsigned long long*>(p);
+    p += kMaxSeg * 8;
+    s.sbin = reinterpret_cast<long long*>(p);
+    p += kMaxSeg * 32 * 8;
+    s.abin = reinterpret_cast<long long*>(p);
+    p += kMaxSeg * 32 * 8;
+    s.ev_v = reinterpret_cast<int32_t*>(p);
+    p += kMaxSeg * 32 * 4;
+    s.ev_c = reinterpret_cast<uint32_t*>(p);
+    p += kMaxSeg * 4;
+    s.ev_tok = reinterpret_cast<int32_t*>(p);
+    p += kMaxSeg * 4;
+    s.qrot = reinterpret_cast<int32_t*>(p);
+    p += 128 * 4;
+    s.krot = reinterpret_cast<int32_t*>(p);
+    p += 128 * 4;
+    s.misc = reinterpret_cast<int*>(p);
+    return s;
+}
+static_assert(2 * kTile * 320 + 320 + kTile * 12 + kMaxSeg * 8 + 2 * kMaxSeg * 32 * 8 + kMaxSeg * 32 * 4 +
+                  2 * kMaxSeg * 4 + 2 * 128 * 4 + 16 * 4 <= kTokUnion,
+              "attention scratch exceeds the union region");
+
+// Attention of one (head, 32-dimension part) item: the same parallel exact
+// algorithm as k_attention, with the state chains of 32 dimensions.
+__device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s, int layer, int item, int cw,
+                                           int lane) {
+    const unsigned FULL = 0xffffffffu;
+    const uint32_t M30 = (1u << 30) - 1u;
+    AttnArgs a = ta.attn;
+    a.layer = layer;
+    const int h = item / kAttnParts, part = item % kAttnParts;
+    const int tid = cw * 32 + lane;
+    TokAttnSmem S = tok_attn_carve(s.uni);
+    int* misc = S.misc;
+    uint32_t* coef_g = a.coef_scratch + static_cast<size_t>(item) * a.stride;
+    const uint32_t* lut = a.exp2_q30;
+
+    const int pos = *a.pos_ptr;
+    const int n = pos + 1;
+    const int ntiles = (n + kTile - 1) / kTile;
+    const uint8_t* head_base = kv_record(a, h, 0);
+    if (tid == 0) {
+        mbar_init(&s.abar[0], 1);
+        mbar_init(&s.abar[1], 1);
+        mbar_fence_init();
+        misc[0] = INT32_MIN;
+        misc[1] = 0;
+    }
+    if (tid < kMaxSeg) S.zbin[tid] = 0;
+    for (int i = tid; i < kMaxSeg * 32; i += 32 * kTokWarps) {
+        S.sbin[i] = 0;
+        S.abin[i] = 0;
+    }
+    tok_bar();
+    if (tid == 0) {
+        // Cached records of earlier tokens are final: stream the first tile
+        // while the other CTAs finish the QKV projection.
+        const int cnt = min(kTile, n);
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&s.abar[0], cnt * 320);
+        bulk_g2s(S.tile[0], head_base, cnt * 320, &s.abar[0]);
+        wait_counter(ta, &ta.sync[kSyncQkv + layer], gridDim.x);
+    }
+    tok_bar();
+
+    // Current token: Q/K/V rows of the head, RoPE, KV record.
+    const int d = tid & 127;
+    int32_t qv = 0, kv = 0, vv = 0;
+    if (tid < 128) {
+        const int row = h * kHeadDim + d;
+        qv = float_to_q17(combine4(a.partials, 3 * kDim, row));
+        kv = float_to_q17(combine4(a.partials, 3 * kDim, kDim + row));
+        vv = float_to_q17(combine4(a.partials, 3 * kDim, 2 * kDim + row));
+        S.qrot[d] = qv;
+        S.krot[d] = kv;
+    }
+    tok_bar();
+    if (tid < 128) {
+        const int pr = d >> 1;
+        const long long c = a.rope_cos[pos * 64 + pr], sn = a.rope_sin[pos * 64 + pr];
+        const long long qa = S.qrot[2 * pr], qb = S.qrot[2 * pr + 1];
+        const long long ka = S.krot[2 * pr], kb = S.krot[2 * pr + 1];
+        qv = (d & 1) ? sat32((qa * sn + qb * c) >> 17) : sat32((qa * c - qb * sn) >> 17);
+        kv = (d & 1) ? sat32((ka * sn + kb * c) >> 17) : sat32((ka * c - kb * sn) >> 17);
+    }
+    tok_bar();
+    uint8_t* grec = kv_record(a, h, pos);
+    if (tid < 128) {
+        S.qrot[d] = qv;
+        const uint32_t kmag = static_cast<uint32_t>(kv < 0 ? -static_cast<long long>(kv) : kv);
+        const uint32_t vmag = static_cast<uint32_t>(vv < 0 ? -static_cast<long long>(vv) : vv);
+        const uint32_t ks = kv_shift_of(__reduce_max_sync(FULL, kmag));
+        const uint32_t vs = kv_shift_of(__reduce_max_sync(FULL, vmag));
+        const uint8_t k8 = static_cast<uint8_t>(kv_quant(kv, ks)), v8 = static_cast<uint8_t>(kv_quant(vv, vs));
+        S.cur[64 + d] = k8;
+        S.cur[192 + d] = v8;
+        if (part == 0) {
+            grec[64 + d] = k8;
+            grec[192 + d] = v8;
+        }
+        if (lane == 0) {
+            misc[8 + cw] = static_cast<int>(ks);
+            misc[12 + cw] = static_cast<int>(vs);
+        }
+    }
+    tok_bar();
+    if (tid < 8) {
+        unsigned long long meta = 0;
+        if (tid == 0)
+            for (int g = 0; g < 4; ++g) {
+                meta |= static_cast<unsigned long long>(misc[8 + g]) << (5 * g);
+                meta |= static_cast<unsigned long long>(misc[12 + g]) << (20 + 5 * g);
+            }
+        reinterpret_cast<unsigned long long*>(S.cur)[tid] = meta;
+        if (part == 0) reinterpret_cast<unsigned long long*>(grec)[tid] = meta;
+    }
+    const int hg = lane & 7;
+    uint32_t qh2[8], ql2[8];
+    tok_bar();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int32_t x0 = S.qrot[hg * 16 + 2 * i], x1 = S.qrot[hg * 16 + 2 * i + 1];
+        qh2[i] = (static_cast<uint32_t>(x0 >> 16) & 0xffffu) | (static_cast<uint32_t>(x1 >> 16) << 16);
+        ql2[i] = (static_cast<uint32_t>(x0) & 0xffffu) | (static_cast<uint32_t>(x1) << 16);
+    }
+
+    const int dl = tid & 31;                 // dimension inside this part
+    const int dim = part * 32 + dl;
+    for (int k = 0; k < ntiles; ++k) {
+        const int T0 = k * kTile, cnt = min(kTile, n - T0);
+        uint8_t* buf = S.tile[k & 1];
+        if (tid == 0 && k + 1 < ntiles) {
+            fence_proxy_async_smem();
+            const int c2 = min(kTile, n - T0 - kTile);
+            mbar_arrive_expect_tx(&s.abar[(k + 1) & 1], c2 * 320);
+            bulk_g2s(S.tile[(k + 1) & 1], head_base + static_cast<size_t>(T0 + kTile) * 320, c2 * 320,
+                     &s.abar[(k + 1) & 1]);
+        }
+        tok_mbar_wait(ta, &s.abar[k & 1], static_cast<uint32_t>((k >> 1) & 1), kErrWaitFull);
+        if (pos < T0 + cnt) {
+            if (tid < 80)
+                reinterpret_cast<uint32_t*>(buf + (pos - T0) * 320)[tid] = reinterpret_cast<const uint32_t*>(S.cur)[tid];
+            tok_bar();
+        }
+        {   // scores: 16 warps x 4 tokens
+            const int tl = cw * 4 + (lane >> 3);
+            long long hv = 0;
+            if (tl < cnt) {
+                const uint8_t* rec = buf + tl * 320;
+                const uint4 kw = *reinterpret_cast<const uint4*>(rec + 64 + hg * 16);
+                const unsigned long long meta = *reinterpret_cast<const unsigned long long*>(rec);
+                const uint32_t sh = static_cast<uint32_t>((meta >> (5 * (hg >> 1))) & 31u);
+                int sh16 = 0, sl16 = 0;
+                sh16 = dp2a_lo_ss(qh2[0], kw.x, sh16);
+                sh16 = dp2a_hi_ss(qh2[1], kw.x, sh16);
+                sh16 = dp2a_lo_ss(qh2[2], kw.y, sh16);
+                sh16 = dp2a_hi_ss(qh2[3], kw.y, sh16);
+                sh16 = dp2a_lo_ss(qh2[4], kw.z, sh16);
+                sh16 = dp2a_hi_ss(qh2[5], kw.z, sh16);
+                sh16 = dp2a_lo_ss(qh2[6], kw.w, sh16);
+                sh16 = dp2a_hi_ss(qh2[7], kw.w, sh16);
+                sl16 = dp2a_lo_us(ql2[0], kw.x, sl16);
+                sl16 = dp2a_hi_us(ql2[1], kw.x, sl16);
+                sl16 = dp2a_lo_us(ql2[2], kw.y, sl16);
+                sl16 = dp2a_hi_us(ql2[3], kw.y, sl16);
+                sl16 = dp2a_lo_us(ql2[4], kw.z, sl16);
+                sl16 = dp2a_hi_us(ql2[5], kw.z, sl16);
+                sl16 = dp2a_lo_us(ql2[6], kw.w, sl16);
+                sl16 = dp2a_hi_us(ql2[7], kw.w, sl16);
+                const long long half = static_cast<long long>(sh16) * 65536 + sl16;
+                hv = wrap_bits(sh >= 10 ? static_cast<long long>(static_cast<unsigned long long>(half) << (sh - 10))
+                                        : (half >> (10 - sh)), 44);
+            }
+            hv += __shfl_xor_sync(FULL, hv, 1);
+            hv += __shfl_xor_sync(FULL, hv, 2);
+            hv += __shfl_xor_sync(FULL, hv, 4);
+            if ((lane & 7) == 0 && tl < cnt) S.score[tl] = sat32(rshift_even(wrap_bits(hv, 44) * a.score_scale, 24));
+        }
+        tok_bar();
+        const int carry = misc[0], ev_before = misc[1];
+        int32_t m_incl = INT32_MIN, m_excl = INT32_MIN, sc = INT32_MIN;
+        if (tid < kTile) {
+            sc = tid < cnt ? S.score[tid] : INT32_MIN;
+            m_incl = sc;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int32_t y = __shfl_up_sync(FULL, m_incl, o);
+                if (lane >= o) m_incl = max(m_incl, y);
+            }
+            m_excl = __shfl_up_sync(FULL, m_incl, 1);
+            if (lane == 0) m_excl = INT32_MIN;
+            if (tid == 31) misc[2] = m_incl;
+        }
+        tok_bar();
+        bool ev = false;
+        uint32_t c = 0;
+        if (tid < kTile) {
+            const int32_t prev = max(max(carry, m_excl), cw == 1 ? misc[2] : INT32_MIN);
+            const int t = T0 + tid;
+            if (tid < cnt) {
+                if (t == 0) {
+                    c = 1u << 17;
+                    ev = true;
+                } else if (sc <= prev) {
+                    c = exp_negative_q17(sat32(static_cast<long long>(sc) - prev), lut, a.log2e_q21);
+                } else {
+                    c = exp_negative_q17(sat32(static_cast<long long>(prev) - sc), lut, a.log2e_q21);
+                    ev = true;
+                }
+            }
+            const unsigned bal = __ballot_sync(FULL, ev);
+            if (tid == 0) misc[4] = __popc(bal);
+            S.coef[tid] = c | (ev ? 0x80000000u : 0u);
+            S.score[tid] = __popc(bal & ((1u << lane) - 1u)) + (ev ? 1 : 0);
+        }
+        tok_bar();
+        if (tid < kTile) {
+            const int e_incl = ev_before + S.score[tid] + (cw == 1 ? misc[4] : 0);
+            const int sg = e_incl - 1;
+            const int t = T0 + tid;
+            S.seg[tid] = sg;
+            if (tid < cnt) {
+                coef_g[t] = S.coef[tid];
+                if (ev && sg < kMaxSeg) {
+                    S.ev_c[sg] = c;
+                    S.ev_tok[sg] = t;
+                } else if (!ev && sg < kMaxSeg) {
+                    atomicAdd(&S.zbin[sg], static_cast<unsigned long long>(c));
+                }
+            }
+            if (tid == kTile - 1) {
+                misc[1] = e_incl;
+                misc[0] = max(carry, max(m_incl, misc[2]));
+            }
+        }
+        tok_bar();
+        {   // per-segment state sums: thread = (dimension, slice of 4 tokens)
+            const int slice = tid >> 5;
+            const int t_lo = slice * 4, t_hi = min(cnt, t_lo + 4);
+            long long acc = 0, aab = 0;
+            int cs = -1;
+            for (int tl = t_lo; tl < t_hi; ++tl) {
+                const int32_t v = rec_v(buf + tl * 320, dim);
+                const uint32_t cf = S.coef[tl];
+                const int sg = S.seg[tl];
+                if (cf >> 31) {
+                    if (cs >= 0 && cs < kMaxSeg) {
+                        atomicAdd(reinterpret_cast<unsigned long long*>(&S.sbin[cs * 32 + dl]), static_cast<unsigned long long>(acc));
+                        atomicAdd(reinterpret_cast<unsigned long long*>(&S.abin[cs * 32 + dl]), static_cast<unsigned long long>(aab));
+                    }
+                    if (sg < kMaxSeg) S.ev_v[sg * 32 + dl] = v;
+                    cs = sg;
+                    acc = 0;
+                    aab = 0;
+                } else {
+                    if (sg != cs) {
+                        if (cs >= 0 && cs < kMaxSeg) {
+                            atomicAdd(reinterpret_cast<unsigned long long*>(&S.sbin[cs * 32 + dl]), static_cast<unsigned long long>(acc));
+                            atomicAdd(reinterpret_cast<unsigned long long*>(&S.abin[cs * 32 + dl]), static_cast<unsigned long long>(aab));
+                        }
+                        cs = sg;
+                        acc = 0;
+                        aab = 0;
+                    }
+                    const int32_t tv = mulq17(v, cf);
+                    acc += tv;
+                    aab += tv < 0 ? -static_cast<long long>(tv) : tv;
+                }
+            }
+            if (cs >= 0 && cs < kMaxSeg) {
+                atomicAdd(reinterpret_cast<unsigned long long*>(&S.sbin[cs * 32 + dl]), static_cast<unsigned long long>(acc));
+                atomicAdd(reinterpret_cast<unsigned long long*>(&S.abin[cs * 32 + dl]), static_cast<unsigned long long>(aab));
+            }
+        }
+        tok_bar();
+    }
+
+    // Compose segments (normaliser: thread 32; state: threads 0..31).
+    const int m = misc[1];
+    const bool overflow = m > kMaxSeg;
+    if (tid == 32) {
+        uint32_t z = 1u << 17;
+        if (!overflow) {
+            z = (z + static_cast<uint32_t>(S.zbin[0] & M30)) & M30;
+            for (int e = 1; e < m; ++e) {
+                z = ((static_cast<uint32_t>(rshift_even(static_cast<long long>(z) * S.ev_c[e], 17)) & M30) + (1u << 17)) & M30;
+                z = (z + static_cast<uint32_t>(S.zbin[e] & M30)) & M30;
+            }
+        } else {
+            for (int t = 1; t < n; ++t) {
+                const uint32_t cf = coef_g[t];
+                const uint32_t cc = cf & 0x7fffffffu;
+                if (cf >> 31) z = ((static_cast<uint32_t>(rshift_even(static_cast<long long>(z) * cc, 17)) & M30) + (1u << 17)) & M30;
+                else z = (z + cc) & M30;
+            }
+        }
+        misc[3] = static_cast<int>(z);
+    }
+    int32_t st = 0;
+    if (tid < 32) {
+        auto vat = [&](int t) -> int32_t { return t == pos ? rec_v(S.cur, dim) : rec_v(kv_record(a, h, t), dim); };
+        if (!overflow) {
+            st = S.ev_v[dl];
+            for (int e = 0; e < m; ++e) {
+                if (e > 0) st = sat32(static_cast<long long>(mulq17(st, S.ev_c[e])) + S.ev_v[e * 32 + dl]);
+                const long long mag = st < 0 ? -static_cast<long long>(st) : st;
+                if (mag + S.abin[e * 32 + dl] <= INT32_MAX) {
+                    st = static_cast<int32_t>(st + S.sbin[e * 32 + dl]);
+                } else {
+                    const int t1 = e + 1 < m ? S.ev_tok[e + 1] : n;
+                    for (int t = S.ev_tok[e] + 1; t < t1; ++t)
+                        st = sat32(static_cast<long long>(st) + mulq17(vat(t), coef_g[t] & 0x7fffffffu));
+                }
+            }
+        } else {
+            st = vat(0);
+            for (int t = 1; t < n; ++t) {
+                const uint32_t cf = coef_g[t];
+                const uint32_t cc = cf & 0x7fffffffu;
+                const int32_t v = vat(t);
+                if (cf >> 31) st = sat32(static_cast<long long>(mulq17(st, cc)) + v);
+                else st = sat32(static_cast<long long>(st) + mulq17(v, cc));
+            }
+        }
+    }
+    tok_bar();
+    if (tid < 32) {  // normalise and quantise this part's 32-value group
+        const uint32_t z = static_cast<uint32_t>(misc[3]);
+        const uint32_t inv = z == 0 ? 0u : static_cast<uint32_t>(((1ull << 34) + (z >> 1)) / z);
+        const int32_t o = mulq17(st, inv);
+        const int32_t mag = o == INT32_MIN ? INT32_MAX : abs(o);
+        const int32_t mx = __reduce_max_sync(FULL, mag);
+        const float maxf = __fmul_rn(__int2float_rn(mx), 1.0f / 131072.0f);
+        int maxe = -127;
+        if (maxf != 0.0f) frexpf(maxf, &maxe);
+        const float inv_scale = maxf == 0.0f ? 0.0f : pow2f(13 - maxe);
+        float r = __fmul_rn(__fmul_rn(__int2float_rn(o), 1.0f / 131072.0f), inv_scale);
+        r = __fadd_rn(r, r >= 0.0f ? 0.5f : -0.5f);
+        r = fmaxf(-8191.0f, fminf(8191.0f, r));
+        ta.ao_q[h * kHeadDim + dim] = static_cast<int16_t>(__float2int_rz(r));
+        if (lane == 0) ta.ao_e[h * 4 + part] = maxf == 0.0f ? 0 : static_cast<uint8_t>(maxe + 127);
+        __threadfence();
+    }
+    tok_bar();
+    if (tid == 0) atomicAdd(&ta.sync[kSyncAtt + layer], 1u);
+}
+
+// ---------------------------------------------------------------- kernel
+
+__global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant__ TokenArgs a) {
+    extern __shared__ __align__(128) uint8_t tok_smem_raw[];
+    TokSmem s = tok_carve(tok_smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bank = blockIdx.x / a.cpb, c = blockIdx.x % a.cpb;
+    auto urange = [&](int st, int* u0, int* u1) {
+        const int U = stage_units(st);
+        *u0 = static_cast<int>((static_cast<long long>(c) * U) / a.cpb);
+        *u1 = static_cast<int>((static_cast<long long>(c + 1) * U) / a.cpb);
+    };
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kTokRing; ++i) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.empty[i], 1);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (warp == 0) {
+        // Producer: this CTA's chunks of every stage, in consumption order.
+        if (lane == 0) {
+            int slot = 0, issued = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int l = 0; l <= a.layers && ok; ++l) {
+                for (int st = TS_QKV; st <= TS_DOWN && ok; ++st) {
+                    const int stage = l == a.layers ? TS_LOGITS : st;
+                    if (l == a.layers && st != TS_QKV) break;
+                    int u0, u1;
+                    urange(stage, &u0, &u1);
+                    const int C = stage_chunks(stage);
+                    const uint8_t* src = a.w + (stage == TS_LOGITS ? a.stage_off[TS_LOGITS]
+                                                                    : l * a.layer_bytes + a.stage_off[stage]) +
+                                         static_cast<size_t>(bank) * a.bank_bytes[stage] +
+                                         static_cast<size_t>(u0) * C * kChunkBytes;
+                    const int n = (u1 - u0) * C;
+                    for (int i = 0; i < n; ++i) {
+                        if (issued >= kTokRing && !tok_mbar_wait(a, &s.empty[slot], phase ^ 1u, kErrWaitEmpty)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&s.full[slot], kChunkBytes);
+                        bulk_g2s(s.ring + static_cast<size_t>(slot) * kChunkBytes,
+                                 src + static_cast<size_t>(i) * kChunkBytes, kChunkBytes, &s.full[slot]);
+                        ++issued;
+                        if (++slot == kTokRing) {
+                            slot = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                }
+            }
+            // Never leave with copies in flight: wait for the last ones to land.
+            for (int k = 0; k < kTokRing && k < issued; ++k) {
+                const int g = issued - 1 - k;
+                const int sl = g % kTokRing;
+                for (uint32_t it = 0; !mbar_try_wait(&s.full[sl], static_cast<uint32_t>((g / kTokRing) & 1)); ++it) {
+                    if (it > (1u << 22)) {
+                        atomicOr(a.err, kErrWaitFull);
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+        }
+        return;
+    }
+
+    const int cw = warp - 1;
+    const int tid = cw * 32 + lane;
+    if (blockIdx.x == 0 && cw == 0) {
+        // RMS reciprocal of the token's input residual (first attention norm).
+        const float r = rms_recip_warp(a.resid);
+        if (lane == 0) {
+            a.recip[0] = r;
+            __threadfence();
+            atomicExch(&a.sync[kSyncRms], 1u);
+        }
+    }
+    StageDesc d;
+    d.bank = bank;
+    d.gbase = 0;
+    for (int l = 0; l <= a.layers; ++l) {
+        for (int st = TS_QKV; st <= TS_DOWN; ++st) {
+            const int stage = l == a.layers ? TS_LOGITS : st;
+            if (l == a.layers && st != TS_QKV) break;
+            d.st = stage;
+            d.layer = l;
+            urange(stage, &d.u0, &d.u1);
+            if (stage == TS_DOWN) tok_gemv_stage<11>(a, s, d, cw, lane);
+            else tok_gemv_stage<4>(a, s, d, cw, lane);
+            d.gbase += (d.u1 - d.u0) * stage_chunks(stage);
+            if (stage == TS_QKV && l < a.layers) {
+                if (blockIdx.x < kAttnItems) tok_attention(a, s, l, blockIdx.x, cw, lane);
+                tok_bar();
+            }
+        }
+    }
+    // The last CTA to finish clears the token's synchronisation words.
+    tok_bar();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned old = atomicAdd(&a.sync[kSyncExit], 1u);
+        if (old + 1 == gridDim.x) {
+            for (int i = kSyncQkv; i < kSyncWords; ++i) a.sync[i] = 0;
+            __threadfence();
+            a.sync[kSyncExit] = 0;
+        }
+    }
+}
+
+}  // namespace i4d

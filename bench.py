@@ -36,9 +36,6 @@ sys.path.insert(0, ROOT)
 METRIC = "batch-1 INT4 Llama-2-7B decode tokens/s"
 UNIT = "tokens/s"
 PROMPT = 16
-# Algorithmic bytes of each GEMV launch (GEMV layout = bank data regions).
-GEMV_BYTES = {"qkv_gemv": 3 * 8_650_752, "o_gemv": 8_650_752, "gate_up_gemv": 2 * 23_789_568,
-              "down_gemv": 23_789_568, "logits_gemv": 68_124_672}
 
 
 def parse():
@@ -283,23 +280,20 @@ def main():
     dev_ms = max_over_ranks(ev0.elapsed_time(ev1))
     replay_ok = bool(np.array_equal(d_logits.cpu().numpy(), last_logits))
 
-    # ---- per-kernel device times (eager, events around every launch) ----
-    prof = None
-    for _ in range(3):
-        p = ctx.profile_token(args.warmup + args.steps // 2, row(tokens[args.warmup]))
-        if prof is None or sum(v[0] for v in p.values()) < sum(v[0] for v in prof.values()):
-            prof = p
-    gemv_ms = sum(prof[k][0] for k in GEMV_BYTES)
-    gemv_launches = sum(prof[k][1] for k in GEMV_BYTES)
-    gemv_bytes = sum(GEMV_BYTES[k] * prof[k][1] for k in GEMV_BYTES)
+    # ---- device time of the token kernel alone (events around the launch) ----
+    mid = args.warmup + args.steps // 2
+    tok_ms = []
+    for _ in range(5):
+        p = ctx.profile_token(mid, row(tokens[mid]))
+        tok_ms.append(p["token"][0])
+    tok_ms = statistics.median(tok_ms)
     peak, peak_kind = measured_peak()
-    achieved = gemv_bytes / (gemv_ms * 1e-3) / 1e9
+    achieved = F.token_bytes(mid) / (tok_ms * 1e-3) / 1e9
     traffic = committed_traffic()
 
     value = world * args.steps / (dev_ms * 1e-3)
     e2e = world * args.steps / (e2e_ms * 1e-3)
-    launches_per_step = 2 + 5 * 32
-    mid = args.warmup + args.steps // 2
+    launches_per_step = 2  # k_set_pos + k_token
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
@@ -307,16 +301,15 @@ def main():
         "config": workload_config(args, world),
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4096 * 4 + 4,
                 "d2h_bytes_per_step": F.PADDED_VOCAB * 4 + 4096 * 4 + 4, "ms_per_step": e2e_ms / args.steps},
-        "roofline": {"bound": "hbm", "kernel": "k_linear (fused dequant-GEMV)", "achieved": achieved,
-                     "peak": peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+        "roofline": {"bound": "hbm", "kernel": "k_token (persistent decode step, 1 launch per token)",
+                     "achieved": achieved, "peak": peak,
+                     "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback", "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic["bytes_per_launch_avg"] if traffic else None,
-                     "algorithmic_bytes_per_token_gemv": gemv_bytes, "gemv_ms_per_token": gemv_ms,
-                     "gemv_launches_per_token": gemv_launches},
+                     "traffic": traffic["bytes_per_launch"] if traffic else None,
+                     "algorithmic_bytes_per_launch": F.token_bytes(mid), "kernel_ms": tok_ms},
         "token_roofline": {"bytes_per_token": F.token_bytes(mid), "achieved_gbs":
                            F.token_bytes(mid) / (dev_ms / args.steps * 1e-3) / 1e9,
                            "frac": F.token_bytes(mid) / (dev_ms / args.steps * 1e-3) / 1e9 / peak},
-        "kernel_ms_per_token": {k: v[0] for k, v in prof.items()},
         "gpu_launches": launches_per_step * args.steps,
         "replay_matches_e2e": replay_ok,
         "clocks": clk,

@@ -57,7 +57,8 @@ typedef int i4d_status;
 
 /* Context flags. */
 #define I4D_FLAG_NO_GRAPH 1u /* launch the token schedule eagerly */
-#define I4D_FLAG_NO_PDL 2u   /* no programmatic dependent launch */
+#define I4D_FLAG_NO_PDL 2u   /* no programmatic dependent launch (staged path) */
+#define I4D_FLAG_STAGED 4u   /* one kernel per stage instead of the persistent token kernel */
 
 typedef struct i4d_ctx i4d_ctx;
 
@@ -116,9 +117,10 @@ i4d_status i4d_decode_token_async(i4d_ctx* ctx, uint32_t position, const float* 
 void* i4d_stream(i4d_ctx* ctx);
 
 /* Measurement hook: runs one step eagerly with a CUDA event pair around every
- * kernel and returns the device time per kernel class in kernel_ms[7] and the
- * launch counts in launches[7]: 0 QKV GEMV, 1 attention, 2 O GEMV,
- * 3 GATE/UP GEMV, 4 DOWN GEMV, 5 LOGITS GEMV, 6 RMS.  No reference
+ * kernel and returns the device time per kernel class in kernel_ms[8] and the
+ * launch counts in launches[8]: 0 QKV GEMV, 1 attention, 2 O GEMV,
+ * 3 GATE/UP GEMV, 4 DOWN GEMV, 5 LOGITS GEMV, 6 RMS (staged path),
+ * 7 persistent token kernel.  No reference
  * counterpart (decode_host's verbose timing, decode_host.cpp:1539-1553, is
  * host-side only). */
 i4d_status i4d_profile_token(i4d_ctx* ctx, uint32_t position, const float* residual_in_dev,

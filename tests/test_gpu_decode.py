@@ -32,7 +32,9 @@ def reference_run(oracle, rope_tables, model):
     return tokens, outs, kv
 
 
-@pytest.mark.parametrize("flags", [0, 1, 2])  # graph+PDL, eager, graph without PDL
+# 0: persistent token kernel in a graph; 1: persistent, eager; 4: one kernel
+# per stage (graph + PDL); 5: staged, eager; 6: staged without PDL
+@pytest.mark.parametrize("flags", [0, 1, 4, 5, 6])
 def test_decode_bit_exact(pkg, model, rope_lut, reference_run, flags):
     banks, emb = model
     tokens, outs, kv = reference_run
