@@ -31,8 +31,11 @@ EXPORTS = [
     "i4d_load_embeddings", "i4d_decode_token", "i4d_kv_reset", "i4d_kv_read", "i4d_kv_write",
     "i4d_sync", "i4d_linear_bank", "i4d_gemv", "i4d_quantize_g32", "i4d_rms_quant",
     "i4d_attention", "i4d_swiglu_quant", "i4d_expf", "i4d_decode_token_async", "i4d_stream",
-    "i4d_profile_token",
+    "i4d_profile_token", "i4d_token_breakdown",
 ]
+
+BREAKDOWN = ["wait", "prologue", "chunks", "epilogue", "attn_wait", "attn", "ring_full", "total",
+             "stage_qkv", "stage_o", "stage_gu", "stage_down", "stage_logits"]
 
 KERNEL_CLASSES = ["qkv_gemv", "attention", "o_gemv", "gate_up_gemv", "down_gemv", "logits_gemv", "rms", "token"]
 
@@ -82,6 +85,7 @@ def load_library():
         "i4d_decode_token_async": [P, ctypes.c_uint32, P, P],
         "i4d_stream": [P],
         "i4d_profile_token": [P, ctypes.c_uint32, P, P, P],
+        "i4d_token_breakdown": [P, ctypes.c_uint32, P, P, ctypes.c_int],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -169,6 +173,12 @@ class Context:
         n = np.zeros(8, np.uint32)
         self._check(self._L.i4d_profile_token(self._h, position, residual_in_dev_ptr, ms.ctypes.data, n.ctypes.data))
         return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(KERNEL_CLASSES)}
+
+    def token_breakdown(self, position, residual_in_dev_ptr):
+        """CTA-averaged microseconds per category of the persistent kernel."""
+        out = np.zeros(len(BREAKDOWN), np.float32)
+        self._check(self._L.i4d_token_breakdown(self._h, position, residual_in_dev_ptr, out.ctypes.data, out.size))
+        return dict(zip(BREAKDOWN, out.tolist()))
 
     def kv_reset(self):
         self._check(self._L.i4d_kv_reset(self._h))

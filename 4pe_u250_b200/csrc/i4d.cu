@@ -132,6 +132,7 @@ struct i4d_ctx {
     int prof_class[256] = {};
     int prof_n = 0;
     bool profiling = false;
+    unsigned long long* d_trace = nullptr;  // optional token-kernel trace
 };
 
 namespace {
@@ -278,6 +279,7 @@ TokenArgs token_args(i4d_ctx* c) {
     t.attn = base_attn(c, 0);
     t.expf = c->expf;
     t.err = c->d_err;
+    t.trace = c->d_trace;
     return t;
 }
 
@@ -401,7 +403,7 @@ void i4d_destroy(i4d_ctx* c) {
         if (ev) cudaEventDestroy(ev);
     void* dev[] = {c->d_w, c->d_gamma, c->d_rope_cos, c->d_rope_sin, c->d_exp2, c->d_expf_slots, c->d_kv,
                    c->d_emb, c->d_resid, c->d_recip, c->d_partials, c->d_ao_q, c->d_ao_e, c->d_ad_q,
-                   c->d_ad_e, c->d_logits, c->d_counters, c->d_err, c->d_pos, c->d_scratch, c->d_attn_coef, c->d_sync, c->d_recips};
+                   c->d_ad_e, c->d_logits, c->d_counters, c->d_err, c->d_pos, c->d_scratch, c->d_attn_coef, c->d_sync, c->d_recips, c->d_trace};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* host[] = {c->h_resid_in, c->h_resid_out, c->h_logits, c->h_pos, c->h_err};
@@ -971,3 +973,32 @@ i4d_status i4d_expf(i4d_ctx* c, const float* x, float* y, size_t n) {
 }
 
 }  // extern "C"
+
+extern "C" i4d_status i4d_token_breakdown(i4d_ctx* c, uint32_t position, const float* residual_in_dev,
+                                          float* us_out, int n_out) {
+    if (!c || !residual_in_dev || !us_out || n_out < kTraceSlots) return c ? fail(c, I4D_ERR_ARG, "bad arguments") : I4D_ERR_ARG;
+    if (c->flags & I4D_FLAG_STAGED) return fail(c, I4D_ERR_STATE, "breakdown needs the persistent token kernel");
+    if (!all_loaded(c)) return fail(c, I4D_ERR_STATE, "banks and rope LUT must be loaded before decoding");
+    if (position >= static_cast<uint32_t>(c->stride)) return fail(c, I4D_ERR_ARG, "position out of range");
+    CK(cudaSetDevice(c->device));
+    const size_t slots = static_cast<size_t>(4 * c->cpb) * kTraceSlots;
+    if (!c->d_trace) CK(cudaMalloc(&c->d_trace, slots * sizeof(unsigned long long)));
+    CK(cudaMemsetAsync(c->d_trace, 0, slots * sizeof(unsigned long long), c->stream));
+    k_set_pos<<<1, 1, 0, c->stream>>>(c->d_pos, static_cast<int>(position));
+    CK(cudaMemcpyAsync(c->d_resid, residual_in_dev, kDim * sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
+    CK(launch_token(c));
+    const i4d_status st = finish(c);
+    std::vector<unsigned long long> h(slots);
+    CK(cudaMemcpy(h.data(), c->d_trace, slots * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+    CK(cudaFree(c->d_trace));
+    c->d_trace = nullptr;
+    if (st != I4D_OK) return st;
+    int khz = 0;
+    CK(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, c->device));
+    for (int k = 0; k < kTraceSlots; ++k) {
+        double sum = 0.0;
+        for (int b = 0; b < 4 * c->cpb; ++b) sum += static_cast<double>(h[static_cast<size_t>(b) * kTraceSlots + k]);
+        us_out[k] = static_cast<float>(sum / (4 * c->cpb) / (khz * 1e-3));
+    }
+    return I4D_OK;
+}

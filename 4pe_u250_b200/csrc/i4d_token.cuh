@@ -68,7 +68,30 @@ struct TokenArgs {
     AttnArgs attn;             // position, RoPE, KV, LUT, coefficient scratch
     ExpfFix expf;
     unsigned* err;
+    unsigned long long* trace;  // optional [gridDim.x][kTraceSlots] cycle sums, or null
 };
+
+// Cycle-sum categories of the optional trace (per CTA, summed over a token).
+enum TraceSlot : int {
+    TR_WAIT = 0,      // consumer: waiting for a stage's input
+    TR_PROLOGUE,      // consumer: building activations
+    TR_CHUNKS,        // consumer: chunk loop
+    TR_EPILOGUE,      // consumer: end-of-stage epilogue
+    TR_ATTN_WAIT,     // attention item: waiting for the QKV partials
+    TR_ATTN,          // attention item: everything else
+    TR_RING_FULL,     // producer: blocked on a full ring
+    TR_TOTAL,         // consumer: whole kernel
+    TR_STAGE_QKV,     // consumer: QKV stage total (incl. wait)
+    TR_STAGE_O,
+    TR_STAGE_GU,
+    TR_STAGE_DOWN,
+    TR_STAGE_LOGITS,
+    kTraceSlots
+};
+
+__device__ __forceinline__ void trace_add(const TokenArgs& a, int slot, long long cycles) {
+    if (a.trace) a.trace[blockIdx.x * kTraceSlots + slot] += static_cast<unsigned long long>(cycles);
+}
 
 __host__ __device__ constexpr int stage_units(int st) {
     return st == TS_QKV ? 384 : st == TS_O ? 128 : st == TS_GU ? 704 : st == TS_DOWN ? 128 : 1008;
@@ -257,6 +280,7 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     ls.act_scale = reinterpret_cast<float*>(s.uni + G * 68);
     float* contrib = reinterpret_cast<float*>(s.uni + align16(G * 72));
     const int tid = cw * 32 + lane;
+    const long long t_begin = clock64();
 
     // Input readiness.
     if (tid == 0) {
@@ -277,8 +301,10 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
         s.slot_ok[tid] = tid;
     }
     tok_bar();
+    const long long t_ready = clock64();
     tok_prologue<C>(v, ls, d.bank, cw, lane);
     tok_bar();
+    const long long t_loop = clock64();
 
     const int nchunks = (d.u1 - d.u0) * C;
     const int rows_total = stage_units(d.st) * 32;
@@ -342,9 +368,18 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     }
     __threadfence();
     tok_bar();
+    const long long t_epi = clock64();
+    if (tid == 0) {
+        trace_add(a, TR_WAIT, t_ready - t_begin);
+        trace_add(a, TR_PROLOGUE, t_loop - t_ready);
+        trace_add(a, TR_CHUNKS, t_epi - t_loop);
+    }
 
     if (d.st == TS_QKV) {
-        if (tid == 0) atomicAdd(&a.sync[kSyncQkv + d.layer], 1u);
+        if (tid == 0) {
+            atomicAdd(&a.sync[kSyncQkv + d.layer], 1u);
+            trace_add(a, TR_STAGE_QKV, clock64() - t_begin);
+        }
         return;
     }
     // Last-arriver epilogue over the stripes this CTA touched.
@@ -378,6 +413,10 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     }
     if (d.st != TS_O && d.st != TS_DOWN) {
         tok_bar();
+        if (tid == 0) {
+            trace_add(a, TR_EPILOGUE, clock64() - t_epi);
+            trace_add(a, d.st == TS_GU ? TR_STAGE_GU : TR_STAGE_LOGITS, clock64() - t_begin);
+        }
         return;
     }
     tok_bar();
@@ -398,6 +437,10 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
         }
     }
     tok_bar();
+    if (tid == 0) {
+        trace_add(a, TR_EPILOGUE, clock64() - t_epi);
+        trace_add(a, d.st == TS_O ? TR_STAGE_O : TR_STAGE_DOWN, clock64() - t_begin);
+    }
 }
 
 // ------------------------------------------------------------ attention item
@@ -485,6 +528,7 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
         S.abin[i] = 0;
     }
     tok_bar();
+    const long long t_a0 = clock64();
     if (tid == 0) {
         // Cached records of earlier tokens are final: stream the first tile
         // while the other CTAs finish the QKV projection.
@@ -495,6 +539,7 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
         wait_counter(ta, &ta.sync[kSyncQkv + layer], gridDim.x);
     }
     tok_bar();
+    const long long t_a1 = clock64();
 
     // Current token: Q/K/V rows of the head, RoPE, KV record.
     const int d = tid & 127;
@@ -775,7 +820,11 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
         __threadfence();
     }
     tok_bar();
-    if (tid == 0) atomicAdd(&ta.sync[kSyncAtt + layer], 1u);
+    if (tid == 0) {
+        atomicAdd(&ta.sync[kSyncAtt + layer], 1u);
+        trace_add(ta, TR_ATTN_WAIT, t_a1 - t_a0);
+        trace_add(ta, TR_ATTN, clock64() - t_a1);
+    }
 }
 
 // ---------------------------------------------------------------- kernel
@@ -818,9 +867,13 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
                                          static_cast<size_t>(u0) * C * kChunkBytes;
                     const int n = (u1 - u0) * C;
                     for (int i = 0; i < n; ++i) {
-                        if (issued >= kTokRing && !tok_mbar_wait(a, &s.empty[slot], phase ^ 1u, kErrWaitEmpty)) {
-                            ok = false;
-                            break;
+                        if (issued >= kTokRing) {
+                            const long long t0 = a.trace ? clock64() : 0;
+                            if (!tok_mbar_wait(a, &s.empty[slot], phase ^ 1u, kErrWaitEmpty)) {
+                                ok = false;
+                                break;
+                            }
+                            if (a.trace) trace_add(a, TR_RING_FULL, clock64() - t0);
                         }
                         mbar_arrive_expect_tx(&s.full[slot], kChunkBytes);
                         bulk_g2s(s.ring + static_cast<size_t>(slot) * kChunkBytes,
@@ -851,6 +904,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
 
     const int cw = warp - 1;
     const int tid = cw * 32 + lane;
+    const long long t_kernel = clock64();
     if (blockIdx.x == 0 && cw == 0) {
         // RMS reciprocal of the token's input residual (first attention norm).
         const float r = rms_recip_warp(a.resid);
@@ -882,6 +936,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
     // The last CTA to finish clears the token's synchronisation words.
     tok_bar();
     if (tid == 0) {
+        trace_add(a, TR_TOTAL, clock64() - t_kernel);
         __threadfence();
         const unsigned old = atomicAdd(&a.sync[kSyncExit], 1u);
         if (old + 1 == gridDim.x) {

@@ -287,6 +287,7 @@ def main():
         p = ctx.profile_token(mid, row(tokens[mid]))
         tok_ms.append(p["token"][0])
     tok_ms = statistics.median(tok_ms)
+    breakdown = ctx.token_breakdown(mid, row(tokens[mid]))
     peak, peak_kind = measured_peak()
     achieved = F.token_bytes(mid) / (tok_ms * 1e-3) / 1e9
     traffic = committed_traffic()
@@ -310,6 +311,7 @@ def main():
         "token_roofline": {"bytes_per_token": F.token_bytes(mid), "achieved_gbs":
                            F.token_bytes(mid) / (dev_ms / args.steps * 1e-3) / 1e9,
                            "frac": F.token_bytes(mid) / (dev_ms / args.steps * 1e-3) / 1e9 / peak},
+        "token_kernel_breakdown_us": {k: round(v, 2) for k, v in breakdown.items()},
         "gpu_launches": launches_per_step * args.steps,
         "replay_matches_e2e": replay_ok,
         "clocks": clk,

@@ -126,6 +126,15 @@ void* i4d_stream(i4d_ctx* ctx);
 i4d_status i4d_profile_token(i4d_ctx* ctx, uint32_t position, const float* residual_in_dev,
                              float* kernel_ms, uint32_t* launches);
 
+/* Measurement hook for the persistent token kernel: runs one step with
+ * per-CTA cycle counters and returns the CTA-averaged microseconds (at the
+ * device's nominal clock) of: 0 stage-input waits, 1 prologues, 2 chunk
+ * loops, 3 epilogues, 4 attention waits for QKV, 5 attention work,
+ * 6 producer blocked on a full ring, 7 whole kernel, 8..12 QKV, O, GATE/UP,
+ * DOWN and LM-head stage totals.  n_out >= 13.  No reference counterpart. */
+i4d_status i4d_token_breakdown(i4d_ctx* ctx, uint32_t position, const float* residual_in_dev, float* us_out,
+                               int n_out);
+
 /* Clears the KV cache (decode_host.cpp:1291-1294 zero_bo). */
 i4d_status i4d_kv_reset(i4d_ctx* ctx);
 /* Reads / writes one 320-byte KV record in the HLS layout
