@@ -127,17 +127,13 @@ __device__ __forceinline__ int32_t sat32(long long v) {
     return v > INT32_MAX ? INT32_MAX : (v < INT32_MIN ? INT32_MIN : static_cast<int32_t>(v));
 }
 
-// Round-half-even arithmetic right shift (emulator:507-517).
+// Round-half-even arithmetic right shift (emulator:507-517), branch-free:
+// floor((v + 2^(sh-1) - 1 + bit_sh(v)) / 2^sh) rounds to nearest with ties to
+// the even quotient for either sign (bit_sh(v) is the parity of floor(v/2^sh)).
+// Every caller has |v| <= (2^31-1)(2^32-1), so the addition cannot overflow.
 __device__ __forceinline__ long long rshift_even(long long v, unsigned sh) {
     if (sh == 0) return v;
-    const bool neg = v < 0;
-    const unsigned long long mag = neg ? static_cast<unsigned long long>(-(v + 1)) + 1ull
-                                       : static_cast<unsigned long long>(v);
-    unsigned long long q = mag >> sh;
-    const unsigned long long rem = mag & ((1ull << sh) - 1ull);
-    const unsigned long long half = 1ull << (sh - 1);
-    if (rem > half || (rem == half && (q & 1ull))) ++q;
-    return neg ? -static_cast<long long>(q) : static_cast<long long>(q);
+    return (v + ((1ll << (sh - 1)) - 1) + ((v >> sh) & 1)) >> sh;
 }
 
 // Low `bits` bits, sign-extended (emulator:519-524).

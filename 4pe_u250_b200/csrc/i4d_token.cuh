@@ -450,14 +450,9 @@ struct TokAttnSmem {
     uint8_t* tile[2];     // kTile records each
     uint8_t* cur;         // current token's record
     int32_t* score;       // [kTile]
-    uint32_t* coef;       // [kTile]
-    int32_t* seg;         // [kTile]
-    unsigned long long* zbin;  // [kMaxSeg]
-    long long* sbin;      // [kMaxSeg][32]
-    long long* abin;      // [kMaxSeg][32]
-    int32_t* ev_v;        // [kMaxSeg][32]; the first 1 KB doubles as RoPE scratch
-    uint32_t* ev_c;       // [kMaxSeg]
-    int32_t* ev_tok;      // [kMaxSeg]
+    uint32_t* coef;       // [kTile]: c | rescale << 31
+    uint32_t* lut;        // [33] exp2 table
+    int32_t* tbuf;        // [kTile][32]: per-token state terms of this part
     int32_t* qrot;        // [128]
     int32_t* krot;        // [128]
     int* misc;            // [16]
@@ -471,20 +466,11 @@ __device__ __forceinline__ TokAttnSmem tok_attn_carve(uint8_t* p) {
     p += 2 * kTile * 320 + 320;
     s.score = reinterpret_cast<int32_t*>(p);
     s.coef = reinterpret_cast<uint32_t*>(p + kTile * 4);
-    s.seg = reinterpret_cast<int32_t*>(p + kTile * 8);
-    p += kTile * 12;
-    s.zbin = reinterpret_cast<unsigned long long*>(p);
-    p += kMaxSeg * 8;
-    s.sbin = reinterpret_cast<long long*>(p);
-    p += kMaxSeg * 32 * 8;
-    s.abin = reinterpret_cast<long long*>(p);
-    p += kMaxSeg * 32 * 8;
-    s.ev_v = reinterpret_cast<int32_t*>(p);
-    p += kMaxSeg * 32 * 4;
-    s.ev_c = reinterpret_cast<uint32_t*>(p);
-    p += kMaxSeg * 4;
-    s.ev_tok = reinterpret_cast<int32_t*>(p);
-    p += kMaxSeg * 4;
+    p += kTile * 8;
+    s.lut = reinterpret_cast<uint32_t*>(p);
+    p += 144;
+    s.tbuf = reinterpret_cast<int32_t*>(p);
+    p += kTile * 32 * 4;
     s.qrot = reinterpret_cast<int32_t*>(p);
     p += 128 * 4;
     s.krot = reinterpret_cast<int32_t*>(p);
@@ -492,12 +478,14 @@ __device__ __forceinline__ TokAttnSmem tok_attn_carve(uint8_t* p) {
     s.misc = reinterpret_cast<int*>(p);
     return s;
 }
-static_assert(2 * kTile * 320 + 320 + kTile * 12 + kMaxSeg * 8 + 2 * kMaxSeg * 32 * 8 + kMaxSeg * 32 * 4 +
-                  2 * kMaxSeg * 4 + 2 * 128 * 4 + 16 * 4 <= kTokUnion,
+static_assert(2 * kTile * 320 + 320 + kTile * 8 + 144 + kTile * 32 * 4 + 2 * 128 * 4 + 16 * 4 <= kTokUnion,
               "attention scratch exceeds the union region");
 
-// Attention of one (head, 32-dimension part) item: the same parallel exact
-// algorithm as k_attention, with the state chains of 32 dimensions.
+// Attention of one (head, 32-dimension part) item.  Scores, the running
+// maximum and the coefficients are computed in parallel as in k_attention;
+// the per-token state terms mulq17(v_t, c_t) are computed in parallel into
+// shared memory, and the reference's saturating recurrence (emulator:656-685)
+// then runs exactly, one lane per dimension, over those terms.
 __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s, int layer, int item, int cw,
                                            int lane) {
     const unsigned FULL = 0xffffffffu;
@@ -508,8 +496,6 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
     const int tid = cw * 32 + lane;
     TokAttnSmem S = tok_attn_carve(s.uni);
     int* misc = S.misc;
-    uint32_t* coef_g = a.coef_scratch + static_cast<size_t>(item) * a.stride;
-    const uint32_t* lut = a.exp2_q30;
 
     const int pos = *a.pos_ptr;
     const int n = pos + 1;
@@ -520,13 +506,8 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
         mbar_init(&s.abar[1], 1);
         mbar_fence_init();
         misc[0] = INT32_MIN;
-        misc[1] = 0;
     }
-    if (tid < kMaxSeg) S.zbin[tid] = 0;
-    for (int i = tid; i < kMaxSeg * 32; i += 32 * kTokWarps) {
-        S.sbin[i] = 0;
-        S.abin[i] = 0;
-    }
+    if (tid < 33) S.lut[tid] = a.exp2_q30[tid];
     tok_bar();
     const long long t_a0 = clock64();
     if (tid == 0) {
@@ -602,8 +583,11 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
         ql2[i] = (static_cast<uint32_t>(x0) & 0xffffu) | (static_cast<uint32_t>(x1) << 16);
     }
 
+
     const int dl = tid & 31;                 // dimension inside this part
     const int dim = part * 32 + dl;
+    int32_t st = 0;                          // state of dimension `dim` (lanes of warp 0)
+    uint32_t z = 1u << 17;                   // normaliser (thread 32)
     for (int k = 0; k < ntiles; ++k) {
         const int T0 = k * kTile, cnt = min(kTile, n - T0);
         uint8_t* buf = S.tile[k & 1];
@@ -615,12 +599,12 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
                      &s.abar[(k + 1) & 1]);
         }
         tok_mbar_wait(ta, &s.abar[k & 1], static_cast<uint32_t>((k >> 1) & 1), kErrWaitFull);
-        if (pos < T0 + cnt) {
+        if (pos < T0 + cnt) {  // the tile holds the current token: use the fresh record
             if (tid < 80)
                 reinterpret_cast<uint32_t*>(buf + (pos - T0) * 320)[tid] = reinterpret_cast<const uint32_t*>(S.cur)[tid];
             tok_bar();
         }
-        {   // scores: 16 warps x 4 tokens
+        {   // scores (emulator:633-655): 16 warps x 4 tokens, 8 lanes per token
             const int tl = cw * 4 + (lane >> 3);
             long long hv = 0;
             if (tl < cnt) {
@@ -655,7 +639,8 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
             if ((lane & 7) == 0 && tl < cnt) S.score[tl] = sat32(rshift_even(wrap_bits(hv, 44) * a.score_scale, 24));
         }
         tok_bar();
-        const int carry = misc[0], ev_before = misc[1];
+        // Coefficients from the running maximum before each token (emulator:656-672).
+        const int carry = misc[0];
         int32_t m_incl = INT32_MIN, m_excl = INT32_MIN, sc = INT32_MIN;
         if (tid < kTile) {
             sc = tid < cnt ? S.score[tid] : INT32_MIN;
@@ -670,141 +655,61 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
             if (tid == 31) misc[2] = m_incl;
         }
         tok_bar();
-        bool ev = false;
-        uint32_t c = 0;
         if (tid < kTile) {
             const int32_t prev = max(max(carry, m_excl), cw == 1 ? misc[2] : INT32_MIN);
             const int t = T0 + tid;
+            uint32_t c = 0;
+            bool ev = false;
             if (tid < cnt) {
                 if (t == 0) {
                     c = 1u << 17;
                     ev = true;
                 } else if (sc <= prev) {
-                    c = exp_negative_q17(sat32(static_cast<long long>(sc) - prev), lut, a.log2e_q21);
+                    c = exp_negative_q17(sat32(static_cast<long long>(sc) - prev), S.lut, a.log2e_q21);
                 } else {
-                    c = exp_negative_q17(sat32(static_cast<long long>(prev) - sc), lut, a.log2e_q21);
+                    c = exp_negative_q17(sat32(static_cast<long long>(prev) - sc), S.lut, a.log2e_q21);
                     ev = true;
                 }
             }
-            const unsigned bal = __ballot_sync(FULL, ev);
-            if (tid == 0) misc[4] = __popc(bal);
             S.coef[tid] = c | (ev ? 0x80000000u : 0u);
-            S.score[tid] = __popc(bal & ((1u << lane) - 1u)) + (ev ? 1 : 0);
+            if (tid == kTile - 1) misc[0] = max(carry, max(m_incl, misc[2]));
         }
         tok_bar();
-        if (tid < kTile) {
-            const int e_incl = ev_before + S.score[tid] + (cw == 1 ? misc[4] : 0);
-            const int sg = e_incl - 1;
-            const int t = T0 + tid;
-            S.seg[tid] = sg;
-            if (tid < cnt) {
-                coef_g[t] = S.coef[tid];
-                if (ev && sg < kMaxSeg) {
-                    S.ev_c[sg] = c;
-                    S.ev_tok[sg] = t;
-                } else if (!ev && sg < kMaxSeg) {
-                    atomicAdd(&S.zbin[sg], static_cast<unsigned long long>(c));
-                }
-            }
-            if (tid == kTile - 1) {
-                misc[1] = e_incl;
-                misc[0] = max(carry, max(m_incl, misc[2]));
-            }
-        }
-        tok_bar();
-        {   // per-segment state sums: thread = (dimension, slice of 4 tokens)
-            const int slice = tid >> 5;
-            const int t_lo = slice * 4, t_hi = min(cnt, t_lo + 4);
-            long long acc = 0, aab = 0;
-            int cs = -1;
+        // State terms in parallel: thread = (dimension, slice of 4 tokens).
+        {
+            const int t_lo = cw * 4, t_hi = min(cnt, t_lo + 4);
             for (int tl = t_lo; tl < t_hi; ++tl) {
                 const int32_t v = rec_v(buf + tl * 320, dim);
                 const uint32_t cf = S.coef[tl];
-                const int sg = S.seg[tl];
-                if (cf >> 31) {
-                    if (cs >= 0 && cs < kMaxSeg) {
-                        atomicAdd(reinterpret_cast<unsigned long long*>(&S.sbin[cs * 32 + dl]), static_cast<unsigned long long>(acc));
-                        atomicAdd(reinterpret_cast<unsigned long long*>(&S.abin[cs * 32 + dl]), static_cast<unsigned long long>(aab));
-                    }
-                    if (sg < kMaxSeg) S.ev_v[sg * 32 + dl] = v;
-                    cs = sg;
-                    acc = 0;
-                    aab = 0;
-                } else {
-                    if (sg != cs) {
-                        if (cs >= 0 && cs < kMaxSeg) {
-                            atomicAdd(reinterpret_cast<unsigned long long*>(&S.sbin[cs * 32 + dl]), static_cast<unsigned long long>(acc));
-                            atomicAdd(reinterpret_cast<unsigned long long*>(&S.abin[cs * 32 + dl]), static_cast<unsigned long long>(aab));
-                        }
-                        cs = sg;
-                        acc = 0;
-                        aab = 0;
-                    }
-                    const int32_t tv = mulq17(v, cf);
-                    acc += tv;
-                    aab += tv < 0 ? -static_cast<long long>(tv) : tv;
-                }
+                S.tbuf[tl * 32 + dl] = (cf >> 31) ? v : mulq17(v, cf);
             }
-            if (cs >= 0 && cs < kMaxSeg) {
-                atomicAdd(reinterpret_cast<unsigned long long*>(&S.sbin[cs * 32 + dl]), static_cast<unsigned long long>(acc));
-                atomicAdd(reinterpret_cast<unsigned long long*>(&S.abin[cs * 32 + dl]), static_cast<unsigned long long>(aab));
+        }
+        tok_bar();
+        if (tid < 32) {  // the saturating state recurrence, in token order
+            for (int tl = 0; tl < cnt; ++tl) {
+                const uint32_t cf = S.coef[tl];
+                const int32_t tv = S.tbuf[tl * 32 + dl];
+                if (T0 + tl == 0) st = tv;
+                else if (cf >> 31) st = sat32(static_cast<long long>(mulq17(st, cf & 0x7fffffffu)) + tv);
+                else st = sat32(static_cast<long long>(st) + tv);
+            }
+        } else if (tid == 32) {  // the normaliser recurrence
+            for (int tl = 0; tl < cnt; ++tl) {
+                const uint32_t cf = S.coef[tl];
+                const uint32_t cc = cf & 0x7fffffffu;
+                if (T0 + tl == 0) z = 1u << 17;
+                else if (cf >> 31)
+                    z = ((static_cast<uint32_t>(rshift_even(static_cast<long long>(z) * cc, 17)) & M30) + (1u << 17)) & M30;
+                else z = (z + cc) & M30;
             }
         }
         tok_bar();
     }
-
-    // Compose segments (normaliser: thread 32; state: threads 0..31).
-    const int m = misc[1];
-    const bool overflow = m > kMaxSeg;
-    if (tid == 32) {
-        uint32_t z = 1u << 17;
-        if (!overflow) {
-            z = (z + static_cast<uint32_t>(S.zbin[0] & M30)) & M30;
-            for (int e = 1; e < m; ++e) {
-                z = ((static_cast<uint32_t>(rshift_even(static_cast<long long>(z) * S.ev_c[e], 17)) & M30) + (1u << 17)) & M30;
-                z = (z + static_cast<uint32_t>(S.zbin[e] & M30)) & M30;
-            }
-        } else {
-            for (int t = 1; t < n; ++t) {
-                const uint32_t cf = coef_g[t];
-                const uint32_t cc = cf & 0x7fffffffu;
-                if (cf >> 31) z = ((static_cast<uint32_t>(rshift_even(static_cast<long long>(z) * cc, 17)) & M30) + (1u << 17)) & M30;
-                else z = (z + cc) & M30;
-            }
-        }
-        misc[3] = static_cast<int>(z);
-    }
-    int32_t st = 0;
-    if (tid < 32) {
-        auto vat = [&](int t) -> int32_t { return t == pos ? rec_v(S.cur, dim) : rec_v(kv_record(a, h, t), dim); };
-        if (!overflow) {
-            st = S.ev_v[dl];
-            for (int e = 0; e < m; ++e) {
-                if (e > 0) st = sat32(static_cast<long long>(mulq17(st, S.ev_c[e])) + S.ev_v[e * 32 + dl]);
-                const long long mag = st < 0 ? -static_cast<long long>(st) : st;
-                if (mag + S.abin[e * 32 + dl] <= INT32_MAX) {
-                    st = static_cast<int32_t>(st + S.sbin[e * 32 + dl]);
-                } else {
-                    const int t1 = e + 1 < m ? S.ev_tok[e + 1] : n;
-                    for (int t = S.ev_tok[e] + 1; t < t1; ++t)
-                        st = sat32(static_cast<long long>(st) + mulq17(vat(t), coef_g[t] & 0x7fffffffu));
-                }
-            }
-        } else {
-            st = vat(0);
-            for (int t = 1; t < n; ++t) {
-                const uint32_t cf = coef_g[t];
-                const uint32_t cc = cf & 0x7fffffffu;
-                const int32_t v = vat(t);
-                if (cf >> 31) st = sat32(static_cast<long long>(mulq17(st, cc)) + v);
-                else st = sat32(static_cast<long long>(st) + mulq17(v, cc));
-            }
-        }
-    }
+    if (tid == 32) misc[3] = static_cast<int>(z);
     tok_bar();
-    if (tid < 32) {  // normalise and quantise this part's 32-value group
-        const uint32_t z = static_cast<uint32_t>(misc[3]);
-        const uint32_t inv = z == 0 ? 0u : static_cast<uint32_t>(((1ull << 34) + (z >> 1)) / z);
+    if (tid < 32) {  // normalise and quantise this part's 32-value group (emulator:686-711)
+        const uint32_t zz = static_cast<uint32_t>(misc[3]);
+        const uint32_t inv = zz == 0 ? 0u : static_cast<uint32_t>(((1ull << 34) + (zz >> 1)) / zz);
         const int32_t o = mulq17(st, inv);
         const int32_t mag = o == INT32_MIN ? INT32_MAX : abs(o);
         const int32_t mx = __reduce_max_sync(FULL, mag);
