@@ -172,7 +172,7 @@ int contrib_slots(int chunks) {
 
 int ring_slots(int chunks) {
     const size_t fixed = linear_smem_bytes(0, chunks, contrib_slots(chunks));
-    return static_cast<int>((kSmemBudget - fixed) / (kChunkBytes + 16));
+    return static_cast<int>((kSmemBudget - fixed - 16) / (kChunkBytes + 16 + 4));
 }
 
 template <typename Kern, typename... Args>

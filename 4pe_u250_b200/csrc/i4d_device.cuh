@@ -85,6 +85,27 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Ring-slot handshake.  Before issuing chunk c into a slot the producer
+// records c in issued[slot]; the consumer of chunk c waits for that record
+// before its parity wait on the slot's full barrier.  Parity alone cannot
+// tell apart phases that are two apart: without the record, a consumer of
+// chunk c + NS could pass while chunk c is still landing and free the slot
+// early, letting a second copy into a slot that still has one in flight.
+__device__ __forceinline__ void publish_issued(int* issued, int c) {
+    *reinterpret_cast<volatile int*>(issued) = c;
+}
+
+__device__ __forceinline__ bool wait_issued(const int* issued, int c, unsigned* err) {
+    for (uint32_t it = 0; *reinterpret_cast<const volatile int*>(issued) != c; ++it) {
+        if (it > (1u << 24)) {
+            atomicOr(err, kErrWaitFull);
+            return false;
+        }
+        __nanosleep(32);
+    }
+    return true;
+}
+
 __device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

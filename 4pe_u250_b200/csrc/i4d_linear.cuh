@@ -73,6 +73,7 @@ struct LinearSmem {
     int* unit_cnt;      // [nu]: chunks of the unit done
     int* slot_ok;       // [nu]: first unit index allowed to use the slot
     int* fin;           // [kFinMax + 2]: count, level-2 flag, stripe list
+    int* issued;        // [ns]: chunk index last issued into each ring slot
 };
 
 __host__ __device__ inline size_t align16(size_t b) { return (b + 15) & ~static_cast<size_t>(15); }
@@ -84,6 +85,7 @@ __host__ __device__ inline size_t linear_smem_bytes(int ns, int chunks, int nu) 
     b += align16(groups * 64) + align16(groups * 8);
     b += static_cast<size_t>(nu) * groups * 32 * 4;
     b += align16(2 * static_cast<size_t>(nu) * 4) + align16((kFinMax + 2) * 4);
+    b += align16(static_cast<size_t>(ns) * 4);
     return b;
 }
 
@@ -108,6 +110,8 @@ __device__ __forceinline__ LinearSmem carve(uint8_t* base, int ns, int chunks, i
     s.slot_ok = s.unit_cnt + nu;
     p += align16(2 * static_cast<size_t>(nu) * 4);
     s.fin = reinterpret_cast<int*>(p);
+    p += align16((kFinMax + 2) * 4);
+    s.issued = reinterpret_cast<int*>(p);
     return s;
 }
 
@@ -251,6 +255,7 @@ __global__ void __launch_bounds__(kLinearThreads, 2) k_linear(const __grid_const
         s.slot_ok[threadIdx.x] = threadIdx.x;
     }
     if (threadIdx.x < 2) s.fin[threadIdx.x] = 0;
+    for (int i = threadIdx.x; i < a.ns; i += blockDim.x) s.issued[i] = -1;
     __syncthreads();
     pdl_trigger();
 
@@ -264,6 +269,7 @@ __global__ void __launch_bounds__(kLinearThreads, 2) k_linear(const __grid_const
             uint32_t phase = 0;
             for (int i = 0; i < nchunks; ++i) {
                 if (i >= a.ns) mbar_wait(&s.empty[slot], phase ^ 1u, a.err, kErrWaitEmpty);
+                publish_issued(&s.issued[slot], i);
                 mbar_arrive_expect_tx(&s.full[slot], kChunkBytes);
                 bulk_g2s(s.ring + static_cast<size_t>(slot) * kChunkBytes,
                          src + static_cast<size_t>(i) * kChunkBytes, kChunkBytes, &s.full[slot]);
@@ -282,6 +288,7 @@ __global__ void __launch_bounds__(kLinearThreads, 2) k_linear(const __grid_const
     const int rows_total = a.units * 32;
     for (int i = cw; i < nchunks; i += kConsumerWarps) {
         const int slot = i % a.ns;
+        wait_issued(&s.issued[slot], i, a.err);
         mbar_wait(&s.full[slot], static_cast<uint32_t>((i / a.ns) & 1), a.err, kErrWaitFull);
         const uint8_t* ch = s.ring + static_cast<size_t>(slot) * kChunkBytes;
         uint4 wv[8];

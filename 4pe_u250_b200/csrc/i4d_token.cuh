@@ -109,11 +109,12 @@ struct TokSmem {
     int* slot_ok;        // [8]
     int* fin;            // [kFinMax + 2]
     int* flag;           // [4] misc
+    int* issued;         // [kTokRing]: chunk sequence number last issued into each slot
 };
 
 __host__ __device__ inline size_t tok_smem_bytes() {
     return static_cast<size_t>(kTokRing) * kChunkBytes + 2 * kTokRing * 8 + 16 + kTokUnion + 16 + 64 +
-           align16((kFinMax + 2) * 4) + 16;
+           align16((kFinMax + 2) * 4) + 16 + align16(kTokRing * 4);
 }
 
 __device__ __forceinline__ TokSmem tok_carve(uint8_t* p) {
@@ -134,6 +135,8 @@ __device__ __forceinline__ TokSmem tok_carve(uint8_t* p) {
     s.fin = reinterpret_cast<int*>(p);
     p += align16((kFinMax + 2) * 4);
     s.flag = reinterpret_cast<int*>(p);
+    p += 16;
+    s.issued = reinterpret_cast<int*>(p);
     return s;
 }
 
@@ -315,6 +318,14 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
         if (i >= nchunks) break;
         const int gi = d.gbase + i;
         const int slot = gi % kTokRing;
+        for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.issued[slot]) != gi; ++it) {
+            if ((it & 63) == 0 && aborted(a)) break;
+            if (it > (1u << 24)) {
+                raise_abort(a, kErrWaitFull);
+                break;
+            }
+            __nanosleep(32);
+        }
         tok_mbar_wait(a, &s.full[slot], static_cast<uint32_t>((gi / kTokRing) & 1), kErrWaitFull);
         const uint8_t* ch = s.ring + static_cast<size_t>(slot) * kChunkBytes;
         uint4 wv[8];
@@ -748,6 +759,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
         for (int i = 0; i < kTokRing; ++i) {
             mbar_init(&s.full[i], 1);
             mbar_init(&s.empty[i], 1);
+            s.issued[i] = -1;
         }
         mbar_fence_init();
     }
@@ -780,6 +792,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
                             }
                             if (a.trace) trace_add(a, TR_RING_FULL, clock64() - t0);
                         }
+                        publish_issued(&s.issued[slot], issued);
                         mbar_arrive_expect_tx(&s.full[slot], kChunkBytes);
                         bulk_g2s(s.ring + static_cast<size_t>(slot) * kChunkBytes,
                                  src + static_cast<size_t>(i) * kChunkBytes, kChunkBytes, &s.full[slot]);
