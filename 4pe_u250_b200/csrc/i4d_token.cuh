@@ -30,7 +30,10 @@ namespace i4d {
 
 constexpr int kTokWarps = 16;
 constexpr int kTokThreads = 32 * (1 + kTokWarps);
-constexpr int kTokRing = 40;               // ring slots of kChunkBytes
+constexpr int kTokRing = 40;               // ring capacity in chunks of kChunkBytes
+constexpr int kTokCpc = 4;                 // chunks per bulk copy (16,896 B: streams near the HBM peak)
+constexpr int kTokSlots = kTokRing / kTokCpc;  // ring slots, one copy each
+constexpr int kTokSlotBytes = kTokCpc * kChunkBytes;
 constexpr int kTokUnion = 55296;           // GEMV activations + contributions, or attention scratch
 constexpr int kTokContribBytes = 32768;
 constexpr int kAttnParts = 4;              // 32-dimension parts per head
@@ -109,12 +112,12 @@ struct TokSmem {
     int* slot_ok;        // [8]
     int* fin;            // [kFinMax + 2]
     int* flag;           // [4] misc
-    int* issued;         // [kTokRing]: chunk sequence number last issued into each slot
+    int* issued;         // [kTokSlots]: copy sequence number last issued into each slot
 };
 
 __host__ __device__ inline size_t tok_smem_bytes() {
-    return static_cast<size_t>(kTokRing) * kChunkBytes + 2 * kTokRing * 8 + 16 + kTokUnion + 16 + 64 +
-           align16((kFinMax + 2) * 4) + 16 + align16(kTokRing * 4);
+    return static_cast<size_t>(kTokRing) * kChunkBytes + 2 * kTokSlots * 8 + 16 + kTokUnion + 16 + 64 +
+           align16((kFinMax + 2) * 4) + 16 + align16(kTokSlots * 4);
 }
 
 __device__ __forceinline__ TokSmem tok_carve(uint8_t* p) {
@@ -122,9 +125,9 @@ __device__ __forceinline__ TokSmem tok_carve(uint8_t* p) {
     s.ring = p;
     p += static_cast<size_t>(kTokRing) * kChunkBytes;
     s.full = reinterpret_cast<uint64_t*>(p);
-    s.empty = s.full + kTokRing;
-    s.abar = s.empty + kTokRing;
-    p += 2 * kTokRing * 8 + 16;
+    s.empty = s.full + kTokSlots;
+    s.abar = s.empty + kTokSlots;
+    p += 2 * kTokSlots * 8 + 16;
     s.uni = p;
     p += kTokUnion;
     s.next = reinterpret_cast<int*>(p);
@@ -188,7 +191,7 @@ struct StageDesc {
     int layer;
     int u0, u1;           // this CTA's units in its bank
     int bank;
-    int gbase;            // global chunk sequence number of the stage's first chunk
+    int cbase;            // global copy sequence number of the stage's first copy
 };
 
 __device__ __forceinline__ int stage_stripes(int st) { return st == TS_GU ? 352 : stage_units(st); }
@@ -316,9 +319,9 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
         if (lane == 0) i = atomicAdd(s.next, 1);
         i = __shfl_sync(FULL, i, 0);
         if (i >= nchunks) break;
-        const int gi = d.gbase + i;
-        const int slot = gi % kTokRing;
-        for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.issued[slot]) != gi; ++it) {
+        const int cp = d.cbase + i / kTokCpc;
+        const int slot = cp % kTokSlots;
+        for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.issued[slot]) != cp; ++it) {
             if ((it & 63) == 0 && aborted(a)) break;
             if (it > (1u << 24)) {
                 raise_abort(a, kErrWaitFull);
@@ -326,8 +329,8 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
             }
             __nanosleep(32);
         }
-        tok_mbar_wait(a, &s.full[slot], static_cast<uint32_t>((gi / kTokRing) & 1), kErrWaitFull);
-        const uint8_t* ch = s.ring + static_cast<size_t>(slot) * kChunkBytes;
+        tok_mbar_wait(a, &s.full[slot], static_cast<uint32_t>((cp / kTokSlots) & 1), kErrWaitFull);
+        const uint8_t* ch = s.ring + static_cast<size_t>(slot) * kTokSlotBytes + (i % kTokCpc) * kChunkBytes;
         uint4 wv[8];
 #pragma unroll
         for (int g = 0; g < 8; ++g)
@@ -335,7 +338,13 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
         const int16_t raw0 = reinterpret_cast<const int16_t*>(ch)[lane * 2];
         const int16_t raw1 = reinterpret_cast<const int16_t*>(ch)[lane * 2 + 1];
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s.empty[slot]);
+        if (lane == 0) {
+            // The empty barrier counts kTokCpc chunk releases; the last chunk of
+            // a short final copy also releases the chunks the copy lacks.
+            uint32_t rel = 1;
+            if (i == nchunks - 1 && nchunks % kTokCpc != 0) rel = kTokCpc - nchunks % kTokCpc + 1;
+            mbar_arrive_cnt(&s.empty[slot], rel);
+        }
 
         const int uidx = i / C, j = i - uidx * C;
         const int us = uidx % NU;
@@ -756,9 +765,9 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
         *u1 = static_cast<int>((static_cast<long long>(c + 1) * U) / a.cpb);
     };
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kTokRing; ++i) {
+        for (int i = 0; i < kTokSlots; ++i) {
             mbar_init(&s.full[i], 1);
-            mbar_init(&s.empty[i], 1);
+            mbar_init(&s.empty[i], kTokCpc);
             s.issued[i] = -1;
         }
         mbar_fence_init();
@@ -783,8 +792,9 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
                                          static_cast<size_t>(bank) * a.bank_bytes[stage] +
                                          static_cast<size_t>(u0) * C * kChunkBytes;
                     const int n = (u1 - u0) * C;
-                    for (int i = 0; i < n; ++i) {
-                        if (issued >= kTokRing) {
+                    for (int i = 0; i < n; i += kTokCpc) {
+                        const int cnt = min(kTokCpc, n - i);
+                        if (issued >= kTokSlots) {
                             const long long t0 = a.trace ? clock64() : 0;
                             if (!tok_mbar_wait(a, &s.empty[slot], phase ^ 1u, kErrWaitEmpty)) {
                                 ok = false;
@@ -793,11 +803,11 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
                             if (a.trace) trace_add(a, TR_RING_FULL, clock64() - t0);
                         }
                         publish_issued(&s.issued[slot], issued);
-                        mbar_arrive_expect_tx(&s.full[slot], kChunkBytes);
-                        bulk_g2s(s.ring + static_cast<size_t>(slot) * kChunkBytes,
-                                 src + static_cast<size_t>(i) * kChunkBytes, kChunkBytes, &s.full[slot]);
+                        mbar_arrive_expect_tx(&s.full[slot], cnt * kChunkBytes);
+                        bulk_g2s(s.ring + static_cast<size_t>(slot) * kTokSlotBytes,
+                                 src + static_cast<size_t>(i) * kChunkBytes, cnt * kChunkBytes, &s.full[slot]);
                         ++issued;
-                        if (++slot == kTokRing) {
+                        if (++slot == kTokSlots) {
                             slot = 0;
                             phase ^= 1u;
                         }
@@ -805,10 +815,10 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
                 }
             }
             // Never leave with copies in flight: wait for the last ones to land.
-            for (int k = 0; k < kTokRing && k < issued; ++k) {
+            for (int k = 0; k < kTokSlots && k < issued; ++k) {
                 const int g = issued - 1 - k;
-                const int sl = g % kTokRing;
-                for (uint32_t it = 0; !mbar_try_wait(&s.full[sl], static_cast<uint32_t>((g / kTokRing) & 1)); ++it) {
+                const int sl = g % kTokSlots;
+                for (uint32_t it = 0; !mbar_try_wait(&s.full[sl], static_cast<uint32_t>((g / kTokSlots) & 1)); ++it) {
                     if (it > (1u << 22)) {
                         atomicOr(a.err, kErrWaitFull);
                         break;
@@ -834,7 +844,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
     }
     StageDesc d;
     d.bank = bank;
-    d.gbase = 0;
+    d.cbase = 0;
     for (int l = 0; l <= a.layers; ++l) {
         for (int st = TS_QKV; st <= TS_DOWN; ++st) {
             const int stage = l == a.layers ? TS_LOGITS : st;
@@ -844,7 +854,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
             urange(stage, &d.u0, &d.u1);
             if (stage == TS_DOWN) tok_gemv_stage<11>(a, s, d, cw, lane);
             else tok_gemv_stage<4>(a, s, d, cw, lane);
-            d.gbase += (d.u1 - d.u0) * stage_chunks(stage);
+            d.cbase += ((d.u1 - d.u0) * stage_chunks(stage) + kTokCpc - 1) / kTokCpc;
             if (stage == TS_QKV && l < a.layers) {
                 if (blockIdx.x < kAttnItems) tok_attention(a, s, l, blockIdx.x, cw, lane);
                 tok_bar();
