@@ -31,7 +31,7 @@ EXPORTS = [
     "i4d_load_embeddings", "i4d_decode_token", "i4d_kv_reset", "i4d_kv_read", "i4d_kv_write",
     "i4d_sync", "i4d_linear_bank", "i4d_gemv", "i4d_quantize_g32", "i4d_rms_quant",
     "i4d_attention", "i4d_swiglu_quant", "i4d_expf", "i4d_decode_token_async", "i4d_stream",
-    "i4d_profile_token", "i4d_token_breakdown",
+    "i4d_profile_token", "i4d_token_breakdown", "i4d_linear_bank_noalloc",
 ]
 
 BREAKDOWN = ["wait", "prologue", "chunks", "epilogue", "attn_wait", "attn", "ring_full", "total",
@@ -86,6 +86,7 @@ def load_library():
         "i4d_stream": [P],
         "i4d_profile_token": [P, ctypes.c_uint32, P, P, P],
         "i4d_token_breakdown": [P, ctypes.c_uint32, P, P, ctypes.c_int],
+        "i4d_linear_bank_noalloc": [P, P, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, P, P, ctypes.c_int, P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -206,6 +207,13 @@ class Context:
                                             q.ctypes.data, e.ctypes.data, int(bool(hls_zero_start)),
                                             out.ctypes.data))
         return out
+
+    def linear_bank_noalloc(self, superblocks_dev_ptr, n_bytes, local_in_tiles, out_tiles, act_q_dev_ptr,
+                            act_e8m0_dev_ptr, partial_out_dev_ptr, hls_zero_start=False):
+        """i4d_linear_bank_noalloc on caller-owned device buffers (raw pointers)."""
+        self._check(self._L.i4d_linear_bank_noalloc(self._h, superblocks_dev_ptr, n_bytes, local_in_tiles,
+                                                    out_tiles, act_q_dev_ptr, act_e8m0_dev_ptr,
+                                                    int(bool(hls_zero_start)), partial_out_dev_ptr))
 
     def gemv(self, layer, mode, act_q, act_e8m0, with_partials=False):
         rows = formats.mode_rows(mode)

@@ -13,6 +13,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -789,6 +790,40 @@ struct DevBuf {
     DevBuf name;            \
     CK(cudaMalloc(&name.p, (bytes)))
 
+namespace {
+
+// ---- Scratch of i4d_linear_bank_noalloc ----
+// A fixed device array replaces the per-call allocations of i4d_linear_bank:
+// bytes [0, 4) are the call's device error word (cleared at the start of
+// every call), the re-tiled weights start at byte 256.  22 superblocks
+// (5,947,392 B) hold one bank's slice of the largest decoder-layer matrix
+// (GATE, UP or DOWN; Q, K, V and O need 8); the LM head (63) does not fit.
+constexpr size_t kNoAllocHeader = 256;
+constexpr size_t kNoAllocMaxBytes = 22ull * 4224 * 64;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocHeader + kNoAllocMaxBytes];
+
+constexpr int kNoAllocDevices = 64;
+std::mutex g_noalloc_mu;
+uint8_t* g_noalloc_ptr[kNoAllocDevices];  // device address of the array, per device ordinal
+
+// Once per device, with that device current: the array's device address.
+i4d_status noalloc_scratch(i4d_ctx* c, uint8_t** out) {
+    if (c->device < 0 || c->device >= kNoAllocDevices)
+        return fail(c, I4D_ERR_ARG, "device ordinal %d out of range for the static scratch", c->device);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[c->device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return fail(c, I4D_ERR_CUDA, "cudaGetSymbolAddress(g_noalloc_scratch) failed: %s", cudaGetErrorString(e));
+        g_noalloc_ptr[c->device] = static_cast<uint8_t*>(p);
+    }
+    *out = g_noalloc_ptr[c->device];
+    return I4D_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 i4d_status i4d_linear_bank(i4d_ctx* c, const void* superblocks, size_t n_bytes, int lit, int out_tiles,
@@ -836,6 +871,65 @@ i4d_status i4d_linear_bank(i4d_ctx* c, const void* superblocks, size_t n_bytes, 
     const i4d_status st = finish(c);
     if (st != I4D_OK) return st;
     CK(cudaMemcpy(partial_out, c->d_partials, static_cast<size_t>(out_tiles) * 128 * sizeof(float), cudaMemcpyDeviceToHost));
+    return I4D_OK;
+}
+
+i4d_status i4d_linear_bank_noalloc(i4d_ctx* c, const void* superblocks_dev, size_t n_bytes, int lit, int out_tiles,
+                                   const int16_t* act_q_dev, const uint8_t* act_e8m0_dev, int hls_zero_start,
+                                   float* partial_out_dev) {
+    if (!c) return I4D_ERR_ARG;
+    if (!superblocks_dev || !act_q_dev || !act_e8m0_dev || !partial_out_dev) return fail(c, I4D_ERR_ARG, "null buffer");
+    if ((reinterpret_cast<uintptr_t>(superblocks_dev) | reinterpret_cast<uintptr_t>(act_q_dev)) & 1 ||
+        reinterpret_cast<uintptr_t>(partial_out_dev) & 3)
+        return fail(c, I4D_ERR_ARG, "misaligned device buffer (superblocks and act_q need 2 bytes, partial_out 4)");
+    if (lit < 1 || lit > 11 || out_tiles < 1 || out_tiles > 1008 || (out_tiles * lit) % 16 != 0)
+        return fail(c, I4D_ERR_ARG, "unsupported linear geometry: %d local input tiles, %d output tiles", lit, out_tiles);
+    const size_t need = static_cast<size_t>(out_tiles) * lit / 16 * 4224 * 64;
+    if (n_bytes != need) return fail(c, I4D_ERR_SIZE, "superblock stream has %zu bytes; expected %zu", n_bytes, need);
+    if (n_bytes > kNoAllocMaxBytes)
+        return fail(c, I4D_ERR_SIZE,
+                    "superblock stream of %zu bytes exceeds the %zu-byte static scratch of "
+                    "i4d_linear_bank_noalloc (22 superblocks); use i4d_linear_bank",
+                    n_bytes, kNoAllocMaxBytes);
+    CK(cudaSetDevice(c->device));
+    uint8_t* scratch = nullptr;
+    const i4d_status st = noalloc_scratch(c, &scratch);
+    if (st != I4D_OK) return st;
+    unsigned* err = reinterpret_cast<unsigned*>(scratch);
+    uint8_t* tiles = scratch + kNoAllocHeader;
+    CK(cudaMemsetAsync(err, 0, sizeof(unsigned), c->stream));
+    RelayoutArgs r;
+    r.src = static_cast<const uint8_t*>(superblocks_dev);
+    r.dst = tiles;
+    r.unit_offset = 0;
+    r.lit = lit;
+    k_relayout<<<out_tiles * 4 * lit, 256, 0, c->stream>>>(r);
+    CK(cudaGetLastError());
+    LinearArgs a = {};
+    a.w = tiles;
+    a.bank_stride = 0;
+    a.nbanks = 1;
+    a.units = out_tiles * 4;
+    a.cpb = a.units < c->num_sms ? a.units : c->num_sms;
+    a.chunks = lit;
+    a.ns = ring_slots(lit);
+    a.nu = contrib_slots(lit);
+    a.in_kind = IN_ACT;
+    a.act_q = act_q_dev;
+    a.act_e = act_e8m0_dev;
+    a.act_bank_stride = 0;
+    a.hls_zero = hls_zero_start ? 1 : 0;
+    a.partials = partial_out_dev;
+    a.epi = EPI_PARTIAL;
+    a.counters = nullptr;  // the partial epilogue uses no stripe counters
+    a.expf = c->expf;
+    a.err = err;
+    CK(run_linear(c, a, false));
+    unsigned e = 0;
+    CK(cudaMemcpyAsync(&e, err, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    if (e & kErrArg) return fail(c, I4D_ERR_ARG, "device rejected an argument (error word 0x%x)", e);
+    if (e) return fail(c, I4D_ERR_TIMEOUT, "a bounded device wait gave up (error word 0x%x)", e);
     return I4D_OK;
 }
 

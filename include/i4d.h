@@ -158,6 +158,27 @@ i4d_status i4d_linear_bank(i4d_ctx* ctx, const void* superblocks, size_t n_bytes
                            int local_in_tiles, int out_tiles, const int16_t* act_q,
                            const uint8_t* act_e8m0, int hls_zero_start, float* partial_out);
 
+/* i4d_linear_bank without any allocation, for callers that must not allocate
+ * once they are running: a serving loop whose device memory is reserved up
+ * front, or one that shares the GPU with other streams (cudaFree waits for
+ * the whole device, so a per-call free stalls them).  No counterpart in the
+ * reference.  Same arithmetic and result as i4d_linear_bank, but every buffer
+ * is a device pointer (superblocks_dev and act_q_dev 2-byte aligned,
+ * partial_out_dev 4-byte aligned) and the re-tiled weights go to a fixed
+ * 5,947,392-byte static device array (22 superblocks: any bank slice of a
+ * decoder-layer matrix); a larger stream, such as the LM head's, is rejected
+ * with I4D_ERR_SIZE.  The array's device error word is cleared at the start
+ * of each call; nothing else needs to start at zero.  The first call on a
+ * device looks up the array's address (cudaGetSymbolAddress), so make one
+ * call before any stream capture.  The call runs on the context's stream and
+ * returns once it has finished.  The array is shared by every context of a
+ * device: calls that overlap on one device, from any thread or context,
+ * race on it and must be serialised by the caller. */
+i4d_status i4d_linear_bank_noalloc(i4d_ctx* ctx, const void* superblocks_dev, size_t n_bytes,
+                                   int local_in_tiles, int out_tiles, const int16_t* act_q_dev,
+                                   const uint8_t* act_e8m0_dev, int hls_zero_start,
+                                   float* partial_out_dev);
+
 /* Full 4-bank GEMV of a loaded matrix: y = (p0+p1)+(p2+p3) (pair reducers and
  * finalizer, int4_linear_controller.hpp:64-93; emulator sharded_gemv_4pe).
  * partials_out ([4][rows], may be NULL) receives the per-bank partials. */
