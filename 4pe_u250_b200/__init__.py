@@ -34,8 +34,10 @@ EXPORTS = [
     "i4d_profile_token", "i4d_token_breakdown", "i4d_linear_bank_noalloc",
 ]
 
-BREAKDOWN = ["wait", "prologue", "chunks", "epilogue", "attn_wait", "attn", "ring_full", "total",
-             "stage_qkv", "stage_o", "stage_gu", "stage_down", "stage_logits"]
+_STAGES = ["qkv", "o", "gu", "down", "logits"]
+BREAKDOWN = ([f"wait_{x}" for x in _STAGES] + [f"prologue_{x}" for x in _STAGES] + [f"chunks_{x}" for x in _STAGES]
+             + ["attn_wait", "attn", "ring_full", "total",
+                "warp_data_wait", "warp_slot_wait", "warp_compute", "warp_chain"])
 
 KERNEL_CLASSES = ["qkv_gemv", "attention", "o_gemv", "gate_up_gemv", "down_gemv", "logits_gemv", "rms", "token"]
 

@@ -267,15 +267,11 @@ TokenArgs token_args(i4d_ctx* c) {
     t.layers = c->layers;
     t.cpb = c->cpb;
     t.resid = c->d_resid;
-    t.recip = c->d_recips;
     t.gamma = c->d_gamma;
     t.partials = c->d_partials;
     t.ao_q = c->d_ao_q;
     t.ao_e = c->d_ao_e;
-    t.ad_q = c->d_ad_q;
-    t.ad_e = c->d_ad_e;
     t.logits = c->d_logits;
-    t.counters = c->d_counters;
     t.sync = c->d_sync;
     t.attn = base_attn(c, 0);
     t.expf = c->expf;
@@ -464,9 +460,9 @@ i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out) {
     c->kv_bytes = 4ull * c->layers * kLocalHeads * static_cast<size_t>(c->stride) * 320;
     CKC(cudaMalloc(&c->d_kv, c->kv_bytes));
     CKC(cudaMemset(c->d_kv, 0, c->kv_bytes));
-    CKC(cudaMalloc(&c->d_resid, kDim * sizeof(float)));
+    CKC(cudaMalloc(&c->d_resid, 2 * kDim * sizeof(float)));  // two buffers for the token kernel
     CKC(cudaMalloc(&c->d_recip, 16));
-    CKC(cudaMalloc(&c->d_partials, 4ull * kPVocab * sizeof(float)));
+    CKC(cudaMalloc(&c->d_partials, 2ull * kPartialBuf * sizeof(float)));  // two buffers for the token kernel
     CKC(cudaMalloc(&c->d_ao_q, kDim * sizeof(int16_t)));
     CKC(cudaMalloc(&c->d_ao_e, kDim / 32));
     CKC(cudaMalloc(&c->d_ad_q, kFfn * sizeof(int16_t)));
@@ -497,28 +493,37 @@ i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out) {
     c->log2e_q21 = static_cast<int>(std::nearbyint(1.4426950408889634 * static_cast<double>(1 << 21)));
     c->score_scale = host_float_to_q17(0.08838834764831845f);
 
-    // Hash table of the measured expf exceptions.
-    uint32_t cap = 1;
-    while (cap < 3u * i4d_expf_fix_count + 1u) cap <<= 1;
-    std::vector<uint32_t> slots(2ull * cap, 0xffffffffu);
-    int max_probe = 1;
-    for (uint32_t i = 0; i < i4d_expf_fix_count; ++i) {
-        const uint32_t key = i4d_expf_fix[2 * i], val = i4d_expf_fix[2 * i + 1];
-        uint32_t s = expf_hash(key) & (cap - 1);
-        int probe = 1;
-        while (slots[2 * s] != 0xffffffffu) {
-            s = (s + 1) & (cap - 1);
-            ++probe;
+    // Two-choice bucketed hash of the measured expf exceptions (layout in
+    // i4d_expf.cuh); grows until every key has a bucket with room.
+    std::vector<uint32_t> buckets;
+    uint32_t nb = 1;
+    while (nb < i4d_expf_fix_count / 2 + 1) nb <<= 1;
+    for (;; nb <<= 1) {
+        buckets.assign(8ull * nb, 0xffffffffu);
+        std::vector<uint8_t> fill(nb, 0);
+        bool ok = true;
+        for (uint32_t i = 0; i < i4d_expf_fix_count && ok; ++i) {
+            const uint32_t key = i4d_expf_fix[2 * i], val = i4d_expf_fix[2 * i + 1];
+            const uint32_t b1 = expf_hash(key) & (nb - 1), b2 = expf_hash(key ^ kExpfSeed2) & (nb - 1);
+            const uint32_t b = fill[b2] < fill[b1] ? b2 : b1;
+            if (fill[b] == 4) {
+                ok = false;
+                break;
+            }
+            buckets[8ull * b + fill[b]] = key;
+            buckets[8ull * b + 4 + fill[b]] = val;
+            ++fill[b];
         }
-        slots[2 * s] = key;
-        slots[2 * s + 1] = val;
-        if (probe > max_probe) max_probe = probe;
+        if (ok) break;
+        if (nb >= (1u << 24)) {
+            fail(c, I4D_ERR_STATE, "expf exception table does not fit");
+            return bail(I4D_ERR_STATE);
+        }
     }
-    CKC(cudaMalloc(&c->d_expf_slots, slots.size() * sizeof(uint32_t)));
-    CKC(cudaMemcpy(c->d_expf_slots, slots.data(), slots.size() * sizeof(uint32_t), cudaMemcpyHostToDevice));
-    c->expf.slots = c->d_expf_slots;
-    c->expf.mask = cap - 1;
-    c->expf.max_probe = max_probe;
+    CKC(cudaMalloc(&c->d_expf_slots, buckets.size() * sizeof(uint32_t)));
+    CKC(cudaMemcpy(c->d_expf_slots, buckets.data(), buckets.size() * sizeof(uint32_t), cudaMemcpyHostToDevice));
+    c->expf.buckets = c->d_expf_slots;
+    c->expf.mask = nb - 1;
 #undef CKC
     *out = c;
     return I4D_OK;
@@ -1092,7 +1097,8 @@ extern "C" i4d_status i4d_token_breakdown(i4d_ctx* c, uint32_t position, const f
     for (int k = 0; k < kTraceSlots; ++k) {
         double sum = 0.0;
         for (int b = 0; b < 4 * c->cpb; ++b) sum += static_cast<double>(h[static_cast<size_t>(b) * kTraceSlots + k]);
-        us_out[k] = static_cast<float>(sum / (4 * c->cpb) / (khz * 1e-3));
+        const double per = k >= TR_W_DATA ? 4.0 * c->cpb * kTokWarps : 4.0 * c->cpb;  // warp slots: per warp
+        us_out[k] = static_cast<float>(sum / per / (khz * 1e-3));
     }
     return I4D_OK;
 }

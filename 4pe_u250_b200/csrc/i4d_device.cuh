@@ -18,6 +18,7 @@ constexpr int kPVocab = 32256;
 constexpr int kHeads = 32;
 constexpr int kHeadDim = 128;
 constexpr int kLocalHeads = 8;
+constexpr int kGammaFinal = 64;      // row of the final norm's gamma in the [65][4096] table
 constexpr int kChunkBytes = 4224;     // 32 rows x 256 columns: 128 B scales + 4096 B weights
 constexpr int kChunkScaleBytes = 128;
 constexpr int kConsumerWarps = 8;
@@ -86,6 +87,20 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// L2 policy for data read once (weights): evict before anything else.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
         : "memory");
 }
 

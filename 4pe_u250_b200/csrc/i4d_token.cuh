@@ -40,13 +40,14 @@ constexpr int kAttnParts = 4;              // 32-dimension parts per head
 constexpr int kAttnItems = kHeads * kAttnParts;
 
 // Global synchronisation words (zeroed by the last CTA at the end of a token).
+// Stage ordinals: QKV, O, GATE/UP, DOWN of layer l are 4l .. 4l+3, the LM
+// head 4L.
 constexpr int kSyncAbort = 0;
 constexpr int kSyncExit = 1;
-constexpr int kSyncQkv = 2;        // + layer: CTAs that stored their QKV partials
-constexpr int kSyncAtt = 34;       // + layer: attention items finished
-constexpr int kSyncSwiglu = 66;    // + layer: SwiGLU stripes finalised
-constexpr int kSyncRms = 98;       // + norm index (2l, 2l+1, 2L): RMS reciprocal ready
-constexpr int kSyncWords = 164;
+constexpr int kSyncStage = 2;                   // + ordinal: CTAs whose partials of that stage are stored
+constexpr int kSyncAtt = kSyncStage + 4 * 32 + 1;  // + layer: attention items finished
+constexpr int kSyncWords = kSyncAtt + 32;
+constexpr int kPartialBuf = 4 * 32256;          // floats of one partial buffer [4 banks][rows]
 
 enum TokStage : int { TS_QKV = 0, TS_O, TS_GU, TS_DOWN, TS_LOGITS };
 
@@ -57,16 +58,12 @@ struct TokenArgs {
     size_t bank_bytes[5];      // one bank's region of each stage
     int layers;
     int cpb;                   // CTAs per bank (gridDim.x == 4 * cpb)
-    float* resid;              // [4096], updated in place
-    float* recip;              // [65]: RMS reciprocal of each norm
+    float* resid;              // [2][4096]: after residual update n, buffer n & 1 (0: token input and output)
     const float* gamma;        // [65][4096]
-    float* partials;           // [4][32256]
+    float* partials;           // [2][4][32256]: stage ordinal k writes buffer k & 1
     int16_t* ao_q;             // attention output
     uint8_t* ao_e;
-    int16_t* ad_q;             // SwiGLU output
-    uint8_t* ad_e;
     float* logits;
-    unsigned* counters;        // stripe counters [kCounterSlots]
     unsigned* sync;            // [kSyncWords]
     AttnArgs attn;             // position, RoPE, KV, LUT, coefficient scratch
     ExpfFix expf;
@@ -76,19 +73,17 @@ struct TokenArgs {
 
 // Cycle-sum categories of the optional trace (per CTA, summed over a token).
 enum TraceSlot : int {
-    TR_WAIT = 0,      // consumer: waiting for a stage's input
-    TR_PROLOGUE,      // consumer: building activations
-    TR_CHUNKS,        // consumer: chunk loop
-    TR_EPILOGUE,      // consumer: end-of-stage epilogue
-    TR_ATTN_WAIT,     // attention item: waiting for the QKV partials
+    TR_WAIT = 0,      // + stage (QKV, O, GATE/UP, DOWN, LM head): waiting for the stage's input
+    TR_PROLOGUE = 5,  // + stage: building the stage's activations
+    TR_CHUNKS = 10,   // + stage: chunk loop up to the CTA barrier
+    TR_ATTN_WAIT = 15,  // attention item: waiting for the QKV partials
     TR_ATTN,          // attention item: everything else
     TR_RING_FULL,     // producer: blocked on a full ring
     TR_TOTAL,         // consumer: whole kernel
-    TR_STAGE_QKV,     // consumer: QKV stage total (incl. wait)
-    TR_STAGE_O,
-    TR_STAGE_GU,
-    TR_STAGE_DOWN,
-    TR_STAGE_LOGITS,
+    TR_W_DATA,        // per consumer warp (summed over warps): waiting for ring data
+    TR_W_SLOT,        // per warp: waiting for a contribution slot
+    TR_W_COMPUTE,     // per warp: chunk arithmetic
+    TR_W_CHAIN,       // per warp: row chains of finished units
     kTraceSlots
 };
 
@@ -194,83 +189,112 @@ struct StageDesc {
     int cbase;            // global copy sequence number of the stage's first copy
 };
 
-__device__ __forceinline__ int stage_stripes(int st) { return st == TS_GU ? 352 : stage_units(st); }
+__device__ __forceinline__ int stage_ordinal(int st, int layer) { return st == TS_LOGITS ? 4 * layer : 4 * layer + st; }
 
-// Linear args view for the shared prologue / finalize helpers.
-__device__ __forceinline__ LinearArgs stage_view(const TokenArgs& a, int st, int layer) {
-    LinearArgs v = {};
-    v.nbanks = 4;
-    v.units = stage_units(st);
-    v.chunks = stage_chunks(st);
-    v.partials = a.partials;
-    v.counters = a.counters;
-    v.expf = a.expf;
-    v.err = a.err;
-    v.hls_zero = 0;
-    if (st == TS_QKV || st == TS_GU || st == TS_LOGITS) {
-        v.in_kind = IN_RMS;
-        v.resid = a.resid;
-        const int norm = st == TS_LOGITS ? 2 * a.layers : (st == TS_QKV ? 2 * layer : 2 * layer + 1);
-        v.gamma = a.gamma + static_cast<size_t>(st == TS_LOGITS ? 64 : (st == TS_QKV ? 2 * layer : 2 * layer + 1)) * kDim;
-        v.recip = a.recip + norm;
-    } else {
-        v.in_kind = IN_ACT;
-        v.act_q = st == TS_O ? a.ao_q : a.ad_q;
-        v.act_e = st == TS_O ? a.ao_e : a.ad_e;
-        v.act_bank_stride = st == TS_O ? 1024 : 2816;
-    }
-    v.epi = st == TS_QKV ? EPI_PARTIAL : st == TS_GU ? EPI_SWIGLU : st == TS_LOGITS ? EPI_STORE : EPI_RESID;
-    v.out = st == TS_LOGITS ? a.logits : a.resid;
-    v.q_out = a.ad_q;
-    v.e_out = a.ad_e;
-    return v;
+__device__ __forceinline__ float* stage_partials(const TokenArgs& a, int ordinal) {
+    return a.partials + static_cast<size_t>(ordinal & 1) * kPartialBuf;
 }
 
-// Activation prologue of the persistent kernel (cross-CTA data is read at L2).
-template <int C>
-__device__ __forceinline__ void tok_prologue(const LinearArgs& v, const LinearSmem& ls, int bank, int cw, int lane) {
-    constexpr int G = C * 8;
+// Input of an RMS-normalised stage (norm index n: 2l before QKV of layer l,
+// 2l+1 before GATE/UP, 2L before the LM head, whose gamma is row 64 whatever
+// L is), built by every CTA from the
+// bank partials of the stage that just ended:
+//   residual_n = residual_{n-1} + ((p0+p1)+(p2+p3))   (emulator:764, 772)
+//   r = RMS reciprocal of residual_n                  (emulator:427-453)
+//   x = fl(fl(residual_n * r) * gamma_n) -> G32 quantizer, this bank's columns.
+// Every CTA computes the same residual; CTA 0 stores it for the next update.
+template <int G>
+__device__ __forceinline__ void tok_input_rms(const TokenArgs& a, const TokSmem& s, const LinearSmem& ls, int bank,
+                                              int norm, int prev_ordinal, float* xs, int cw, int lane) {
     constexpr int kPer = (G + kTokWarps - 1) / kTokWarps;
-    int qv[kPer];
-    uint32_t ev[kPer];
-    if (v.in_kind == IN_RMS) {
-        const float r = __ldcg(v.recip);
-        float x[kPer], g[kPer];
-#pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-            const int lg = cw + k * kTokWarps;
-            if (lg < G) {
-                const int col = bank * G * 32 + lg * 32 + lane;
-                x[k] = __ldcg(v.resid + col);
-                g[k] = v.gamma[col];
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-            const int lg = cw + k * kTokWarps;
-            if (lg < G) qv[k] = quantize_g32_lane(__fmul_rn(__fmul_rn(x[k], r), g[k]), &ev[k]);
-        }
-    } else {
-        const size_t base = static_cast<size_t>(bank) * v.act_bank_stride;
-#pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-            const int lg = cw + k * kTokWarps;
-            if (lg < G) {
-                qv[k] = __ldcg(v.act_q + base + lg * 32 + lane);
-                ev[k] = __ldcg(v.act_e + base / 32 + lg);
-            }
-        }
-    }
+    const int tid = cw * 32 + lane;
+    const int gamma_row = norm == 2 * a.layers ? kGammaFinal : norm;
+    float g[kPer];
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
         const int lg = cw + k * kTokWarps;
-        if (lg < G) put_act(ls, lg, lane, qv[k], ev[k]);
+        if (lg < G) g[k] = a.gamma[static_cast<size_t>(gamma_row) * kDim + bank * G * 32 + lg * 32 + lane];
+    }
+    const float4* rin = reinterpret_cast<const float4*>(a.resid + (norm == 0 ? 0 : ((norm - 1) & 1) * kDim));
+    float4* rout = reinterpret_cast<float4*>(a.resid + (norm & 1) * kDim);
+    const float4* P = reinterpret_cast<const float4*>(stage_partials(a, prev_ordinal));
+    constexpr int kQ = kDim / 4;  // float4 per vector
+#pragma unroll
+    for (int k = 0; k < kQ / (32 * kTokWarps); ++k) {
+        const int i = tid + k * 32 * kTokWarps;
+        float4 x = __ldcg(rin + i);
+        if (norm > 0) {
+            const float4 p0 = __ldcg(P + i), p1 = __ldcg(P + kQ + i);
+            const float4 p2 = __ldcg(P + 2 * kQ + i), p3 = __ldcg(P + 3 * kQ + i);
+            x.x = __fadd_rn(x.x, __fadd_rn(__fadd_rn(p0.x, p1.x), __fadd_rn(p2.x, p3.x)));
+            x.y = __fadd_rn(x.y, __fadd_rn(__fadd_rn(p0.y, p1.y), __fadd_rn(p2.y, p3.y)));
+            x.z = __fadd_rn(x.z, __fadd_rn(__fadd_rn(p0.z, p1.z), __fadd_rn(p2.z, p3.z)));
+            x.w = __fadd_rn(x.w, __fadd_rn(__fadd_rn(p0.w, p1.w), __fadd_rn(p2.w, p3.w)));
+            if (blockIdx.x == 0) __stcg(rout + i, x);
+        }
+        reinterpret_cast<float4*>(xs)[i] = x;
+    }
+    tok_bar();
+    if (cw == 0) {
+        const float r = rms_recip_warp(xs);
+        if (lane == 0) reinterpret_cast<float*>(s.flag)[0] = r;
+    }
+    tok_bar();
+    const float r = reinterpret_cast<const float*>(s.flag)[0];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const int lg = cw + k * kTokWarps;
+        if (lg < G) {
+            uint32_t e8;
+            const float v = __fmul_rn(__fmul_rn(xs[bank * G * 32 + lg * 32 + lane], r), g[k]);
+            const int q = quantize_g32_lane(v, &e8);
+            put_act(ls, lg, lane, q, e8);
+        }
     }
 }
 
-// One GEMV stage of this CTA: wait for its input, build the split
-// activations, consume the stage's chunks from the ring (dynamic chunk
-// assignment across warps), chain units, then the last-arriver epilogue.
+// Input of DOWN: SwiGLU of this bank's 2816 FFN columns from the GATE/UP
+// partials (gate rows [0, 11264), up rows [11264, 22528)), then the G32
+// quantizer (emulator:716-722, 769-770).
+__device__ __forceinline__ void tok_input_swiglu(const TokenArgs& a, const LinearSmem& ls, int bank, int layer, int cw,
+                                                 int lane) {
+    constexpr int G = 88;
+    constexpr int kPer = (G + kTokWarps - 1) / kTokWarps;
+    constexpr int kRows = 22528;
+    const float* P = stage_partials(a, stage_ordinal(TS_GU, layer));
+    float gv[kPer], uv[kPer], sw[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const int lg = min(cw + k * kTokWarps, G - 1);  // warps with 5 groups repeat their last one
+        const int f = bank * G * 32 + lg * 32 + lane;
+        gv[k] = combine4(P, kRows, f);
+        uv[k] = combine4(P, kRows, kFfn + f);
+    }
+    swiglu_n<kPer>(gv, uv, sw, a.expf);
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const int lg = cw + k * kTokWarps;
+        if (lg < G) {
+            uint32_t e8;
+            const int q = quantize_g32_lane(sw[k], &e8);
+            put_act(ls, lg, lane, q, e8);
+        }
+    }
+}
+
+// Input of O: the attention output of this bank's 8 heads.
+__device__ __forceinline__ void tok_input_attention(const TokenArgs& a, const LinearSmem& ls, int bank, int cw, int lane) {
+    constexpr int G = 32;
+    constexpr int kPer = G / kTokWarps;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const int lg = cw + k * kTokWarps;
+        const int q = __ldcg(a.ao_q + bank * 1024 + lg * 32 + lane);
+        const uint32_t e8 = __ldcg(a.ao_e + bank * 32 + lg);
+        put_act(ls, lg, lane, q, e8);
+    }
+}
+
 template <int C>
 __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s, const StageDesc& d, int cw,
                                             int lane) {
@@ -278,7 +302,6 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     constexpr int NU = kTokContribBytes / (G * 128) > 8 ? 8 : kTokContribBytes / (G * 128);
     static_assert(NU >= 2, "contribution slots");
     const unsigned FULL = 0xffffffffu;
-    const LinearArgs v = stage_view(a, d.st, d.layer);
     LinearSmem ls;
     ls.act_hi = reinterpret_cast<int8_t*>(s.uni);
     ls.act_lo = s.uni + G * 32;
@@ -286,21 +309,15 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     ls.act_scale = reinterpret_cast<float*>(s.uni + G * 68);
     float* contrib = reinterpret_cast<float*>(s.uni + align16(G * 72));
     const int tid = cw * 32 + lane;
+    const int ord = stage_ordinal(d.st, d.layer);
     const long long t_begin = clock64();
 
-    // Input readiness.
+    // Input readiness: the previous stage's partials from every CTA, or the
+    // attention items of this layer.
     if (tid == 0) {
-        const unsigned* word;
-        unsigned target = 1;
-        if (d.st == TS_QKV) word = &a.sync[kSyncRms + 2 * d.layer];
-        else if (d.st == TS_O) { word = &a.sync[kSyncAtt + d.layer]; target = kAttnItems; }
-        else if (d.st == TS_GU) word = &a.sync[kSyncRms + 2 * d.layer + 1];
-        else if (d.st == TS_DOWN) { word = &a.sync[kSyncSwiglu + d.layer]; target = 352; }
-        else word = &a.sync[kSyncRms + 2 * a.layers];
-        wait_counter(a, word, target);
+        if (d.st == TS_O) wait_counter(a, &a.sync[kSyncAtt + d.layer], kAttnItems);
+        else if (ord > 0) wait_counter(a, &a.sync[kSyncStage + ord - 1], gridDim.x);
         *s.next = 0;
-        s.fin[0] = 0;
-        s.fin[1] = 0;
     }
     if (tid < NU) {
         s.unit_cnt[tid] = 0;
@@ -308,13 +325,24 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     }
     tok_bar();
     const long long t_ready = clock64();
-    tok_prologue<C>(v, ls, d.bank, cw, lane);
+    if (d.st == TS_O) {
+        tok_input_attention(a, ls, d.bank, cw, lane);
+    } else if (d.st == TS_DOWN) {
+        tok_input_swiglu(a, ls, d.bank, d.layer, cw, lane);
+    } else {
+        const int norm = d.st == TS_QKV ? 2 * d.layer : d.st == TS_GU ? 2 * d.layer + 1 : 2 * d.layer;
+        if constexpr (G == 32) tok_input_rms<32>(a, s, ls, d.bank, norm, ord - 1, contrib, cw, lane);
+    }
     tok_bar();
     const long long t_loop = clock64();
 
+    float* partials = stage_partials(a, ord);
     const int nchunks = (d.u1 - d.u0) * C;
     const int rows_total = stage_units(d.st) * 32;
+    const bool tr = a.trace != nullptr;
+    long long w_data = 0, w_slot = 0, w_comp = 0, w_chain = 0;
     for (;;) {
+        const long long c0 = tr ? clock64() : 0;
         int i = 0;
         if (lane == 0) i = atomicAdd(s.next, 1);
         i = __shfl_sync(FULL, i, 0);
@@ -346,6 +374,7 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
             mbar_arrive_cnt(&s.empty[slot], rel);
         }
 
+        const long long c1 = tr ? clock64() : 0;
         const int uidx = i / C, j = i - uidx * C;
         const int us = uidx % NU;
         if (*reinterpret_cast<volatile int*>(&s.slot_ok[us]) < uidx) {
@@ -358,6 +387,7 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
                 }
             }
         }
+        const long long c2 = tr ? clock64() : 0;
         float* cb = contrib + us * G * 32;
         const float ws0 = __fmul_rn(static_cast<float>(raw0), 1.0f / 32768.0f);
         const float ws1 = __fmul_rn(static_cast<float>(raw1), 1.0f / 32768.0f);
@@ -372,12 +402,13 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
         int old = 0;
         if (lane == 0) old = atomicAdd(&s.unit_cnt[us], 1);
         old = __shfl_sync(FULL, old, 0);
+        const long long c3 = tr ? clock64() : 0;
         if (old == C - 1) {
             __threadfence_block();
             float acc = __fadd_rn(0.0f, cb[lane]);
 #pragma unroll 8
             for (int lg = 1; lg < G; ++lg) acc = __fadd_rn(acc, cb[lg * 32 + lane]);
-            a.partials[static_cast<size_t>(d.bank) * rows_total + static_cast<size_t>(d.u0 + uidx) * 32 + lane] = acc;
+            partials[static_cast<size_t>(d.bank) * rows_total + static_cast<size_t>(d.u0 + uidx) * 32 + lane] = acc;
             __syncwarp();
             __threadfence_block();
             if (lane == 0) {
@@ -385,82 +416,43 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
                 *reinterpret_cast<volatile int*>(&s.slot_ok[us]) = uidx + NU;
             }
         }
+        if (tr) {
+            const long long c4 = clock64();
+            w_data += c1 - c0;
+            w_slot += c2 - c1;
+            w_comp += c3 - c2;
+            w_chain += c4 - c3;
+        }
+    }
+    if (tr && lane == 0) {
+        unsigned long long* t = a.trace + blockIdx.x * kTraceSlots;
+        atomicAdd(t + TR_W_DATA, static_cast<unsigned long long>(w_data));
+        atomicAdd(t + TR_W_SLOT, static_cast<unsigned long long>(w_slot));
+        atomicAdd(t + TR_W_COMPUTE, static_cast<unsigned long long>(w_comp));
+        atomicAdd(t + TR_W_CHAIN, static_cast<unsigned long long>(w_chain));
     }
     __threadfence();
     tok_bar();
     const long long t_epi = clock64();
     if (tid == 0) {
-        trace_add(a, TR_WAIT, t_ready - t_begin);
-        trace_add(a, TR_PROLOGUE, t_loop - t_ready);
-        trace_add(a, TR_CHUNKS, t_epi - t_loop);
+        atomicAdd(&a.sync[kSyncStage + ord], 1u);
+        trace_add(a, TR_WAIT + d.st, t_ready - t_begin);
+        trace_add(a, TR_PROLOGUE + d.st, t_loop - t_ready);
+        trace_add(a, TR_CHUNKS + d.st, t_epi - t_loop);
     }
+}
 
-    if (d.st == TS_QKV) {
-        if (tid == 0) {
-            atomicAdd(&a.sync[kSyncQkv + d.layer], 1u);
-            trace_add(a, TR_STAGE_QKV, clock64() - t_begin);
-        }
-        return;
-    }
-    // Last-arriver epilogue over the stripes this CTA touched.
-    const int stripes = stage_stripes(d.st);
-    const unsigned need = d.st == TS_GU ? 8u : 4u;
-    if (cw == 0) {
-        for (int b = d.u0; b < d.u1; b += 32) {
-            const int u = b + lane;
-            if (u < d.u1) {
-                const int stripe = u % stripes;
-                const unsigned old = atomicAdd(&a.counters[stripe], 1u);
-                if (old + 1 == need) {
-                    a.counters[stripe] = 0;
-                    const int k = atomicAdd(&s.fin[0], 1);
-                    if (k < kFinMax) s.fin[2 + k] = stripe;
-                    else atomicOr(a.err, kErrArg);
-                }
-            }
-        }
-        __threadfence();
-    }
+// Logits: every CTA combines a slice of the LM-head rows once all partials
+// are stored ((p0+p1)+(p2+p3), emulator sharded_gemv_4pe).
+__device__ __noinline__ void tok_logits(const TokenArgs& a, int cw, int lane) {
+    const int tid = cw * 32 + lane;
+    const int ord = stage_ordinal(TS_LOGITS, a.layers);
+    if (tid == 0) wait_counter(a, &a.sync[kSyncStage + ord], gridDim.x);
     tok_bar();
-    const int nfin = min(s.fin[0], kFinMax);
-    for (int k = cw; k < nfin; k += kTokWarps) {
-        linear_finalize(v, s.fin[2 + k], &s.fin[1]);
-        if (d.st == TS_GU) {
-            __threadfence();
-            __syncwarp();
-            if (lane == 0) atomicAdd(&a.sync[kSyncSwiglu + d.layer], 1u);
-        }
-    }
-    if (d.st != TS_O && d.st != TS_DOWN) {
-        tok_bar();
-        if (tid == 0) {
-            trace_add(a, TR_EPILOGUE, clock64() - t_epi);
-            trace_add(a, d.st == TS_GU ? TR_STAGE_GU : TR_STAGE_LOGITS, clock64() - t_begin);
-        }
-        return;
-    }
-    tok_bar();
-    if (s.fin[1] != 0) {
-        // This CTA finalised the last residual stripe: RMS reciprocal.
-        float* xs = reinterpret_cast<float*>(s.uni);
-        for (int k = tid; k < kDim / 4; k += 32 * kTokWarps)
-            reinterpret_cast<float4*>(xs)[k] = __ldcg(reinterpret_cast<const float4*>(a.resid) + k);
-        tok_bar();
-        if (cw == 0) {
-            const int norm = d.st == TS_O ? 2 * d.layer + 1 : 2 * d.layer + 2;
-            const float r = rms_recip_warp(xs);
-            if (lane == 0) {
-                a.recip[norm] = r;
-                __threadfence();
-                atomicExch(&a.sync[kSyncRms + norm], 1u);
-            }
-        }
-    }
-    tok_bar();
-    if (tid == 0) {
-        trace_add(a, TR_EPILOGUE, clock64() - t_epi);
-        trace_add(a, d.st == TS_O ? TR_STAGE_O : TR_STAGE_DOWN, clock64() - t_begin);
-    }
+    const float* P = stage_partials(a, ord);
+    const int r0 = static_cast<int>((static_cast<long long>(blockIdx.x) * kPVocab) / gridDim.x);
+    const int r1 = static_cast<int>((static_cast<long long>(blockIdx.x + 1) * kPVocab) / gridDim.x);
+    for (int r = r0 + tid; r < r1; r += 32 * kTokWarps) a.logits[r] = combine4(P, kPVocab, r);
 }
 
 // ------------------------------------------------------------ attention item
@@ -512,6 +504,7 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
     const uint32_t M30 = (1u << 30) - 1u;
     AttnArgs a = ta.attn;
     a.layer = layer;
+    a.partials = stage_partials(ta, stage_ordinal(TS_QKV, layer));
     const int h = item / kAttnParts, part = item % kAttnParts;
     const int tid = cw * 32 + lane;
     TokAttnSmem S = tok_attn_carve(s.uni);
@@ -537,7 +530,7 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
         fence_proxy_async_smem();
         mbar_arrive_expect_tx(&s.abar[0], cnt * 320);
         bulk_g2s(S.tile[0], head_base, cnt * 320, &s.abar[0]);
-        wait_counter(ta, &ta.sync[kSyncQkv + layer], gridDim.x);
+        wait_counter(ta, &ta.sync[kSyncStage + stage_ordinal(TS_QKV, layer)], gridDim.x);
     }
     tok_bar();
     const long long t_a1 = clock64();
@@ -754,6 +747,55 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
 
 // ---------------------------------------------------------------- kernel
 
+// This CTA's units [u0, u1) of a stage in its bank.
+__device__ __forceinline__ void stage_urange(const TokenArgs& a, int c, int st, int* u0, int* u1) {
+    const int U = stage_units(st);
+    *u0 = static_cast<int>((static_cast<long long>(c) * U) / a.cpb);
+    *u1 = static_cast<int>((static_cast<long long>(c + 1) * U) / a.cpb);
+}
+
+// Position in the CTA's sequence of weight copies: layer, stage, first chunk
+// of the copy, chunks in the stage and the stage's source bytes.
+struct CopyCursor {
+    int l, st, i, n;
+    const uint8_t* src;
+};
+
+__device__ __forceinline__ void cursor_stage(const TokenArgs& a, int bank, int c, CopyCursor& k) {
+    int u0, u1;
+    stage_urange(a, c, k.st, &u0, &u1);
+    const int C = stage_chunks(k.st);
+    k.i = 0;
+    k.n = (u1 - u0) * C;
+    k.src = a.w + (k.st == TS_LOGITS ? a.stage_off[TS_LOGITS] : k.l * a.layer_bytes + a.stage_off[k.st]) +
+            static_cast<size_t>(bank) * a.bank_bytes[k.st] + static_cast<size_t>(u0) * C * kChunkBytes;
+}
+
+__device__ __forceinline__ bool cursor_valid(const TokenArgs& a, const CopyCursor& k) { return k.l <= a.layers; }
+
+__device__ __forceinline__ void cursor_begin(const TokenArgs& a, int bank, int c, CopyCursor& k) {
+    k.l = 0;
+    k.st = a.layers == 0 ? TS_LOGITS : TS_QKV;
+    cursor_stage(a, bank, c, k);
+}
+
+__device__ __forceinline__ void cursor_advance(const TokenArgs& a, int bank, int c, CopyCursor& k) {
+    k.i += kTokCpc;
+    while (k.l <= a.layers && k.i >= k.n) {
+        if (k.st == TS_LOGITS) {
+            k.l = a.layers + 1;
+            return;
+        }
+        if (k.st == TS_DOWN) {
+            ++k.l;
+            k.st = k.l == a.layers ? TS_LOGITS : TS_QKV;
+        } else {
+            ++k.st;
+        }
+        cursor_stage(a, bank, c, k);
+    }
+}
+
 __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant__ TokenArgs a) {
     extern __shared__ __align__(128) uint8_t tok_smem_raw[];
     TokSmem s = tok_carve(tok_smem_raw);
@@ -779,40 +821,29 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
         if (lane == 0) {
             int slot = 0, issued = 0;
             uint32_t phase = 0;
-            bool ok = true;
-            for (int l = 0; l <= a.layers && ok; ++l) {
-                for (int st = TS_QKV; st <= TS_DOWN && ok; ++st) {
-                    const int stage = l == a.layers ? TS_LOGITS : st;
-                    if (l == a.layers && st != TS_QKV) break;
-                    int u0, u1;
-                    urange(stage, &u0, &u1);
-                    const int C = stage_chunks(stage);
-                    const uint8_t* src = a.w + (stage == TS_LOGITS ? a.stage_off[TS_LOGITS]
-                                                                    : l * a.layer_bytes + a.stage_off[stage]) +
-                                         static_cast<size_t>(bank) * a.bank_bytes[stage] +
-                                         static_cast<size_t>(u0) * C * kChunkBytes;
-                    const int n = (u1 - u0) * C;
-                    for (int i = 0; i < n; i += kTokCpc) {
-                        const int cnt = min(kTokCpc, n - i);
-                        if (issued >= kTokSlots) {
-                            const long long t0 = a.trace ? clock64() : 0;
-                            if (!tok_mbar_wait(a, &s.empty[slot], phase ^ 1u, kErrWaitEmpty)) {
-                                ok = false;
-                                break;
-                            }
-                            if (a.trace) trace_add(a, TR_RING_FULL, clock64() - t0);
-                        }
-                        publish_issued(&s.issued[slot], issued);
-                        mbar_arrive_expect_tx(&s.full[slot], cnt * kChunkBytes);
-                        bulk_g2s(s.ring + static_cast<size_t>(slot) * kTokSlotBytes,
-                                 src + static_cast<size_t>(i) * kChunkBytes, cnt * kChunkBytes, &s.full[slot]);
-                        ++issued;
-                        if (++slot == kTokSlots) {
-                            slot = 0;
-                            phase ^= 1u;
-                        }
-                    }
+            CopyCursor cur;
+            // Weights are read once per token: evict them first, so the
+            // partials, residual and counters of the stage handoffs stay in L2.
+            const uint64_t pol_first = l2_policy_evict_first();
+            cursor_begin(a, bank, c, cur);
+            while (cursor_valid(a, cur)) {
+                const int cnt = min(kTokCpc, cur.n - cur.i);
+                if (issued >= kTokSlots) {
+                    const long long t0 = a.trace ? clock64() : 0;
+                    if (!tok_mbar_wait(a, &s.empty[slot], phase ^ 1u, kErrWaitEmpty)) break;
+                    if (a.trace) trace_add(a, TR_RING_FULL, clock64() - t0);
                 }
+                publish_issued(&s.issued[slot], issued);
+                mbar_arrive_expect_tx(&s.full[slot], cnt * kChunkBytes);
+                bulk_g2s_hint(s.ring + static_cast<size_t>(slot) * kTokSlotBytes,
+                              cur.src + static_cast<size_t>(cur.i) * kChunkBytes, cnt * kChunkBytes, &s.full[slot],
+                              pol_first);
+                ++issued;
+                if (++slot == kTokSlots) {
+                    slot = 0;
+                    phase ^= 1u;
+                }
+                cursor_advance(a, bank, c, cur);
             }
             // Never leave with copies in flight: wait for the last ones to land.
             for (int k = 0; k < kTokSlots && k < issued; ++k) {
@@ -833,15 +864,6 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
     const int cw = warp - 1;
     const int tid = cw * 32 + lane;
     const long long t_kernel = clock64();
-    if (blockIdx.x == 0 && cw == 0) {
-        // RMS reciprocal of the token's input residual (first attention norm).
-        const float r = rms_recip_warp(a.resid);
-        if (lane == 0) {
-            a.recip[0] = r;
-            __threadfence();
-            atomicExch(&a.sync[kSyncRms], 1u);
-        }
-    }
     StageDesc d;
     d.bank = bank;
     d.cbase = 0;
@@ -861,6 +883,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
             }
         }
     }
+    tok_logits(a, cw, lane);
     // The last CTA to finish clears the token's synchronisation words.
     tok_bar();
     if (tid == 0) {
@@ -868,7 +891,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
         __threadfence();
         const unsigned old = atomicAdd(&a.sync[kSyncExit], 1u);
         if (old + 1 == gridDim.x) {
-            for (int i = kSyncQkv; i < kSyncWords; ++i) a.sync[i] = 0;
+            for (int i = kSyncStage; i < kSyncWords; ++i) a.sync[i] = 0;
             __threadfence();
             a.sync[kSyncExit] = 0;
         }

@@ -128,10 +128,13 @@ i4d_status i4d_profile_token(i4d_ctx* ctx, uint32_t position, const float* resid
 
 /* Measurement hook for the persistent token kernel: runs one step with
  * per-CTA cycle counters and returns the CTA-averaged microseconds (at the
- * device's nominal clock) of: 0 stage-input waits, 1 prologues, 2 chunk
- * loops, 3 epilogues, 4 attention waits for QKV, 5 attention work,
- * 6 producer blocked on a full ring, 7 whole kernel, 8..12 QKV, O, GATE/UP,
- * DOWN and LM-head stage totals.  n_out >= 13.  No reference counterpart. */
+ * device's nominal clock) of: 0..4 waiting for the input of the QKV, O,
+ * GATE/UP, DOWN and LM-head stages, 5..9 building their activations,
+ * 10..14 their chunk loops, 15 attention waits for QKV, 16 attention work,
+ * 17 producer blocked on a full ring, 18 whole kernel, and per consumer warp
+ * (averaged over warps): 19 waiting for ring data, 20 waiting for a
+ * contribution slot, 21 chunk arithmetic, 22 row chains.  n_out >= 23.  No
+ * reference counterpart. */
 i4d_status i4d_token_breakdown(i4d_ctx* ctx, uint32_t position, const float* residual_in_dev, float* us_out,
                                int n_out);
 
