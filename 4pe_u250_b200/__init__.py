@@ -32,12 +32,13 @@ EXPORTS = [
     "i4d_sync", "i4d_linear_bank", "i4d_gemv", "i4d_quantize_g32", "i4d_rms_quant",
     "i4d_attention", "i4d_swiglu_quant", "i4d_expf", "i4d_decode_token_async", "i4d_stream",
     "i4d_profile_token", "i4d_token_breakdown", "i4d_linear_bank_noalloc",
+    "i4d_token_timeline",
 ]
 
 _STAGES = ["qkv", "o", "gu", "down", "logits"]
 BREAKDOWN = ([f"wait_{x}" for x in _STAGES] + [f"prologue_{x}" for x in _STAGES] + [f"chunks_{x}" for x in _STAGES]
-             + ["attn_wait", "attn", "ring_full", "total",
-                "warp_data_wait", "warp_slot_wait", "warp_compute", "warp_chain"])
+             + ["attn_wait", "attn", "ring_full", "total"]
+             + [f"warp_{k}_{x}" for x in _STAGES for k in ("data_wait", "slot_wait", "compute", "chain")])
 
 KERNEL_CLASSES = ["qkv_gemv", "attention", "o_gemv", "gate_up_gemv", "down_gemv", "logits_gemv", "rms", "token"]
 
@@ -89,6 +90,7 @@ def load_library():
         "i4d_profile_token": [P, ctypes.c_uint32, P, P, P],
         "i4d_token_breakdown": [P, ctypes.c_uint32, P, P, ctypes.c_int],
         "i4d_linear_bank_noalloc": [P, P, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, P, P, ctypes.c_int, P],
+        "i4d_token_timeline": [P, ctypes.c_uint32, P, ctypes.c_int, P, ctypes.c_int, P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -182,6 +184,14 @@ class Context:
         out = np.zeros(len(BREAKDOWN), np.float32)
         self._check(self._L.i4d_token_breakdown(self._h, position, residual_in_dev_ptr, out.ctypes.data, out.size))
         return dict(zip(BREAKDOWN, out.tolist()))
+
+    def token_timeline(self, position, residual_in_dev_ptr, layer):
+        """[CTAs, 24] global-timer stamps (ns) of one layer's events (see i4d_token_timeline)."""
+        out = np.zeros((1024, 24), np.uint64)
+        n = ctypes.c_int(0)
+        self._check(self._L.i4d_token_timeline(self._h, position, residual_in_dev_ptr, layer, out.ctypes.data,
+                                               out.shape[0], ctypes.byref(n)))
+        return out[: n.value]
 
     def kv_reset(self):
         self._check(self._L.i4d_kv_reset(self._h))

@@ -134,6 +134,8 @@ struct i4d_ctx {
     int prof_n = 0;
     bool profiling = false;
     unsigned long long* d_trace = nullptr;  // optional token-kernel trace
+    unsigned long long* d_timeline = nullptr;  // optional token-kernel timeline
+    int tl_layer = -1;
 };
 
 namespace {
@@ -277,6 +279,8 @@ TokenArgs token_args(i4d_ctx* c) {
     t.expf = c->expf;
     t.err = c->d_err;
     t.trace = c->d_trace;
+    t.timeline = c->d_timeline;
+    t.tl_layer = c->tl_layer;
     return t;
 }
 
@@ -1100,5 +1104,35 @@ extern "C" i4d_status i4d_token_breakdown(i4d_ctx* c, uint32_t position, const f
         const double per = k >= TR_W_DATA ? 4.0 * c->cpb * kTokWarps : 4.0 * c->cpb;  // warp slots: per warp
         us_out[k] = static_cast<float>(sum / per / (khz * 1e-3));
     }
+    return I4D_OK;
+}
+
+extern "C" i4d_status i4d_token_timeline(i4d_ctx* c, uint32_t position, const float* residual_in_dev, int layer,
+                                         uint64_t* out, int max_ctas, int* n_ctas) {
+    if (!c || !residual_in_dev || !out || !n_ctas) return c ? fail(c, I4D_ERR_ARG, "bad arguments") : I4D_ERR_ARG;
+    if (c->flags & I4D_FLAG_STAGED) return fail(c, I4D_ERR_STATE, "timeline needs the persistent token kernel");
+    if (!all_loaded(c)) return fail(c, I4D_ERR_STATE, "banks and rope LUT must be loaded before decoding");
+    if (position >= static_cast<uint32_t>(c->stride)) return fail(c, I4D_ERR_ARG, "position out of range");
+    if (layer < 0 || layer >= c->layers) return fail(c, I4D_ERR_ARG, "layer out of range");
+    const int grid = 4 * c->cpb;
+    *n_ctas = grid;
+    if (max_ctas < grid) return fail(c, I4D_ERR_SIZE, "timeline needs room for %d CTAs", grid);
+    CK(cudaSetDevice(c->device));
+    const size_t n = static_cast<size_t>(grid) * kTlEvents;
+    CK(cudaMalloc(&c->d_timeline, n * sizeof(unsigned long long)));
+    c->tl_layer = layer;
+    cudaError_t e = cudaMemsetAsync(c->d_timeline, 0, n * sizeof(unsigned long long), c->stream);
+    if (e == cudaSuccess) {
+        k_set_pos<<<1, 1, 0, c->stream>>>(c->d_pos, static_cast<int>(position));
+        e = cudaMemcpyAsync(c->d_resid, residual_in_dev, kDim * sizeof(float), cudaMemcpyDeviceToDevice, c->stream);
+    }
+    if (e == cudaSuccess) e = launch_token(c);
+    const i4d_status st = e == cudaSuccess ? finish(c) : fail(c, I4D_ERR_CUDA, "%s", cudaGetErrorString(e));
+    if (st == I4D_OK) e = cudaMemcpy(out, c->d_timeline, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    cudaFree(c->d_timeline);
+    c->d_timeline = nullptr;
+    c->tl_layer = -1;
+    if (st != I4D_OK) return st;
+    if (e != cudaSuccess) return fail(c, I4D_ERR_CUDA, "%s", cudaGetErrorString(e));
     return I4D_OK;
 }

@@ -15,6 +15,14 @@
  * The same operation sequence runs on host and device (only IEEE mul, fma,
  * rint and conversions), so both produce identical bits.  Define
  * I4D_EXPF_DEVICE before including for the CUDA form.
+ *
+ * Where the table can matter: a function whose error is below 0.502 ulp (the
+ * C library's stated bound) returns the correctly rounded value unless the
+ * exact result lies within 0.002 ulp of a rounding midpoint.  The core's
+ * binary64 value locates that midpoint; i4d_expf_near_tie flags results
+ * within 1/128 ulp of one (and zero, subnormal or overflowing results), and
+ * only those consult the table.  gen_expf_table.c checks, on every input,
+ * that each recorded difference is flagged.
  */
 #ifndef I4D_EXPF_IMPL_H
 #define I4D_EXPF_IMPL_H
@@ -29,6 +37,8 @@
 #define I4D_D2F(a) __double2float_rn(a)
 #define I4D_D_AS_U64(d) ((unsigned long long)__double_as_longlong(d))
 #define I4D_U64_AS_D(u) __longlong_as_double((long long)(u))
+#define I4D_F_AS_U32(f) __float_as_uint(f)
+#define I4D_U32_AS_F(u) __uint_as_float(u)
 #else
 #include <math.h>
 #include <string.h>
@@ -39,9 +49,32 @@
 #define I4D_D2F(a) ((float)(a))
 static inline double i4d_u64_as_d(unsigned long long u) { double d; memcpy(&d, &u, 8); return d; }
 #define I4D_U64_AS_D(u) i4d_u64_as_d(u)
+static inline unsigned i4d_f_as_u32(float f) { unsigned u; memcpy(&u, &f, 4); return u; }
+static inline float i4d_u32_as_f(unsigned u) { float f; memcpy(&f, &u, 4); return f; }
+#define I4D_F_AS_U32(f) i4d_f_as_u32(f)
+#define I4D_U32_AS_F(u) i4d_u32_as_f(u)
 #endif
 
-I4D_EXPF_QUAL float i4d_expf_core(float x, const double* table) {
+/* Nonzero when the binary64 value yd, rounded to the binary32 f, lies within
+ * 1/128 of f's spacing from a rounding midpoint, or when f is zero,
+ * subnormal, the largest finite value or infinite.  Every operation is exact:
+ * yd - f and the spacings are differences of nearby values. */
+I4D_EXPF_QUAL int i4d_expf_near_tie(double yd, float f) {
+    const unsigned u = I4D_F_AS_U32(f);
+    if (u < 0x00800000u || u >= 0x7f7fffffu) return 1;
+    const double fd = (double)f;
+    const double r = yd - fd;
+    const double up = (double)I4D_U32_AS_F(u + 1u) - fd;
+    const double dn = fd - (double)I4D_U32_AS_F(u - 1u);
+    const double sp = r >= 0.0 ? up : dn;
+    const double dist = 0.5 * sp - (r >= 0.0 ? r : -r);
+    return dist < sp * (1.0 / 128.0);
+}
+
+/* expf(x) by the method above; *near_tie as i4d_expf_near_tie (0 for NaN,
+ * x > 100 and x < -110, whose results every implementation shares). */
+I4D_EXPF_QUAL float i4d_expf_core2(float x, const double* table, int* near_tie) {
+    *near_tie = 0;
     if (x != x) return x;
     if (x > 100.0f) return __builtin_inff();
     if (x < -110.0f) return 0.0f;
@@ -59,7 +92,15 @@ I4D_EXPF_QUAL float i4d_expf_core(float x, const double* table) {
     const double y = I4D_FMA(t, q, t);
     const int m = k >> 6;
     const double two_m = I4D_U64_AS_D((unsigned long long)(m + 1023) << 52);
-    return I4D_D2F(I4D_DMUL(y, two_m));
+    const double yd = I4D_DMUL(y, two_m);
+    const float f = I4D_D2F(yd);
+    *near_tie = i4d_expf_near_tie(yd, f);
+    return f;
+}
+
+I4D_EXPF_QUAL float i4d_expf_core(float x, const double* table) {
+    int near_tie;
+    return i4d_expf_core2(x, table, &near_tie);
 }
 
 #endif

@@ -69,6 +69,8 @@ struct TokenArgs {
     ExpfFix expf;
     unsigned* err;
     unsigned long long* trace;  // optional [gridDim.x][kTraceSlots] cycle sums, or null
+    unsigned long long* timeline;  // optional [gridDim.x][kTlEvents] global-timer stamps of layer tl_layer
+    int tl_layer;
 };
 
 // Cycle-sum categories of the optional trace (per CTA, summed over a token).
@@ -80,12 +82,28 @@ enum TraceSlot : int {
     TR_ATTN,          // attention item: everything else
     TR_RING_FULL,     // producer: blocked on a full ring
     TR_TOTAL,         // consumer: whole kernel
-    TR_W_DATA,        // per consumer warp (summed over warps): waiting for ring data
-    TR_W_SLOT,        // per warp: waiting for a contribution slot
-    TR_W_COMPUTE,     // per warp: chunk arithmetic
-    TR_W_CHAIN,       // per warp: row chains of finished units
-    kTraceSlots
+    TR_W_DATA,        // + 4 * stage, per consumer warp (summed over warps): waiting for ring data
+    TR_W_SLOT,        // + 4 * stage, per warp: waiting for a contribution slot
+    TR_W_COMPUTE,     // + 4 * stage, per warp: chunk arithmetic
+    TR_W_CHAIN,       // + 4 * stage, per warp: row chains of finished units
+    kTraceSlots = TR_W_DATA + 20
 };
+
+// Timeline events (per CTA, one layer): stage s (QKV, O, GATE/UP, DOWN, LM
+// head) at 4s + {0 begin, 1 input ready, 2 chunk loop start, 3 arrival};
+// attention 20 start, 21 QKV ready, 22 end; 23 producer's first copy of the
+// layer.
+constexpr int kTlEvents = 24;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void tl_mark(const TokenArgs& a, int layer, int event) {
+    if (a.timeline && layer == a.tl_layer) a.timeline[blockIdx.x * kTlEvents + event] = global_ns();
+}
 
 __device__ __forceinline__ void trace_add(const TokenArgs& a, int slot, long long cycles) {
     if (a.trace) a.trace[blockIdx.x * kTraceSlots + slot] += static_cast<unsigned long long>(cycles);
@@ -161,7 +179,7 @@ __device__ bool wait_counter(const TokenArgs& a, const unsigned* word, unsigned 
             raise_abort(a, kErrWaitFull);
             return false;
         }
-        __nanosleep(it < 64 ? 32 : 256);
+        if (it >= 256) __nanosleep(it < 1024 ? 32 : 256);
     }
 }
 
@@ -175,7 +193,7 @@ __device__ __forceinline__ bool tok_mbar_wait(const TokenArgs& a, uint64_t* bar,
             raise_abort(a, code);
             return false;
         }
-        __nanosleep(64);
+        if (it >= 256) __nanosleep(64);
     }
 }
 
@@ -270,7 +288,8 @@ __device__ __forceinline__ void tok_input_swiglu(const TokenArgs& a, const Linea
         gv[k] = combine4(P, kRows, f);
         uv[k] = combine4(P, kRows, kFfn + f);
     }
-    swiglu_n<kPer>(gv, uv, sw, a.expf);
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) sw[k] = swiglu1(gv[k], uv[k], a.expf);
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
         const int lg = cw + k * kTokWarps;
@@ -310,6 +329,8 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     float* contrib = reinterpret_cast<float*>(s.uni + align16(G * 72));
     const int tid = cw * 32 + lane;
     const int ord = stage_ordinal(d.st, d.layer);
+    const int tl_layer = d.st == TS_LOGITS ? a.tl_layer : d.layer;  // the LM head is recorded with any layer
+    tl_mark(a, tl_layer, 4 * d.st);
     const long long t_begin = clock64();
 
     // Input readiness: the previous stage's partials from every CTA, or the
@@ -325,6 +346,7 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     }
     tok_bar();
     const long long t_ready = clock64();
+    if (tid == 0) tl_mark(a, tl_layer, 4 * d.st + 1);
     if (d.st == TS_O) {
         tok_input_attention(a, ls, d.bank, cw, lane);
     } else if (d.st == TS_DOWN) {
@@ -335,6 +357,7 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     }
     tok_bar();
     const long long t_loop = clock64();
+    if (tid == 0) tl_mark(a, tl_layer, 4 * d.st + 2);
 
     float* partials = stage_partials(a, ord);
     const int nchunks = (d.u1 - d.u0) * C;
@@ -355,7 +378,7 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
                 raise_abort(a, kErrWaitFull);
                 break;
             }
-            __nanosleep(32);
+            if (it >= 256) __nanosleep(32);
         }
         tok_mbar_wait(a, &s.full[slot], static_cast<uint32_t>((cp / kTokSlots) & 1), kErrWaitFull);
         const uint8_t* ch = s.ring + static_cast<size_t>(slot) * kTokSlotBytes + (i % kTokCpc) * kChunkBytes;
@@ -379,7 +402,7 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
         const int us = uidx % NU;
         if (*reinterpret_cast<volatile int*>(&s.slot_ok[us]) < uidx) {
             for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.slot_ok[us]) < uidx; ++it) {
-                __nanosleep(32);
+                if (it >= 256) __nanosleep(32);
                 if ((it & 63) == 0 && aborted(a)) break;
                 if (it > (1u << 24)) {
                     raise_abort(a, kErrWaitFull);
@@ -426,15 +449,18 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     }
     if (tr && lane == 0) {
         unsigned long long* t = a.trace + blockIdx.x * kTraceSlots;
-        atomicAdd(t + TR_W_DATA, static_cast<unsigned long long>(w_data));
-        atomicAdd(t + TR_W_SLOT, static_cast<unsigned long long>(w_slot));
-        atomicAdd(t + TR_W_COMPUTE, static_cast<unsigned long long>(w_comp));
-        atomicAdd(t + TR_W_CHAIN, static_cast<unsigned long long>(w_chain));
+        atomicAdd(t + TR_W_DATA + 4 * d.st, static_cast<unsigned long long>(w_data));
+        atomicAdd(t + TR_W_SLOT + 4 * d.st, static_cast<unsigned long long>(w_slot));
+        atomicAdd(t + TR_W_COMPUTE + 4 * d.st, static_cast<unsigned long long>(w_comp));
+        atomicAdd(t + TR_W_CHAIN + 4 * d.st, static_cast<unsigned long long>(w_chain));
     }
-    __threadfence();
+    // Release: the CTA barrier orders every warp's partial stores before
+    // thread 0's GPU-scope fence and arrival (the grid-sync pattern).
     tok_bar();
     const long long t_epi = clock64();
     if (tid == 0) {
+        tl_mark(a, tl_layer, 4 * d.st + 3);
+        __threadfence();
         atomicAdd(&a.sync[kSyncStage + ord], 1u);
         trace_add(a, TR_WAIT + d.st, t_ready - t_begin);
         trace_add(a, TR_PROLOGUE + d.st, t_loop - t_ready);
@@ -523,6 +549,7 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
     if (tid < 33) S.lut[tid] = a.exp2_q30[tid];
     tok_bar();
     const long long t_a0 = clock64();
+    if (tid == 0) tl_mark(ta, layer, 20);
     if (tid == 0) {
         // Cached records of earlier tokens are final: stream the first tile
         // while the other CTAs finish the QKV projection.
@@ -534,6 +561,7 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
     }
     tok_bar();
     const long long t_a1 = clock64();
+    if (tid == 0) tl_mark(ta, layer, 21);
 
     // Current token: Q/K/V rows of the head, RoPE, KV record.
     const int d = tid & 127;
@@ -735,13 +763,14 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
         r = fmaxf(-8191.0f, fminf(8191.0f, r));
         ta.ao_q[h * kHeadDim + dim] = static_cast<int16_t>(__float2int_rz(r));
         if (lane == 0) ta.ao_e[h * 4 + part] = maxf == 0.0f ? 0 : static_cast<uint8_t>(maxe + 127);
-        __threadfence();
     }
     tok_bar();
     if (tid == 0) {
+        __threadfence();
         atomicAdd(&ta.sync[kSyncAtt + layer], 1u);
         trace_add(ta, TR_ATTN_WAIT, t_a1 - t_a0);
         trace_add(ta, TR_ATTN, clock64() - t_a1);
+        tl_mark(ta, layer, 22);
     }
 }
 
@@ -833,6 +862,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
                     if (!tok_mbar_wait(a, &s.empty[slot], phase ^ 1u, kErrWaitEmpty)) break;
                     if (a.trace) trace_add(a, TR_RING_FULL, clock64() - t0);
                 }
+                if (cur.i == 0 && cur.st == TS_QKV) tl_mark(a, cur.l, 23);
                 publish_issued(&s.issued[slot], issued);
                 mbar_arrive_expect_tx(&s.full[slot], cnt * kChunkBytes);
                 bulk_g2s_hint(s.ring + static_cast<size_t>(slot) * kTokSlotBytes,

@@ -132,11 +132,21 @@ i4d_status i4d_profile_token(i4d_ctx* ctx, uint32_t position, const float* resid
  * GATE/UP, DOWN and LM-head stages, 5..9 building their activations,
  * 10..14 their chunk loops, 15 attention waits for QKV, 16 attention work,
  * 17 producer blocked on a full ring, 18 whole kernel, and per consumer warp
- * (averaged over warps): 19 waiting for ring data, 20 waiting for a
- * contribution slot, 21 chunk arithmetic, 22 row chains.  n_out >= 23.  No
- * reference counterpart. */
+ * (averaged over warps) for each stage s: 19+4s waiting for ring data,
+ * 20+4s waiting for a contribution slot, 21+4s chunk arithmetic, 22+4s row
+ * chains.  n_out >= 39.  No reference counterpart. */
 i4d_status i4d_token_breakdown(i4d_ctx* ctx, uint32_t position, const float* residual_in_dev, float* us_out,
                                int n_out);
+
+/* Measurement hook for the persistent token kernel: runs one step and
+ * returns, per CTA, global-timer stamps (ns) of 24 events of `layer`: for
+ * the QKV, O, GATE/UP, DOWN and LM-head stages s, 4s+0 begin, 4s+1 input
+ * ready, 4s+2 chunk loop start, 4s+3 arrival; 20..22 attention start, QKV
+ * ready, end (CTAs with an attention item); 23 the producer's first copy of
+ * the layer.  out holds max_ctas x 24 values; *n_ctas receives the grid size.
+ * No reference counterpart. */
+i4d_status i4d_token_timeline(i4d_ctx* ctx, uint32_t position, const float* residual_in_dev, int layer,
+                              uint64_t* out, int max_ctas, int* n_ctas);
 
 /* Clears the KV cache (decode_host.cpp:1291-1294 zero_bo). */
 i4d_status i4d_kv_reset(i4d_ctx* ctx);
