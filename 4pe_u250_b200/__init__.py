@@ -186,8 +186,8 @@ class Context:
         return dict(zip(BREAKDOWN, out.tolist()))
 
     def token_timeline(self, position, residual_in_dev_ptr, layer):
-        """[CTAs, 24] global-timer stamps (ns) of one layer's events (see i4d_token_timeline)."""
-        out = np.zeros((1024, 24), np.uint64)
+        """[CTAs, 162] global-timer stamps (ns) and counts of one layer (see i4d_token_timeline)."""
+        out = np.zeros((1024, 162), np.uint64)
         n = ctypes.c_int(0)
         self._check(self._L.i4d_token_timeline(self._h, position, residual_in_dev_ptr, layer, out.ctypes.data,
                                                out.shape[0], ctypes.byref(n)))

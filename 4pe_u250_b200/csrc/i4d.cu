@@ -296,7 +296,9 @@ cudaError_t launch_token(i4d_ctx* c) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, k_token, token_args(c));
+    // The measurement hooks run the instantiation with cycle counters and stamps.
+    if (c->d_trace || c->d_timeline) return cudaLaunchKernelEx(&cfg, k_token<true>, token_args(c));
+    return cudaLaunchKernelEx(&cfg, k_token<false>, token_args(c));
 }
 
 // The kernels of one token (position and residual already in device memory).
@@ -448,12 +450,15 @@ i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out) {
     CKC(cudaFuncSetAttribute(k_linear, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBudget)));
     CKC(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(attn_smem_bytes())));
-    CKC(cudaFuncSetAttribute(k_token, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    CKC(cudaFuncSetAttribute(k_token<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(tok_smem_bytes())));
+    CKC(cudaFuncSetAttribute(k_token<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(tok_smem_bytes())));
     {
-        int per_sm = 0;
-        CKC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_token, kTokThreads, tok_smem_bytes()));
-        if (per_sm < 1 || 4 * c->cpb > c->num_sms) c->flags |= I4D_FLAG_STAGED;
+        int per_sm = 0, per_sm_tr = 0;
+        CKC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_token<false>, kTokThreads, tok_smem_bytes()));
+        CKC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_tr, k_token<true>, kTokThreads, tok_smem_bytes()));
+        if (per_sm < 1 || per_sm_tr < 1 || 4 * c->cpb > c->num_sms) c->flags |= I4D_FLAG_STAGED;
     }
 
     c->w_bytes = stage_offset(c, 0, ST_LOGITS) + 4 * stage_bank_bytes(ST_LOGITS);

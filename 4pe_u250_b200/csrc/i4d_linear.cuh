@@ -7,10 +7,12 @@
 // bank image): a "unit" is 32 output rows x one bank's local columns; it is
 // stored as chunks of 32 rows x 256 columns, 4224 bytes each:
 //   [  0,128): Q1.15 scales, int16 at (row*2 + g128)*2
-//   [128,4224): 8 groups x 32 rows x 16 bytes; the 16 bytes of (group, row)
-//               are its 32 INT4 weights: uint32 word j, byte b holds column
-//               4j+b in the low nibble as offset binary (w+8) and column
-//               16+4j+b in the high nibble as two's complement.
+//   [128,4224): 256 pieces of 16 bytes, one per (row, group), placed by
+//               chunk_piece (row-block major, group XOR-swizzled); a piece
+//               holds the 32 INT4 weights of its row and group: uint32 word
+//               j, byte b holds column 4j+b in the low nibble as offset
+//               binary (w+8) and column 16+4j+b in the high nibble as two's
+//               complement.
 // The units of one stage and bank are contiguous, so every CTA streams one
 // contiguous range with 1-D bulk copies.
 //
@@ -128,12 +130,18 @@ __device__ __forceinline__ void put_act(const LinearSmem& s, int lg, int lane, i
     }
 }
 
-// Exact G32 dot of one (row, group): weights w (16 bytes), split activations.
-__device__ __forceinline__ int group_dot(uint4 w, const int8_t* hi, const uint8_t* lo, int corr) {
-    const uint4 h0 = *reinterpret_cast<const uint4*>(hi);
-    const uint4 h1 = *reinterpret_cast<const uint4*>(hi + 16);
-    const uint4 l0 = *reinterpret_cast<const uint4*>(lo);
-    const uint4 l1 = *reinterpret_cast<const uint4*>(lo + 16);
+// Byte offset inside a chunk of the 16 weight bytes of (row, group).  Row
+// r = 8*rb + k is stored k-major and the group index is XOR-swizzled by k,
+// so that a warp reading one group of 32 rows (lane = row) and a warp
+// reading 8 groups x 4 row blocks (lane = group + 8*rb, one k per load) both
+// touch every shared-memory bank once per 8-lane phase.
+__host__ __device__ constexpr int chunk_piece(int row, int g) {
+    return kChunkScaleBytes + (((row & 7) * 4 + (row >> 3)) * 8 + (g ^ (row & 7))) * 16;
+}
+
+// Exact G32 dot of one (row, group): weights w (16 bytes), split activations
+// held in registers (h0/l0: columns 0..15, h1/l1: columns 16..31).
+__device__ __forceinline__ int group_dot_r(uint4 w, uint4 h0, uint4 h1, uint4 l0, uint4 l1, int corr) {
     int Lh = 0, Ll = 0, Hh = 0, Hl = 0;
     const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
     const uint32_t h0v[4] = {h0.x, h0.y, h0.z, h0.w};
@@ -150,6 +158,12 @@ __device__ __forceinline__ int group_dot(uint4 w, const int8_t* hi, const uint8_
         Hl = dp4a_su(h, l1v[j], Hl);
     }
     return ((Lh + (Hh >> 4)) << 7) + Ll + (Hl >> 4) - corr;
+}
+
+// The same with the activations read from shared memory.
+__device__ __forceinline__ int group_dot(uint4 w, const int8_t* hi, const uint8_t* lo, int corr) {
+    return group_dot_r(w, *reinterpret_cast<const uint4*>(hi), *reinterpret_cast<const uint4*>(hi + 16),
+                       *reinterpret_cast<const uint4*>(lo), *reinterpret_cast<const uint4*>(lo + 16), corr);
 }
 
 // Builds this bank's split activations in shared memory (consumer warps).
@@ -294,7 +308,7 @@ __global__ void __launch_bounds__(kLinearThreads, 2) k_linear(const __grid_const
         uint4 wv[8];
 #pragma unroll
         for (int g = 0; g < 8; ++g)
-            wv[g] = *reinterpret_cast<const uint4*>(ch + kChunkScaleBytes + (g * 32 + lane) * 16);
+            wv[g] = *reinterpret_cast<const uint4*>(ch + chunk_piece(lane, g));
         const int16_t raw0 = reinterpret_cast<const int16_t*>(ch)[lane * 2];
         const int16_t raw1 = reinterpret_cast<const int16_t*>(ch)[lane * 2 + 1];
         __syncwarp();
@@ -432,7 +446,7 @@ __global__ void __launch_bounds__(256) k_relayout(const RelayoutArgs a) {
         }
         out[jj] = v;
     }
-    *reinterpret_cast<uint4*>(chunk + kChunkScaleBytes + (g * 32 + row) * 16) = make_uint4(out[0], out[1], out[2], out[3]);
+    *reinterpret_cast<uint4*>(chunk + chunk_piece(row, g)) = make_uint4(out[0], out[1], out[2], out[3]);
 }
 
 }  // namespace i4d

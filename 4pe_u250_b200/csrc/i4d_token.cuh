@@ -92,8 +92,11 @@ enum TraceSlot : int {
 // Timeline events (per CTA, one layer): stage s (QKV, O, GATE/UP, DOWN, LM
 // head) at 4s + {0 begin, 1 input ready, 2 chunk loop start, 3 arrival};
 // attention 20 start, 21 QKV ready, 22 end; 23 producer's first copy of the
-// layer.
-constexpr int kTlEvents = 24;
+// layer; 24 + s: copies of stage s already landed when its chunk loop
+// starts (a count, not a time); 29 + s: copies of stage s; 34 + 8w + k:
+// consumer warp w in the QKV stage: k < 6 time of its k-th unit grab, 6 loop
+// exit, 7 number of grabs.
+constexpr int kTlEvents = 34 + 8 * 16;
 
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
@@ -101,12 +104,16 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 
+template <bool TR>
 __device__ __forceinline__ void tl_mark(const TokenArgs& a, int layer, int event) {
-    if (a.timeline && layer == a.tl_layer) a.timeline[blockIdx.x * kTlEvents + event] = global_ns();
+    if constexpr (TR)
+        if (a.timeline && layer == a.tl_layer) a.timeline[blockIdx.x * kTlEvents + event] = global_ns();
 }
 
+template <bool TR>
 __device__ __forceinline__ void trace_add(const TokenArgs& a, int slot, long long cycles) {
-    if (a.trace) a.trace[blockIdx.x * kTraceSlots + slot] += static_cast<unsigned long long>(cycles);
+    if constexpr (TR)
+        if (a.trace) a.trace[blockIdx.x * kTraceSlots + slot] += static_cast<unsigned long long>(cycles);
 }
 
 __host__ __device__ constexpr int stage_units(int st) {
@@ -314,56 +321,48 @@ __device__ __forceinline__ void tok_input_attention(const TokenArgs& a, const Li
     }
 }
 
-template <int C>
-__device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s, const StageDesc& d, int cw,
-                                            int lane) {
+// Waits until copy `cp` is issued into `slot` and has landed.
+__device__ __forceinline__ void tok_wait_copy(const TokenArgs& a, const TokSmem& s, int cp, int slot) {
+    for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.issued[slot]) != cp; ++it) {
+        if ((it & 63) == 0 && aborted(a)) break;
+        if (it > (1u << 24)) {
+            raise_abort(a, kErrWaitFull);
+            break;
+        }
+        if (it >= 256) __nanosleep(32);
+    }
+    tok_mbar_wait(a, &s.full[slot], static_cast<uint32_t>((cp / kTokSlots) & 1), kErrWaitFull);
+}
+
+// Waits until contribution slot `us` may take unit `uidx`.
+__device__ __forceinline__ void tok_wait_slot(const TokenArgs& a, const TokSmem& s, int us, int uidx) {
+    if (*reinterpret_cast<volatile int*>(&s.slot_ok[us]) >= uidx) return;
+    for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.slot_ok[us]) < uidx; ++it) {
+        if (it >= 256) __nanosleep(32);
+        if ((it & 63) == 0 && aborted(a)) break;
+        if (it > (1u << 24)) {
+            raise_abort(a, kErrWaitFull);
+            break;
+        }
+    }
+}
+
+struct WarpTimes {
+    long long data = 0, slot = 0, comp = 0, chain = 0;
+};
+
+// Chunk loop, one row per lane (any chunks per unit; used for DOWN): a warp
+// takes whole chunks in order, activations come from shared memory.
+template <int C, bool TR>
+__device__ __forceinline__ void tok_chunks_rows(const TokenArgs& a, const TokSmem& s, const StageDesc& d,
+                                                const LinearSmem& ls, float* contrib, float* partials, int lane,
+                                                WarpTimes& wt) {
     constexpr int G = C * 8;
     constexpr int NU = kTokContribBytes / (G * 128) > 8 ? 8 : kTokContribBytes / (G * 128);
-    static_assert(NU >= 2, "contribution slots");
     const unsigned FULL = 0xffffffffu;
-    LinearSmem ls;
-    ls.act_hi = reinterpret_cast<int8_t*>(s.uni);
-    ls.act_lo = s.uni + G * 32;
-    ls.corr = reinterpret_cast<int*>(s.uni + G * 64);
-    ls.act_scale = reinterpret_cast<float*>(s.uni + G * 68);
-    float* contrib = reinterpret_cast<float*>(s.uni + align16(G * 72));
-    const int tid = cw * 32 + lane;
-    const int ord = stage_ordinal(d.st, d.layer);
-    const int tl_layer = d.st == TS_LOGITS ? a.tl_layer : d.layer;  // the LM head is recorded with any layer
-    tl_mark(a, tl_layer, 4 * d.st);
-    const long long t_begin = clock64();
-
-    // Input readiness: the previous stage's partials from every CTA, or the
-    // attention items of this layer.
-    if (tid == 0) {
-        if (d.st == TS_O) wait_counter(a, &a.sync[kSyncAtt + d.layer], kAttnItems);
-        else if (ord > 0) wait_counter(a, &a.sync[kSyncStage + ord - 1], gridDim.x);
-        *s.next = 0;
-    }
-    if (tid < NU) {
-        s.unit_cnt[tid] = 0;
-        s.slot_ok[tid] = tid;
-    }
-    tok_bar();
-    const long long t_ready = clock64();
-    if (tid == 0) tl_mark(a, tl_layer, 4 * d.st + 1);
-    if (d.st == TS_O) {
-        tok_input_attention(a, ls, d.bank, cw, lane);
-    } else if (d.st == TS_DOWN) {
-        tok_input_swiglu(a, ls, d.bank, d.layer, cw, lane);
-    } else {
-        const int norm = d.st == TS_QKV ? 2 * d.layer : d.st == TS_GU ? 2 * d.layer + 1 : 2 * d.layer;
-        if constexpr (G == 32) tok_input_rms<32>(a, s, ls, d.bank, norm, ord - 1, contrib, cw, lane);
-    }
-    tok_bar();
-    const long long t_loop = clock64();
-    if (tid == 0) tl_mark(a, tl_layer, 4 * d.st + 2);
-
-    float* partials = stage_partials(a, ord);
     const int nchunks = (d.u1 - d.u0) * C;
     const int rows_total = stage_units(d.st) * 32;
-    const bool tr = a.trace != nullptr;
-    long long w_data = 0, w_slot = 0, w_comp = 0, w_chain = 0;
+    const bool tr = TR && a.trace != nullptr;
     for (;;) {
         const long long c0 = tr ? clock64() : 0;
         int i = 0;
@@ -372,20 +371,11 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
         if (i >= nchunks) break;
         const int cp = d.cbase + i / kTokCpc;
         const int slot = cp % kTokSlots;
-        for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.issued[slot]) != cp; ++it) {
-            if ((it & 63) == 0 && aborted(a)) break;
-            if (it > (1u << 24)) {
-                raise_abort(a, kErrWaitFull);
-                break;
-            }
-            if (it >= 256) __nanosleep(32);
-        }
-        tok_mbar_wait(a, &s.full[slot], static_cast<uint32_t>((cp / kTokSlots) & 1), kErrWaitFull);
+        tok_wait_copy(a, s, cp, slot);
         const uint8_t* ch = s.ring + static_cast<size_t>(slot) * kTokSlotBytes + (i % kTokCpc) * kChunkBytes;
         uint4 wv[8];
 #pragma unroll
-        for (int g = 0; g < 8; ++g)
-            wv[g] = *reinterpret_cast<const uint4*>(ch + kChunkScaleBytes + (g * 32 + lane) * 16);
+        for (int g = 0; g < 8; ++g) wv[g] = *reinterpret_cast<const uint4*>(ch + chunk_piece(lane, g));
         const int16_t raw0 = reinterpret_cast<const int16_t*>(ch)[lane * 2];
         const int16_t raw1 = reinterpret_cast<const int16_t*>(ch)[lane * 2 + 1];
         __syncwarp();
@@ -396,20 +386,10 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
             if (i == nchunks - 1 && nchunks % kTokCpc != 0) rel = kTokCpc - nchunks % kTokCpc + 1;
             mbar_arrive_cnt(&s.empty[slot], rel);
         }
-
         const long long c1 = tr ? clock64() : 0;
         const int uidx = i / C, j = i - uidx * C;
         const int us = uidx % NU;
-        if (*reinterpret_cast<volatile int*>(&s.slot_ok[us]) < uidx) {
-            for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.slot_ok[us]) < uidx; ++it) {
-                if (it >= 256) __nanosleep(32);
-                if ((it & 63) == 0 && aborted(a)) break;
-                if (it > (1u << 24)) {
-                    raise_abort(a, kErrWaitFull);
-                    break;
-                }
-            }
-        }
+        tok_wait_slot(a, s, us, uidx);
         const long long c2 = tr ? clock64() : 0;
         float* cb = contrib + us * G * 32;
         const float ws0 = __fmul_rn(static_cast<float>(raw0), 1.0f / 32768.0f);
@@ -441,12 +421,176 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
         }
         if (tr) {
             const long long c4 = clock64();
-            w_data += c1 - c0;
-            w_slot += c2 - c1;
-            w_comp += c3 - c2;
-            w_chain += c4 - c3;
+            wt.data += c1 - c0;
+            wt.slot += c2 - c1;
+            wt.comp += c3 - c2;
+            wt.chain += c4 - c3;
         }
     }
+}
+
+// Chunk loop of the 4-chunk stages, one column chunk per warp: warp cw
+// takes chunk j = cw % 4 of units in order; lane (g = lane % 8, rb = lane / 8)
+// computes the G32 dots of group g for rows 8rb .. 8rb+7, with its group's
+// split activations held in registers for the whole stage.  Per chunk a lane
+// reads only its 128 weight bytes and 32 scale bytes from shared memory.
+// Contributions are stored at [group][row] with a stride of 33 floats (no
+// bank conflicts for either writer or chain).
+constexpr int kColContribStride = 33;
+constexpr int kColNU = kTokContribBytes / (32 * kColContribStride * 4);  // 7
+
+template <bool TR>
+__device__ __forceinline__ void tok_chunks_cols(const TokenArgs& a, const TokSmem& s, const StageDesc& d,
+                                                const LinearSmem& ls, float* contrib, float* partials, int cw,
+                                                int lane, WarpTimes& wt) {
+    constexpr int G = 32;
+    constexpr int NU = kColNU;
+    const unsigned FULL = 0xffffffffu;
+    const int j = cw & 3, g = lane & 7, rb = lane >> 3, g128 = g >> 2;
+    const int lg = j * 8 + g;
+    const uint4 h0 = *reinterpret_cast<const uint4*>(ls.act_hi + lg * 32);
+    const uint4 h1 = *reinterpret_cast<const uint4*>(ls.act_hi + lg * 32 + 16);
+    const uint4 l0 = *reinterpret_cast<const uint4*>(ls.act_lo + lg * 32);
+    const uint4 l1 = *reinterpret_cast<const uint4*>(ls.act_lo + lg * 32 + 16);
+    const int corr = ls.corr[lg];
+    const float as = ls.act_scale[lg];
+    const int nunits = d.u1 - d.u0;
+    const int rows_total = stage_units(d.st) * 32;
+    const bool tr = TR && a.trace != nullptr;
+    const bool tl = TR && a.timeline && d.st == TS_QKV && d.layer == a.tl_layer;
+    int ngrab = 0;
+    for (;;) {
+        const long long c0 = tr ? clock64() : 0;
+        int u = 0;
+        if (lane == 0) u = atomicAdd(&s.next[j], 1);
+        u = __shfl_sync(FULL, u, 0);
+        if (tl && lane == 0) {
+            if (ngrab < 6) a.timeline[blockIdx.x * kTlEvents + 34 + 8 * cw + ngrab] = global_ns();
+            ++ngrab;
+        }
+        if (u >= nunits) break;
+        const int cp = d.cbase + u;  // one copy per unit
+        const int slot = cp % kTokSlots;
+        tok_wait_copy(a, s, cp, slot);
+        const uint8_t* ch = s.ring + static_cast<size_t>(slot) * kTokSlotBytes + j * kChunkBytes;
+        uint4 wv[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) wv[k] = *reinterpret_cast<const uint4*>(ch + chunk_piece(rb * 8 + k, g));
+        // Scales of rows 8rb .. 8rb+7: int16 at (row * 2 + g128) * 2.
+        const uint4 sa = *reinterpret_cast<const uint4*>(ch + rb * 32);
+        const uint4 sb = *reinterpret_cast<const uint4*>(ch + rb * 32 + 16);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.empty[slot]);
+        const long long c1 = tr ? clock64() : 0;
+        const int us = u % NU;
+        tok_wait_slot(a, s, us, u);
+        const long long c2 = tr ? clock64() : 0;
+        float* cb = contrib + us * G * kColContribStride;
+        const uint32_t sw[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int16_t raw = static_cast<int16_t>(g128 ? (sw[k] >> 16) : (sw[k] & 0xffffu));
+            const float ws = __fmul_rn(static_cast<float>(raw), 1.0f / 32768.0f);
+            const int dot = group_dot_r(wv[k], h0, h1, l0, l1, corr);
+            cb[lg * kColContribStride + rb * 8 + k] = __fmul_rn(static_cast<float>(dot), __fmul_rn(ws, as));
+        }
+        __syncwarp();
+        __threadfence_block();
+        int old = 0;
+        if (lane == 0) old = atomicAdd(&s.unit_cnt[us], 1);
+        old = __shfl_sync(FULL, old, 0);
+        const long long c3 = tr ? clock64() : 0;
+        if (old == 3) {
+            __threadfence_block();
+            float acc = __fadd_rn(0.0f, cb[lane]);
+#pragma unroll 8
+            for (int q = 1; q < G; ++q) acc = __fadd_rn(acc, cb[q * kColContribStride + lane]);
+            partials[static_cast<size_t>(d.bank) * rows_total + static_cast<size_t>(d.u0 + u) * 32 + lane] = acc;
+            __syncwarp();
+            __threadfence_block();
+            if (lane == 0) {
+                s.unit_cnt[us] = 0;
+                *reinterpret_cast<volatile int*>(&s.slot_ok[us]) = u + NU;
+            }
+        }
+        if (tr) {
+            const long long c4 = clock64();
+            wt.data += c1 - c0;
+            wt.slot += c2 - c1;
+            wt.comp += c3 - c2;
+            wt.chain += c4 - c3;
+        }
+    }
+    if (tl && lane == 0) {
+        a.timeline[blockIdx.x * kTlEvents + 34 + 8 * cw + 6] = global_ns();
+        a.timeline[blockIdx.x * kTlEvents + 34 + 8 * cw + 7] = static_cast<unsigned long long>(ngrab);
+    }
+}
+
+template <int C, bool TR>
+__device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s, const StageDesc& d, int cw,
+                                            int lane) {
+    constexpr int G = C * 8;
+    constexpr int NU = kTokContribBytes / (G * 128) > 8 ? 8 : kTokContribBytes / (G * 128);
+    static_assert(NU >= 2, "contribution slots");
+    LinearSmem ls;
+    ls.act_hi = reinterpret_cast<int8_t*>(s.uni);
+    ls.act_lo = s.uni + G * 32;
+    ls.corr = reinterpret_cast<int*>(s.uni + G * 64);
+    ls.act_scale = reinterpret_cast<float*>(s.uni + G * 68);
+    float* contrib = reinterpret_cast<float*>(s.uni + align16(G * 72));
+    const int tid = cw * 32 + lane;
+    const int ord = stage_ordinal(d.st, d.layer);
+    const int tl_layer = d.st == TS_LOGITS ? a.tl_layer : d.layer;  // the LM head is recorded with any layer
+    tl_mark<TR>(a, tl_layer, 4 * d.st);
+    const long long t_begin = clock64();
+
+    // Input readiness: the previous stage's partials from every CTA, or the
+    // attention items of this layer.
+    if (tid == 0) {
+        if (d.st == TS_O) wait_counter(a, &a.sync[kSyncAtt + d.layer], kAttnItems);
+        else if (ord > 0) wait_counter(a, &a.sync[kSyncStage + ord - 1], gridDim.x);
+        s.next[0] = s.next[1] = s.next[2] = s.next[3] = 0;
+    }
+    if (tid < 8) {
+        s.unit_cnt[tid] = 0;
+        s.slot_ok[tid] = tid;
+    }
+    tok_bar();
+    const long long t_ready = clock64();
+    if (tid == 0) tl_mark<TR>(a, tl_layer, 4 * d.st + 1);
+    if (d.st == TS_O) {
+        tok_input_attention(a, ls, d.bank, cw, lane);
+    } else if (d.st == TS_DOWN) {
+        tok_input_swiglu(a, ls, d.bank, d.layer, cw, lane);
+    } else {
+        const int norm = d.st == TS_QKV ? 2 * d.layer : d.st == TS_GU ? 2 * d.layer + 1 : 2 * d.layer;
+        if constexpr (G == 32) tok_input_rms<32>(a, s, ls, d.bank, norm, ord - 1, contrib, cw, lane);
+    }
+    tok_bar();
+    const long long t_loop = clock64();
+    if (tid == 0) {
+        tl_mark<TR>(a, tl_layer, 4 * d.st + 2);
+        if (TR && a.timeline && tl_layer == a.tl_layer) {
+            const int ncp = ((d.u1 - d.u0) * C + kTokCpc - 1) / kTokCpc;
+            int landed = 0;
+            for (int q = 0; q < ncp; ++q) {
+                const int cp = d.cbase + q, sl = cp % kTokSlots;
+                if (*reinterpret_cast<volatile int*>(&s.issued[sl]) == cp &&
+                    mbar_test_wait(&s.full[sl], static_cast<uint32_t>((cp / kTokSlots) & 1)))
+                    ++landed;
+            }
+            a.timeline[blockIdx.x * kTlEvents + 24 + d.st] = static_cast<unsigned long long>(landed);
+            a.timeline[blockIdx.x * kTlEvents + 29 + d.st] = static_cast<unsigned long long>(ncp);
+        }
+    }
+
+    float* partials = stage_partials(a, ord);
+    const bool tr = TR && a.trace != nullptr;
+    WarpTimes wt;
+    if constexpr (C == 4) tok_chunks_cols<TR>(a, s, d, ls, contrib, partials, cw, lane, wt);
+    else tok_chunks_rows<C, TR>(a, s, d, ls, contrib, partials, lane, wt);
+    const long long w_data = wt.data, w_slot = wt.slot, w_comp = wt.comp, w_chain = wt.chain;
     if (tr && lane == 0) {
         unsigned long long* t = a.trace + blockIdx.x * kTraceSlots;
         atomicAdd(t + TR_W_DATA + 4 * d.st, static_cast<unsigned long long>(w_data));
@@ -459,12 +603,12 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     tok_bar();
     const long long t_epi = clock64();
     if (tid == 0) {
-        tl_mark(a, tl_layer, 4 * d.st + 3);
+        tl_mark<TR>(a, tl_layer, 4 * d.st + 3);
         __threadfence();
         atomicAdd(&a.sync[kSyncStage + ord], 1u);
-        trace_add(a, TR_WAIT + d.st, t_ready - t_begin);
-        trace_add(a, TR_PROLOGUE + d.st, t_loop - t_ready);
-        trace_add(a, TR_CHUNKS + d.st, t_epi - t_loop);
+        trace_add<TR>(a, TR_WAIT + d.st, t_ready - t_begin);
+        trace_add<TR>(a, TR_PROLOGUE + d.st, t_loop - t_ready);
+        trace_add<TR>(a, TR_CHUNKS + d.st, t_epi - t_loop);
     }
 }
 
@@ -524,6 +668,7 @@ static_assert(2 * kTile * 320 + 320 + kTile * 8 + 144 + kTile * 32 * 4 + 2 * 128
 // the per-token state terms mulq17(v_t, c_t) are computed in parallel into
 // shared memory, and the reference's saturating recurrence (emulator:656-685)
 // then runs exactly, one lane per dimension, over those terms.
+template <bool TR>
 __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s, int layer, int item, int cw,
                                            int lane) {
     const unsigned FULL = 0xffffffffu;
@@ -549,7 +694,7 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
     if (tid < 33) S.lut[tid] = a.exp2_q30[tid];
     tok_bar();
     const long long t_a0 = clock64();
-    if (tid == 0) tl_mark(ta, layer, 20);
+    if (tid == 0) tl_mark<TR>(ta, layer, 20);
     if (tid == 0) {
         // Cached records of earlier tokens are final: stream the first tile
         // while the other CTAs finish the QKV projection.
@@ -561,7 +706,7 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
     }
     tok_bar();
     const long long t_a1 = clock64();
-    if (tid == 0) tl_mark(ta, layer, 21);
+    if (tid == 0) tl_mark<TR>(ta, layer, 21);
 
     // Current token: Q/K/V rows of the head, RoPE, KV record.
     const int d = tid & 127;
@@ -768,9 +913,9 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
     if (tid == 0) {
         __threadfence();
         atomicAdd(&ta.sync[kSyncAtt + layer], 1u);
-        trace_add(ta, TR_ATTN_WAIT, t_a1 - t_a0);
-        trace_add(ta, TR_ATTN, clock64() - t_a1);
-        tl_mark(ta, layer, 22);
+        trace_add<TR>(ta, TR_ATTN_WAIT, t_a1 - t_a0);
+        trace_add<TR>(ta, TR_ATTN, clock64() - t_a1);
+        tl_mark<TR>(ta, layer, 22);
     }
 }
 
@@ -825,6 +970,7 @@ __device__ __forceinline__ void cursor_advance(const TokenArgs& a, int bank, int
     }
 }
 
+template <bool TR>
 __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant__ TokenArgs a) {
     extern __shared__ __align__(128) uint8_t tok_smem_raw[];
     TokSmem s = tok_carve(tok_smem_raw);
@@ -858,11 +1004,11 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
             while (cursor_valid(a, cur)) {
                 const int cnt = min(kTokCpc, cur.n - cur.i);
                 if (issued >= kTokSlots) {
-                    const long long t0 = a.trace ? clock64() : 0;
+                    const long long t0 = TR && a.trace ? clock64() : 0;
                     if (!tok_mbar_wait(a, &s.empty[slot], phase ^ 1u, kErrWaitEmpty)) break;
-                    if (a.trace) trace_add(a, TR_RING_FULL, clock64() - t0);
+                    if (TR && a.trace) trace_add<TR>(a, TR_RING_FULL, clock64() - t0);
                 }
-                if (cur.i == 0 && cur.st == TS_QKV) tl_mark(a, cur.l, 23);
+                if (cur.i == 0 && cur.st == TS_QKV) tl_mark<TR>(a, cur.l, 23);
                 publish_issued(&s.issued[slot], issued);
                 mbar_arrive_expect_tx(&s.full[slot], cnt * kChunkBytes);
                 bulk_g2s_hint(s.ring + static_cast<size_t>(slot) * kTokSlotBytes,
@@ -904,11 +1050,11 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
             d.st = stage;
             d.layer = l;
             urange(stage, &d.u0, &d.u1);
-            if (stage == TS_DOWN) tok_gemv_stage<11>(a, s, d, cw, lane);
-            else tok_gemv_stage<4>(a, s, d, cw, lane);
+            if (stage == TS_DOWN) tok_gemv_stage<11, TR>(a, s, d, cw, lane);
+            else tok_gemv_stage<4, TR>(a, s, d, cw, lane);
             d.cbase += ((d.u1 - d.u0) * stage_chunks(stage) + kTokCpc - 1) / kTokCpc;
             if (stage == TS_QKV && l < a.layers) {
-                if (blockIdx.x < kAttnItems) tok_attention(a, s, l, blockIdx.x, cw, lane);
+                if (blockIdx.x < kAttnItems) tok_attention<TR>(a, s, l, blockIdx.x, cw, lane);
                 tok_bar();
             }
         }
@@ -917,7 +1063,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
     // The last CTA to finish clears the token's synchronisation words.
     tok_bar();
     if (tid == 0) {
-        trace_add(a, TR_TOTAL, clock64() - t_kernel);
+        trace_add<TR>(a, TR_TOTAL, clock64() - t_kernel);
         __threadfence();
         const unsigned old = atomicAdd(&a.sync[kSyncExit], 1u);
         if (old + 1 == gridDim.x) {

@@ -143,7 +143,11 @@ i4d_status i4d_token_breakdown(i4d_ctx* ctx, uint32_t position, const float* res
  * the QKV, O, GATE/UP, DOWN and LM-head stages s, 4s+0 begin, 4s+1 input
  * ready, 4s+2 chunk loop start, 4s+3 arrival; 20..22 attention start, QKV
  * ready, end (CTAs with an attention item); 23 the producer's first copy of
- * the layer.  out holds max_ctas x 24 values; *n_ctas receives the grid size.
+ * the layer; then counts, not times: 24+s copies of stage s already landed
+ * when its chunk loop starts, 29+s copies of stage s; 34+8w+k for consumer
+ * warp w in the QKV stage: k < 6 the time of its k-th unit grab, 6 its loop
+ * exit, 7 its number of grabs.  out holds max_ctas x 162 values; *n_ctas
+ * receives the grid size.
  * No reference counterpart. */
 i4d_status i4d_token_timeline(i4d_ctx* ctx, uint32_t position, const float* residual_in_dev, int layer,
                               uint64_t* out, int max_ctas, int* n_ctas);
