@@ -90,7 +90,7 @@ def load_library():
         "i4d_profile_token": [P, ctypes.c_uint32, P, P, P],
         "i4d_token_breakdown": [P, ctypes.c_uint32, P, P, ctypes.c_int],
         "i4d_linear_bank_noalloc": [P, P, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, P, P, ctypes.c_int, P],
-        "i4d_token_timeline": [P, ctypes.c_uint32, P, ctypes.c_int, P, ctypes.c_int, P],
+        "i4d_token_timeline": [P, ctypes.c_uint32, P, ctypes.c_int, ctypes.c_int, P, ctypes.c_int, P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -185,12 +185,12 @@ class Context:
         self._check(self._L.i4d_token_breakdown(self._h, position, residual_in_dev_ptr, out.ctypes.data, out.size))
         return dict(zip(BREAKDOWN, out.tolist()))
 
-    def token_timeline(self, position, residual_in_dev_ptr, layer):
+    def token_timeline(self, position, residual_in_dev_ptr, layer, detail=False):
         """[CTAs, 162] global-timer stamps (ns) and counts of one layer (see i4d_token_timeline)."""
         out = np.zeros((1024, 162), np.uint64)
         n = ctypes.c_int(0)
-        self._check(self._L.i4d_token_timeline(self._h, position, residual_in_dev_ptr, layer, out.ctypes.data,
-                                               out.shape[0], ctypes.byref(n)))
+        self._check(self._L.i4d_token_timeline(self._h, position, residual_in_dev_ptr, layer, int(bool(detail)),
+                                               out.ctypes.data, out.shape[0], ctypes.byref(n)))
         return out[: n.value]
 
     def kv_reset(self):

@@ -136,6 +136,7 @@ struct i4d_ctx {
     unsigned long long* d_trace = nullptr;  // optional token-kernel trace
     unsigned long long* d_timeline = nullptr;  // optional token-kernel timeline
     int tl_layer = -1;
+    bool tl_detail = false;
 };
 
 namespace {
@@ -297,7 +298,7 @@ cudaError_t launch_token(i4d_ctx* c) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     // The measurement hooks run the instantiation with cycle counters and stamps.
-    if (c->d_trace || c->d_timeline) return cudaLaunchKernelEx(&cfg, k_token<true>, token_args(c));
+    if (c->d_trace || (c->d_timeline && c->tl_detail)) return cudaLaunchKernelEx(&cfg, k_token<true>, token_args(c));
     return cudaLaunchKernelEx(&cfg, k_token<false>, token_args(c));
 }
 
@@ -1113,7 +1114,7 @@ extern "C" i4d_status i4d_token_breakdown(i4d_ctx* c, uint32_t position, const f
 }
 
 extern "C" i4d_status i4d_token_timeline(i4d_ctx* c, uint32_t position, const float* residual_in_dev, int layer,
-                                         uint64_t* out, int max_ctas, int* n_ctas) {
+                                         int detail, uint64_t* out, int max_ctas, int* n_ctas) {
     if (!c || !residual_in_dev || !out || !n_ctas) return c ? fail(c, I4D_ERR_ARG, "bad arguments") : I4D_ERR_ARG;
     if (c->flags & I4D_FLAG_STAGED) return fail(c, I4D_ERR_STATE, "timeline needs the persistent token kernel");
     if (!all_loaded(c)) return fail(c, I4D_ERR_STATE, "banks and rope LUT must be loaded before decoding");
@@ -1126,6 +1127,7 @@ extern "C" i4d_status i4d_token_timeline(i4d_ctx* c, uint32_t position, const fl
     const size_t n = static_cast<size_t>(grid) * kTlEvents;
     CK(cudaMalloc(&c->d_timeline, n * sizeof(unsigned long long)));
     c->tl_layer = layer;
+    c->tl_detail = detail != 0;
     cudaError_t e = cudaMemsetAsync(c->d_timeline, 0, n * sizeof(unsigned long long), c->stream);
     if (e == cudaSuccess) {
         k_set_pos<<<1, 1, 0, c->stream>>>(c->d_pos, static_cast<int>(position));
@@ -1133,10 +1135,14 @@ extern "C" i4d_status i4d_token_timeline(i4d_ctx* c, uint32_t position, const fl
     }
     if (e == cudaSuccess) e = launch_token(c);
     const i4d_status st = e == cudaSuccess ? finish(c) : fail(c, I4D_ERR_CUDA, "%s", cudaGetErrorString(e));
-    if (st == I4D_OK) e = cudaMemcpy(out, c->d_timeline, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    // The stamps are returned even when a bounded wait gave up: they show how
+    // far each CTA got.
+    if (st == I4D_OK || st == I4D_ERR_TIMEOUT)
+        e = cudaMemcpy(out, c->d_timeline, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
     cudaFree(c->d_timeline);
     c->d_timeline = nullptr;
     c->tl_layer = -1;
+    c->tl_detail = false;
     if (st != I4D_OK) return st;
     if (e != cudaSuccess) return fail(c, I4D_ERR_CUDA, "%s", cudaGetErrorString(e));
     return I4D_OK;

@@ -31,6 +31,14 @@ constexpr int kCounterLevel2 = 4095;
 constexpr unsigned kErrWaitFull = 1u;
 constexpr unsigned kErrWaitEmpty = 2u;
 constexpr unsigned kErrArg = 4u;
+// Which bounded wait gave up (token kernel): stage counter, ring copy,
+// contribution slot, unit completion, attention tile, producer drain.
+constexpr unsigned kErrWaitCounter = 8u;
+constexpr unsigned kErrWaitCopy = 16u;
+constexpr unsigned kErrWaitSlot = 32u;
+constexpr unsigned kErrWaitUnit = 64u;
+constexpr unsigned kErrWaitTile = 128u;
+constexpr unsigned kErrWaitDrain = 256u;
 
 // ------------------------------------------------------------------ PTX
 
@@ -40,6 +48,10 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_inval(uint64_t* bar) {
+    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void mbar_fence_init() {

@@ -28,7 +28,9 @@
 
 namespace i4d {
 
-constexpr int kTokWarps = 16;
+constexpr int kTokColWarps = 16;             // consumer warps that compute chunks
+constexpr int kTokRedWarps = 2;              // consumer warps that chain finished units
+constexpr int kTokWarps = kTokColWarps + kTokRedWarps;
 constexpr int kTokThreads = 32 * (1 + kTokWarps);
 constexpr int kTokRing = 40;               // ring capacity in chunks of kChunkBytes
 constexpr int kTokCpc = 4;                 // chunks per bulk copy (16,896 B: streams near the HBM peak)
@@ -104,10 +106,12 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 
+// Stage-level stamps are cheap (a few stores per stage) and compiled into
+// both instantiations; per-chunk counters and per-warp stamps only into the
+// traced one.
 template <bool TR>
 __device__ __forceinline__ void tl_mark(const TokenArgs& a, int layer, int event) {
-    if constexpr (TR)
-        if (a.timeline && layer == a.tl_layer) a.timeline[blockIdx.x * kTlEvents + event] = global_ns();
+    if (a.timeline && layer == a.tl_layer) a.timeline[blockIdx.x * kTlEvents + event] = global_ns();
 }
 
 template <bool TR>
@@ -128,7 +132,7 @@ struct TokSmem {
     uint64_t* abar;      // [2] attention tile barriers
     uint8_t* uni;        // union region
     int* next;           // dynamic chunk counter
-    int* unit_cnt;       // [8]
+    int* unit_cnt;       // [8]: chunk arrivals per contribution slot in this stage
     int* slot_ok;        // [8]
     int* fin;            // [kFinMax + 2]
     int* flag;           // [4] misc
@@ -163,7 +167,7 @@ __device__ __forceinline__ TokSmem tok_carve(uint8_t* p) {
     return s;
 }
 
-__device__ __forceinline__ void tok_bar() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+__device__ __forceinline__ void tok_bar() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kTokWarps) : "memory"); }
 
 __device__ __forceinline__ bool aborted(const TokenArgs& a) {
     return *reinterpret_cast<volatile unsigned*>(&a.sync[kSyncAbort]) != 0;
@@ -183,7 +187,7 @@ __device__ bool wait_counter(const TokenArgs& a, const unsigned* word, unsigned 
         }
         if (aborted(a)) return false;
         if (it > (1u << 24)) {
-            raise_abort(a, kErrWaitFull);
+            raise_abort(a, kErrWaitFull | kErrWaitCounter);
             return false;
         }
         if (it >= 256) __nanosleep(it < 1024 ? 32 : 256);
@@ -244,9 +248,7 @@ __device__ __forceinline__ void tok_input_rms(const TokenArgs& a, const TokSmem&
     float4* rout = reinterpret_cast<float4*>(a.resid + (norm & 1) * kDim);
     const float4* P = reinterpret_cast<const float4*>(stage_partials(a, prev_ordinal));
     constexpr int kQ = kDim / 4;  // float4 per vector
-#pragma unroll
-    for (int k = 0; k < kQ / (32 * kTokWarps); ++k) {
-        const int i = tid + k * 32 * kTokWarps;
+    for (int i = tid; i < kQ; i += 32 * kTokWarps) {
         float4 x = __ldcg(rin + i);
         if (norm > 0) {
             const float4 p0 = __ldcg(P + i), p1 = __ldcg(P + kQ + i);
@@ -311,10 +313,11 @@ __device__ __forceinline__ void tok_input_swiglu(const TokenArgs& a, const Linea
 // Input of O: the attention output of this bank's 8 heads.
 __device__ __forceinline__ void tok_input_attention(const TokenArgs& a, const LinearSmem& ls, int bank, int cw, int lane) {
     constexpr int G = 32;
-    constexpr int kPer = G / kTokWarps;
+    constexpr int kPer = (G + kTokWarps - 1) / kTokWarps;
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
         const int lg = cw + k * kTokWarps;
+        if (lg >= G) break;
         const int q = __ldcg(a.ao_q + bank * 1024 + lg * 32 + lane);
         const uint32_t e8 = __ldcg(a.ao_e + bank * 32 + lg);
         put_act(ls, lg, lane, q, e8);
@@ -326,26 +329,40 @@ __device__ __forceinline__ void tok_wait_copy(const TokenArgs& a, const TokSmem&
     for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.issued[slot]) != cp; ++it) {
         if ((it & 63) == 0 && aborted(a)) break;
         if (it > (1u << 24)) {
-            raise_abort(a, kErrWaitFull);
+            raise_abort(a, kErrWaitFull | kErrWaitCopy);
             break;
         }
         if (it >= 256) __nanosleep(32);
     }
-    tok_mbar_wait(a, &s.full[slot], static_cast<uint32_t>((cp / kTokSlots) & 1), kErrWaitFull);
+    tok_mbar_wait(a, &s.full[slot], static_cast<uint32_t>((cp / kTokSlots) & 1), kErrWaitFull | kErrWaitCopy);
 }
 
-// Waits until contribution slot `us` may take unit `uidx`.
+// Waits until contribution slot `us` may take unit `uidx`.  On a timeout
+// with a timeline attached, records the slot's state in events 24..29.
 __device__ __forceinline__ void tok_wait_slot(const TokenArgs& a, const TokSmem& s, int us, int uidx) {
     if (*reinterpret_cast<volatile int*>(&s.slot_ok[us]) >= uidx) return;
     for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.slot_ok[us]) < uidx; ++it) {
         if (it >= 256) __nanosleep(32);
         if ((it & 63) == 0 && aborted(a)) break;
         if (it > (1u << 24)) {
-            raise_abort(a, kErrWaitFull);
+            raise_abort(a, kErrWaitFull | kErrWaitSlot);
+            if (a.timeline) {
+                unsigned long long* t = a.timeline + blockIdx.x * kTlEvents;
+                t[24] = static_cast<unsigned long long>(us);
+                t[25] = static_cast<unsigned long long>(uidx);
+                t[26] = static_cast<unsigned long long>(*reinterpret_cast<volatile int*>(&s.slot_ok[us]));
+                t[27] = static_cast<unsigned long long>(*reinterpret_cast<volatile int*>(&s.unit_cnt[us])) + 1;
+                t[28] = static_cast<unsigned long long>(*reinterpret_cast<volatile int*>(&s.flag[2]));
+                t[29] = static_cast<unsigned long long>(*reinterpret_cast<volatile int*>(&s.flag[3]));
+            }
             break;
         }
     }
 }
+
+template <int C>
+constexpr int kRowNU = (kTokContribBytes / (C * 8 * 128) > 8 ? 8 : kTokContribBytes / (C * 8 * 128)) / kTokRedWarps *
+                       kTokRedWarps;
 
 struct WarpTimes {
     long long data = 0, slot = 0, comp = 0, chain = 0;
@@ -355,13 +372,11 @@ struct WarpTimes {
 // takes whole chunks in order, activations come from shared memory.
 template <int C, bool TR>
 __device__ __forceinline__ void tok_chunks_rows(const TokenArgs& a, const TokSmem& s, const StageDesc& d,
-                                                const LinearSmem& ls, float* contrib, float* partials, int lane,
-                                                WarpTimes& wt) {
+                                                const LinearSmem& ls, float* contrib, int lane, WarpTimes& wt) {
     constexpr int G = C * 8;
-    constexpr int NU = kTokContribBytes / (G * 128) > 8 ? 8 : kTokContribBytes / (G * 128);
+    constexpr int NU = kRowNU<C>;
     const unsigned FULL = 0xffffffffu;
     const int nchunks = (d.u1 - d.u0) * C;
-    const int rows_total = stage_units(d.st) * 32;
     const bool tr = TR && a.trace != nullptr;
     for (;;) {
         const long long c0 = tr ? clock64() : 0;
@@ -400,25 +415,10 @@ __device__ __forceinline__ void tok_chunks_rows(const TokenArgs& a, const TokSme
             const int dot = group_dot(wv[g], ls.act_hi + lg * 32, ls.act_lo + lg * 32, ls.corr[lg]);
             cb[lg * 32 + lane] = __fmul_rn(static_cast<float>(dot), __fmul_rn(g < 4 ? ws0 : ws1, ls.act_scale[lg]));
         }
-        __syncwarp();
         __threadfence_block();
-        int old = 0;
-        if (lane == 0) old = atomicAdd(&s.unit_cnt[us], 1);
-        old = __shfl_sync(FULL, old, 0);
+        __syncwarp();
+        if (lane == 0) atomicAdd(&s.unit_cnt[us], 1);  // the reducer chains the unit
         const long long c3 = tr ? clock64() : 0;
-        if (old == C - 1) {
-            __threadfence_block();
-            float acc = __fadd_rn(0.0f, cb[lane]);
-#pragma unroll 8
-            for (int lg = 1; lg < G; ++lg) acc = __fadd_rn(acc, cb[lg * 32 + lane]);
-            partials[static_cast<size_t>(d.bank) * rows_total + static_cast<size_t>(d.u0 + uidx) * 32 + lane] = acc;
-            __syncwarp();
-            __threadfence_block();
-            if (lane == 0) {
-                s.unit_cnt[us] = 0;
-                *reinterpret_cast<volatile int*>(&s.slot_ok[us]) = uidx + NU;
-            }
-        }
         if (tr) {
             const long long c4 = clock64();
             wt.data += c1 - c0;
@@ -437,12 +437,15 @@ __device__ __forceinline__ void tok_chunks_rows(const TokenArgs& a, const TokSme
 // Contributions are stored at [group][row] with a stride of 33 floats (no
 // bank conflicts for either writer or chain).
 constexpr int kColContribStride = 33;
-constexpr int kColNU = kTokContribBytes / (32 * kColContribStride * 4);  // 7
+// Contribution slots: a multiple of the reducer count, so that every slot is
+// owned by one reducer, which waits on its barrier phases strictly in order
+// (a parity wait cannot tell phases two apart).
+constexpr int kColNU = kTokContribBytes / (32 * kColContribStride * 4) / kTokRedWarps * kTokRedWarps;  // 6
 
 template <bool TR>
 __device__ __forceinline__ void tok_chunks_cols(const TokenArgs& a, const TokSmem& s, const StageDesc& d,
-                                                const LinearSmem& ls, float* contrib, float* partials, int cw,
-                                                int lane, WarpTimes& wt) {
+                                                const LinearSmem& ls, float* contrib, int cw, int lane,
+                                                WarpTimes& wt) {
     constexpr int G = 32;
     constexpr int NU = kColNU;
     const unsigned FULL = 0xffffffffu;
@@ -455,7 +458,6 @@ __device__ __forceinline__ void tok_chunks_cols(const TokenArgs& a, const TokSme
     const int corr = ls.corr[lg];
     const float as = ls.act_scale[lg];
     const int nunits = d.u1 - d.u0;
-    const int rows_total = stage_units(d.st) * 32;
     const bool tr = TR && a.trace != nullptr;
     const bool tl = TR && a.timeline && d.st == TS_QKV && d.layer == a.tl_layer;
     int ngrab = 0;
@@ -494,25 +496,10 @@ __device__ __forceinline__ void tok_chunks_cols(const TokenArgs& a, const TokSme
             const int dot = group_dot_r(wv[k], h0, h1, l0, l1, corr);
             cb[lg * kColContribStride + rb * 8 + k] = __fmul_rn(static_cast<float>(dot), __fmul_rn(ws, as));
         }
-        __syncwarp();
         __threadfence_block();
-        int old = 0;
-        if (lane == 0) old = atomicAdd(&s.unit_cnt[us], 1);
-        old = __shfl_sync(FULL, old, 0);
+        __syncwarp();
+        if (lane == 0) atomicAdd(&s.unit_cnt[us], 1);  // the reducer chains the unit
         const long long c3 = tr ? clock64() : 0;
-        if (old == 3) {
-            __threadfence_block();
-            float acc = __fadd_rn(0.0f, cb[lane]);
-#pragma unroll 8
-            for (int q = 1; q < G; ++q) acc = __fadd_rn(acc, cb[q * kColContribStride + lane]);
-            partials[static_cast<size_t>(d.bank) * rows_total + static_cast<size_t>(d.u0 + u) * 32 + lane] = acc;
-            __syncwarp();
-            __threadfence_block();
-            if (lane == 0) {
-                s.unit_cnt[us] = 0;
-                *reinterpret_cast<volatile int*>(&s.slot_ok[us]) = u + NU;
-            }
-        }
         if (tr) {
             const long long c4 = clock64();
             wt.data += c1 - c0;
@@ -524,6 +511,42 @@ __device__ __forceinline__ void tok_chunks_cols(const TokenArgs& a, const TokSme
     if (tl && lane == 0) {
         a.timeline[blockIdx.x * kTlEvents + 34 + 8 * cw + 6] = global_ns();
         a.timeline[blockIdx.x * kTlEvents + 34 + 8 * cw + 7] = static_cast<unsigned long long>(ngrab);
+    }
+}
+
+// Reducer warps: reducer r chains units r, r + kTokRedWarps, ... in order
+// once all their chunks have stored contributions (lane = row):
+// acc = fl(acc + contrib[g]) over the unit's groups from +0.0f
+// (emulator:216-264), stores the bank partial and frees the slot.
+template <int G, int STRIDE, int NU>
+__device__ __forceinline__ void tok_reduce_units(const TokenArgs& a, const TokSmem& s, const StageDesc& d,
+                                                 const float* contrib, float* partials, int r, int lane) {
+    static_assert(NU % kTokRedWarps == 0, "each contribution slot must belong to one reducer");
+    const int nunits = d.u1 - d.u0;
+    const int rows_total = stage_units(d.st) * 32;
+    for (int u = r; u < nunits; u += kTokRedWarps) {
+        const int us = u % NU;
+        if (lane == 0) *reinterpret_cast<volatile int*>(&s.flag[2 + r]) = u;  // progress, for diagnostics
+        // The slot's arrival count only grows within a stage: its k-th unit is
+        // complete at (k + 1) * chunks arrivals.
+        const int target = (u / NU + 1) * (G / 8);
+        for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.unit_cnt[us]) < target; ++it) {
+            if (it >= 64) __nanosleep(32);
+            if ((it & 63) == 0 && aborted(a)) return;
+            if (it > (1u << 24)) {
+                raise_abort(a, kErrWaitFull | kErrWaitUnit);
+                return;
+            }
+        }
+        __threadfence_block();
+        const float* cb = contrib + us * G * STRIDE;
+        float acc = __fadd_rn(0.0f, cb[lane]);
+#pragma unroll 8
+        for (int q = 1; q < G; ++q) acc = __fadd_rn(acc, cb[q * STRIDE + lane]);
+        partials[static_cast<size_t>(d.bank) * rows_total + static_cast<size_t>(d.u0 + u) * 32 + lane] = acc;
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) *reinterpret_cast<volatile int*>(&s.slot_ok[us]) = u + NU;
     }
 }
 
@@ -553,7 +576,7 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
         s.next[0] = s.next[1] = s.next[2] = s.next[3] = 0;
     }
     if (tid < 8) {
-        s.unit_cnt[tid] = 0;
+        s.unit_cnt[tid] = 0;  // chunk arrivals per contribution slot, this stage
         s.slot_ok[tid] = tid;
     }
     tok_bar();
@@ -588,8 +611,16 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     float* partials = stage_partials(a, ord);
     const bool tr = TR && a.trace != nullptr;
     WarpTimes wt;
-    if constexpr (C == 4) tok_chunks_cols<TR>(a, s, d, ls, contrib, partials, cw, lane, wt);
-    else tok_chunks_rows<C, TR>(a, s, d, ls, contrib, partials, lane, wt);
+    if (cw >= kTokColWarps) {
+        if constexpr (C == 4)
+            tok_reduce_units<32, kColContribStride, kColNU>(a, s, d, contrib, partials, cw - kTokColWarps, lane);
+        else
+            tok_reduce_units<C * 8, 32, kRowNU<C>>(a, s, d, contrib, partials, cw - kTokColWarps, lane);
+    } else if constexpr (C == 4) {
+        tok_chunks_cols<TR>(a, s, d, ls, contrib, cw, lane, wt);
+    } else {
+        tok_chunks_rows<C, TR>(a, s, d, ls, contrib, lane, wt);
+    }
     const long long w_data = wt.data, w_slot = wt.slot, w_comp = wt.comp, w_chain = wt.chain;
     if (tr && lane == 0) {
         unsigned long long* t = a.trace + blockIdx.x * kTraceSlots;
@@ -784,7 +815,7 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
             bulk_g2s(S.tile[(k + 1) & 1], head_base + static_cast<size_t>(T0 + kTile) * 320, c2 * 320,
                      &s.abar[(k + 1) & 1]);
         }
-        tok_mbar_wait(ta, &s.abar[k & 1], static_cast<uint32_t>((k >> 1) & 1), kErrWaitFull);
+        tok_mbar_wait(ta, &s.abar[k & 1], static_cast<uint32_t>((k >> 1) & 1), kErrWaitFull | kErrWaitTile);
         if (pos < T0 + cnt) {  // the tile holds the current token: use the fresh record
             if (tid < 80)
                 reinterpret_cast<uint32_t*>(buf + (pos - T0) * 320)[tid] = reinterpret_cast<const uint32_t*>(S.cur)[tid];
@@ -1027,7 +1058,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
                 const int sl = g % kTokSlots;
                 for (uint32_t it = 0; !mbar_try_wait(&s.full[sl], static_cast<uint32_t>((g / kTokSlots) & 1)); ++it) {
                     if (it > (1u << 22)) {
-                        atomicOr(a.err, kErrWaitFull);
+                        atomicOr(a.err, kErrWaitFull | kErrWaitDrain);
                         break;
                     }
                     __nanosleep(64);

@@ -138,8 +138,9 @@ i4d_status i4d_profile_token(i4d_ctx* ctx, uint32_t position, const float* resid
 i4d_status i4d_token_breakdown(i4d_ctx* ctx, uint32_t position, const float* residual_in_dev, float* us_out,
                                int n_out);
 
-/* Measurement hook for the persistent token kernel: runs one step and
- * returns, per CTA, global-timer stamps (ns) of 24 events of `layer`: for
+/* Measurement hook for the persistent token kernel: runs one step (with
+ * detail != 0 the instrumented kernel, which also records per-warp stamps)
+ * and returns, per CTA, global-timer stamps (ns) of 24 events of `layer`: for
  * the QKV, O, GATE/UP, DOWN and LM-head stages s, 4s+0 begin, 4s+1 input
  * ready, 4s+2 chunk loop start, 4s+3 arrival; 20..22 attention start, QKV
  * ready, end (CTAs with an attention item); 23 the producer's first copy of
@@ -150,7 +151,7 @@ i4d_status i4d_token_breakdown(i4d_ctx* ctx, uint32_t position, const float* res
  * receives the grid size.
  * No reference counterpart. */
 i4d_status i4d_token_timeline(i4d_ctx* ctx, uint32_t position, const float* residual_in_dev, int layer,
-                              uint64_t* out, int max_ctas, int* n_ctas);
+                              int detail, uint64_t* out, int max_ctas, int* n_ctas);
 
 /* Clears the KV cache (decode_host.cpp:1291-1294 zero_bo). */
 i4d_status i4d_kv_reset(i4d_ctx* ctx);
