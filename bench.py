@@ -117,9 +117,9 @@ def measured_peak():
 
 
 def committed_traffic():
-    """DRAM bytes per GEMV launch from the committed ncu summary, if any."""
+    """DRAM bytes per k_token launch (32 layers) from the committed ncu summary, if any."""
     try:
-        return json.load(open(os.path.join(ROOT, "profiles", "k_linear_traffic.json")))
+        return json.load(open(os.path.join(ROOT, "profiles", "k_token_traffic.json")))
     except (OSError, ValueError):
         return None
 
