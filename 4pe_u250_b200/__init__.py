@@ -32,7 +32,7 @@ EXPORTS = [
     "i4d_sync", "i4d_linear_bank", "i4d_gemv", "i4d_quantize_g32", "i4d_rms_quant",
     "i4d_attention", "i4d_swiglu_quant", "i4d_expf", "i4d_decode_token_async", "i4d_stream",
     "i4d_profile_token", "i4d_token_breakdown", "i4d_linear_bank_noalloc",
-    "i4d_token_timeline",
+    "i4d_token_timeline", "i4d_create_shard", "i4d_shard_export", "i4d_shard_attach",
 ]
 
 _STAGES = ["qkv", "o", "gu", "down", "logits"]
@@ -41,6 +41,15 @@ BREAKDOWN = ([f"wait_{x}" for x in _STAGES] + [f"prologue_{x}" for x in _STAGES]
              + [f"warp_{k}_{x}" for x in _STAGES for k in ("data_wait", "slot_wait", "compute", "chain")])
 
 KERNEL_CLASSES = ["qkv_gemv", "attention", "o_gemv", "gate_up_gemv", "down_gemv", "logits_gemv", "rms", "token"]
+
+
+def gather_handles(handle, group=None):
+    """All ranks' shard handles in rank order, by a torch.distributed
+    all-gather (any backend: the handles are host bytes)."""
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, handle, group=group)
+    return out
 
 
 class I4DError(RuntimeError):
@@ -91,6 +100,9 @@ def load_library():
         "i4d_token_breakdown": [P, ctypes.c_uint32, P, P, ctypes.c_int],
         "i4d_linear_bank_noalloc": [P, P, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, P, P, ctypes.c_int, P],
         "i4d_token_timeline": [P, ctypes.c_uint32, P, ctypes.c_int, ctypes.c_int, P, ctypes.c_int, P],
+        "i4d_create_shard": [P, ctypes.c_int, ctypes.c_int, P],
+        "i4d_shard_export": [P, P, ctypes.c_size_t],
+        "i4d_shard_attach": [P, P, ctypes.c_size_t],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -107,19 +119,54 @@ def _ptr(a):
     return a.ctypes.data if a is not None else None
 
 
-class Context:
-    """One decode context on one GPU (i4d_ctx)."""
+SHARD_HANDLE_BYTES = 64
 
-    def __init__(self, device=0, num_layers=32, kv_capacity=4096, flags=0):
+
+def shard_banks(rank, world):
+    """Banks held by `rank` of a bank-sharded group of `world` GPUs."""
+    n = 4 // world
+    return list(range(rank * n, rank * n + n))
+
+
+class Context:
+    """One decode context on one GPU (i4d_ctx).  With world > 1 it is rank
+    `rank` of a bank-sharded group (i4d_create_shard): it holds the banks
+    shard_banks(rank, world) and must be attached to its peers (attach_peers)
+    before decoding."""
+
+    def __init__(self, device=0, num_layers=32, kv_capacity=4096, flags=0, rank=0, world=1):
         self._L = load_library()
         cfg = _Config(device, num_layers, kv_capacity, flags)
         h = ctypes.c_void_p()
-        st = self._L.i4d_create(ctypes.byref(cfg), ctypes.byref(h))
+        if world == 1:
+            st = self._L.i4d_create(ctypes.byref(cfg), ctypes.byref(h))
+        else:
+            st = self._L.i4d_create_shard(ctypes.byref(cfg), rank, world, ctypes.byref(h))
         if st != OK:
             raise I4DError(st, "i4d_create failed (see stderr)")
         self._h = h
         self.num_layers = num_layers
         self.kv_capacity = kv_capacity
+        self.rank, self.world = rank, world
+        self.banks = shard_banks(rank, world)
+
+    # -- bank sharding ------------------------------------------------------
+    def shard_handle(self):
+        """This context's opaque peer handle (bytes)."""
+        buf = ctypes.create_string_buffer(SHARD_HANDLE_BYTES)
+        self._check(self._L.i4d_shard_export(self._h, buf, SHARD_HANDLE_BYTES))
+        return buf.raw
+
+    def attach_handles(self, handles):
+        """Maps the peers from all ranks' handles, in rank order."""
+        if len(handles) != self.world or any(len(x) != SHARD_HANDLE_BYTES for x in handles):
+            raise I4DError(ERR_SIZE, "need one handle of SHARD_HANDLE_BYTES per rank")
+        blob = b"".join(handles)
+        self._check(self._L.i4d_shard_attach(self._h, blob, len(blob)))
+
+    def attach_peers(self, group=None):
+        """Exchanges handles over torch.distributed (all ranks call this)."""
+        self.attach_handles(gather_handles(self.shard_handle(), group))
 
     def close(self):
         if getattr(self, "_h", None):
@@ -145,8 +192,10 @@ class Context:
         self._check(self._L.i4d_load_bank(self._h, bank, image.ctypes.data, image.nbytes))
 
     def load_banks(self, images):
+        """Loads the held banks from the four images (the others are skipped)."""
         for p, img in enumerate(images):
-            self.load_bank(p, img)
+            if p in self.banks:
+                self.load_bank(p, img)
 
     def load_rope(self, lut=None):
         lut = formats.generate_rope_lut() if lut is None else lut

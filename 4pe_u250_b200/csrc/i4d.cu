@@ -85,6 +85,14 @@ int32_t host_float_to_q17(float value) {
 
 struct i4d_ctx {
     int device = 0, layers = 32, stride = 4096, num_sms = 148, cpb = 37;
+    // Bank sharding: this context holds banks [bank0, bank0 + nbanks) of a
+    // group of `world` contexts, one per GPU (world 1: all four banks).
+    int rank = 0, world = 1, nbanks = 4, bank0 = 0;
+    bool attached = false;                   // peers mapped (world > 1)
+    void* d_shared = nullptr;                // partials + synchronisation words, exported to peers
+    float* peer_partials[4] = {};
+    unsigned* peer_sync[4] = {};
+    void* peer_base[4] = {};                 // opened IPC mappings
     unsigned flags = 0;
     cudaStream_t stream = nullptr;
     std::string err;
@@ -160,10 +168,10 @@ i4d_status fail(i4d_ctx* c, i4d_status st, const char* fmt, ...) {
 
 size_t stage_offset(const i4d_ctx* c, int layer, int st) {
     size_t per_layer = 0;
-    for (int s = 0; s < ST_LOGITS; ++s) per_layer += 4 * stage_bank_bytes(s);
+    for (int s = 0; s < ST_LOGITS; ++s) per_layer += c->nbanks * stage_bank_bytes(s);
     if (st == ST_LOGITS) return static_cast<size_t>(c->layers) * per_layer;
     size_t off = static_cast<size_t>(layer) * per_layer;
-    for (int s = 0; s < st; ++s) off += 4 * stage_bank_bytes(s);
+    for (int s = 0; s < st; ++s) off += c->nbanks * stage_bank_bytes(s);
     return off;
 }
 
@@ -229,6 +237,7 @@ AttnArgs base_attn(i4d_ctx* c, int layer) {
     a.log2e_q21 = c->log2e_q21;
     a.score_scale = c->score_scale;
     a.kv = c->d_kv;
+    a.bank0 = c->bank0;
     a.layers = c->layers;
     a.stride = c->stride;
     a.layer = layer;
@@ -269,6 +278,14 @@ TokenArgs token_args(i4d_ctx* c) {
     }
     t.layers = c->layers;
     t.cpb = c->cpb;
+    t.bank0 = c->bank0;
+    t.nbanks = c->nbanks;
+    t.world = c->world;
+    for (int p = 0; p < 4; ++p) {
+        t.peer_partials[p] = c->peer_partials[p];
+        t.peer_sync[p] = c->peer_sync[p];
+    }
+    t.epoch = c->d_sync + kSyncEpoch;
     t.resid = c->d_resid;
     t.gamma = c->d_gamma;
     t.partials = c->d_partials;
@@ -288,7 +305,7 @@ TokenArgs token_args(i4d_ctx* c) {
 // One token as a single cooperative launch of the persistent kernel.
 cudaError_t launch_token(i4d_ctx* c) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(4 * c->cpb);
+    cfg.gridDim = dim3(c->nbanks * c->cpb);
     cfg.blockDim = dim3(kTokThreads);
     cfg.dynamicSmemBytes = tok_smem_bytes();
     cfg.stream = c->stream;
@@ -387,7 +404,9 @@ i4d_status finish(i4d_ctx* c) {
 }
 
 bool all_loaded(const i4d_ctx* c) {
-    return c->bank_loaded[0] && c->bank_loaded[1] && c->bank_loaded[2] && c->bank_loaded[3] && c->rope_loaded;
+    for (int b = c->bank0; b < c->bank0 + c->nbanks; ++b)
+        if (!c->bank_loaded[b]) return false;
+    return c->rope_loaded && (c->world == 1 || c->attached);
 }
 
 }  // namespace
@@ -405,9 +424,11 @@ void i4d_destroy(i4d_ctx* c) {
     if (c->graph_dev) cudaGraphExecDestroy(c->graph_dev);
     for (cudaEvent_t ev : c->prof_ev)
         if (ev) cudaEventDestroy(ev);
+    for (void* p : c->peer_base)
+        if (p) cudaIpcCloseMemHandle(p);
     void* dev[] = {c->d_w, c->d_gamma, c->d_rope_cos, c->d_rope_sin, c->d_exp2, c->d_expf_slots, c->d_kv,
-                   c->d_emb, c->d_resid, c->d_recip, c->d_partials, c->d_ao_q, c->d_ao_e, c->d_ad_q,
-                   c->d_ad_e, c->d_logits, c->d_counters, c->d_err, c->d_pos, c->d_scratch, c->d_attn_coef, c->d_sync, c->d_recips, c->d_trace};
+                   c->d_emb, c->d_resid, c->d_recip, c->d_shared, c->d_ao_q, c->d_ao_e, c->d_ad_q,
+                   c->d_ad_e, c->d_logits, c->d_counters, c->d_err, c->d_pos, c->d_scratch, c->d_attn_coef, c->d_recips, c->d_trace};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* host[] = {c->h_resid_in, c->h_resid_out, c->h_logits, c->h_pos, c->h_err};
@@ -417,10 +438,14 @@ void i4d_destroy(i4d_ctx* c) {
     delete c;
 }
 
-i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out) {
-    if (!cfg || !out) return I4D_ERR_ARG;
+static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ctx** out) {
+    if (!cfg || !out || (world != 1 && world != 2 && world != 4) || rank < 0 || rank >= world) return I4D_ERR_ARG;
     *out = nullptr;
     i4d_ctx* c = new i4d_ctx();
+    c->rank = rank;
+    c->world = world;
+    c->nbanks = 4 / world;
+    c->bank0 = rank * c->nbanks;
     c->device = cfg->device;
     c->layers = cfg->num_layers;
     c->stride = cfg->kv_capacity == 0 ? 4096 : cfg->kv_capacity;
@@ -446,7 +471,7 @@ i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out) {
     } while (0)
     CKC(cudaSetDevice(c->device));
     CKC(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, c->device));
-    c->cpb = c->num_sms / 4 > 0 ? c->num_sms / 4 : 1;
+    c->cpb = c->num_sms / c->nbanks > 0 ? c->num_sms / c->nbanks : 1;
     CKC(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     CKC(cudaFuncSetAttribute(k_linear, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBudget)));
     CKC(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -459,20 +484,31 @@ i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out) {
         int per_sm = 0, per_sm_tr = 0;
         CKC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_token<false>, kTokThreads, tok_smem_bytes()));
         CKC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_tr, k_token<true>, kTokThreads, tok_smem_bytes()));
-        if (per_sm < 1 || per_sm_tr < 1 || 4 * c->cpb > c->num_sms) c->flags |= I4D_FLAG_STAGED;
+        if (per_sm < 1 || per_sm_tr < 1 || c->nbanks * c->cpb > c->num_sms) c->flags |= I4D_FLAG_STAGED;
+        if (world > 1 && (c->flags & I4D_FLAG_STAGED)) {
+            fail(c, I4D_ERR_STATE, "bank sharding needs the persistent token kernel");
+            return bail(I4D_ERR_STATE);
+        }
     }
 
-    c->w_bytes = stage_offset(c, 0, ST_LOGITS) + 4 * stage_bank_bytes(ST_LOGITS);
+    c->w_bytes = stage_offset(c, 0, ST_LOGITS) + c->nbanks * stage_bank_bytes(ST_LOGITS);
     CKC(cudaMalloc(&c->d_w, c->w_bytes));
     CKC(cudaMalloc(&c->d_gamma, 65ull * kDim * sizeof(float)));
     CKC(cudaMalloc(&c->d_rope_cos, 4096ull * 64 * sizeof(int32_t)));
     CKC(cudaMalloc(&c->d_rope_sin, 4096ull * 64 * sizeof(int32_t)));
-    c->kv_bytes = 4ull * c->layers * kLocalHeads * static_cast<size_t>(c->stride) * 320;
+    c->kv_bytes = static_cast<size_t>(c->nbanks) * c->layers * kLocalHeads * static_cast<size_t>(c->stride) * 320;
     CKC(cudaMalloc(&c->d_kv, c->kv_bytes));
     CKC(cudaMemset(c->d_kv, 0, c->kv_bytes));
     CKC(cudaMalloc(&c->d_resid, 2 * kDim * sizeof(float)));  // two buffers for the token kernel
     CKC(cudaMalloc(&c->d_recip, 16));
-    CKC(cudaMalloc(&c->d_partials, 2ull * kPartialBuf * sizeof(float)));  // two buffers for the token kernel
+    // Partials (two buffers for the token kernel) and the synchronisation words
+    // share one allocation, which the ranks of a sharded group map.
+    const size_t partial_bytes = 2ull * kPartialBuf * sizeof(float);
+    CKC(cudaMalloc(&c->d_shared, partial_bytes + kSyncWords * sizeof(unsigned)));
+    c->d_partials = static_cast<float*>(c->d_shared);
+    c->d_sync = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(c->d_shared) + partial_bytes);
+    c->peer_partials[rank] = c->d_partials;
+    c->peer_sync[rank] = c->d_sync;
     CKC(cudaMalloc(&c->d_ao_q, kDim * sizeof(int16_t)));
     CKC(cudaMalloc(&c->d_ao_e, kDim / 32));
     CKC(cudaMalloc(&c->d_ad_q, kFfn * sizeof(int16_t)));
@@ -484,7 +520,6 @@ i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out) {
     CKC(cudaMemset(c->d_err, 0, sizeof(unsigned)));
     CKC(cudaMalloc(&c->d_pos, sizeof(int)));
     CKC(cudaMalloc(&c->d_attn_coef, 128ull * c->stride * sizeof(uint32_t)));
-    CKC(cudaMalloc(&c->d_sync, kSyncWords * sizeof(unsigned)));
     CKC(cudaMemset(c->d_sync, 0, kSyncWords * sizeof(unsigned)));
     CKC(cudaMalloc(&c->d_recips, 80 * sizeof(float)));
     CKC(cudaMalloc(&c->d_scratch, 3ull * kPVocab * sizeof(float)));
@@ -539,11 +574,60 @@ i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out) {
     return I4D_OK;
 }
 
+i4d_status i4d_create(const i4d_config* cfg, i4d_ctx** out) { return create_impl(cfg, 0, 1, out); }
+
+i4d_status i4d_create_shard(const i4d_config* cfg, int rank, int world, i4d_ctx** out) {
+    return create_impl(cfg, rank, world, out);
+}
+
+i4d_status i4d_shard_export(i4d_ctx* c, void* handle, size_t n) {
+    if (!c || !handle || n < I4D_SHARD_HANDLE_BYTES) return c ? fail(c, I4D_ERR_ARG, "bad handle buffer") : I4D_ERR_ARG;
+    static_assert(sizeof(cudaIpcMemHandle_t) <= I4D_SHARD_HANDLE_BYTES, "IPC handle size");
+    CK(cudaSetDevice(c->device));
+    cudaIpcMemHandle_t h;
+    CK(cudaIpcGetMemHandle(&h, c->d_shared));
+    std::memset(handle, 0, I4D_SHARD_HANDLE_BYTES);
+    std::memcpy(handle, &h, sizeof(h));
+    return I4D_OK;
+}
+
+i4d_status i4d_shard_attach(i4d_ctx* c, const void* handles, size_t n) {
+    if (!c || !handles) return c ? fail(c, I4D_ERR_ARG, "null handles") : I4D_ERR_ARG;
+    if (n != static_cast<size_t>(c->world) * I4D_SHARD_HANDLE_BYTES)
+        return fail(c, I4D_ERR_SIZE, "expected %d handles of %d bytes", c->world, I4D_SHARD_HANDLE_BYTES);
+    if (c->attached) return fail(c, I4D_ERR_STATE, "peers already attached");
+    CK(cudaSetDevice(c->device));
+    const size_t partial_bytes = 2ull * kPartialBuf * sizeof(float);
+    for (int p = 0; p < c->world; ++p) {
+        if (p == c->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t*>(handles) + static_cast<size_t>(p) * I4D_SHARD_HANDLE_BYTES, sizeof(h));
+        void* ptr = nullptr;
+        CK(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+        c->peer_base[p] = ptr;
+        c->peer_partials[p] = static_cast<float*>(ptr);
+        c->peer_sync[p] = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ptr) + partial_bytes);
+    }
+    if (c->graph) {
+        cudaGraphExecDestroy(c->graph);
+        c->graph = nullptr;
+    }
+    if (c->graph_dev) {
+        cudaGraphExecDestroy(c->graph_dev);
+        c->graph_dev = nullptr;
+    }
+    c->attached = true;
+    return I4D_OK;
+}
+
 i4d_status i4d_load_bank(i4d_ctx* c, int bank, const void* bytes, size_t n) {
     if (!c || !bytes || bank < 0 || bank > 3) return c ? fail(c, I4D_ERR_ARG, "bad bank or pointer") : I4D_ERR_ARG;
     if (n == I4D_LEGACY_BANK_BYTES)
         return fail(c, I4D_ERR_SIZE, "legacy 891,277,312-byte bank layout is not supported; repack dense");
     if (n != I4D_BANK_BYTES) return fail(c, I4D_ERR_SIZE, "bank image has %zu bytes; expected 865071104", n);
+    if (bank < c->bank0 || bank >= c->bank0 + c->nbanks)
+        return fail(c, I4D_ERR_ARG, "bank %d is not held by this shard (banks %d..%d)", bank, c->bank0,
+                    c->bank0 + c->nbanks - 1);
     CK(cudaSetDevice(c->device));
     if (c->graph) {
         cudaGraphExecDestroy(c->graph);
@@ -562,7 +646,7 @@ i4d_status i4d_load_bank(i4d_ctx* c, int bank, const void* bytes, size_t n) {
             const int st = mode_stage(m);
             RelayoutArgs r;
             r.src = stage + matrix_word_offset(l, m) * 64;
-            r.dst = c->d_w + stage_offset(c, l, st) + static_cast<size_t>(bank) * stage_bank_bytes(st);
+            r.dst = c->d_w + stage_offset(c, l, st) + static_cast<size_t>(bank - c->bank0) * stage_bank_bytes(st);
             r.unit_offset = mode_unit_offset(m);
             r.lit = mode_lit(m);
             k_relayout<<<mode_rows(m) / 32 * r.lit, 256, 0, c->stream>>>(r);
@@ -677,9 +761,10 @@ i4d_status i4d_kv_reset(i4d_ctx* c) {
 }
 
 static i4d_status kv_addr(i4d_ctx* c, int bank, int layer, int lh, int token, size_t* off) {
-    if (bank < 0 || bank > 3 || layer < 0 || layer >= c->layers || lh < 0 || lh > 7 || token < 0 || token >= c->stride)
-        return fail(c, I4D_ERR_ARG, "KV record index out of range");
-    *off = ((((static_cast<size_t>(bank) * c->layers + layer) * kLocalHeads + lh) * c->stride) + token) * 320;
+    if (bank < c->bank0 || bank >= c->bank0 + c->nbanks || layer < 0 || layer >= c->layers || lh < 0 || lh > 7 ||
+        token < 0 || token >= c->stride)
+        return fail(c, I4D_ERR_ARG, "KV record index out of range (or bank not held by this shard)");
+    *off = ((((static_cast<size_t>(bank - c->bank0) * c->layers + layer) * kLocalHeads + lh) * c->stride) + token) * 320;
     return I4D_OK;
 }
 
@@ -758,6 +843,7 @@ i4d_status i4d_decode_token_async(i4d_ctx* c, uint32_t position, const float* re
 
 i4d_status i4d_profile_token(i4d_ctx* c, uint32_t position, const float* residual_in_dev, float* kernel_ms,
                              uint32_t* launches) {
+    if (c && c->world > 1) return fail(c, I4D_ERR_STATE, "not available on a bank shard");
     if (!c || !residual_in_dev || !kernel_ms || !launches) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
     if (!all_loaded(c)) return fail(c, I4D_ERR_STATE, "banks and rope LUT must be loaded before decoding");
     if (position >= static_cast<uint32_t>(c->stride)) return fail(c, I4D_ERR_ARG, "position out of range");
@@ -950,6 +1036,7 @@ i4d_status i4d_linear_bank_noalloc(i4d_ctx* c, const void* superblocks_dev, size
 
 i4d_status i4d_gemv(i4d_ctx* c, int layer, int mode, const int16_t* act_q, const uint8_t* act_e8m0, float* y_out,
                     float* partials_out) {
+    if (c && c->world > 1) return fail(c, I4D_ERR_STATE, "not available on a bank shard");
     if (!c || !act_q || !act_e8m0 || !y_out) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
     if (mode < 0 || mode > 7 || (mode < 7 && (layer < 0 || layer >= c->layers)))
         return fail(c, I4D_ERR_ARG, "bad layer %d / mode %d", layer, mode);
@@ -1020,6 +1107,7 @@ i4d_status i4d_rms_quant(i4d_ctx* c, const float* x, const float* gamma, int16_t
 
 i4d_status i4d_attention(i4d_ctx* c, int layer, uint32_t position, const int32_t* q, const int32_t* k,
                          const int32_t* v, int16_t* out_q, uint8_t* out_e8m0) {
+    if (c && c->world > 1) return fail(c, I4D_ERR_STATE, "not available on a bank shard");
     if (!c || !q || !k || !v || !out_q || !out_e8m0) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
     if (!c->rope_loaded) return fail(c, I4D_ERR_STATE, "rope LUT not loaded");
     if (layer < 0 || layer >= c->layers || position >= static_cast<uint32_t>(c->stride))
@@ -1085,6 +1173,7 @@ i4d_status i4d_expf(i4d_ctx* c, const float* x, float* y, size_t n) {
 
 extern "C" i4d_status i4d_token_breakdown(i4d_ctx* c, uint32_t position, const float* residual_in_dev,
                                           float* us_out, int n_out) {
+    if (c && c->world > 1) return fail(c, I4D_ERR_STATE, "not available on a bank shard");
     if (!c || !residual_in_dev || !us_out || n_out < kTraceSlots) return c ? fail(c, I4D_ERR_ARG, "bad arguments") : I4D_ERR_ARG;
     if (c->flags & I4D_FLAG_STAGED) return fail(c, I4D_ERR_STATE, "breakdown needs the persistent token kernel");
     if (!all_loaded(c)) return fail(c, I4D_ERR_STATE, "banks and rope LUT must be loaded before decoding");
@@ -1115,6 +1204,7 @@ extern "C" i4d_status i4d_token_breakdown(i4d_ctx* c, uint32_t position, const f
 
 extern "C" i4d_status i4d_token_timeline(i4d_ctx* c, uint32_t position, const float* residual_in_dev, int layer,
                                          int detail, uint64_t* out, int max_ctas, int* n_ctas) {
+    if (c && c->world > 1) return fail(c, I4D_ERR_STATE, "not available on a bank shard");
     if (!c || !residual_in_dev || !out || !n_ctas) return c ? fail(c, I4D_ERR_ARG, "bad arguments") : I4D_ERR_ARG;
     if (c->flags & I4D_FLAG_STAGED) return fail(c, I4D_ERR_STATE, "timeline needs the persistent token kernel");
     if (!all_loaded(c)) return fail(c, I4D_ERR_STATE, "banks and rope LUT must be loaded before decoding");

@@ -37,8 +37,9 @@ struct AttnArgs {
     const uint32_t* exp2_q30; // 33-entry LUT
     int log2e_q21;
     int32_t score_scale;      // float_to_q17(1/sqrt(128))
-    uint8_t* kv;              // [4][layers][8][stride][320]
+    uint8_t* kv;              // [banks held][layers][8][stride][320]
     int layers, stride, layer;
+    int bank0;                // first bank whose KV this context holds (bank sharding)
     uint32_t* coef_scratch;   // [32][stride]: c_t | rescale << 31 (fallback paths)
     int16_t* out_q;
     uint8_t* out_e;
@@ -110,7 +111,7 @@ __device__ __forceinline__ int dp2a_hi_us(uint32_t a, uint32_t b, int c) {
 }
 
 __device__ __forceinline__ uint8_t* kv_record(const AttnArgs& a, int head, int token) {
-    const int bank = head / kLocalHeads, lh = head % kLocalHeads;
+    const int bank = head / kLocalHeads - a.bank0, lh = head % kLocalHeads;
     const size_t rec = ((static_cast<size_t>(bank) * a.layers + a.layer) * kLocalHeads + lh) *
                            static_cast<size_t>(a.stride) + static_cast<size_t>(token);
     return a.kv + rec * 320;

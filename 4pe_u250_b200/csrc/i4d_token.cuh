@@ -41,14 +41,17 @@ constexpr int kTokContribBytes = 32768;
 constexpr int kAttnParts = 4;              // 32-dimension parts per head
 constexpr int kAttnItems = kHeads * kAttnParts;
 
-// Global synchronisation words (zeroed by the last CTA at the end of a token).
+// Global synchronisation words.  They only grow, token after token; the
+// epoch word (tokens completed) sets each token's targets.  The host clears
+// them, with the epoch, after a failed step.
 // Stage ordinals: QKV, O, GATE/UP, DOWN of layer l are 4l .. 4l+3, the LM
 // head 4L.
 constexpr int kSyncAbort = 0;
 constexpr int kSyncExit = 1;
 constexpr int kSyncStage = 2;                   // + ordinal: CTAs whose partials of that stage are stored
 constexpr int kSyncAtt = kSyncStage + 4 * 32 + 1;  // + layer: attention items finished
-constexpr int kSyncWords = kSyncAtt + 32;
+constexpr int kSyncEpoch = kSyncAtt + 32;
+constexpr int kSyncWords = kSyncEpoch + 1;
 constexpr int kPartialBuf = 4 * 32256;          // floats of one partial buffer [4 banks][rows]
 
 enum TokStage : int { TS_QKV = 0, TS_O, TS_GU, TS_DOWN, TS_LOGITS };
@@ -59,7 +62,12 @@ struct TokenArgs {
     size_t stage_off[5];       // offset of each stage inside its layer (LOGITS: absolute)
     size_t bank_bytes[5];      // one bank's region of each stage
     int layers;
-    int cpb;                   // CTAs per bank (gridDim.x == 4 * cpb)
+    int cpb;                   // CTAs per bank held (gridDim.x == nbanks * cpb)
+    int bank0, nbanks;         // banks held: [bank0, bank0 + nbanks) (all four without sharding)
+    int world;                 // ranks of the bank-sharded group (1 without sharding)
+    float* peer_partials[4];   // every rank's partial buffers, as mapped here ([rank]; own at [rank])
+    unsigned* peer_sync[4];    // every rank's synchronisation words, as mapped here
+    const unsigned* epoch;     // tokens completed by this context (counter targets are epoch based)
     float* resid;              // [2][4096]: after residual update n, buffer n & 1 (0: token input and output)
     const float* gamma;        // [65][4096]
     float* partials;           // [2][4][32256]: stage ordinal k writes buffer k & 1
@@ -176,12 +184,17 @@ __device__ __forceinline__ bool aborted(const TokenArgs& a) {
 __device__ __forceinline__ void raise_abort(const TokenArgs& a, unsigned code) {
     atomicOr(a.err, code);
     atomicExch(&a.sync[kSyncAbort], 1u);
+    // The other ranks of a sharded group leave their waits too.
+    for (int p = 0; p < a.world; ++p)
+        if (a.peer_sync[p] != a.sync) atomicExch(&a.peer_sync[p][kSyncAbort], 1u);
 }
 
-// Spins (bounded) until *word >= target; false on abort or timeout.
+// Spins (bounded) until the counter *word has reached target; false on
+// abort or timeout.  Counters only grow (mod 2^32), so the comparison is
+// taken on the signed difference.
 __device__ bool wait_counter(const TokenArgs& a, const unsigned* word, unsigned target) {
     for (uint32_t it = 0;; ++it) {
-        if (*reinterpret_cast<const volatile unsigned*>(word) >= target) {
+        if (static_cast<int>(*reinterpret_cast<const volatile unsigned*>(word) - target) >= 0) {
             __threadfence();
             return true;
         }
@@ -216,6 +229,8 @@ struct StageDesc {
     int u0, u1;           // this CTA's units in its bank
     int bank;
     int cbase;            // global copy sequence number of the stage's first copy
+    unsigned tgt_stage;   // stage counter value once every CTA of every rank arrived (this token)
+    unsigned tgt_att;     // attention counter value once this rank's items finished (this token)
 };
 
 __device__ __forceinline__ int stage_ordinal(int st, int layer) { return st == TS_LOGITS ? 4 * layer : 4 * layer + st; }
@@ -543,7 +558,11 @@ __device__ __forceinline__ void tok_reduce_units(const TokenArgs& a, const TokSm
         float acc = __fadd_rn(0.0f, cb[lane]);
 #pragma unroll 8
         for (int q = 1; q < G; ++q) acc = __fadd_rn(acc, cb[q * STRIDE + lane]);
-        partials[static_cast<size_t>(d.bank) * rows_total + static_cast<size_t>(d.u0 + u) * 32 + lane] = acc;
+        const size_t off = static_cast<size_t>(d.bank) * rows_total + static_cast<size_t>(d.u0 + u) * 32 + lane;
+        partials[off] = acc;
+        // Bank sharding: every rank receives every bank's partials.
+        for (int p = 0; p < a.world; ++p)
+            if (a.peer_partials[p] != a.partials) a.peer_partials[p][(stage_ordinal(d.st, d.layer) & 1) * kPartialBuf + off] = acc;
         __threadfence_block();
         __syncwarp();
         if (lane == 0) *reinterpret_cast<volatile int*>(&s.slot_ok[us]) = u + NU;
@@ -571,8 +590,8 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     // Input readiness: the previous stage's partials from every CTA, or the
     // attention items of this layer.
     if (tid == 0) {
-        if (d.st == TS_O) wait_counter(a, &a.sync[kSyncAtt + d.layer], kAttnItems);
-        else if (ord > 0) wait_counter(a, &a.sync[kSyncStage + ord - 1], gridDim.x);
+        if (d.st == TS_O) wait_counter(a, &a.sync[kSyncAtt + d.layer], d.tgt_att);
+        else if (ord > 0) wait_counter(a, &a.sync[kSyncStage + ord - 1], d.tgt_stage);
         s.next[0] = s.next[1] = s.next[2] = s.next[3] = 0;
     }
     if (tid < 8) {
@@ -635,8 +654,11 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     const long long t_epi = clock64();
     if (tid == 0) {
         tl_mark<TR>(a, tl_layer, 4 * d.st + 3);
-        __threadfence();
-        atomicAdd(&a.sync[kSyncStage + ord], 1u);
+        // Arrive on every rank's counter (one rank: just this one); the
+        // system-scope fence covers the partials stored to peer memory.
+        if (a.world > 1) __threadfence_system();
+        else __threadfence();
+        for (int p = 0; p < a.world; ++p) atomicAdd(&a.peer_sync[p][kSyncStage + ord], 1u);
         trace_add<TR>(a, TR_WAIT + d.st, t_ready - t_begin);
         trace_add<TR>(a, TR_PROLOGUE + d.st, t_loop - t_ready);
         trace_add<TR>(a, TR_CHUNKS + d.st, t_epi - t_loop);
@@ -645,10 +667,10 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
 
 // Logits: every CTA combines a slice of the LM-head rows once all partials
 // are stored ((p0+p1)+(p2+p3), emulator sharded_gemv_4pe).
-__device__ __noinline__ void tok_logits(const TokenArgs& a, int cw, int lane) {
+__device__ __noinline__ void tok_logits(const TokenArgs& a, unsigned tgt_stage, int cw, int lane) {
     const int tid = cw * 32 + lane;
     const int ord = stage_ordinal(TS_LOGITS, a.layers);
-    if (tid == 0) wait_counter(a, &a.sync[kSyncStage + ord], gridDim.x);
+    if (tid == 0) wait_counter(a, &a.sync[kSyncStage + ord], tgt_stage);
     tok_bar();
     const float* P = stage_partials(a, ord);
     const int r0 = static_cast<int>((static_cast<long long>(blockIdx.x) * kPVocab) / gridDim.x);
@@ -701,7 +723,8 @@ static_assert(2 * kTile * 320 + 320 + kTile * 8 + 144 + kTile * 32 * 4 + 2 * 128
 // then runs exactly, one lane per dimension, over those terms.
 template <bool TR>
 __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s, int layer, int item, int cw,
-                                           int lane) {
+                                           int lane,
+                                           unsigned tgt_qkv) {
     const unsigned FULL = 0xffffffffu;
     const uint32_t M30 = (1u << 30) - 1u;
     AttnArgs a = ta.attn;
@@ -733,7 +756,7 @@ __device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s
         fence_proxy_async_smem();
         mbar_arrive_expect_tx(&s.abar[0], cnt * 320);
         bulk_g2s(S.tile[0], head_base, cnt * 320, &s.abar[0]);
-        wait_counter(ta, &ta.sync[kSyncStage + stage_ordinal(TS_QKV, layer)], gridDim.x);
+        wait_counter(ta, &ta.sync[kSyncStage + stage_ordinal(TS_QKV, layer)], tgt_qkv);
     }
     tok_bar();
     const long long t_a1 = clock64();
@@ -1006,7 +1029,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
     extern __shared__ __align__(128) uint8_t tok_smem_raw[];
     TokSmem s = tok_carve(tok_smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bank = blockIdx.x / a.cpb, c = blockIdx.x % a.cpb;
+    const int lbank = blockIdx.x / a.cpb, c = blockIdx.x % a.cpb;  // bank index among the banks held
     auto urange = [&](int st, int* u0, int* u1) {
         const int U = stage_units(st);
         *u0 = static_cast<int>((static_cast<long long>(c) * U) / a.cpb);
@@ -1031,7 +1054,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
             // Weights are read once per token: evict them first, so the
             // partials, residual and counters of the stage handoffs stay in L2.
             const uint64_t pol_first = l2_policy_evict_first();
-            cursor_begin(a, bank, c, cur);
+            cursor_begin(a, lbank, c, cur);
             while (cursor_valid(a, cur)) {
                 const int cnt = min(kTokCpc, cur.n - cur.i);
                 if (issued >= kTokSlots) {
@@ -1050,7 +1073,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
                     slot = 0;
                     phase ^= 1u;
                 }
-                cursor_advance(a, bank, c, cur);
+                cursor_advance(a, lbank, c, cur);
             }
             // Never leave with copies in flight: wait for the last ones to land.
             for (int k = 0; k < kTokSlots && k < issued; ++k) {
@@ -1072,7 +1095,13 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
     const int tid = cw * 32 + lane;
     const long long t_kernel = clock64();
     StageDesc d;
-    d.bank = bank;
+    d.bank = a.bank0 + lbank;
+    // Counter targets of this token: counters only grow, by world * grid
+    // arrivals per stage and by this rank's attention items per layer.
+    const unsigned epoch = *reinterpret_cast<const volatile unsigned*>(a.epoch);
+    const int att_items = kAttnItems / a.world;
+    d.tgt_stage = (epoch + 1u) * static_cast<unsigned>(a.world) * gridDim.x;
+    d.tgt_att = (epoch + 1u) * static_cast<unsigned>(att_items);
     d.cbase = 0;
     for (int l = 0; l <= a.layers; ++l) {
         for (int st = TS_QKV; st <= TS_DOWN; ++st) {
@@ -1085,22 +1114,24 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
             else tok_gemv_stage<4, TR>(a, s, d, cw, lane);
             d.cbase += ((d.u1 - d.u0) * stage_chunks(stage) + kTokCpc - 1) / kTokCpc;
             if (stage == TS_QKV && l < a.layers) {
-                if (blockIdx.x < kAttnItems) tok_attention<TR>(a, s, l, blockIdx.x, cw, lane);
+                if (blockIdx.x < att_items)
+                    tok_attention<TR>(a, s, l, a.bank0 * kLocalHeads * kAttnParts + blockIdx.x, cw, lane, d.tgt_stage);
                 tok_bar();
             }
         }
     }
-    tok_logits(a, cw, lane);
-    // The last CTA to finish clears the token's synchronisation words.
+    tok_logits(a, d.tgt_stage, cw, lane);
+    // The last CTA to finish advances the epoch: the counters are never
+    // cleared (a faster rank may already be arriving for the next token), the
+    // next token's targets are one token's arrivals higher.
     tok_bar();
     if (tid == 0) {
         trace_add<TR>(a, TR_TOTAL, clock64() - t_kernel);
         __threadfence();
         const unsigned old = atomicAdd(&a.sync[kSyncExit], 1u);
-        if (old + 1 == gridDim.x) {
-            for (int i = kSyncStage; i < kSyncWords; ++i) a.sync[i] = 0;
+        if (old + 1 == (epoch + 1u) * gridDim.x) {
             __threadfence();
-            a.sync[kSyncExit] = 0;
+            atomicAdd(const_cast<unsigned*>(a.epoch), 1u);
         }
     }
 }

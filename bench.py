@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--cpu-steps", type=int, default=6)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--soak", type=int, default=400, help="untimed steps before timing (clock steady state)")
+    ap.add_argument("--shard", action="store_true",
+                    help="N GPUs (2 or 4) decode one stream as one bank-sharded group instead of N replicas")
     return ap.parse_args()
 
 
@@ -191,10 +193,11 @@ def run_reference(args, world, rank):
 
 
 def workload_config(args, world):
+    par = (f"bank-shard{world}" if args.shard else f"replicas{world}") if world > 1 else "1gpu"
     return {"workload": "config3: full 32-layer INT4 Llama-2-7B decode, 16-token prompt then greedy, "
                         "KV capacity 2048, seed 2",
             "layers": 32, "kv_capacity": args.kv_capacity, "positions": [args.warmup, args.warmup + args.steps - 1],
-            "parallelism": f"replicas{world}" if world > 1 else "1gpu",
+            "parallelism": par,
             "l2": "weights 3.46 GB/token exceed the 126 MB L2 (no flush needed)"}
 
 
@@ -220,12 +223,20 @@ def main():
     total = args.warmup + args.steps
     assert total <= args.kv_capacity
 
+    shard = args.shard and world > 1
+    if shard and world not in (2, 4):
+        raise SystemExit("--shard needs 2 or 4 GPUs")
     banks = syn.model_banks(32, args.seed)
     emb = syn.embeddings(args.seed)
     lut = F.generate_rope_lut()
-    ctx = pkg.Context(device=local, num_layers=32, kv_capacity=args.kv_capacity)
+    if shard:
+        ctx = pkg.Context(device=local, num_layers=32, kv_capacity=args.kv_capacity, rank=rank, world=world)
+    else:
+        ctx = pkg.Context(device=local, num_layers=32, kv_capacity=args.kv_capacity)
     ctx.load_banks(banks)
     ctx.load_rope(lut)
+    if shard:
+        ctx.attach_peers()
     stream = torch.cuda.ExternalStream(ctx.stream_handle())
     prompt = np.random.default_rng(args.seed).integers(3, 32000, size=PROMPT).tolist()
 
@@ -282,32 +293,41 @@ def main():
 
     # ---- device time of the token kernel alone (events around the launch) ----
     mid = args.warmup + args.steps // 2
-    tok_ms = []
-    for _ in range(5):
-        p = ctx.profile_token(mid, row(tokens[mid]))
-        tok_ms.append(p["token"][0])
-    tok_ms = statistics.median(tok_ms)
-    breakdown = ctx.token_breakdown(mid, row(tokens[mid]))
+    if shard:  # the per-kernel hooks run one context alone; use the replay time
+        tok_ms = dev_ms / args.steps
+        breakdown = {}
+    else:
+        tok_ms = []
+        for _ in range(5):
+            p = ctx.profile_token(mid, row(tokens[mid]))
+            tok_ms.append(p["token"][0])
+        tok_ms = statistics.median(tok_ms)
+        breakdown = ctx.token_breakdown(mid, row(tokens[mid]))
     peak, peak_kind = measured_peak()
-    achieved = F.token_bytes(mid) / (tok_ms * 1e-3) / 1e9
+    # A shard streams its banks' share of the bytes: per-GPU bandwidth.
+    achieved = F.token_bytes(mid) / (world if shard else 1) / (tok_ms * 1e-3) / 1e9
     traffic = committed_traffic()
 
-    value = world * args.steps / (dev_ms * 1e-3)
-    e2e = world * args.steps / (e2e_ms * 1e-3)
+    streams = 1 if shard else world  # a sharded group decodes one stream
+    value = streams * args.steps / (dev_ms * 1e-3)
+    e2e = streams * args.steps / (e2e_ms * 1e-3)
     launches_per_step = 2  # k_set_pos + k_token
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int4xint14/fp32", "data": "synthetic",
-        "config": workload_config(args, world),
+        "scaling": "strong" if shard else "weak", "vs_baseline": None, "dtype": "int4xint14/fp32",
+        "data": "synthetic", "config": workload_config(args, world),
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4096 * 4 + 4,
                 "d2h_bytes_per_step": F.PADDED_VOCAB * 4 + 4096 * 4 + 4, "ms_per_step": e2e_ms / args.steps},
-        "roofline": {"bound": "hbm", "kernel": "k_token (persistent decode step, 1 launch per token)",
+        "roofline": {"bound": "hbm", "kernel": "k_token (persistent decode step, 1 launch per token" +
+                               (f" on each of {world} bank shards; achieved = per-GPU share of the bytes)" if shard
+                                else ")"),
                      "achieved": achieved, "peak": peak,
                      "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback", "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic["bytes_per_launch"] if traffic else None,
-                     "algorithmic_bytes_per_launch": F.token_bytes(mid), "kernel_ms": tok_ms},
+                     "traffic": (traffic["bytes_per_launch"] if traffic and not shard else None),
+                     "algorithmic_bytes_per_launch": F.token_bytes(mid) // (world if shard else 1),
+                     "kernel_ms": tok_ms},
         "token_roofline": {"bytes_per_token": F.token_bytes(mid), "achieved_gbs":
                            F.token_bytes(mid) / (dev_ms / args.steps * 1e-3) / 1e9,
                            "frac": F.token_bytes(mid) / (dev_ms / args.steps * 1e-3) / 1e9 / peak},

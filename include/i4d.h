@@ -77,6 +77,31 @@ void i4d_destroy(i4d_ctx* ctx);
 /* Message of the last failing call on ctx (never NULL). */
 const char* i4d_last_error(const i4d_ctx* ctx);
 
+/* ---- Bank sharding across GPUs (one process per GPU) ----
+ * The reference's four processing elements each hold one bank image and
+ * exchange bank partials through its pair reducers and finalizer
+ * (int4_linear_controller.cpp:1339-1439, int4_decoder_multikernel.hpp:11-65).
+ * Here `world` contexts (2 or 4, one per GPU) split the banks: rank r holds
+ * banks [r*4/world, (r+1)*4/world) and runs attention for their heads with
+ * their KV records; the token kernel stores every bank partial into every
+ * rank's memory over NVLink and counts arrivals in every rank's counters, so
+ * each rank ends the step with the full residual and all logits, bit-exact
+ * with a single context.  All ranks must decode the same positions and
+ * inputs, step by step.
+ *
+ * i4d_create_shard: as i4d_create, for rank `rank` of `world` (world 1 is
+ * i4d_create).  Only the banks it holds may be loaded.
+ * i4d_shard_export: writes this context's handle (I4D_SHARD_HANDLE_BYTES,
+ * opaque) for the other ranks.
+ * i4d_shard_attach: takes all ranks' handles in rank order (world *
+ * I4D_SHARD_HANDLE_BYTES bytes) and maps the peers; decoding needs it.
+ * The per-kernel measurement hooks, i4d_gemv and i4d_attention are not
+ * available on a shard (I4D_ERR_STATE). */
+#define I4D_SHARD_HANDLE_BYTES 64
+i4d_status i4d_create_shard(const i4d_config* cfg, int rank, int world, i4d_ctx** out);
+i4d_status i4d_shard_export(i4d_ctx* ctx, void* handle, size_t n);
+i4d_status i4d_shard_attach(i4d_ctx* ctx, const void* handles, size_t n);
+
 /* Loads one unchanged bank image (n must be I4D_BANK_BYTES; the legacy
  * 891,277,312-byte layout is rejected with I4D_ERR_SIZE as
  * decode_host.cpp:1218-1227 detects it).  The image is re-tiled on the device
