@@ -37,7 +37,8 @@ constexpr int kTokCpc = 4;                 // chunks per bulk copy (16,896 B: st
 constexpr int kTokSlots = kTokRing / kTokCpc;  // ring slots, one copy each
 constexpr int kTokSlotBytes = kTokCpc * kChunkBytes;
 constexpr int kTokUnion = 55296;           // GEMV activations + contributions, or attention scratch
-constexpr int kTokContribBytes = 32768;
+constexpr int kTokContribBytes = 50688;     // contribution slots: 12 units of 4 chunks, 4 of DOWN
+constexpr int kTokMaxSlots = 16;
 constexpr int kAttnParts = 4;              // 32-dimension parts per head
 constexpr int kAttnItems = kHeads * kAttnParts;
 
@@ -105,8 +106,10 @@ enum TraceSlot : int {
 // layer; 24 + s: copies of stage s already landed when its chunk loop
 // starts (a count, not a time); 29 + s: copies of stage s; 34 + 8w + k:
 // consumer warp w in the QKV stage: k < 6 time of its k-th unit grab, 6 loop
-// exit, 7 number of grabs.
-constexpr int kTlEvents = 34 + 8 * 16;
+// exit, 7 number of grabs; 162 + q: GATE/UP stage, time the producer issued
+// copy q of the stage (q < 24); 186 + q: time the first compute warp found
+// copy q landed.
+constexpr int kTlEvents = 34 + 8 * 16 + 48;
 
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
@@ -140,15 +143,15 @@ struct TokSmem {
     uint64_t* abar;      // [2] attention tile barriers
     uint8_t* uni;        // union region
     int* next;           // dynamic chunk counter
-    int* unit_cnt;       // [8]: chunk arrivals per contribution slot in this stage
-    int* slot_ok;        // [8]
+    int* unit_cnt;       // [kTokMaxSlots]: chunk arrivals per contribution slot in this stage
+    int* slot_ok;        // [kTokMaxSlots]: first unit index the slot may take
     int* fin;            // [kFinMax + 2]
     int* flag;           // [4] misc
     int* issued;         // [kTokSlots]: copy sequence number last issued into each slot
 };
 
 __host__ __device__ inline size_t tok_smem_bytes() {
-    return static_cast<size_t>(kTokRing) * kChunkBytes + 2 * kTokSlots * 8 + 16 + kTokUnion + 16 + 64 +
+    return static_cast<size_t>(kTokRing) * kChunkBytes + 2 * kTokSlots * 8 + 16 + kTokUnion + 16 + 2 * kTokMaxSlots * 4 +
            align16((kFinMax + 2) * 4) + 16 + align16(kTokSlots * 4);
 }
 
@@ -165,8 +168,8 @@ __device__ __forceinline__ TokSmem tok_carve(uint8_t* p) {
     s.next = reinterpret_cast<int*>(p);
     p += 16;
     s.unit_cnt = reinterpret_cast<int*>(p);
-    s.slot_ok = s.unit_cnt + 8;
-    p += 64;
+    s.slot_ok = s.unit_cnt + kTokMaxSlots;
+    p += 2 * kTokMaxSlots * 4;
     s.fin = reinterpret_cast<int*>(p);
     p += align16((kFinMax + 2) * 4);
     s.flag = reinterpret_cast<int*>(p);
@@ -376,8 +379,8 @@ __device__ __forceinline__ void tok_wait_slot(const TokenArgs& a, const TokSmem&
 }
 
 template <int C>
-constexpr int kRowNU = (kTokContribBytes / (C * 8 * 128) > 8 ? 8 : kTokContribBytes / (C * 8 * 128)) / kTokRedWarps *
-                       kTokRedWarps;
+constexpr int kRowNU = (kTokContribBytes / (C * 8 * 128) > kTokMaxSlots ? kTokMaxSlots : kTokContribBytes / (C * 8 * 128)) /
+                       kTokRedWarps * kTokRedWarps;
 
 struct WarpTimes {
     long long data = 0, slot = 0, comp = 0, chain = 0;
@@ -455,7 +458,8 @@ constexpr int kColContribStride = 33;
 // Contribution slots: a multiple of the reducer count, so that every slot is
 // owned by one reducer, which waits on its barrier phases strictly in order
 // (a parity wait cannot tell phases two apart).
-constexpr int kColNU = kTokContribBytes / (32 * kColContribStride * 4) / kTokRedWarps * kTokRedWarps;  // 6
+constexpr int kColNU = kTokContribBytes / (32 * kColContribStride * 4) / kTokRedWarps * kTokRedWarps;  // 12
+static_assert(kColNU <= kTokMaxSlots, "contribution slots");
 
 template <bool TR>
 __device__ __forceinline__ void tok_chunks_cols(const TokenArgs& a, const TokSmem& s, const StageDesc& d,
@@ -489,6 +493,8 @@ __device__ __forceinline__ void tok_chunks_cols(const TokenArgs& a, const TokSme
         const int cp = d.cbase + u;  // one copy per unit
         const int slot = cp % kTokSlots;
         tok_wait_copy(a, s, cp, slot);
+        if (TR && lane == 0 && a.timeline && d.st == TS_GU && d.layer == a.tl_layer && u < 24)
+            atomicCAS(&a.timeline[blockIdx.x * kTlEvents + 186 + u], 0ull, global_ns());
         const uint8_t* ch = s.ring + static_cast<size_t>(slot) * kTokSlotBytes + j * kChunkBytes;
         uint4 wv[8];
 #pragma unroll
@@ -555,15 +561,27 @@ __device__ __forceinline__ void tok_reduce_units(const TokenArgs& a, const TokSm
         }
         __threadfence_block();
         const float* cb = contrib + us * G * STRIDE;
-        float acc = __fadd_rn(0.0f, cb[lane]);
-#pragma unroll 8
-        for (int q = 1; q < G; ++q) acc = __fadd_rn(acc, cb[q * STRIDE + lane]);
+        // All of a batch's loads are in flight before the dependent adds.
+        constexpr int kBatch = G <= 32 ? G : (G + 1) / 2;
+        float acc = 0.0f;
+#pragma unroll
+        for (int q0 = 0; q0 < G; q0 += kBatch) {
+            float v[kBatch];
+#pragma unroll
+            for (int q = 0; q < kBatch; ++q) v[q] = q0 + q < G ? cb[(q0 + q) * STRIDE + lane] : 0.0f;
+#pragma unroll
+            for (int q = 0; q < kBatch; ++q)
+                if (q0 + q < G) acc = __fadd_rn(acc, v[q]);
+        }
         const size_t off = static_cast<size_t>(d.bank) * rows_total + static_cast<size_t>(d.u0 + u) * 32 + lane;
         partials[off] = acc;
         // Bank sharding: every rank receives every bank's partials.
         for (int p = 0; p < a.world; ++p)
             if (a.peer_partials[p] != a.partials) a.peer_partials[p][(stage_ordinal(d.st, d.layer) & 1) * kPartialBuf + off] = acc;
-        __threadfence_block();
+        // Every lane has consumed its contribution loads (acc depends on
+        // them), so the slot may be reused.  No fence here: one would also
+        // wait for the partial store above to reach L2; the stage-end CTA
+        // barrier and thread 0's fence publish the partials.
         __syncwarp();
         if (lane == 0) *reinterpret_cast<volatile int*>(&s.slot_ok[us]) = u + NU;
     }
@@ -573,8 +591,10 @@ template <int C, bool TR>
 __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s, const StageDesc& d, int cw,
                                             int lane) {
     constexpr int G = C * 8;
-    constexpr int NU = kTokContribBytes / (G * 128) > 8 ? 8 : kTokContribBytes / (G * 128);
-    static_assert(NU >= 2, "contribution slots");
+    static_assert(kRowNU<C> >= 2 && kColNU >= 2, "contribution slots");
+    static_assert((G * 72 + 15) / 16 * 16 +
+                      (C == 4 ? kColNU * 32 * kColContribStride * 4 : kRowNU<C> * G * 128) <= kTokUnion,
+                  "union region");
     LinearSmem ls;
     ls.act_hi = reinterpret_cast<int8_t*>(s.uni);
     ls.act_lo = s.uni + G * 32;
@@ -594,7 +614,7 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
         else if (ord > 0) wait_counter(a, &a.sync[kSyncStage + ord - 1], d.tgt_stage);
         s.next[0] = s.next[1] = s.next[2] = s.next[3] = 0;
     }
-    if (tid < 8) {
+    if (tid < kTokMaxSlots) {
         s.unit_cnt[tid] = 0;  // chunk arrivals per contribution slot, this stage
         s.slot_ok[tid] = tid;
     }
@@ -1063,6 +1083,8 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
                     if (TR && a.trace) trace_add<TR>(a, TR_RING_FULL, clock64() - t0);
                 }
                 if (cur.i == 0 && cur.st == TS_QKV) tl_mark<TR>(a, cur.l, 23);
+                if (TR && a.timeline && cur.st == TS_GU && cur.l == a.tl_layer && cur.i / kTokCpc < 24)
+                    a.timeline[blockIdx.x * kTlEvents + 162 + cur.i / kTokCpc] = global_ns();
                 publish_issued(&s.issued[slot], issued);
                 mbar_arrive_expect_tx(&s.full[slot], cnt * kChunkBytes);
                 bulk_g2s_hint(s.ring + static_cast<size_t>(slot) * kTokSlotBytes,

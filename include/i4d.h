@@ -172,8 +172,9 @@ i4d_status i4d_token_breakdown(i4d_ctx* ctx, uint32_t position, const float* res
  * the layer; then counts, not times: 24+s copies of stage s already landed
  * when its chunk loop starts, 29+s copies of stage s; 34+8w+k for consumer
  * warp w in the QKV stage: k < 6 the time of its k-th unit grab, 6 its loop
- * exit, 7 its number of grabs.  out holds max_ctas x 162 values; *n_ctas
- * receives the grid size.
+ * exit, 7 its number of grabs; 162+q / 186+q (q < 24) the times copy q of
+ * the GATE/UP stage was issued by the producer / found landed by a compute
+ * warp.  out holds max_ctas x 210 values; *n_ctas receives the grid size.
  * No reference counterpart. */
 i4d_status i4d_token_timeline(i4d_ctx* ctx, uint32_t position, const float* residual_in_dev, int layer,
                               int detail, uint64_t* out, int max_ctas, int* n_ctas);
