@@ -33,6 +33,7 @@ EXPORTS = [
     "i4d_attention", "i4d_swiglu_quant", "i4d_expf", "i4d_decode_token_async", "i4d_stream",
     "i4d_profile_token", "i4d_token_breakdown", "i4d_linear_bank_noalloc",
     "i4d_token_timeline", "i4d_create_shard", "i4d_shard_export", "i4d_shard_attach",
+    "i4d_decode_greedy", "i4d_argmax",
 ]
 
 _STAGES = ["qkv", "o", "gu", "down", "logits"]
@@ -103,6 +104,8 @@ def load_library():
         "i4d_create_shard": [P, ctypes.c_int, ctypes.c_int, P],
         "i4d_shard_export": [P, P, ctypes.c_size_t],
         "i4d_shard_attach": [P, P, ctypes.c_size_t],
+        "i4d_decode_greedy": [P, ctypes.c_uint32, ctypes.c_int32, P, P],
+        "i4d_argmax": [P, P, ctypes.c_size_t, P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -214,6 +217,20 @@ class Context:
         res = np.empty(formats.DIM, dtype=np.float32) if want_residual else None
         self._check(self._L.i4d_decode_token(self._h, position, x.ctypes.data, logits.ctypes.data, _ptr(res)))
         return (logits, res) if want_residual else logits
+
+    def decode_greedy(self, position, token_id, want_logits=False):
+        """One greedy step from a token id (embeddings loaded): (next id, logits or None)."""
+        nxt = ctypes.c_int32(0)
+        logits = np.empty(formats.PADDED_VOCAB, dtype=np.float32) if want_logits else None
+        self._check(self._L.i4d_decode_greedy(self._h, position, int(token_id), ctypes.byref(nxt), _ptr(logits)))
+        return nxt.value, logits
+
+    def argmax(self, logits):
+        """The device argmax of i4d_decode_greedy over a host array."""
+        x = np.ascontiguousarray(logits, dtype=np.float32)
+        idx = ctypes.c_int32(0)
+        self._check(self._L.i4d_argmax(self._h, x.ctypes.data, x.size, ctypes.byref(idx)))
+        return idx.value
 
     def decode_token_async(self, position, residual_in_dev_ptr, logits_out_dev_ptr):
         """Enqueue one step on device pointers (e.g. torch tensor data_ptr())."""

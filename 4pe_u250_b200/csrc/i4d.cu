@@ -122,6 +122,8 @@ struct i4d_ctx {
     unsigned* d_counters = nullptr;
     unsigned* d_err = nullptr;
     int* d_pos = nullptr;
+    int* d_tok = nullptr;                    // greedy: input token id
+    unsigned long long* d_argmax = nullptr;  // greedy: argmax key of the step's logits
     uint32_t* d_attn_coef = nullptr;  // [128][stride] attention coefficients
     unsigned* d_sync = nullptr;       // persistent-kernel synchronisation words
     float* d_recips = nullptr;        // [65] RMS reciprocal of every norm of a token
@@ -131,11 +133,14 @@ struct i4d_ctx {
     float* h_resid_out = nullptr;
     float* h_logits = nullptr;
     int* h_pos = nullptr;
+    int* h_tok = nullptr;
+    unsigned long long* h_argmax = nullptr;
     unsigned* h_err = nullptr;
     bool bank_loaded[4] = {false, false, false, false};
     bool rope_loaded = false;
     cudaGraphExec_t graph = nullptr;       // H2D + token kernels + D2H
     cudaGraphExec_t graph_dev = nullptr;   // token kernels only
+    cudaGraphExec_t graph_greedy = nullptr;  // token id in, next token id out
     // profiling: when set, enqueue_token brackets every kernel with events
     cudaEvent_t prof_ev[2 * 256] = {};
     int prof_class[256] = {};
@@ -286,6 +291,9 @@ TokenArgs token_args(i4d_ctx* c) {
         t.peer_sync[p] = c->peer_sync[p];
     }
     t.epoch = c->d_sync + kSyncEpoch;
+    t.emb = nullptr;
+    t.token_in = nullptr;
+    t.argmax = nullptr;
     t.resid = c->d_resid;
     t.gamma = c->d_gamma;
     t.partials = c->d_partials;
@@ -303,7 +311,7 @@ TokenArgs token_args(i4d_ctx* c) {
 }
 
 // One token as a single cooperative launch of the persistent kernel.
-cudaError_t launch_token(i4d_ctx* c) {
+cudaError_t launch_token_with(i4d_ctx* c, const TokenArgs& t) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(c->nbanks * c->cpb);
     cfg.blockDim = dim3(kTokThreads);
@@ -315,8 +323,25 @@ cudaError_t launch_token(i4d_ctx* c) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     // The measurement hooks run the instantiation with cycle counters and stamps.
-    if (c->d_trace || (c->d_timeline && c->tl_detail)) return cudaLaunchKernelEx(&cfg, k_token<true>, token_args(c));
-    return cudaLaunchKernelEx(&cfg, k_token<false>, token_args(c));
+    if (c->d_trace || (c->d_timeline && c->tl_detail)) return cudaLaunchKernelEx(&cfg, k_token<true>, t);
+    return cudaLaunchKernelEx(&cfg, k_token<false>, t);
+}
+
+cudaError_t launch_token(i4d_ctx* c) { return launch_token_with(c, token_args(c)); }
+
+// Greedy step: H2D position + token id, the token kernel with the embedding
+// lookup and argmax, D2H argmax key + error word.
+i4d_status enqueue_greedy(i4d_ctx* c) {
+    CK(cudaMemcpyAsync(c->d_pos, c->h_pos, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->d_tok, c->h_tok, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    TokenArgs t = token_args(c);
+    t.emb = c->d_emb;
+    t.token_in = c->d_tok;
+    t.argmax = c->d_argmax;
+    CK(launch_token_with(c, t));
+    CK(cudaMemcpyAsync(c->h_argmax, c->d_argmax, sizeof(unsigned long long), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream));
+    return I4D_OK;
 }
 
 // The kernels of one token (position and residual already in device memory).
@@ -422,16 +447,18 @@ void i4d_destroy(i4d_ctx* c) {
     cudaSetDevice(c->device);
     if (c->graph) cudaGraphExecDestroy(c->graph);
     if (c->graph_dev) cudaGraphExecDestroy(c->graph_dev);
+    if (c->graph_greedy) cudaGraphExecDestroy(c->graph_greedy);
     for (cudaEvent_t ev : c->prof_ev)
         if (ev) cudaEventDestroy(ev);
     for (void* p : c->peer_base)
         if (p) cudaIpcCloseMemHandle(p);
     void* dev[] = {c->d_w, c->d_gamma, c->d_rope_cos, c->d_rope_sin, c->d_exp2, c->d_expf_slots, c->d_kv,
                    c->d_emb, c->d_resid, c->d_recip, c->d_shared, c->d_ao_q, c->d_ao_e, c->d_ad_q,
-                   c->d_ad_e, c->d_logits, c->d_counters, c->d_err, c->d_pos, c->d_scratch, c->d_attn_coef, c->d_recips, c->d_trace};
+                   c->d_ad_e, c->d_logits, c->d_counters, c->d_err, c->d_pos, c->d_scratch, c->d_attn_coef, c->d_recips, c->d_trace,
+                   c->d_tok, c->d_argmax};
     for (void* p : dev)
         if (p) cudaFree(p);
-    void* host[] = {c->h_resid_in, c->h_resid_out, c->h_logits, c->h_pos, c->h_err};
+    void* host[] = {c->h_resid_in, c->h_resid_out, c->h_logits, c->h_pos, c->h_err, c->h_tok, c->h_argmax};
     for (void* p : host)
         if (p) cudaFreeHost(p);
     if (c->stream) cudaStreamDestroy(c->stream);
@@ -519,6 +546,8 @@ static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ct
     CKC(cudaMalloc(&c->d_err, sizeof(unsigned)));
     CKC(cudaMemset(c->d_err, 0, sizeof(unsigned)));
     CKC(cudaMalloc(&c->d_pos, sizeof(int)));
+    CKC(cudaMalloc(&c->d_tok, sizeof(int)));
+    CKC(cudaMalloc(&c->d_argmax, sizeof(unsigned long long)));
     CKC(cudaMalloc(&c->d_attn_coef, 128ull * c->stride * sizeof(uint32_t)));
     CKC(cudaMemset(c->d_sync, 0, kSyncWords * sizeof(unsigned)));
     CKC(cudaMalloc(&c->d_recips, 80 * sizeof(float)));
@@ -527,6 +556,8 @@ static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ct
     CKC(cudaMallocHost(&c->h_resid_out, kDim * sizeof(float)));
     CKC(cudaMallocHost(&c->h_logits, kPVocab * sizeof(float)));
     CKC(cudaMallocHost(&c->h_pos, sizeof(int)));
+    CKC(cudaMallocHost(&c->h_tok, sizeof(int)));
+    CKC(cudaMallocHost(&c->h_argmax, sizeof(unsigned long long)));
     CKC(cudaMallocHost(&c->h_err, sizeof(unsigned)));
 
     // exp2 LUT of the online softmax: round(2^(30 + i/32)), and log2(e) in
@@ -534,7 +565,7 @@ static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ct
     uint32_t lut[33];
     for (int i = 0; i <= 32; ++i) lut[i] = static_cast<uint32_t>(llroundl(exp2l(30.0L + i / 32.0L)));
     CKC(cudaMalloc(&c->d_exp2, sizeof(lut)));
-    CKC(cudaMemcpy(c->d_exp2, lut, sizeof(lut), cudaMemcpyHostToDevice));
+    CKC(cudaMemcpyAsync(c->d_exp2, lut, sizeof(lut), cudaMemcpyHostToDevice, c->stream));
     c->log2e_q21 = static_cast<int>(std::nearbyint(1.4426950408889634 * static_cast<double>(1 << 21)));
     c->score_scale = host_float_to_q17(0.08838834764831845f);
 
@@ -566,7 +597,8 @@ static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ct
         }
     }
     CKC(cudaMalloc(&c->d_expf_slots, buckets.size() * sizeof(uint32_t)));
-    CKC(cudaMemcpy(c->d_expf_slots, buckets.data(), buckets.size() * sizeof(uint32_t), cudaMemcpyHostToDevice));
+    CKC(cudaMemcpyAsync(c->d_expf_slots, buckets.data(), buckets.size() * sizeof(uint32_t), cudaMemcpyHostToDevice,
+                        c->stream));
     c->expf.buckets = c->d_expf_slots;
     c->expf.mask = nb - 1;
 #undef CKC
@@ -616,6 +648,10 @@ i4d_status i4d_shard_attach(i4d_ctx* c, const void* handles, size_t n) {
         cudaGraphExecDestroy(c->graph_dev);
         c->graph_dev = nullptr;
     }
+    if (c->graph_greedy) {
+        cudaGraphExecDestroy(c->graph_greedy);
+        c->graph_greedy = nullptr;
+    }
     c->attached = true;
     return I4D_OK;
 }
@@ -637,9 +673,15 @@ i4d_status i4d_load_bank(i4d_ctx* c, int bank, const void* bytes, size_t n) {
         cudaGraphExecDestroy(c->graph_dev);
         c->graph_dev = nullptr;
     }
+    if (c->graph_greedy) {
+        cudaGraphExecDestroy(c->graph_greedy);
+        c->graph_greedy = nullptr;
+    }
     uint8_t* stage = nullptr;
     CK(cudaMalloc(&stage, n));
-    cudaError_t e = cudaMemcpy(stage, bytes, n, cudaMemcpyHostToDevice);
+    // Stream-ordered: a plain cudaMemcpy from pageable memory may return
+    // before its DMA lands, and the context stream does not wait for it.
+    cudaError_t e = cudaMemcpyAsync(stage, bytes, n, cudaMemcpyHostToDevice, c->stream);
     for (int l = 0; e == cudaSuccess && l <= c->layers; ++l) {
         for (int m = 0; m < 8; ++m) {
             if ((l == c->layers) != (m == 7)) continue;
@@ -692,8 +734,8 @@ i4d_status i4d_load_rope(i4d_ctx* c, const void* bytes, size_t n) {
             }
         }
     CK(cudaSetDevice(c->device));
-    CK(cudaMemcpy(c->d_rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(c->d_rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(c->d_rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->d_rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, c->stream));
     c->rope_loaded = true;
     return I4D_OK;
 }
@@ -703,7 +745,55 @@ i4d_status i4d_load_embeddings(i4d_ctx* c, const float* emb, size_t n_floats) {
     if (n_floats != 32000ull * kDim) return fail(c, I4D_ERR_SIZE, "embeddings have %zu floats; expected 131072000", n_floats);
     CK(cudaSetDevice(c->device));
     if (!c->d_emb) CK(cudaMalloc(&c->d_emb, n_floats * sizeof(float)));
-    CK(cudaMemcpy(c->d_emb, emb, n_floats * sizeof(float), cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(c->d_emb, emb, n_floats * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    return I4D_OK;
+}
+
+i4d_status i4d_decode_greedy(i4d_ctx* c, uint32_t position, int32_t token_id, int32_t* next_id, float* logits_out) {
+    if (!c || !next_id) return c ? fail(c, I4D_ERR_ARG, "null next_id") : I4D_ERR_ARG;
+    if (!all_loaded(c) || !c->d_emb)
+        return fail(c, I4D_ERR_STATE, "banks, rope LUT and embeddings must be loaded before greedy decoding");
+    if (c->flags & I4D_FLAG_STAGED) return fail(c, I4D_ERR_STATE, "greedy decoding needs the persistent token kernel");
+    if (position >= static_cast<uint32_t>(c->stride))
+        return fail(c, I4D_ERR_ARG, "position %u out of range (KV capacity %d)", position, c->stride);
+    if (token_id < 0 || token_id >= kVocab) return fail(c, I4D_ERR_ARG, "token id %d out of range", token_id);
+    CK(cudaSetDevice(c->device));
+    *c->h_pos = static_cast<int>(position);
+    *c->h_tok = token_id;
+    *c->h_err = 0;
+    if (c->flags & I4D_FLAG_NO_GRAPH) {
+        const i4d_status st = enqueue_greedy(c);
+        if (st != I4D_OK) return st;
+    } else {
+        if (!c->graph_greedy) {
+            cudaGraph_t g = nullptr;
+            CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+            const i4d_status st = enqueue_greedy(c);
+            cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+            if (st != I4D_OK) {
+                if (g) cudaGraphDestroy(g);
+                return st;
+            }
+            if (e != cudaSuccess) return fail(c, I4D_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+            e = cudaGraphInstantiate(&c->graph_greedy, g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) {
+                c->graph_greedy = nullptr;
+                return fail(c, I4D_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+            }
+        }
+        CK(cudaGraphLaunch(c->graph_greedy, c->stream));
+    }
+    CK(cudaStreamSynchronize(c->stream));
+    if (*c->h_err) {
+        const unsigned e = *c->h_err;
+        CK(cudaMemset(c->d_err, 0, sizeof(unsigned)));
+        CK(cudaMemset(c->d_sync, 0, kSyncWords * sizeof(unsigned)));
+        return fail(c, (e & kErrArg) ? I4D_ERR_ARG : I4D_ERR_TIMEOUT, "device error word 0x%x", e);
+    }
+    const unsigned long long k = *c->h_argmax;
+    *next_id = k == 0ull ? -1 : static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(k & 0xffffffffu));
+    if (logits_out) CK(cudaMemcpy(logits_out, c->d_logits, kPVocab * sizeof(float), cudaMemcpyDeviceToHost));
     return I4D_OK;
 }
 
@@ -786,7 +876,7 @@ i4d_status i4d_kv_write(i4d_ctx* c, int bank, int layer, int lh, int token, cons
     if (st != I4D_OK) return st;
     CK(cudaSetDevice(c->device));
     CK(cudaStreamSynchronize(c->stream));
-    CK(cudaMemcpy(c->d_kv + off, record, 320, cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(c->d_kv + off, record, 320, cudaMemcpyHostToDevice, c->stream));
     return I4D_OK;
 }
 
@@ -939,9 +1029,9 @@ i4d_status i4d_linear_bank(i4d_ctx* c, const void* superblocks, size_t n_bytes, 
     DEVBUF(gem, n_bytes);
     DEVBUF(aq, lit * 256 * sizeof(int16_t));
     DEVBUF(ae, lit * 8);
-    CK(cudaMemcpy(src.p, superblocks, n_bytes, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(aq.p, act_q, lit * 256 * sizeof(int16_t), cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(ae.p, act_e8m0, lit * 8, cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(src.p, superblocks, n_bytes, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(aq.p, act_q, lit * 256 * sizeof(int16_t), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(ae.p, act_e8m0, lit * 8, cudaMemcpyHostToDevice, c->stream));
     RelayoutArgs r;
     r.src = src.as<uint8_t>();
     r.dst = gem.as<uint8_t>();
@@ -1048,8 +1138,8 @@ i4d_status i4d_gemv(i4d_ctx* c, int layer, int mode, const int16_t* act_q, const
     DEVBUF(aq, cols * sizeof(int16_t));
     DEVBUF(ae, cols / 32);
     DEVBUF(y, rows * sizeof(float));
-    CK(cudaMemcpy(aq.p, act_q, cols * sizeof(int16_t), cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(ae.p, act_e8m0, cols / 32, cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(aq.p, act_q, cols * sizeof(int16_t), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(ae.p, act_e8m0, cols / 32, cudaMemcpyHostToDevice, c->stream));
     LinearArgs a = base_linear(c, mode == 7 ? 0 : layer, st);
     a.w += static_cast<size_t>(mode_unit_offset(mode)) * a.chunks * kChunkBytes;
     a.units = rows / 32;
@@ -1074,7 +1164,7 @@ i4d_status i4d_quantize_g32(i4d_ctx* c, const float* x, int n, int16_t* q, uint8
     DEVBUF(dx, n * sizeof(float));
     DEVBUF(dq, n * sizeof(int16_t));
     DEVBUF(de, n / 32);
-    CK(cudaMemcpy(dx.p, x, n * sizeof(float), cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(dx.p, x, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     k_quant_g32<<<(n + 127) / 128, 128, 0, c->stream>>>(dx.as<float>(), n, dq.as<int16_t>(), de.as<uint8_t>());
     CK(cudaGetLastError());
     const i4d_status st = finish(c);
@@ -1092,8 +1182,8 @@ i4d_status i4d_rms_quant(i4d_ctx* c, const float* x, const float* gamma, int16_t
     DEVBUF(dr, 16);
     DEVBUF(dq, kDim * sizeof(int16_t));
     DEVBUF(de, kDim / 32);
-    CK(cudaMemcpy(dx.p, x, kDim * sizeof(float), cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(dg.p, gamma, kDim * sizeof(float), cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(dx.p, x, kDim * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(dg.p, gamma, kDim * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     k_rms_recip<<<1, 32, 0, c->stream>>>(dx.as<float>(), dr.as<float>());
     k_norm_quant<<<kDim / 128, 128, 0, c->stream>>>(dx.as<float>(), dg.as<float>(), dr.as<float>(), dq.as<int16_t>(),
                                                     de.as<uint8_t>());
@@ -1116,11 +1206,11 @@ i4d_status i4d_attention(i4d_ctx* c, int layer, uint32_t position, const int32_t
     DEVBUF(dqkv, 3ull * kDim * sizeof(int32_t));
     DEVBUF(dq, kDim * sizeof(int16_t));
     DEVBUF(de, kDim / 32);
-    CK(cudaMemcpy(dqkv.as<int32_t>(), q, kDim * 4, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(dqkv.as<int32_t>() + kDim, k, kDim * 4, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(dqkv.as<int32_t>() + 2 * kDim, v, kDim * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(dqkv.as<int32_t>(), q, kDim * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(dqkv.as<int32_t>() + kDim, k, kDim * 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(dqkv.as<int32_t>() + 2 * kDim, v, kDim * 4, cudaMemcpyHostToDevice, c->stream));
     const int p = static_cast<int>(position);
-    CK(cudaMemcpy(c->d_pos, &p, sizeof(int), cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(c->d_pos, &p, sizeof(int), cudaMemcpyHostToDevice, c->stream));
     AttnArgs a = base_attn(c, layer);
     a.partials = nullptr;
     a.direct = dqkv.as<int32_t>();
@@ -1142,8 +1232,8 @@ i4d_status i4d_swiglu_quant(i4d_ctx* c, const float* gate, const float* up, int1
     DEVBUF(du, kFfn * sizeof(float));
     DEVBUF(dq, kFfn * sizeof(int16_t));
     DEVBUF(de, kFfn / 32);
-    CK(cudaMemcpy(dg.p, gate, kFfn * sizeof(float), cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(du.p, up, kFfn * sizeof(float), cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(dg.p, gate, kFfn * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(du.p, up, kFfn * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     k_swiglu_quant<<<kFfn / 128, 128, 0, c->stream>>>(dg.as<float>(), du.as<float>(), kFfn, c->expf, dq.as<int16_t>(),
                                                       de.as<uint8_t>());
     CK(cudaGetLastError());
@@ -1154,13 +1244,29 @@ i4d_status i4d_swiglu_quant(i4d_ctx* c, const float* gate, const float* up, int1
     return I4D_OK;
 }
 
+i4d_status i4d_argmax(i4d_ctx* c, const float* logits, size_t n, int32_t* index) {
+    if (!c || !logits || !index || n == 0 || n > static_cast<size_t>(kPVocab))
+        return c ? fail(c, I4D_ERR_ARG, "bad arguments") : I4D_ERR_ARG;
+    CK(cudaSetDevice(c->device));
+    DEVBUF(x, n * sizeof(float));
+    DEVBUF(k, sizeof(unsigned long long));
+    CK(cudaMemcpyAsync(x.p, logits, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    k_argmax<<<1, 1024, 0, c->stream>>>(x.as<float>(), static_cast<int>(n), k.as<unsigned long long>());
+    CK(cudaGetLastError());
+    unsigned long long key = 0;
+    CK(cudaMemcpyAsync(&key, k.p, sizeof(key), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    *index = key == 0ull ? -1 : static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(key & 0xffffffffu));
+    return I4D_OK;
+}
+
 i4d_status i4d_expf(i4d_ctx* c, const float* x, float* y, size_t n) {
     if (!c || !x || !y) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
     if (n == 0) return I4D_OK;
     CK(cudaSetDevice(c->device));
     DEVBUF(dx, n * sizeof(float));
     DEVBUF(dy, n * sizeof(float));
-    CK(cudaMemcpy(dx.p, x, n * sizeof(float), cudaMemcpyHostToDevice));
+    CK(cudaMemcpyAsync(dx.p, x, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     k_expf<<<static_cast<unsigned>((n + 255) / 256), 256, 0, c->stream>>>(dx.as<float>(), dy.as<float>(), n, c->expf);
     CK(cudaGetLastError());
     const i4d_status st = finish(c);

@@ -15,6 +15,7 @@ namespace i4d {
 constexpr int kDim = 4096;
 constexpr int kFfn = 11264;
 constexpr int kPVocab = 32256;
+constexpr int kVocab = 32000;
 constexpr int kHeads = 32;
 constexpr int kHeadDim = 128;
 constexpr int kLocalHeads = 8;

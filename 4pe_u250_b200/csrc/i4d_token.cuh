@@ -69,6 +69,12 @@ struct TokenArgs {
     float* peer_partials[4];   // every rank's partial buffers, as mapped here ([rank]; own at [rank])
     unsigned* peer_sync[4];    // every rank's synchronisation words, as mapped here
     const unsigned* epoch;     // tokens completed by this context (counter targets are epoch based)
+    // Greedy steps (emb != null): the input is row *token_in of emb, and the
+    // kernel leaves the first index of the maximum logit (NaN skipped) in
+    // *argmax as argmax_key(value, index).
+    const float* emb;
+    const int* token_in;
+    unsigned long long* argmax;
     float* resid;              // [2][4096]: after residual update n, buffer n & 1 (0: token input and output)
     const float* gamma;        // [65][4096]
     float* partials;           // [2][4][32256]: stage ordinal k writes buffer k & 1
@@ -262,7 +268,12 @@ __device__ __forceinline__ void tok_input_rms(const TokenArgs& a, const TokSmem&
         const int lg = cw + k * kTokWarps;
         if (lg < G) g[k] = a.gamma[static_cast<size_t>(gamma_row) * kDim + bank * G * 32 + lg * 32 + lane];
     }
-    const float4* rin = reinterpret_cast<const float4*>(a.resid + (norm == 0 ? 0 : ((norm - 1) & 1) * kDim));
+    // Greedy steps take the token's input from the embedding table (CTA 0
+    // stores it as the residual input, read again by the first update).
+    const bool embed = norm == 0 && a.emb != nullptr;
+    const float4* rin = reinterpret_cast<const float4*>(
+        embed ? a.emb + static_cast<size_t>(*reinterpret_cast<const volatile int*>(a.token_in)) * kDim
+              : a.resid + (norm == 0 ? 0 : ((norm - 1) & 1) * kDim));
     float4* rout = reinterpret_cast<float4*>(a.resid + (norm & 1) * kDim);
     const float4* P = reinterpret_cast<const float4*>(stage_partials(a, prev_ordinal));
     constexpr int kQ = kDim / 4;  // float4 per vector
@@ -276,6 +287,8 @@ __device__ __forceinline__ void tok_input_rms(const TokenArgs& a, const TokSmem&
             x.z = __fadd_rn(x.z, __fadd_rn(__fadd_rn(p0.z, p1.z), __fadd_rn(p2.z, p3.z)));
             x.w = __fadd_rn(x.w, __fadd_rn(__fadd_rn(p0.w, p1.w), __fadd_rn(p2.w, p3.w)));
             if (blockIdx.x == 0) __stcg(rout + i, x);
+        } else if (embed && blockIdx.x == 0) {
+            __stcg(rout + i, x);
         }
         reinterpret_cast<float4*>(xs)[i] = x;
     }
@@ -685,6 +698,44 @@ __device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s
     }
 }
 
+// Key of a logit for the greedy argmax: larger keys win; equal values favour
+// the smaller index (the first maximum, as emulator:1428-1438 and
+// decode_host.cpp:703-717 scan); -0.0 counts as +0.0; NaN never wins (key 0).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    if (v != v) return 0ull;
+    unsigned b = __float_as_uint(v == 0.0f ? 0.0f : v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return (static_cast<unsigned long long>(b) << 32) | (0xffffffffu - static_cast<unsigned>(idx));
+}
+
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long k) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long y = __shfl_xor_sync(0xffffffffu, k, o);
+        k = y > k ? y : k;
+    }
+    return k;
+}
+
+// First index of the maximum of x[0, n) (NaN skipped; -1 encoded as key 0):
+// the argmax of the greedy step, as an op-level test hook.  One block.
+__global__ void __launch_bounds__(1024) k_argmax(const float* x, int n, unsigned long long* out) {
+    __shared__ unsigned long long w[32];
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const unsigned long long k = argmax_key(x[i], i);
+        best = k > best ? k : best;
+    }
+    best = warp_max_u64(best);
+    if ((threadIdx.x & 31) == 0) w[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        unsigned long long v = threadIdx.x < (blockDim.x >> 5) ? w[threadIdx.x] : 0ull;
+        v = warp_max_u64(v);
+        if (threadIdx.x == 0) *out = v;
+    }
+}
+
 // Logits: every CTA combines a slice of the LM-head rows once all partials
 // are stored ((p0+p1)+(p2+p3), emulator sharded_gemv_4pe).
 __device__ __noinline__ void tok_logits(const TokenArgs& a, unsigned tgt_stage, int cw, int lane) {
@@ -695,7 +746,19 @@ __device__ __noinline__ void tok_logits(const TokenArgs& a, unsigned tgt_stage, 
     const float* P = stage_partials(a, ord);
     const int r0 = static_cast<int>((static_cast<long long>(blockIdx.x) * kPVocab) / gridDim.x);
     const int r1 = static_cast<int>((static_cast<long long>(blockIdx.x + 1) * kPVocab) / gridDim.x);
-    for (int r = r0 + tid; r < r1; r += 32 * kTokWarps) a.logits[r] = combine4(P, kPVocab, r);
+    unsigned long long best = 0ull;
+    for (int r = r0 + tid; r < r1; r += 32 * kTokWarps) {
+        const float v = combine4(P, kPVocab, r);
+        a.logits[r] = v;
+        if (r < kVocab) {
+            const unsigned long long k = argmax_key(v, r);
+            best = k > best ? k : best;
+        }
+    }
+    if (a.emb) {  // greedy step: the CTA's best, then one atomic per warp
+        best = warp_max_u64(best);
+        if (lane == 0 && best != 0ull) atomicMax(a.argmax, best);
+    }
 }
 
 // ------------------------------------------------------------ attention item
@@ -1116,6 +1179,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
     const int cw = warp - 1;
     const int tid = cw * 32 + lane;
     const long long t_kernel = clock64();
+    if (a.emb && blockIdx.x == 0 && tid == 0) *a.argmax = 0ull;  // read by the host after the step
     StageDesc d;
     d.bank = a.bank0 + lbank;
     // Counter targets of this token: counters only grow, by world * grid

@@ -129,6 +129,16 @@ i4d_status i4d_load_embeddings(i4d_ctx* ctx, const float* emb, size_t n_floats);
 i4d_status i4d_decode_token(i4d_ctx* ctx, uint32_t position, const float* residual_in,
                             float* logits_out, float* residual_out);
 
+/* Greedy step on the device (SURVEY-(f): the embedding lookup and the
+ * sampler of decode_host.cpp:666-676 and 703-717 moved onto the GPU): the
+ * input is row token_id of the embeddings loaded by i4d_load_embeddings, and
+ * next_id receives the first index of the maximum of logits[0, 32000), NaN
+ * skipped (-1 if every logit is NaN), as argmax_logits.  logits_out (may be
+ * NULL) receives the 32256 padded logits.  Per step only the position and id
+ * go to the device and the id back. */
+i4d_status i4d_decode_greedy(i4d_ctx* ctx, uint32_t position, int32_t token_id, int32_t* next_id,
+                             float* logits_out);
+
 /* Device-resident form of i4d_decode_token for pipelines that keep their
  * data on the GPU: residual_in_dev / logits_out_dev are device pointers
  * (4096 / 32256 floats).  The step is only enqueued on the context stream;
@@ -248,6 +258,10 @@ i4d_status i4d_attention(i4d_ctx* ctx, int layer, uint32_t position, const int32
  * int4_decoder_blocks.cpp:487-521). */
 i4d_status i4d_swiglu_quant(i4d_ctx* ctx, const float* gate, const float* up, int16_t* q,
                             uint8_t* e8m0);
+
+/* The device argmax of i4d_decode_greedy over a host buffer of n <= 32256
+ * values (test hook). */
+i4d_status i4d_argmax(i4d_ctx* ctx, const float* logits, size_t n, int32_t* index);
 
 /* The device expf used by SwiGLU, element-wise (test hook: its results must
  * equal the host C library's expf, which the reference emulator calls). */
