@@ -235,6 +235,7 @@ def main():
         ctx = pkg.Context(device=local, num_layers=32, kv_capacity=args.kv_capacity)
     ctx.load_banks(banks)
     ctx.load_rope(lut)
+    ctx.load_embeddings(emb)
     if shard:
         ctx.attach_peers()
     stream = torch.cuda.ExternalStream(ctx.stream_handle())
@@ -252,8 +253,10 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- e2e through the public C ABI (host buffers), greedy ----
-    tokens, nxt, last_logits = [], None, None
+    # ---- e2e through the public C ABI: the greedy step (token id in, next id
+    # out: i4d_decode_greedy), then the logits contract (i4d_decode_token:
+    # embedding row in, 32256 logits out, host argmax) on the same sequence ----
+    tokens, nxt = [], None
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for pos in range(total):
         if pos == args.warmup:
@@ -261,11 +264,22 @@ def main():
             ev0.record(stream)
         tok = prompt[pos] if pos < PROMPT else nxt
         tokens.append(tok)
-        last_logits = ctx.decode_token(pos, emb[tok * 4096:(tok + 1) * 4096])
-        nxt = int(np.argmax(last_logits[:F.VOCAB]))
+        nxt, _ = ctx.decode_greedy(pos, tok)
     ev1.record(stream)
     barrier()
     e2e_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    last_logits = None
+    for pos in range(total):
+        if pos == args.warmup:
+            barrier()
+            ev0.record(stream)
+        tok = tokens[pos]
+        last_logits = ctx.decode_token(pos, emb[tok * 4096:(tok + 1) * 4096])
+        if pos + 1 < total and pos + 1 >= PROMPT:
+            assert int(np.argmax(last_logits[:F.VOCAB])) == tokens[pos + 1]  # same greedy sequence
+    ev1.record(stream)
+    barrier()
+    e2e_logits_ms = max_over_ranks(ev0.elapsed_time(ev1))
 
     # ---- device-resident replay of the same token sequence ----
     d_emb = torch.from_numpy(emb).to("cuda")
@@ -311,14 +325,19 @@ def main():
     streams = 1 if shard else world  # a sharded group decodes one stream
     value = streams * args.steps / (dev_ms * 1e-3)
     e2e = streams * args.steps / (e2e_ms * 1e-3)
+    e2e_logits = streams * args.steps / (e2e_logits_ms * 1e-3)
     launches_per_step = 2  # k_set_pos + k_token
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
         "scaling": "strong" if shard else "weak", "vs_baseline": None, "dtype": "int4xint14/fp32",
         "data": "synthetic", "config": workload_config(args, world),
-        "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4096 * 4 + 4,
-                "d2h_bytes_per_step": F.PADDED_VOCAB * 4 + 4096 * 4 + 4, "ms_per_step": e2e_ms / args.steps},
+        "e2e": {"value": e2e, "unit": UNIT, "api": "i4d_decode_greedy (token id in, next token id out)",
+                "h2d_bytes_per_step": 4 + 4, "d2h_bytes_per_step": 8 + 4, "ms_per_step": e2e_ms / args.steps},
+        "e2e_logits": {"value": e2e_logits, "unit": UNIT,
+                       "api": "i4d_decode_token (embedding row in, 32256 logits out, host argmax)",
+                       "h2d_bytes_per_step": 4096 * 4 + 4, "d2h_bytes_per_step": F.PADDED_VOCAB * 4 + 4096 * 4 + 4,
+                       "ms_per_step": e2e_logits_ms / args.steps},
         "roofline": {"bound": "hbm", "kernel": "k_token (persistent decode step, 1 launch per token" +
                                (f" on each of {world} bank shards; achieved = per-GPU share of the bytes)" if shard
                                 else ")"),
