@@ -250,5 +250,10 @@ class RefEmulator:
         self.L.ref_kv_get(bank, layer, lh, token, k8.ctypes.data, ks.ctypes.data, v8.ctypes.data, vs.ctypes.data)
         return ks, vs, k8, v8
 
+    def argmax(self, logits):
+        """The emulator's sample_argmax over 32000 logits (emulator:1428-1438)."""
+        x = np.ascontiguousarray(logits, dtype=np.float32)
+        return int(self.L.ref_argmax(x.ctypes.data, x.size))
+
     def threads(self):
         return self.L.ref_threads()
