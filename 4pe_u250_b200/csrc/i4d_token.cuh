@@ -256,17 +256,21 @@ __device__ __forceinline__ float* stage_partials(const TokenArgs& a, int ordinal
 //   r = RMS reciprocal of residual_n                  (emulator:427-453)
 //   x = fl(fl(residual_n * r) * gamma_n) -> G32 quantizer, this bank's columns.
 // Every CTA computes the same residual; CTA 0 stores it for the next update.
+// All loads (gammas, residual_{n-1}, the four partials) are issued as one
+// batch after the stage wait; loading before the wait was measured slower.
 template <int G>
 __device__ __forceinline__ void tok_input_rms(const TokenArgs& a, const TokSmem& s, const LinearSmem& ls, int bank,
                                               int norm, int prev_ordinal, float* xs, int cw, int lane) {
     constexpr int kPer = (G + kTokWarps - 1) / kTokWarps;
+    constexpr int kQ = kDim / 4;                                      // float4 per vector
+    constexpr int kRmsQ = (kQ + 32 * kTokWarps - 1) / (32 * kTokWarps);  // float4 per thread
     const int tid = cw * 32 + lane;
     const int gamma_row = norm == 2 * a.layers ? kGammaFinal : norm;
     float g[kPer];
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
         const int lg = cw + k * kTokWarps;
-        if (lg < G) g[k] = a.gamma[static_cast<size_t>(gamma_row) * kDim + bank * G * 32 + lg * 32 + lane];
+        g[k] = lg < G ? a.gamma[static_cast<size_t>(gamma_row) * kDim + bank * G * 32 + lg * 32 + lane] : 0.0f;
     }
     // Greedy steps take the token's input from the embedding table (CTA 0
     // stores it as the residual input, read again by the first update).
@@ -274,11 +278,19 @@ __device__ __forceinline__ void tok_input_rms(const TokenArgs& a, const TokSmem&
     const float4* rin = reinterpret_cast<const float4*>(
         embed ? a.emb + static_cast<size_t>(*reinterpret_cast<const volatile int*>(a.token_in)) * kDim
               : a.resid + (norm == 0 ? 0 : ((norm - 1) & 1) * kDim));
+    float4 xin[kRmsQ];
+#pragma unroll
+    for (int k = 0; k < kRmsQ; ++k) {
+        const int i = tid + k * 32 * kTokWarps;
+        xin[k] = i < kQ ? __ldcg(rin + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
     float4* rout = reinterpret_cast<float4*>(a.resid + (norm & 1) * kDim);
     const float4* P = reinterpret_cast<const float4*>(stage_partials(a, prev_ordinal));
-    constexpr int kQ = kDim / 4;  // float4 per vector
-    for (int i = tid; i < kQ; i += 32 * kTokWarps) {
-        float4 x = __ldcg(rin + i);
+#pragma unroll
+    for (int k = 0; k < kRmsQ; ++k) {
+        const int i = tid + k * 32 * kTokWarps;
+        if (i >= kQ) break;
+        float4 x = xin[k];
         if (norm > 0) {
             const float4 p0 = __ldcg(P + i), p1 = __ldcg(P + kQ + i);
             const float4 p2 = __ldcg(P + 2 * kQ + i), p3 = __ldcg(P + 3 * kQ + i);
@@ -1138,9 +1150,6 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
             // partials, residual and counters of the stage handoffs stay in L2.
             const uint64_t pol_first = l2_policy_evict_first();
             cursor_begin(a, lbank, c, cur);
-            while (cursor_valid(a, cur)) {
-                const int cnt = min(kTokCpc, cur.n - cur.i);
-                if (issued >= kTokSlots) {
                     const long long t0 = TR && a.trace ? clock64() : 0;
                     if (!tok_mbar_wait(a, &s.empty[slot], phase ^ 1u, kErrWaitEmpty)) break;
                     if (TR && a.trace) trace_add<TR>(a, TR_RING_FULL, clock64() - t0);
