@@ -1150,6 +1150,9 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
             // partials, residual and counters of the stage handoffs stay in L2.
             const uint64_t pol_first = l2_policy_evict_first();
             cursor_begin(a, lbank, c, cur);
+            while (cursor_valid(a, cur)) {
+                const int cnt = min(kTokCpc, cur.n - cur.i);
+                if (issued >= kTokSlots) {
                     const long long t0 = TR && a.trace ? clock64() : 0;
                     if (!tok_mbar_wait(a, &s.empty[slot], phase ^ 1u, kErrWaitEmpty)) break;
                     if (TR && a.trace) trace_add<TR>(a, TR_RING_FULL, clock64() - t0);
