@@ -612,8 +612,16 @@ __device__ __forceinline__ void tok_reduce_units(const TokenArgs& a, const TokSm
     }
 }
 
+// The stage, attention and LM-head functions are inlined into k_token on
+// purpose.  Out of line, they receive the shared-memory carve and the stage
+// descriptor through references to the caller's stack: the carve's pointers
+// are then generic (not provably shared), and every inline-asm memory clobber
+// (mbarrier operations, fences) reloads them from local memory, which misses
+// the 28 KB of L1 left beside 225 KB of shared memory.  That cost about
+// 500 cycles per shared-memory step of the chunk loop; inlined, the token
+// step runs about 1.4x faster.
 template <int C, bool TR>
-__device__ __noinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s, const StageDesc& d, int cw,
+__device__ __forceinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s, const StageDesc& d, int cw,
                                             int lane) {
     constexpr int G = C * 8;
     static_assert(kRowNU<C> >= 2 && kColNU >= 2, "contribution slots");
@@ -750,7 +758,7 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* x, int n, unsigned
 
 // Logits: every CTA combines a slice of the LM-head rows once all partials
 // are stored ((p0+p1)+(p2+p3), emulator sharded_gemv_4pe).
-__device__ __noinline__ void tok_logits(const TokenArgs& a, unsigned tgt_stage, int cw, int lane) {
+__device__ __forceinline__ void tok_logits(const TokenArgs& a, unsigned tgt_stage, int cw, int lane) {
     const int tid = cw * 32 + lane;
     const int ord = stage_ordinal(TS_LOGITS, a.layers);
     if (tid == 0) wait_counter(a, &a.sync[kSyncStage + ord], tgt_stage);
@@ -817,7 +825,7 @@ static_assert(2 * kTile * 320 + 320 + kTile * 8 + 144 + kTile * 32 * 4 + 2 * 128
 // shared memory, and the reference's saturating recurrence (emulator:656-685)
 // then runs exactly, one lane per dimension, over those terms.
 template <bool TR>
-__device__ __noinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s, int layer, int item, int cw,
+__device__ __forceinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s, int layer, int item, int cw,
                                            int lane,
                                            unsigned tgt_qkv) {
     const unsigned FULL = 0xffffffffu;
