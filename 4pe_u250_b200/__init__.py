@@ -38,7 +38,7 @@ EXPORTS = [
 
 _STAGES = ["qkv", "o", "gu", "down", "logits"]
 BREAKDOWN = ([f"wait_{x}" for x in _STAGES] + [f"prologue_{x}" for x in _STAGES] + [f"chunks_{x}" for x in _STAGES]
-             + ["attn_wait", "attn", "ring_full", "total"]
+             + ["attn_wait", "attn", "ring_full", "total"] + [f"arrive_{x}" for x in _STAGES]
              + [f"warp_{k}_{x}" for x in _STAGES for k in ("data_wait", "slot_wait", "compute", "chain")])
 
 KERNEL_CLASSES = ["qkv_gemv", "attention", "o_gemv", "gate_up_gemv", "down_gemv", "logits_gemv", "rms", "token"]

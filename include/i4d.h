@@ -166,10 +166,11 @@ i4d_status i4d_profile_token(i4d_ctx* ctx, uint32_t position, const float* resid
  * device's nominal clock) of: 0..4 waiting for the input of the QKV, O,
  * GATE/UP, DOWN and LM-head stages, 5..9 building their activations,
  * 10..14 their chunk loops, 15 attention waits for QKV, 16 attention work,
- * 17 producer blocked on a full ring, 18 whole kernel, and per consumer warp
- * (averaged over warps) for each stage s: 19+4s waiting for ring data,
- * 20+4s waiting for a contribution slot, 21+4s chunk arithmetic, 22+4s row
- * chains.  n_out >= 39.  No reference counterpart. */
+ * 17 producer blocked on a full ring, 18 whole kernel, 19..23 thread 0's
+ * release fence and counter arrival after each stage, and per consumer warp
+ * (averaged over warps) for each stage s: 24+4s waiting for ring data,
+ * 25+4s waiting for a contribution slot, 26+4s chunk arithmetic, 27+4s row
+ * chains.  n_out >= 44.  No reference counterpart. */
 i4d_status i4d_token_breakdown(i4d_ctx* ctx, uint32_t position, const float* residual_in_dev, float* us_out,
                                int n_out);
 
