@@ -55,16 +55,18 @@ __device__ __noinline__ float expf_table_fix(float x, float y, const ExpfFix& fx
 }
 
 // The host C library's expf: the core, corrected from the table only where
-// the core's result is near a rounding midpoint.
-__device__ __forceinline__ float expf_libc(float x, const ExpfFix& fx) {
+// the core's result is near a rounding midpoint.  `table` is g_expf_table or
+// a copy of it in shared memory (kernels whose L1 is mostly carved out for
+// shared memory would otherwise fetch it from L2).
+__device__ __forceinline__ float expf_libc(float x, const ExpfFix& fx, const double* table = g_expf_table) {
     int near_tie;
-    const float y = i4d_expf_core2(x, g_expf_table, &near_tie);
+    const float y = i4d_expf_core2(x, table, &near_tie);
     return near_tie ? expf_table_fix(x, y, fx) : y;
 }
 
 // SwiGLU of one element (emulator:716-722): (g * (1 / (1 + expf(-g)))) * u.
-__device__ __forceinline__ float swiglu1(float g, float u, const ExpfFix& fx) {
-    const float e = expf_libc(-g, fx);
+__device__ __forceinline__ float swiglu1(float g, float u, const ExpfFix& fx, const double* table = g_expf_table) {
+    const float e = expf_libc(-g, fx, table);
     const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
     return __fmul_rn(__fmul_rn(g, sig), u);
 }

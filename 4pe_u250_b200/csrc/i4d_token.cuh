@@ -155,11 +155,12 @@ struct TokSmem {
     int* fin;            // [kFinMax + 2]
     int* flag;           // [4] misc
     int* issued;         // [kTokSlots]: copy sequence number last issued into each slot
+    double* expf_tab;    // [64]: the expf core's 2^(j/64) table
 };
 
 __host__ __device__ inline size_t tok_smem_bytes() {
     return static_cast<size_t>(kTokRing) * kChunkBytes + 2 * kTokSlots * 8 + 16 + kTokUnion + 16 + 2 * kTokMaxSlots * 4 +
-           align16((kFinMax + 2) * 4) + 16 + align16(kTokSlots * 4);
+           align16((kFinMax + 2) * 4) + 16 + align16(kTokSlots * 4) + 64 * 8;
 }
 
 __device__ __forceinline__ TokSmem tok_carve(uint8_t* p) {
@@ -182,6 +183,8 @@ __device__ __forceinline__ TokSmem tok_carve(uint8_t* p) {
     s.flag = reinterpret_cast<int*>(p);
     p += 16;
     s.issued = reinterpret_cast<int*>(p);
+    p += align16(kTokSlots * 4);
+    s.expf_tab = reinterpret_cast<double*>(p);
     return s;
 }
 
@@ -327,8 +330,8 @@ __device__ __forceinline__ void tok_input_rms(const TokenArgs& a, const TokSmem&
 // Input of DOWN: SwiGLU of this bank's 2816 FFN columns from the GATE/UP
 // partials (gate rows [0, 11264), up rows [11264, 22528)), then the G32
 // quantizer (emulator:716-722, 769-770).
-__device__ __forceinline__ void tok_input_swiglu(const TokenArgs& a, const LinearSmem& ls, int bank, int layer, int cw,
-                                                 int lane) {
+__device__ __forceinline__ void tok_input_swiglu(const TokenArgs& a, const TokSmem& s, const LinearSmem& ls, int bank,
+                                                 int layer, int cw, int lane) {
     constexpr int G = 88;
     constexpr int kPer = (G + kTokWarps - 1) / kTokWarps;
     constexpr int kRows = 22528;
@@ -342,7 +345,7 @@ __device__ __forceinline__ void tok_input_swiglu(const TokenArgs& a, const Linea
         uv[k] = combine4(P, kRows, kFfn + f);
     }
 #pragma unroll
-    for (int k = 0; k < kPer; ++k) sw[k] = swiglu1(gv[k], uv[k], a.expf);
+    for (int k = 0; k < kPer; ++k) sw[k] = swiglu1(gv[k], uv[k], a.expf, s.expf_tab);
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
         const int lg = cw + k * kTokWarps;
@@ -658,7 +661,7 @@ __device__ __forceinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem
     if (d.st == TS_O) {
         tok_input_attention(a, ls, d.bank, cw, lane);
     } else if (d.st == TS_DOWN) {
-        tok_input_swiglu(a, ls, d.bank, d.layer, cw, lane);
+        tok_input_swiglu(a, s, ls, d.bank, d.layer, cw, lane);
     } else {
         const int norm = d.st == TS_QKV ? 2 * d.layer : d.st == TS_GU ? 2 * d.layer + 1 : 2 * d.layer;
         if constexpr (G == 32) tok_input_rms<32>(a, s, ls, d.bank, norm, ord - 1, contrib, cw, lane);
@@ -694,14 +697,6 @@ __device__ __forceinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem
     } else {
         tok_chunks_rows<C, TR>(a, s, d, ls, contrib, lane, wt);
     }
-    const long long w_data = wt.data, w_slot = wt.slot, w_comp = wt.comp, w_chain = wt.chain;
-    if (tr && lane == 0) {
-        unsigned long long* t = a.trace + blockIdx.x * kTraceSlots;
-        atomicAdd(t + TR_W_DATA + 4 * d.st, static_cast<unsigned long long>(w_data));
-        atomicAdd(t + TR_W_SLOT + 4 * d.st, static_cast<unsigned long long>(w_slot));
-        atomicAdd(t + TR_W_COMPUTE + 4 * d.st, static_cast<unsigned long long>(w_comp));
-        atomicAdd(t + TR_W_CHAIN + 4 * d.st, static_cast<unsigned long long>(w_chain));
-    }
     // Release: the CTA barrier orders every warp's partial stores before
     // thread 0's release arrival (the grid-sync pattern).
     tok_bar();
@@ -720,6 +715,14 @@ __device__ __forceinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem
         trace_add<TR>(a, TR_WAIT + d.st, t_ready - t_begin);
         trace_add<TR>(a, TR_PROLOGUE + d.st, t_loop - t_ready);
         trace_add<TR>(a, TR_CHUNKS + d.st, t_epi - t_loop);
+    }
+    // Per-warp sums after the arrival, so the release does not wait for them.
+    if (tr && lane == 0) {
+        unsigned long long* t = a.trace + blockIdx.x * kTraceSlots;
+        atomicAdd(t + TR_W_DATA + 4 * d.st, static_cast<unsigned long long>(wt.data));
+        atomicAdd(t + TR_W_SLOT + 4 * d.st, static_cast<unsigned long long>(wt.slot));
+        atomicAdd(t + TR_W_COMPUTE + 4 * d.st, static_cast<unsigned long long>(wt.comp));
+        atomicAdd(t + TR_W_CHAIN + 4 * d.st, static_cast<unsigned long long>(wt.chain));
     }
 }
 
@@ -1150,6 +1153,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
         }
         mbar_fence_init();
     }
+    if (threadIdx.x < 64) s.expf_tab[threadIdx.x] = g_expf_table[threadIdx.x];
     __syncthreads();
 
     if (warp == 0) {
