@@ -311,6 +311,17 @@ TokenArgs token_args(i4d_ctx* c) {
 }
 
 // One token as a single cooperative launch of the persistent kernel.
+// After a failed step: the error word, counters and epoch back to zero.
+// Ordered on the context's stream and waited for: a plain cudaMemset runs on
+// the legacy stream, which does not order with the non-blocking context
+// stream, so it could land inside the next step.
+cudaError_t reset_sync(i4d_ctx* c) {
+    cudaError_t e = cudaMemsetAsync(c->d_err, 0, sizeof(unsigned), c->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(c->d_sync, 0, kSyncWords * sizeof(unsigned), c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    return e;
+}
+
 cudaError_t launch_token_with(i4d_ctx* c, const TokenArgs& t) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(c->nbanks * c->cpb);
@@ -420,8 +431,7 @@ i4d_status finish(i4d_ctx* c) {
     unsigned e = 0;
     CK(cudaMemcpy(&e, c->d_err, sizeof(unsigned), cudaMemcpyDeviceToHost));
     if (e) {
-        CK(cudaMemset(c->d_err, 0, sizeof(unsigned)));
-        CK(cudaMemset(c->d_sync, 0, kSyncWords * sizeof(unsigned)));
+        CK(reset_sync(c));
         if (e & kErrArg) return fail(c, I4D_ERR_ARG, "device rejected an argument (error word 0x%x)", e);
         return fail(c, I4D_ERR_TIMEOUT, "a bounded device wait gave up (error word 0x%x)", e);
     }
@@ -601,6 +611,9 @@ static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ct
                         c->stream));
     c->expf.buckets = c->d_expf_slots;
     c->expf.mask = nb - 1;
+    // The initialising cudaMemset calls above run on the legacy stream, which
+    // does not order with the context's non-blocking stream.
+    CKC(cudaDeviceSynchronize());
 #undef CKC
     *out = c;
     return I4D_OK;
@@ -787,8 +800,7 @@ i4d_status i4d_decode_greedy(i4d_ctx* c, uint32_t position, int32_t token_id, in
     CK(cudaStreamSynchronize(c->stream));
     if (*c->h_err) {
         const unsigned e = *c->h_err;
-        CK(cudaMemset(c->d_err, 0, sizeof(unsigned)));
-        CK(cudaMemset(c->d_sync, 0, kSyncWords * sizeof(unsigned)));
+        CK(reset_sync(c));
         return fail(c, (e & kErrArg) ? I4D_ERR_ARG : I4D_ERR_TIMEOUT, "device error word 0x%x", e);
     }
     const unsigned long long k = *c->h_argmax;
@@ -833,8 +845,7 @@ i4d_status i4d_decode_token(i4d_ctx* c, uint32_t position, const float* residual
     CK(cudaStreamSynchronize(c->stream));
     if (*c->h_err) {
         const unsigned e = *c->h_err;
-        CK(cudaMemset(c->d_err, 0, sizeof(unsigned)));
-        CK(cudaMemset(c->d_sync, 0, kSyncWords * sizeof(unsigned)));
+        CK(reset_sync(c));
         return fail(c, (e & kErrArg) ? I4D_ERR_ARG : I4D_ERR_TIMEOUT, "device error word 0x%x", e);
     }
     std::memcpy(logits_out, c->h_logits, kPVocab * sizeof(float));
