@@ -64,11 +64,14 @@ __device__ __forceinline__ float expf_libc(float x, const ExpfFix& fx, const dou
     return near_tie ? expf_table_fix(x, y, fx) : y;
 }
 
-// SwiGLU of one element (emulator:716-722): (g * (1 / (1 + expf(-g)))) * u.
-__device__ __forceinline__ float swiglu1(float g, float u, const ExpfFix& fx, const double* table = g_expf_table) {
-    const float e = expf_libc(-g, fx, table);
+// SwiGLU of one element (emulator:716-722): (g * (1 / (1 + e))) * u with
+// e = expf(-g).
+__device__ __forceinline__ float swiglu_e(float g, float u, float e) {
     const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
     return __fmul_rn(__fmul_rn(g, sig), u);
+}
+__device__ __forceinline__ float swiglu1(float g, float u, const ExpfFix& fx, const double* table = g_expf_table) {
+    return swiglu_e(g, u, expf_libc(-g, fx, table));
 }
 
 }  // namespace i4d

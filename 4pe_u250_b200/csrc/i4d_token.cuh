@@ -309,12 +309,28 @@ __device__ __forceinline__ void tok_input_rms(const TokenArgs& a, const TokSmem&
         reinterpret_cast<float4*>(xs)[i] = x;
     }
     tok_bar();
-    if (cw == 0) {
-        const float r = rms_recip_warp(xs);
-        if (lane == 0) reinterpret_cast<float*>(s.flag)[0] = r;
+    // RMS reciprocal in the reference's order (emulator:427-447): warp b sums
+    // bank b, lane s its slot s (elements b*1024 + s + 8i, i = 0..127, in
+    // order), then the bank total is ((0 + s0) + s1) ... + s7.  One bank per
+    // warp keeps the eight lanes' loads on distinct shared-memory banks (a
+    // single warp over all four banks met a 4-way conflict on every load).
+    float* bank_total = xs + kDim;
+    if (cw < 4 && lane < 8) {
+        const float* base = xs + cw * 1024 + lane;
+        float acc = 0.0f;
+#pragma unroll 32
+        for (int i = 0; i < 128; ++i) {
+            const float v = base[i * 8];
+            acc = __fadd_rn(acc, __fmul_rn(v, v));
+        }
+        float total = 0.0f;
+#pragma unroll
+        for (int sl = 0; sl < 8; ++sl) total = __fadd_rn(total, __shfl_sync(0xffu, acc, sl));
+        if (lane == 0) bank_total[cw] = total;
     }
     tok_bar();
-    const float r = reinterpret_cast<const float*>(s.flag)[0];
+    const float sum = __fadd_rn(__fadd_rn(bank_total[0], bank_total[1]), __fadd_rn(bank_total[2], bank_total[3]));
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(sum, 1.0f / 4096.0f), 1.0e-5f)));
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
         const int lg = cw + k * kTokWarps;
@@ -344,8 +360,36 @@ __device__ __forceinline__ void tok_input_swiglu(const TokenArgs& a, const TokSm
         gv[k] = combine4(P, kRows, f);
         uv[k] = combine4(P, kRows, kFfn + f);
     }
+    // expf(-g) of every value first; the rare near-midpoint results then take
+    // the exception table, one lookup per lane at a time, so that a warp pays
+    // one table round trip for its first flagged values (taken value by value,
+    // every flagged k cost a warp one more trip).
+    float e[kPer];
+    int nt[kPer];
 #pragma unroll
-    for (int k = 0; k < kPer; ++k) sw[k] = swiglu1(gv[k], uv[k], a.expf, s.expf_tab);
+    for (int k = 0; k < kPer; ++k) e[k] = i4d_expf_core2(-gv[k], s.expf_tab, &nt[k]);
+    int pending = 0;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) pending |= nt[k] << k;
+    while (__any_sync(0xffffffffu, pending != 0)) {
+        const int k0 = pending ? __ffs(pending) - 1 : -1;
+        float xf = 0.0f, yf = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kPer; ++k)
+            if (k == k0) {
+                xf = -gv[k];
+                yf = e[k];
+            }
+        if (k0 >= 0) {
+            const float fixed = expf_table_fix(xf, yf, a.expf);
+#pragma unroll
+            for (int k = 0; k < kPer; ++k)
+                if (k == k0) e[k] = fixed;
+            pending &= pending - 1;
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) sw[k] = swiglu_e(gv[k], uv[k], e[k]);
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
         const int lg = cw + k * kTokWarps;
@@ -857,6 +901,13 @@ __device__ __forceinline__ void tok_attention(const TokenArgs& ta, const TokSmem
         misc[0] = INT32_MIN;
     }
     if (tid < 33) S.lut[tid] = a.exp2_q30[tid];
+    // RoPE factors of this position: independent of the QKV projection, so
+    // loaded before waiting for it.
+    long long rope_c = 0, rope_s = 0;
+    if (tid < 128) {
+        rope_c = a.rope_cos[pos * 64 + ((tid & 127) >> 1)];
+        rope_s = a.rope_sin[pos * 64 + ((tid & 127) >> 1)];
+    }
     tok_bar();
     const long long t_a0 = clock64();
     if (tid == 0) tl_mark<TR>(ta, layer, 20);
@@ -887,7 +938,7 @@ __device__ __forceinline__ void tok_attention(const TokenArgs& ta, const TokSmem
     tok_bar();
     if (tid < 128) {
         const int pr = d >> 1;
-        const long long c = a.rope_cos[pos * 64 + pr], sn = a.rope_sin[pos * 64 + pr];
+        const long long c = rope_c, sn = rope_s;
         const long long qa = S.qrot[2 * pr], qb = S.qrot[2 * pr + 1];
         const long long ka = S.krot[2 * pr], kb = S.krot[2 * pr + 1];
         qv = (d & 1) ? sat32((qa * sn + qb * c) >> 17) : sat32((qa * c - qb * sn) >> 17);
