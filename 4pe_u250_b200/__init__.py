@@ -33,8 +33,24 @@ EXPORTS = [
     "i4d_attention", "i4d_swiglu_quant", "i4d_expf", "i4d_decode_token_async", "i4d_stream",
     "i4d_profile_token", "i4d_token_breakdown", "i4d_linear_bank_noalloc",
     "i4d_token_timeline", "i4d_create_shard", "i4d_shard_export", "i4d_shard_attach",
-    "i4d_decode_greedy", "i4d_argmax",
+    "i4d_decode_greedy", "i4d_argmax", "i4d_sampler_init", "i4d_sample", "i4d_decode_sample",
 ]
+
+SAMPLER_HOST = 0      # decode_host.cpp:724-868
+SAMPLER_EMULATOR = 1  # emulator:1411-1569
+
+
+class Sampler(ctypes.Structure):
+    """i4d_sampler: temperature, top-p, repeat penalty, mode and the xorshift64*
+    state that every coin flip advances (the reference Sampler's members)."""
+    _fields_ = [("temperature", ctypes.c_float), ("top_p", ctypes.c_float), ("repeat_penalty", ctypes.c_float),
+                ("mode", ctypes.c_int32), ("rng_state", ctypes.c_uint64)]
+
+    @classmethod
+    def make(cls, temperature, top_p=0.0, repeat_penalty=1.0, seed=0, mode=SAMPLER_HOST):
+        s = cls()
+        load_library().i4d_sampler_init(ctypes.byref(s), temperature, top_p, repeat_penalty, seed, mode)
+        return s
 
 _STAGES = ["qkv", "o", "gu", "down", "logits"]
 BREAKDOWN = ([f"wait_{x}" for x in _STAGES] + [f"prologue_{x}" for x in _STAGES] + [f"chunks_{x}" for x in _STAGES]
@@ -106,11 +122,15 @@ def load_library():
         "i4d_shard_attach": [P, P, ctypes.c_size_t],
         "i4d_decode_greedy": [P, ctypes.c_uint32, ctypes.c_int32, P, P],
         "i4d_argmax": [P, P, ctypes.c_size_t, P],
+        "i4d_sample": [P, P, P, ctypes.c_uint32, P, P],
+        "i4d_decode_sample": [P, ctypes.c_uint32, ctypes.c_int32, P, ctypes.c_uint32, P, P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
         fn.argtypes = args
         fn.restype = ctypes.c_int
+    L.i4d_sampler_init.argtypes = [P, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_uint64, ctypes.c_int32]
+    L.i4d_sampler_init.restype = None
     L.i4d_destroy.restype = None
     L.i4d_last_error.restype = ctypes.c_char_p
     L.i4d_stream.restype = ctypes.c_void_p
@@ -224,6 +244,22 @@ class Context:
         logits = np.empty(formats.PADDED_VOCAB, dtype=np.float32) if want_logits else None
         self._check(self._L.i4d_decode_greedy(self._h, position, int(token_id), ctypes.byref(nxt), _ptr(logits)))
         return nxt.value, logits
+
+    def sample(self, logits_dev_ptr, history, sampler):
+        """One device draw over 32000 logits at a device pointer; advances sampler.rng_state."""
+        h = np.ascontiguousarray(history, dtype=np.int32)
+        tok = ctypes.c_int32(0)
+        self._check(self._L.i4d_sample(self._h, logits_dev_ptr, h.ctypes.data if h.size else None, h.size,
+                                       ctypes.byref(sampler), ctypes.byref(tok)))
+        return tok.value
+
+    def decode_sample(self, position, token_id, history, sampler):
+        """One decode step from a token id, then one device draw over its logits: the next id."""
+        h = np.ascontiguousarray(history, dtype=np.int32)
+        nxt = ctypes.c_int32(0)
+        self._check(self._L.i4d_decode_sample(self._h, position, int(token_id), h.ctypes.data if h.size else None,
+                                              h.size, ctypes.byref(sampler), ctypes.byref(nxt)))
+        return nxt.value
 
     def argmax(self, logits):
         """The device argmax of i4d_decode_greedy over a host array."""

@@ -22,6 +22,7 @@
 #include "i4d_blocks.cuh"
 #include "i4d_linear.cuh"
 #include "i4d_token.cuh"
+#include "i4d_sample.cuh"
 
 extern "C" {
 extern const unsigned int i4d_expf_fix_count;
@@ -135,6 +136,14 @@ struct i4d_ctx {
     int* h_pos = nullptr;
     int* h_tok = nullptr;
     unsigned long long* h_argmax = nullptr;
+    // Sampler: history, radix-sort scratch, state and result words.
+    int* d_sample_hist = nullptr;
+    uint32_t* d_sample_keys = nullptr;
+    uint32_t* d_sample_idx = nullptr;
+    unsigned long long* d_sample_state = nullptr;
+    int* d_sample_out = nullptr;
+    unsigned long long* h_sample_state = nullptr;
+    int* h_sample_out = nullptr;
     unsigned* h_err = nullptr;
     bool bank_loaded[4] = {false, false, false, false};
     bool rope_loaded = false;
@@ -465,10 +474,12 @@ void i4d_destroy(i4d_ctx* c) {
     void* dev[] = {c->d_w, c->d_gamma, c->d_rope_cos, c->d_rope_sin, c->d_exp2, c->d_expf_slots, c->d_kv,
                    c->d_emb, c->d_resid, c->d_recip, c->d_shared, c->d_ao_q, c->d_ao_e, c->d_ad_q,
                    c->d_ad_e, c->d_logits, c->d_counters, c->d_err, c->d_pos, c->d_scratch, c->d_attn_coef, c->d_recips, c->d_trace,
-                   c->d_tok, c->d_argmax};
+                   c->d_tok, c->d_argmax, c->d_sample_hist, c->d_sample_keys, c->d_sample_idx,
+                   c->d_sample_state, c->d_sample_out};
     for (void* p : dev)
         if (p) cudaFree(p);
-    void* host[] = {c->h_resid_in, c->h_resid_out, c->h_logits, c->h_pos, c->h_err, c->h_tok, c->h_argmax};
+    void* host[] = {c->h_resid_in, c->h_resid_out, c->h_logits, c->h_pos, c->h_err, c->h_tok, c->h_argmax,
+                    c->h_sample_state, c->h_sample_out};
     for (void* p : host)
         if (p) cudaFreeHost(p);
     if (c->stream) cudaStreamDestroy(c->stream);
@@ -513,6 +524,8 @@ static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ct
     CKC(cudaFuncSetAttribute(k_linear, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBudget)));
     CKC(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(attn_smem_bytes())));
+    CKC(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(sample_smem_bytes())));
     CKC(cudaFuncSetAttribute(k_token<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(tok_smem_bytes())));
     CKC(cudaFuncSetAttribute(k_token<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -568,6 +581,13 @@ static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ct
     CKC(cudaMallocHost(&c->h_pos, sizeof(int)));
     CKC(cudaMallocHost(&c->h_tok, sizeof(int)));
     CKC(cudaMallocHost(&c->h_argmax, sizeof(unsigned long long)));
+    CKC(cudaMalloc(&c->d_sample_hist, kSampleMaxHistory * sizeof(int)));
+    CKC(cudaMalloc(&c->d_sample_keys, 2ull * kSampleMaxVocab * sizeof(uint32_t)));
+    CKC(cudaMalloc(&c->d_sample_idx, 2ull * kSampleMaxVocab * sizeof(uint32_t)));
+    CKC(cudaMalloc(&c->d_sample_state, sizeof(unsigned long long)));
+    CKC(cudaMalloc(&c->d_sample_out, sizeof(int)));
+    CKC(cudaMallocHost(&c->h_sample_state, sizeof(unsigned long long)));
+    CKC(cudaMallocHost(&c->h_sample_out, sizeof(int)));
     CKC(cudaMallocHost(&c->h_err, sizeof(unsigned)));
 
     // exp2 LUT of the online softmax: round(2^(30 + i/32)), and log2(e) in
@@ -807,6 +827,113 @@ i4d_status i4d_decode_greedy(i4d_ctx* c, uint32_t position, int32_t token_id, in
     *next_id = k == 0ull ? -1 : static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(k & 0xffffffffu));
     if (logits_out) CK(cudaMemcpy(logits_out, c->d_logits, kPVocab * sizeof(float), cudaMemcpyDeviceToHost));
     return I4D_OK;
+}
+
+void i4d_sampler_init(i4d_sampler* s, float temperature, float top_p, float repeat_penalty, uint64_t seed,
+                      int32_t mode) {
+    if (!s) return;
+    s->temperature = temperature;
+    s->top_p = top_p;
+    s->repeat_penalty = repeat_penalty;
+    s->mode = mode;
+    // The host sampler never starts from a zero state (decode_host.cpp:731);
+    // the emulator takes the seed as it is (emulator:1499).
+    s->rng_state = (mode == I4D_SAMPLER_HOST && seed == 0) ? 1 : seed;
+}
+
+static i4d_status check_sampler(i4d_ctx* c, const int32_t* history, uint32_t n_history, const i4d_sampler* s) {
+    if (!s) return fail(c, I4D_ERR_ARG, "null sampler");
+    if (s->mode != I4D_SAMPLER_HOST && s->mode != I4D_SAMPLER_EMULATOR)
+        return fail(c, I4D_ERR_ARG, "sampler mode %d unknown", s->mode);
+    if (!(s->temperature >= 0.0f) || !(s->repeat_penalty > 0.0f) || s->top_p != s->top_p)
+        return fail(c, I4D_ERR_ARG, "sampler parameters out of range (temperature %g, top_p %g, penalty %g)",
+                    s->temperature, s->top_p, s->repeat_penalty);
+    if (n_history > static_cast<uint32_t>(kSampleMaxHistory))
+        return fail(c, I4D_ERR_SIZE, "history of %u tokens exceeds %d", n_history, kSampleMaxHistory);
+    if (n_history && !history) return fail(c, I4D_ERR_ARG, "null history");
+    return I4D_OK;
+}
+
+// Enqueues one draw over logits_dev[0, 32000) on the context stream.
+static i4d_status enqueue_sample(i4d_ctx* c, const float* logits_dev, const int32_t* history, uint32_t n_history,
+                                 const i4d_sampler* s) {
+    if (n_history)
+        CK(cudaMemcpyAsync(c->d_sample_hist, history, n_history * sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
+    *c->h_sample_state = s->rng_state;
+    CK(cudaMemcpyAsync(c->d_sample_state, c->h_sample_state, sizeof(unsigned long long), cudaMemcpyHostToDevice,
+                       c->stream));
+    SampleArgs a = {};
+    a.logits = logits_dev;
+    a.n = kVocab;
+    a.history = c->d_sample_hist;
+    a.n_history = static_cast<int>(n_history);
+    a.temperature = s->temperature;
+    a.top_p = s->top_p;
+    a.penalty = s->repeat_penalty;
+    a.mode = s->mode;
+    a.state = c->d_sample_state;
+    a.expf = c->expf;
+    a.keys = c->d_sample_keys;
+    a.idx = c->d_sample_idx;
+    a.out = c->d_sample_out;
+    k_sample<<<1, kSampleThreads, sample_smem_bytes(), c->stream>>>(a);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(c->h_sample_out, c->d_sample_out, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(c->h_sample_state, c->d_sample_state, sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                       c->stream));
+    return I4D_OK;
+}
+
+// After the stream has finished: the token and the advanced state, or the
+// host sampler's exceptions as errors.
+static i4d_status finish_sample(i4d_ctx* c, i4d_sampler* s, int32_t* token_out) {
+    const int r = *c->h_sample_out;
+    if (r == kSampleAllNan) return fail(c, I4D_ERR_ARG, "all valid-vocabulary logits are NaN");
+    if (r == kSampleNoFinite) return fail(c, I4D_ERR_ARG, "all valid-vocabulary logits are non-finite");
+    if (r == kSampleBadSum) return fail(c, I4D_ERR_ARG, "invalid probability sum during sampling");
+    s->rng_state = *c->h_sample_state;
+    *token_out = r;
+    return I4D_OK;
+}
+
+i4d_status i4d_sample(i4d_ctx* c, const float* logits_dev, const int32_t* history, uint32_t n_history,
+                      i4d_sampler* s, int32_t* token_out) {
+    if (!c || !logits_dev || !token_out) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    const i4d_status chk = check_sampler(c, history, n_history, s);
+    if (chk != I4D_OK) return chk;
+    CK(cudaSetDevice(c->device));
+    const i4d_status st = enqueue_sample(c, logits_dev, history, n_history, s);
+    if (st != I4D_OK) return st;
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaGetLastError());
+    return finish_sample(c, s, token_out);
+}
+
+i4d_status i4d_decode_sample(i4d_ctx* c, uint32_t position, int32_t token_id, const int32_t* history,
+                             uint32_t n_history, i4d_sampler* s, int32_t* next_id) {
+    if (!c || !next_id) return c ? fail(c, I4D_ERR_ARG, "null next_id") : I4D_ERR_ARG;
+    if (!all_loaded(c) || !c->d_emb)
+        return fail(c, I4D_ERR_STATE, "banks, rope LUT and embeddings must be loaded before sampled decoding");
+    if (c->flags & I4D_FLAG_STAGED) return fail(c, I4D_ERR_STATE, "sampled decoding needs the persistent token kernel");
+    if (position >= static_cast<uint32_t>(c->stride))
+        return fail(c, I4D_ERR_ARG, "position %u out of range (KV capacity %d)", position, c->stride);
+    if (token_id < 0 || token_id >= kVocab) return fail(c, I4D_ERR_ARG, "token id %d out of range", token_id);
+    const i4d_status chk = check_sampler(c, history, n_history, s);
+    if (chk != I4D_OK) return chk;
+    CK(cudaSetDevice(c->device));
+    *c->h_pos = static_cast<int>(position);
+    *c->h_tok = token_id;
+    *c->h_err = 0;
+    i4d_status st = enqueue_greedy(c);
+    if (st == I4D_OK) st = enqueue_sample(c, c->d_logits, history, n_history, s);
+    if (st != I4D_OK) return st;
+    CK(cudaStreamSynchronize(c->stream));
+    if (*c->h_err) {
+        const unsigned e = *c->h_err;
+        CK(reset_sync(c));
+        return fail(c, (e & kErrArg) ? I4D_ERR_ARG : I4D_ERR_TIMEOUT, "device error word 0x%x", e);
+    }
+    return finish_sample(c, s, next_id);
 }
 
 i4d_status i4d_decode_token(i4d_ctx* c, uint32_t position, const float* residual_in, float* logits_out,

@@ -139,6 +139,47 @@ i4d_status i4d_decode_token(i4d_ctx* ctx, uint32_t position, const float* residu
 i4d_status i4d_decode_greedy(i4d_ctx* ctx, uint32_t position, int32_t token_id, int32_t* next_id,
                              float* logits_out);
 
+/* Token sampler (temperature, top-p, repeat penalty) on the device.
+ * Replaces the host's Sampler (decode_host.cpp:724-868, mode
+ * I4D_SAMPLER_HOST) and also reproduces the emulator's llama2.c sampler
+ * (emulator:1411-1569, mode I4D_SAMPLER_EMULATOR).  Temperature 0 is greedy.
+ * A top_p outside (0, 1) samples the whole softmax (multinomial). Only
+ * rng_state changes between draws: each draw that flips a coin advances it,
+ * as the reference's member state does. */
+#define I4D_SAMPLER_HOST 0
+#define I4D_SAMPLER_EMULATOR 1
+typedef struct i4d_sampler {
+    float temperature;
+    float top_p;
+    float repeat_penalty; /* 1: off; applied once per distinct token of the history */
+    int32_t mode;         /* I4D_SAMPLER_HOST or I4D_SAMPLER_EMULATOR */
+    uint64_t rng_state;   /* xorshift64* state */
+} i4d_sampler;
+
+/* Fills *s as the reference's constructors do (the host sampler replaces a
+ * zero seed by 1, decode_host.cpp:731; the emulator keeps it). */
+void i4d_sampler_init(i4d_sampler* s, float temperature, float top_p, float repeat_penalty, uint64_t seed,
+                      int32_t mode);
+
+/* One draw over logits_dev[0, 32000) (a device pointer, e.g. the logits of
+ * i4d_decode_token_async); history (host, n_history <= 16384 ids; ids outside
+ * the vocabulary are ignored) feeds the repeat penalty.  Writes the token and
+ * advances s->rng_state.  The host sampler's exceptions (all logits NaN, none
+ * finite, invalid probability sum) return I4D_ERR_ARG.  Top-p candidates with
+ * exactly equal probabilities are taken in index order, where the references'
+ * unstable library sorts leave the order unspecified.  One CTA; the serial
+ * sums and walks of the references stay serial (FP32 addition is not
+ * associative). */
+i4d_status i4d_sample(i4d_ctx* ctx, const float* logits_dev, const int32_t* history, uint32_t n_history,
+                      i4d_sampler* s, int32_t* token_out);
+
+/* i4d_decode_greedy with the sampler in place of the argmax: one decode step
+ * from token_id at position, then one draw (as i4d_sample) over its logits,
+ * all on the device; per step only the position, the id and the history go to
+ * the device and the id and state back (no logits).  Needs i4d_load_embeddings. */
+i4d_status i4d_decode_sample(i4d_ctx* ctx, uint32_t position, int32_t token_id, const int32_t* history,
+                             uint32_t n_history, i4d_sampler* s, int32_t* next_id);
+
 /* Device-resident form of i4d_decode_token for pipelines that keep their
  * data on the GPU: residual_in_dev / logits_out_dev are device pointers
  * (4096 / 32256 floats).  The step is only enqueued on the context stream;

@@ -43,10 +43,13 @@ class Oracle:
             "i4o_expf_array": [P, P, ctypes.c_size_t],
             "i4o_argmax": [P, ctypes.c_int],
             "i4o_exp_negative_q17": [ctypes.c_int32],
+            "i4o_sample": [ctypes.c_int, P, ctypes.c_int, P, ctypes.c_int, ctypes.c_float, ctypes.c_float,
+                           ctypes.c_float, P],
         }
         for k, v in sigs.items():
             getattr(L, k).argtypes = v
         L.i4o_argmax.restype = ctypes.c_int
+        L.i4o_sample.restype = ctypes.c_int
         L.i4o_exp_negative_q17.restype = ctypes.c_uint32
         self.L = L
         self._rope = None
@@ -159,6 +162,16 @@ class Oracle:
         x = np.ascontiguousarray(logits, dtype=np.float32)
         return self.L.i4o_argmax(x.ctypes.data, n)
 
+    def sample(self, mode, logits, history, temperature, top_p, repeat_penalty, state):
+        """One sampler draw (mode 0: decode_host.cpp:724-868, 1: emulator:1411-1569);
+        returns (token, advanced state)."""
+        x = np.ascontiguousarray(logits, dtype=np.float32)
+        h = np.ascontiguousarray(history, dtype=np.int32)
+        st = np.array([state], np.uint64)
+        t = self.L.i4o_sample(mode, x.ctypes.data, x.size, h.ctypes.data if h.size else None, h.size,
+                              temperature, top_p, repeat_penalty, st.ctypes.data)
+        return t, int(st[0])
+
 
 def ref_available():
     return os.path.exists(REF_SO)
@@ -188,11 +201,21 @@ class RefEmulator:
             "ref_swiglu": [P, P, ctypes.c_int, P],
             "ref_kv_get": [ctypes.c_int] * 4 + [P, P, P, P],
             "ref_argmax": [P, ctypes.c_int],
+            "ref_sample": [P, ctypes.c_int, P, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_float, P],
         }
         for k, v in sigs.items():
             getattr(L, k).argtypes = v
         L.ref_float_to_q17.restype = ctypes.c_int32
         self.L = L
+
+    def sample(self, logits, history, temperature, top_p, repeat_penalty, state):
+        """The emulator's own sampler (emulator:1411-1569): (token, advanced state)."""
+        x = np.array(logits, dtype=np.float32)  # the emulator edits it
+        h = np.ascontiguousarray(history, dtype=np.int32)
+        st = (ctypes.c_ulonglong * 1)(state)
+        t = self.L.ref_sample(x.ctypes.data, x.size, h.ctypes.data if h.size else None, h.size, temperature, top_p,
+                              repeat_penalty, ctypes.addressof(st))
+        return t, int(st[0])
 
     def load(self, directory, layers, stride):
         if self.L.ref_load(directory.encode(), layers, stride) != 0:

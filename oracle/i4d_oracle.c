@@ -578,6 +578,151 @@ int i4o_argmax(const float* logits, int n) {
     return best;
 }
 
+/* ---- sampler (decode_host.cpp:724-868, emulator:1411-1569) ---- */
+
+/* decode_host.cpp:703-717: first strict maximum, NaN skipped; -1 if none. */
+static int sample_argmax_host(const float* p, int n) {
+    int best = -1;
+    for (int i = 0; i < n; ++i) {
+        if (isnan(p[i])) continue;
+        if (best < 0 || p[i] > p[best]) best = i;
+    }
+    return best;
+}
+
+/* Both references: xorshift64* (decode_host.cpp:806-816, emulator:1509-1518). */
+static float sample_coin(uint64_t* st) {
+    *st ^= *st >> 12;
+    *st ^= *st << 25;
+    *st ^= *st >> 27;
+    const uint32_t u = (uint32_t)((*st * 0x2545F4914F6CDD1DULL) >> 32);
+    return (float)(u >> 8) / 16777216.0f;
+}
+
+typedef struct {
+    float p;
+    int i;
+} SampleCand;
+
+static int cand_desc(const void* a, const void* b) {
+    const SampleCand* x = (const SampleCand*)a;
+    const SampleCand* y = (const SampleCand*)b;
+    if (x->p > y->p) return -1;
+    if (x->p < y->p) return 1;
+    return (x->i > y->i) - (x->i < y->i);
+}
+
+int i4o_sample(int mode, const float* logits, int n, const int32_t* history, int n_history,
+               float temperature, float top_p, float repeat_penalty, uint64_t* rng_state) {
+    const int host = mode == 0;
+    if (host && temperature == 0.0f && repeat_penalty == 1.0f) return sample_argmax_host(logits, n);
+    float* p = (float*)malloc(sizeof(float) * (size_t)n);
+    unsigned char* pen = (unsigned char*)calloc((size_t)n, 1);
+    memcpy(p, logits, sizeof(float) * (size_t)n);
+    int result = -3;
+    if (repeat_penalty != 1.0f) {
+        for (int h = 0; h < n_history; ++h) {
+            const int t = history[h];
+            if (t < 0 || t >= n || pen[t]) continue;
+            if (!host || isfinite(p[t])) p[t] = p[t] < 0.0f ? p[t] * repeat_penalty : p[t] / repeat_penalty;
+            pen[t] = 1;
+        }
+    }
+    if (temperature == 0.0f) {
+        result = host ? sample_argmax_host(p, n) : i4o_argmax(p, n);
+        goto done;
+    }
+    float mx;
+    if (host) {
+        mx = -INFINITY;
+        for (int i = 0; i < n; ++i)
+            if (isfinite(p[i]) && p[i] > mx) mx = p[i];
+        if (!isfinite(mx)) {
+            result = -2;
+            goto done;
+        }
+    } else {
+        for (int i = 0; i < n; ++i) p[i] /= temperature;
+        mx = p[0];
+        for (int i = 1; i < n; ++i)
+            if (p[i] > mx) mx = p[i];
+    }
+    float sum = 0.0f;
+    for (int i = 0; i < n; ++i) {
+        if (host) p[i] = isfinite(p[i]) ? expf((p[i] - mx) / temperature) : 0.0f;
+        else p[i] = expf(p[i] - mx);
+        sum += p[i];
+    }
+    if (host && (!(sum > 0.0f) || !isfinite(sum))) {
+        result = -3;
+        goto done;
+    }
+    for (int i = 0; i < n; ++i) p[i] /= sum;
+    const float coin = sample_coin(rng_state);
+    if (top_p <= 0.0f || top_p >= 1.0f) {
+        float cdf = 0.0f;
+        result = n - 1;
+        for (int i = 0; i < n; ++i) {
+            cdf += p[i];
+            if (coin < cdf) {
+                result = i;
+                break;
+            }
+        }
+        goto done;
+    }
+    {
+        const float cutoff = (1.0f - top_p) / (float)(n - 1);
+        SampleCand* c = (SampleCand*)malloc(sizeof(SampleCand) * (size_t)n);
+        int m = 0;
+        for (int i = 0; i < n; ++i)
+            if (p[i] >= cutoff) {
+                c[m].p = p[i];
+                c[m].i = i;
+                ++m;
+            }
+        if (m == 0) {
+            result = sample_argmax_host(p, n);
+            free(c);
+            goto done;
+        }
+        qsort(c, (size_t)m, sizeof(SampleCand), cand_desc);
+        float cum = 0.0f;
+        int last;
+        if (host) {
+            for (last = 0; last < m; ++last) {
+                cum += c[last].p;
+                if (cum >= top_p) break;
+            }
+            if (last > m - 1) last = m - 1;
+        } else {
+            last = m - 1;
+            for (int i = 0; i < m; ++i) {
+                cum += c[i].p;
+                if (cum > top_p) {
+                    last = i;
+                    break;
+                }
+            }
+        }
+        const float target = coin * cum;
+        float cdf = 0.0f;
+        result = c[last].i;
+        for (int i = 0; i <= last; ++i) {
+            cdf += c[i].p;
+            if (target < cdf) {
+                result = c[i].i;
+                break;
+            }
+        }
+        free(c);
+    }
+done:
+    free(p);
+    free(pen);
+    return result;
+}
+
 void i4o_float_to_q17_array(const float* x, int n, int32_t* out) {
     for (int i = 0; i < n; ++i) out[i] = i4o_float_to_q17(x[i]);
 }

@@ -137,6 +137,16 @@ void i4o_expf_array(const float* x, float* y, size_t n); /* host C library expf 
 /* emulator:1428-1438: index of the first strict maximum over n. */
 int i4o_argmax(const float* logits, int n);
 
+/* One sampler draw over logits[0, n), the state advanced in place.
+ * mode 0: decode_host.cpp:724-868 (the hardware host's Sampler); mode 1:
+ * emulator:1411-1569 (llama2.c's).  Top-p candidates are ordered by
+ * probability, descending, equal probabilities by index (both references
+ * leave that order to an unstable library sort).  Returns the token, or
+ * -1 (every logit NaN), -2 (no finite logit), -3 (invalid probability sum):
+ * the host's exceptions. */
+int i4o_sample(int mode, const float* logits, int n, const int32_t* history, int n_history,
+               float temperature, float top_p, float repeat_penalty, uint64_t* rng_state);
+
 #ifdef __cplusplus
 }
 #endif

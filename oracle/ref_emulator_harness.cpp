@@ -138,4 +138,18 @@ void ref_kv_get(int bank, int layer, int lh, int token, int8_t* k8, uint8_t* ksh
 
 int ref_argmax(const float* logits, int n) { return sample_argmax(const_cast<float*>(logits), n); }
 
+// The emulator's sampler (emulator:1411-1569): one draw with the given state,
+// which is advanced in place.  `logits` is modified (penalty, softmax) as the
+// emulator does; pass a copy.
+int ref_sample(float* logits, int n, const int32_t* history, int n_history, float temperature, float topp,
+               float repeat_penalty, unsigned long long* rng_state) {
+    Sampler s;
+    build_sampler(&s, n, temperature, topp, repeat_penalty, *rng_state);
+    const std::vector<int> h(history, history + n_history);
+    const int t = sample(&s, logits, h);
+    *rng_state = s.rng_state;
+    free_sampler(&s);
+    return t;
+}
+
 }  // extern "C"
