@@ -95,6 +95,58 @@ __device__ __forceinline__ int sample_argmax(const float* p, int n, unsigned lon
     return best == 0ull ? -1 : static_cast<int>(0xffffffffu - static_cast<uint32_t>(best & 0xffffffffu));
 }
 
+// Serial FP32 sum of v[0, m), in order, from +0.0f.  Batches of 32 values
+// are loaded before their chain of adds, so the loop runs at the add latency.
+__device__ __forceinline__ float sample_serial_sum(const float* v, int m) {
+    float s = 0.0f;
+    int i = 0;
+    for (; i + 32 <= m; i += 32) {
+        float x[32];
+#pragma unroll
+        for (int k = 0; k < 32; k += 4) *reinterpret_cast<float4*>(x + k) = *reinterpret_cast<const float4*>(v + i + k);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) s = __fadd_rn(s, x[k]);
+    }
+    for (; i < m; ++i) s = __fadd_rn(s, v[i]);
+    return s;
+}
+
+// Serial running sums c_i = fl(c_{i-1} + v_i) (c_{-1} = +0.0f) written over
+// v, up to the first i where stop(c_i) holds; returns that i, or m.  Batches
+// of 32 are summed first and then checked element by element (a NaN makes
+// every later sum NaN, so the end of a batch alone cannot tell).  v must be
+// 16-byte aligned.
+template <typename Stop>
+__device__ __forceinline__ int sample_serial_prefix(float* v, int m, Stop stop) {
+    float c = 0.0f;
+    int i = 0;
+    for (; i + 32 <= m; i += 32) {
+        float x[32];
+#pragma unroll
+        for (int k = 0; k < 32; k += 4) *reinterpret_cast<float4*>(x + k) = *reinterpret_cast<const float4*>(v + i + k);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+            c = __fadd_rn(c, x[k]);
+            x[k] = c;
+        }
+#pragma unroll
+        for (int k = 0; k < 32; k += 4) *reinterpret_cast<float4*>(v + i + k) = *reinterpret_cast<const float4*>(x + k);
+        bool any = false;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) any |= stop(x[k]);
+        if (any) {
+            for (int k = 0; k < 32; ++k)
+                if (stop(x[k])) return i + k;
+        }
+    }
+    for (; i < m; ++i) {
+        c = __fadd_rn(c, v[i]);
+        v[i] = c;
+        if (stop(c)) return i;
+    }
+    return m;
+}
+
 __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const __grid_constant__ SampleArgs a) {
     extern __shared__ __align__(16) uint8_t sample_smem[];
     float* p = reinterpret_cast<float*>(sample_smem);
@@ -157,11 +209,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const __grid_const
         else p[i] = expf_libc(__fsub_rn(v, mx), a.expf);
     }
     __syncthreads();
-    if (tid == 0) {  // the serial sum of both references
-        float s = 0.0f;
-        for (int i = 0; i < n; ++i) s = __fadd_rn(s, p[i]);
-        redf[0] = s;
-    }
+    if (tid == 0) redf[0] = sample_serial_sum(p, n);  // the serial sum of both references
     __syncthreads();
     const float sum = redf[0];
     if (host && (!(sum > 0.0f) || !isfinite(sum))) {
@@ -178,17 +226,9 @@ __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const __grid_const
     const float coin = s_coin;
     const float top_p = a.top_p;
     if (top_p <= 0.0f || top_p >= 1.0f) {
-        if (tid == 0) {  // multinomial walk
-            float cdf = 0.0f;
-            int r = n - 1;
-            for (int i = 0; i < n; ++i) {
-                cdf = __fadd_rn(cdf, p[i]);
-                if (coin < cdf) {
-                    r = i;
-                    break;
-                }
-            }
-            *a.out = r;
+        if (tid == 0) {  // multinomial walk: the first running sum above the coin
+            const int r = sample_serial_prefix(p, n, [coin](float c) { return coin < c; });
+            *a.out = r < n ? r : n - 1;
         }
         return;
     }
@@ -307,38 +347,25 @@ __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const __grid_const
         }
         __syncthreads();
     }
-    if (tid == 0) {  // nucleus and the walk inside it, serially
-        const uint32_t* ks = a.keys;  // four passes end in buffer 0
-        const uint32_t* is = a.idx;
-        float cum = 0.0f;
+    // Nucleus and the walk inside it: the sorted probabilities to shared
+    // memory (p is free now), running sums in place, serially.
+    for (int i = tid; i < m; i += kSampleThreads) p[i] = __uint_as_float(~a.keys[i]);  // four passes end in buffer 0
+    __syncthreads();
+    if (tid == 0) {
         int last;
-        if (host) {
-            for (last = 0; last < m; ++last) {
-                cum = __fadd_rn(cum, __uint_as_float(~ks[last]));
-                if (cum >= top_p) break;
-            }
-            if (last > m - 1) last = m - 1;
-        } else {
-            last = m - 1;
-            for (int i = 0; i < m; ++i) {
-                cum = __fadd_rn(cum, __uint_as_float(~ks[i]));
-                if (cum > top_p) {
-                    last = i;
-                    break;
-                }
-            }
-        }
+        if (host) last = sample_serial_prefix(p, m, [top_p](float c) { return c >= top_p; });
+        else last = sample_serial_prefix(p, m, [top_p](float c) { return c > top_p; });
+        if (last > m - 1) last = m - 1;  // no break: the sum of every candidate
+        const float cum = p[last];
         const float target = __fmul_rn(coin, cum);
-        float cdf = 0.0f;
-        int r = static_cast<int>(is[last]);
-        for (int i = 0; i <= last; ++i) {
-            cdf = __fadd_rn(cdf, __uint_as_float(~ks[i]));
-            if (target < cdf) {
-                r = static_cast<int>(is[i]);
-                break;
-            }
+        // First i <= last with target < c_i (the running sums do not decrease).
+        int lo = 0, hi = last + 1;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (target < p[mid]) hi = mid;
+            else lo = mid + 1;
         }
-        *a.out = r;
+        *a.out = static_cast<int>(a.idx[lo <= last ? lo : last]);
     }
 }
 
