@@ -34,6 +34,7 @@ EXPORTS = [
     "i4d_profile_token", "i4d_token_breakdown", "i4d_linear_bank_noalloc",
     "i4d_token_timeline", "i4d_create_shard", "i4d_shard_export", "i4d_shard_attach",
     "i4d_decode_greedy", "i4d_argmax", "i4d_sampler_init", "i4d_sample", "i4d_decode_sample",
+    "i4d_pack_autoround_matrix", "i4d_pack_fp32_head",
 ]
 
 SAMPLER_HOST = 0      # decode_host.cpp:724-868
@@ -124,6 +125,8 @@ def load_library():
         "i4d_argmax": [P, P, ctypes.c_size_t, P],
         "i4d_sample": [P, P, P, ctypes.c_uint32, P, P],
         "i4d_decode_sample": [P, ctypes.c_uint32, ctypes.c_int32, P, ctypes.c_uint32, P, P],
+        "i4d_pack_autoround_matrix": [P, ctypes.c_int, ctypes.c_int, P, P, P],
+        "i4d_pack_fp32_head": [P, P, P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -213,6 +216,20 @@ class Context:
     def load_bank(self, bank, image):
         image = np.ascontiguousarray(image, dtype=np.uint8)
         self._check(self._L.i4d_load_bank(self._h, bank, image.ctypes.data, image.nbytes))
+
+    def load_bank_device(self, bank, image_dev_ptr):
+        """Load one bank image that is already in device memory (e.g. GPU-packed)."""
+        self._check(self._L.i4d_load_bank(self._h, bank, image_dev_ptr, formats.BANK_BYTES))
+
+    def pack_autoround_matrix(self, layer, mode, nibbles_dev_ptr, scales_dev_ptr, image_dev_ptrs):
+        """Pack one AutoRound projection into four device bank images (i4d_pack_autoround_matrix)."""
+        arr = (ctypes.c_void_p * 4)(*image_dev_ptrs)
+        self._check(self._L.i4d_pack_autoround_matrix(self._h, layer, mode, nibbles_dev_ptr, scales_dev_ptr, arr))
+
+    def pack_fp32_head(self, head_dev_ptr, image_dev_ptrs):
+        """Quantise and pack an FP32 LM head into four device bank images (i4d_pack_fp32_head)."""
+        arr = (ctypes.c_void_p * 4)(*image_dev_ptrs)
+        self._check(self._L.i4d_pack_fp32_head(self._h, head_dev_ptr, arr))
 
     def load_banks(self, images):
         """Loads the held banks from the four images (the others are skipped)."""

@@ -23,6 +23,7 @@
 #include "i4d_linear.cuh"
 #include "i4d_token.cuh"
 #include "i4d_sample.cuh"
+#include "i4d_pack.cuh"
 
 extern "C" {
 extern const unsigned int i4d_expf_fix_count;
@@ -714,7 +715,8 @@ i4d_status i4d_load_bank(i4d_ctx* c, int bank, const void* bytes, size_t n) {
     CK(cudaMalloc(&stage, n));
     // Stream-ordered: a plain cudaMemcpy from pageable memory may return
     // before its DMA lands, and the context stream does not wait for it.
-    cudaError_t e = cudaMemcpyAsync(stage, bytes, n, cudaMemcpyHostToDevice, c->stream);
+    // The image may be in host or device memory (a bank packed on the GPU).
+    cudaError_t e = cudaMemcpyAsync(stage, bytes, n, cudaMemcpyDefault, c->stream);
     for (int l = 0; e == cudaSuccess && l <= c->layers; ++l) {
         for (int m = 0; m < 8; ++m) {
             if ((l == c->layers) != (m == 7)) continue;
@@ -827,6 +829,74 @@ i4d_status i4d_decode_greedy(i4d_ctx* c, uint32_t position, int32_t token_id, in
     *next_id = k == 0ull ? -1 : static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(k & 0xffffffffu));
     if (logits_out) CK(cudaMemcpy(logits_out, c->d_logits, kPVocab * sizeof(float), cudaMemcpyDeviceToHost));
     return I4D_OK;
+}
+
+static i4d_status launch_pack(i4d_ctx* c, const PackArgs& a) {
+    const long long threads = 4ll * a.blocks * kPackWordsPerBlock;
+    k_pack_matrix<<<static_cast<unsigned>((threads + kPackThreads - 1) / kPackThreads), kPackThreads, 0, c->stream>>>(a);
+    CK(cudaGetLastError());
+    return I4D_OK;
+}
+
+static bool images_ok(uint8_t* const images[4]) {
+    for (int p = 0; p < 4; ++p)
+        if (!images[p]) return false;
+    return true;
+}
+
+i4d_status i4d_pack_autoround_matrix(i4d_ctx* c, int layer, int mode, const uint8_t* nibbles_dev,
+                                     const float* scales_dev, uint8_t* const bank_images_dev[4]) {
+    if (!c || !nibbles_dev || !scales_dev || !bank_images_dev || !images_ok(bank_images_dev))
+        return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    if (mode < 0 || mode > 6) return fail(c, I4D_ERR_ARG, "mode %d is not an AutoRound projection (0..6)", mode);
+    if (layer < 0 || layer >= 32) return fail(c, I4D_ERR_ARG, "layer %d out of range", layer);
+    CK(cudaSetDevice(c->device));
+    PackArgs a = {};
+    a.nib = nibbles_dev;
+    a.scales = scales_dev;
+    a.Mv = (mode == 4 || mode == 5) ? 11008 : 4096;
+    a.Kv = mode == 6 ? 11008 : 4096;
+    a.lit = mode_lit(mode);
+    a.blocks = static_cast<int>(mode_words(mode) / kPackWordsPerBlock);
+    a.permute_qk = mode <= 1;
+    const uint64_t off = matrix_word_offset(layer, mode) * 64;
+    for (int p = 0; p < 4; ++p) a.dst[p] = bank_images_dev[p] + off;
+    const i4d_status st = launch_pack(c, a);
+    if (st != I4D_OK) return st;
+    CK(cudaStreamSynchronize(c->stream));
+    return I4D_OK;
+}
+
+i4d_status i4d_pack_fp32_head(i4d_ctx* c, const float* head_dev, uint8_t* const bank_images_dev[4]) {
+    if (!c || !head_dev || !bank_images_dev || !images_ok(bank_images_dev))
+        return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    CK(cudaSetDevice(c->device));
+    int8_t* w8 = nullptr;
+    float* sc = nullptr;
+    if (cudaMalloc(&w8, static_cast<size_t>(kPVocab) * 4096) != cudaSuccess ||
+        cudaMalloc(&sc, static_cast<size_t>(kPVocab) * 32 * sizeof(float)) != cudaSuccess) {
+        cudaFree(w8);
+        return fail(c, I4D_ERR_NOMEM, "no device memory for the quantised head (137 MB)");
+    }
+    HeadQuantArgs q = {head_dev, kVocab, kPVocab, w8, sc};
+    const long long threads = static_cast<long long>(kPVocab) * 32 * 32;
+    k_quant_head<<<static_cast<unsigned>(threads / kPackThreads), kPackThreads, 0, c->stream>>>(q);
+    cudaError_t e = cudaGetLastError();
+    PackArgs a = {};
+    a.w8 = w8;
+    a.scales = sc;
+    a.Mv = kPVocab;  // the padded rows are zero already
+    a.Kv = 4096;
+    a.lit = mode_lit(7);
+    a.blocks = static_cast<int>(mode_words(7) / kPackWordsPerBlock);
+    const uint64_t off = matrix_word_offset(0, 7) * 64;
+    for (int p = 0; p < 4; ++p) a.dst[p] = bank_images_dev[p] + off;
+    i4d_status st = e == cudaSuccess ? launch_pack(c, a) : I4D_ERR_CUDA;
+    if (e == cudaSuccess && st == I4D_OK) e = cudaStreamSynchronize(c->stream);
+    cudaFree(w8);
+    cudaFree(sc);
+    if (e != cudaSuccess) return fail(c, I4D_ERR_CUDA, "head packing: %s", cudaGetErrorString(e));
+    return st;
 }
 
 void i4d_sampler_init(i4d_sampler* s, float temperature, float top_p, float repeat_penalty, uint64_t seed,

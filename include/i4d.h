@@ -102,7 +102,8 @@ i4d_status i4d_create_shard(const i4d_config* cfg, int rank, int world, i4d_ctx*
 i4d_status i4d_shard_export(i4d_ctx* ctx, void* handle, size_t n);
 i4d_status i4d_shard_attach(i4d_ctx* ctx, const void* handles, size_t n);
 
-/* Loads one unchanged bank image (n must be I4D_BANK_BYTES; the legacy
+/* Loads one unchanged bank image, from host or device memory (n must be
+ * I4D_BANK_BYTES; the legacy
  * 891,277,312-byte layout is rejected with I4D_ERR_SIZE as
  * decode_host.cpp:1218-1227 detects it).  The image is re-tiled on the device
  * into the GEMV layout; gammas are extracted from its norm words.
@@ -138,6 +139,26 @@ i4d_status i4d_decode_token(i4d_ctx* ctx, uint32_t position, const float* residu
  * go to the device and the id back. */
 i4d_status i4d_decode_greedy(i4d_ctx* ctx, uint32_t position, int32_t token_id, int32_t* next_id,
                              float* logits_out);
+
+/* Bank-image producer on the device (scripts/autoround_pack_llama2_u250.py).
+ * bank_images_dev: four device buffers of I4D_BANK_BYTES, the images being
+ * built (i4d_load_bank accepts them as they are).
+ * i4d_pack_autoround_matrix writes projection `mode` (0..6: Q, K, V, O, GATE,
+ * UP, DOWN) of `layer` into all four images at the reference's offsets, from
+ * the AutoRound export's raw data: nibbles_dev = uint8 [rows][cols/2] (column
+ * 2i in the low nibble, offset binary) and scales_dev = FP32 [rows][cols/128]
+ * for the unpadded shape (GATE/UP 11008 x 4096, DOWN 4096 x 11008, others
+ * 4096 x 4096).  It unpacks as read_ar_matrix (:413-424), permutes Q/K rows
+ * as permute_qk_rows (:101-113), pads, and lays out superblocks as
+ * pack_matrix_to_super_blocks (:115-188).  Norm words are plain FP32 copies
+ * the caller writes.  i4d_pack_fp32_head quantises an FP32 LM head
+ * (32000 x 4096, device) with the max-abs RTN of pack_logits_into_banks
+ * (:268-307) and packs it; it allocates 137 MB of scratch for the call.
+ * Both return when the images are written.  Scales outside Q1.15 saturate as
+ * the reference's clip; NaN inputs are not supported. */
+i4d_status i4d_pack_autoround_matrix(i4d_ctx* ctx, int layer, int mode, const uint8_t* nibbles_dev,
+                                     const float* scales_dev, uint8_t* const bank_images_dev[4]);
+i4d_status i4d_pack_fp32_head(i4d_ctx* ctx, const float* head_dev, uint8_t* const bank_images_dev[4]);
 
 /* Token sampler (temperature, top-p, repeat penalty) on the device.
  * Replaces the host's Sampler (decode_host.cpp:724-868, mode

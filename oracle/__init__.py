@@ -173,6 +173,46 @@ class Oracle:
         return t, int(st[0])
 
 
+def pack_autoround_banks(mode, raw=None, scales=None, head=None):
+    """CPU restatement of the reference packer for one matrix: the four banks'
+    superblock bytes.  AutoRound matrices (modes 0-6): read_ar_matrix's unpack
+    and Q1.15 scales (autoround_pack_llama2_u250.py:413-424), permute_qk_rows
+    for Q/K (:101-113), zero padding (:483-488); the FP32 LM head (mode 7):
+    pack_logits_into_banks' max-abs RTN (:268-307).  The superblock layout is
+    the C restatement of pack_matrix_to_super_blocks in csrc/synth.c."""
+    from importlib import import_module
+    synth = import_module("4pe_u250_b200.synth")
+    F = import_module("4pe_u250_b200.formats")
+    rows = {0: 4096, 1: 4096, 2: 4096, 3: 4096, 4: 11264, 5: 11264, 6: 4096, 7: 32256}[mode]
+    cols = 11264 if mode == 6 else 4096
+    if mode == 7:
+        M, K = head.shape
+        hp = np.zeros((rows, cols), np.float32)
+        hp[:M, :K] = head
+        hr = hp.reshape(rows, cols // 128, 128)
+        mx = np.maximum(np.max(np.abs(hr), axis=2, keepdims=True), np.float32(1e-8))
+        sf = (mx / np.float32(7.0)).squeeze(axis=2)
+        w = np.clip(np.round(hr / (sf[:, :, None] + np.float32(1e-12))), -8, 7).astype(np.int8).reshape(rows, cols)
+        s = np.clip(np.round(sf * np.float32(32768.0)), -32768, 32767).astype(np.int16)
+    else:
+        M, K = raw.shape[0], raw.shape[1] * 2
+        w0 = np.empty((M, K), np.int8)
+        w0[:, 0::2] = (raw & 0x0F).astype(np.int8) - 8
+        w0[:, 1::2] = (raw >> 4).astype(np.int8) - 8
+        s0 = np.clip(np.round(scales * np.float32(32768.0)), -32768, 32767).astype(np.int16)
+        if mode in (0, 1):
+            perm = np.arange(4096).reshape(32, 128)
+            src = np.empty_like(perm)
+            src[:, 0::2] = perm[:, :64]
+            src[:, 1::2] = perm[:, 64:]
+            w0, s0 = w0[src.reshape(-1)], s0[src.reshape(-1)]
+        w = np.zeros((rows, cols), np.int8)
+        w[:M, :K] = w0
+        s = np.zeros((rows, cols // 128), np.int16)
+        s[:M, :K // 128] = s0
+    return [synth.pack_arrays(w, s, p, rows // 128, cols // 1024) for p in range(4)]
+
+
 def ref_available():
     return os.path.exists(REF_SO)
 
