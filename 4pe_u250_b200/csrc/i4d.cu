@@ -143,6 +143,8 @@ struct i4d_ctx {
     uint32_t* d_sample_idx = nullptr;
     unsigned long long* d_sample_state = nullptr;
     int* d_sample_out = nullptr;
+    float* d_sample_v = nullptr;
+    float* d_sample_smax = nullptr;
     unsigned long long* h_sample_state = nullptr;
     int* h_sample_out = nullptr;
     unsigned* h_err = nullptr;
@@ -476,7 +478,7 @@ void i4d_destroy(i4d_ctx* c) {
                    c->d_emb, c->d_resid, c->d_recip, c->d_shared, c->d_ao_q, c->d_ao_e, c->d_ad_q,
                    c->d_ad_e, c->d_logits, c->d_counters, c->d_err, c->d_pos, c->d_scratch, c->d_attn_coef, c->d_recips, c->d_trace,
                    c->d_tok, c->d_argmax, c->d_sample_hist, c->d_sample_keys, c->d_sample_idx,
-                   c->d_sample_state, c->d_sample_out};
+                   c->d_sample_state, c->d_sample_out, c->d_sample_v, c->d_sample_smax};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* host[] = {c->h_resid_in, c->h_resid_out, c->h_logits, c->h_pos, c->h_err, c->h_tok, c->h_argmax,
@@ -587,6 +589,8 @@ static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ct
     CKC(cudaMalloc(&c->d_sample_idx, 2ull * kSampleMaxVocab * sizeof(uint32_t)));
     CKC(cudaMalloc(&c->d_sample_state, sizeof(unsigned long long)));
     CKC(cudaMalloc(&c->d_sample_out, sizeof(int)));
+    CKC(cudaMalloc(&c->d_sample_v, kSampleMaxVocab * sizeof(float)));
+    CKC(cudaMalloc(&c->d_sample_smax, kSampleSlices * sizeof(float)));
     CKC(cudaMallocHost(&c->h_sample_state, sizeof(unsigned long long)));
     CKC(cudaMallocHost(&c->h_sample_out, sizeof(int)));
     CKC(cudaMallocHost(&c->h_err, sizeof(unsigned)));
@@ -946,6 +950,10 @@ static i4d_status enqueue_sample(i4d_ctx* c, const float* logits_dev, const int3
     a.keys = c->d_sample_keys;
     a.idx = c->d_sample_idx;
     a.out = c->d_sample_out;
+    a.v = c->d_sample_v;
+    a.slice_max = c->d_sample_smax;
+    k_sample_prep<<<kSampleSlices, kSampleThreads, 0, c->stream>>>(a);
+    if (s->temperature != 0.0f) k_sample_exp<<<kSampleSlices, kSampleThreads, 0, c->stream>>>(a);
     k_sample<<<1, kSampleThreads, sample_smem_bytes(), c->stream>>>(a);
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(c->h_sample_out, c->d_sample_out, sizeof(int), cudaMemcpyDeviceToHost, c->stream));

@@ -13,7 +13,8 @@
 // Sums and walks that the references run serially (the softmax sum, the
 // multinomial and nucleus walks) run serially here too, on one thread over
 // shared memory: FP32 addition is not associative.  Everything else is
-// parallel.  Top-p candidates (p >= (1 - top_p) / (n - 1)) are ordered by a
+// parallel: the repeat penalty, the per-slice maxima (k_sample_prep) and the
+// expf of every value (k_sample_exp) run over kSampleSlices CTAs first.  Top-p candidates (p >= (1 - top_p) / (n - 1)) are ordered by a
 // stable LSD radix sort on the probability bits, so equal probabilities keep
 // index order (both references use an unstable library sort there).
 #pragma once
@@ -27,6 +28,7 @@ constexpr int kSampleThreads = 1024;
 constexpr int kSampleWarps = kSampleThreads / 32;
 constexpr int kSampleMaxVocab = 32256;
 constexpr int kSampleMaxHistory = 16384;
+constexpr int kSampleSlices = 32;    // CTAs of the parallel passes, 1000 values each for 32000
 enum SampleMode : int { SAMPLE_HOST = 0, SAMPLE_EMULATOR = 1 };
 // Results below zero: the host sampler's exceptions.
 constexpr int kSampleAllNan = -1;      // every logit NaN (argmax)
@@ -42,13 +44,15 @@ struct SampleArgs {
     int mode;
     unsigned long long* state;  // xorshift64* state, advanced when a coin is drawn
     ExpfFix expf;
+    float* v;                 // scratch [n]: penalised (and, emulator, temperature-divided) values, then expf
+    float* slice_max;         // scratch [kSampleSlices]
     uint32_t* keys;           // scratch [2][kSampleMaxVocab]
     uint32_t* idx;            // scratch [2][kSampleMaxVocab]
     int* out;                 // token, or a negative code above
 };
 
 __host__ __device__ inline size_t sample_smem_bytes() {
-    return static_cast<size_t>(kSampleMaxVocab) * 4 + kSampleMaxVocab / 32 * 4 + kSampleWarps * 256 * 4;
+    return static_cast<size_t>(kSampleMaxVocab) * 4 + kSampleWarps * 256 * 4;
 }
 
 __device__ __forceinline__ float sample_coin(unsigned long long* st) {
@@ -147,11 +151,63 @@ __device__ __forceinline__ int sample_serial_prefix(float* v, int m, Stop stop) 
     return m;
 }
 
+__device__ __forceinline__ int sample_slice_len(int n) { return (n + kSampleSlices - 1) / kSampleSlices; }
+
+// Pass 1 (kSampleSlices CTAs, one value per thread): the repeat penalty, once
+// per distinct token (a token belongs to one slice, whose CTA marks it from
+// the whole history), the emulator's division by the temperature, and the
+// slice's maximum (host: finite values; emulator: non-NaN values).
+__global__ void __launch_bounds__(kSampleThreads) k_sample_prep(const __grid_constant__ SampleArgs a) {
+    __shared__ uint32_t marks[kSampleThreads / 32];
+    __shared__ float red[32];
+    const int tid = threadIdx.x;
+    const int len = sample_slice_len(a.n), i0 = blockIdx.x * len, i1 = min(a.n, i0 + len);
+    const bool host = a.mode == SAMPLE_HOST;
+    if (tid < kSampleThreads / 32) marks[tid] = 0u;
+    __syncthreads();
+    if (a.penalty != 1.0f)
+        for (int h = tid; h < a.n_history; h += kSampleThreads) {
+            const int t = a.history[h];
+            if (t >= i0 && t < i1) atomicOr(&marks[(t - i0) >> 5], 1u << ((t - i0) & 31));
+        }
+    __syncthreads();
+    const int i = i0 + tid;
+    float mx = -INFINITY;
+    if (i < i1) {
+        float v = a.logits[i];
+        if ((marks[tid >> 5] >> (tid & 31)) & 1u)
+            if (!host || isfinite(v)) v = v < 0.0f ? __fmul_rn(v, a.penalty) : __fdiv_rn(v, a.penalty);
+        if (!host && a.temperature != 0.0f) v = __fdiv_rn(v, a.temperature);
+        a.v[i] = v;
+        if (host ? isfinite(v) : v == v) mx = v;
+    }
+    mx = sample_block_reduce(mx, red, [](float x, float y) { return fmaxf(x, y); });
+    if (tid == 0) a.slice_max[blockIdx.x] = mx;
+}
+
+// The softmax maximum of the slice maxima (the emulator's stays NaN when its
+// scan starts from a NaN at index 0).
+__device__ __forceinline__ float sample_max(const SampleArgs& a) {
+    float mx = -INFINITY;
+    for (int s = 0; s < kSampleSlices; ++s) mx = fmaxf(mx, a.slice_max[s]);
+    if (a.mode != SAMPLE_HOST && a.v[0] != a.v[0]) mx = a.v[0];
+    return mx;
+}
+
+// Pass 2 (temperature > 0): the softmax numerators, expf as the C library.
+__global__ void __launch_bounds__(kSampleThreads) k_sample_exp(const __grid_constant__ SampleArgs a) {
+    const int len = sample_slice_len(a.n), i = blockIdx.x * len + threadIdx.x;
+    if (threadIdx.x >= len || i >= a.n) return;
+    const float mx = sample_max(a);
+    const float v = a.v[i];
+    if (a.mode == SAMPLE_HOST) a.v[i] = isfinite(v) ? expf_libc(__fdiv_rn(__fsub_rn(v, mx), a.temperature), a.expf) : 0.0f;
+    else a.v[i] = expf_libc(__fsub_rn(v, mx), a.expf);
+}
+
 __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const __grid_constant__ SampleArgs a) {
     extern __shared__ __align__(16) uint8_t sample_smem[];
     float* p = reinterpret_cast<float*>(sample_smem);
-    uint32_t* pen = reinterpret_cast<uint32_t*>(p + kSampleMaxVocab);
-    uint32_t* hist = pen + kSampleMaxVocab / 32;  // [warp][256] radix counts
+    uint32_t* hist = reinterpret_cast<uint32_t*>(p + kSampleMaxVocab);  // [warp][256] radix counts
     __shared__ unsigned long long red64[32];
     __shared__ float redf[32];
     __shared__ int s_m;
@@ -161,54 +217,19 @@ __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const __grid_const
     const bool host = a.mode == SAMPLE_HOST;
     const float T = a.temperature;
 
-    for (int i = tid; i < n; i += kSampleThreads) p[i] = a.logits[i];
-    for (int w = tid; w < (n + 31) / 32; w += kSampleThreads) pen[w] = 0u;
+    // The values of pass 1 (temperature 0) or the numerators of pass 2.
+    for (int i = tid; i < n; i += kSampleThreads) p[i] = a.v[i];
     __syncthreads();
-    // Repeat penalty, once per distinct token (whichever thread claims it
-    // first: the change depends on the token only).
-    if (a.penalty != 1.0f) {
-        for (int h = tid; h < a.n_history; h += kSampleThreads) {
-            const int t = a.history[h];
-            if (t < 0 || t >= n) continue;
-            const uint32_t bit = 1u << (t & 31);
-            if (atomicOr(&pen[t >> 5], bit) & bit) continue;
-            const float v = p[t];
-            if (!host || isfinite(v)) p[t] = v < 0.0f ? __fmul_rn(v, a.penalty) : __fdiv_rn(v, a.penalty);
-        }
-        __syncthreads();
-    }
     if (T == 0.0f) {
         int r = sample_argmax(p, n, red64);
         if (!host && p[0] != p[0]) r = 0;  // the emulator's scan starts from a NaN at 0 and never leaves it
         if (tid == 0) *a.out = r < 0 ? kSampleAllNan : r;
         return;
     }
-    // Softmax numerators.
-    if (!host) {
-        for (int i = tid; i < n; i += kSampleThreads) p[i] = __fdiv_rn(p[i], T);
-        __syncthreads();
+    if (host && !isfinite(sample_max(a))) {
+        if (tid == 0) *a.out = kSampleNoFinite;
+        return;
     }
-    float mx = -INFINITY;
-    if (!host && p[0] != p[0]) {
-        mx = p[0];  // the emulator's running maximum stays NaN
-    } else {
-        for (int i = tid; i < n; i += kSampleThreads) {
-            const float v = p[i];
-            if (host ? isfinite(v) : v == v) mx = fmaxf(mx, v);
-        }
-        mx = sample_block_reduce(mx, redf, [](float x, float y) { return fmaxf(x, y); });
-        if (host && !isfinite(mx)) {
-            if (tid == 0) *a.out = kSampleNoFinite;
-            return;
-        }
-    }
-    __syncthreads();
-    for (int i = tid; i < n; i += kSampleThreads) {
-        const float v = p[i];
-        if (host) p[i] = isfinite(v) ? expf_libc(__fdiv_rn(__fsub_rn(v, mx), T), a.expf) : 0.0f;
-        else p[i] = expf_libc(__fsub_rn(v, mx), a.expf);
-    }
-    __syncthreads();
     if (tid == 0) redf[0] = sample_serial_sum(p, n);  // the serial sum of both references
     __syncthreads();
     const float sum = redf[0];
