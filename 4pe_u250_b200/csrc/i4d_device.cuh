@@ -266,7 +266,9 @@ __device__ __forceinline__ int quantize_g32_lane(float v, uint32_t* e8m0) {
     int mraw = 0;
     if (v != 0.0f) {
         const float m = frexpf(v, &ex);
-        mraw = static_cast<int>(floor(static_cast<double>(m) * 8192.0));
+        // m * 8192 is exact in binary32 (a power-of-two scaling of a float),
+        // so the single-precision floor equals the emulator's double one.
+        mraw = static_cast<int>(floorf(__fmul_rn(m, 8192.0f)));
     }
     int maxe = __reduce_max_sync(0xffffffffu, ex);
     if (maxe < -127) maxe = -127;
