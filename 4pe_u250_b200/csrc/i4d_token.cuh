@@ -36,7 +36,7 @@ constexpr int kTokRing = 40;               // ring capacity in chunks of kChunkB
 constexpr int kTokCpc = 4;                 // chunks per bulk copy (16,896 B: streams near the HBM peak)
 constexpr int kTokSlots = kTokRing / kTokCpc;  // ring slots, one copy each
 constexpr int kTokSlotBytes = kTokCpc * kChunkBytes;
-constexpr int kTokUnion = 55296;           // GEMV activations + contributions, or attention scratch
+constexpr int kTokUnion = 59904;           // GEMV activations + contributions, or attention scratch
 constexpr int kTokContribBytes = 50688;     // contribution slots: 12 units of 4 chunks, 4 of DOWN
 constexpr int kTokMaxSlots = 16;
 constexpr int kAttnParts = 4;              // 32-dimension parts per head
@@ -840,9 +840,9 @@ struct TokAttnSmem {
     uint8_t* tile[2];     // kTile records each
     uint8_t* cur;         // current token's record
     int32_t* score;       // [kTile]
-    uint32_t* coef;       // [kTile]: c | rescale << 31
+    uint32_t* coef;       // [2][kTile]: c | rescale << 31, by tile parity
     uint32_t* lut;        // [33] exp2 table
-    int32_t* tbuf;        // [kTile][32]: per-token state terms of this part
+    int32_t* tbuf;        // [2][kTile][32]: per-token state terms of this part, by tile parity
     int32_t* qrot;        // [128]
     int32_t* krot;        // [128]
     int* misc;            // [16]
@@ -856,11 +856,11 @@ __device__ __forceinline__ TokAttnSmem tok_attn_carve(uint8_t* p) {
     p += 2 * kTile * 320 + 320;
     s.score = reinterpret_cast<int32_t*>(p);
     s.coef = reinterpret_cast<uint32_t*>(p + kTile * 4);
-    p += kTile * 8;
+    p += kTile * 12;
     s.lut = reinterpret_cast<uint32_t*>(p);
     p += 144;
     s.tbuf = reinterpret_cast<int32_t*>(p);
-    p += kTile * 32 * 4;
+    p += 2 * kTile * 32 * 4;
     s.qrot = reinterpret_cast<int32_t*>(p);
     p += 128 * 4;
     s.krot = reinterpret_cast<int32_t*>(p);
@@ -868,8 +868,11 @@ __device__ __forceinline__ TokAttnSmem tok_attn_carve(uint8_t* p) {
     s.misc = reinterpret_cast<int*>(p);
     return s;
 }
-static_assert(2 * kTile * 320 + 320 + kTile * 8 + 144 + kTile * 32 * 4 + 2 * 128 * 4 + 16 * 4 <= kTokUnion,
+static_assert(2 * kTile * 320 + 320 + kTile * 12 + 144 + 2 * kTile * 32 * 4 + 2 * 128 * 4 + 16 * 4 <= kTokUnion,
               "attention scratch exceeds the union region");
+
+// Barrier of the attention item's 16 worker warps (warps 2..17).
+__device__ __forceinline__ void tok_wbar() { asm volatile("bar.sync 2, %0;" ::"n"(32 * (kTokWarps - 2)) : "memory"); }
 
 // Attention of one (head, 32-dimension part) item.  Scores, the running
 // maximum and the coefficients are computed in parallel as in k_attention;
@@ -990,119 +993,134 @@ __device__ __forceinline__ void tok_attention(const TokenArgs& ta, const TokSmem
     const int dim = part * 32 + dl;
     int32_t st = 0;                          // state of dimension `dim` (lanes of warp 0)
     uint32_t z = 1u << 17;                   // normaliser (thread 32)
-    for (int k = 0; k < ntiles; ++k) {
-        const int T0 = k * kTile, cnt = min(kTile, n - T0);
-        uint8_t* buf = S.tile[k & 1];
-        if (tid == 0 && k + 1 < ntiles) {
-            fence_proxy_async_smem();
-            const int c2 = min(kTile, n - T0 - kTile);
-            mbar_arrive_expect_tx(&s.abar[(k + 1) & 1], c2 * 320);
-            bulk_g2s(S.tile[(k + 1) & 1], head_base + static_cast<size_t>(T0 + kTile) * 320, c2 * 320,
-                     &s.abar[(k + 1) & 1]);
-        }
-        tok_mbar_wait(ta, &s.abar[k & 1], static_cast<uint32_t>((k >> 1) & 1), kErrWaitFull | kErrWaitTile);
-        if (pos < T0 + cnt) {  // the tile holds the current token: use the fresh record
-            if (tid < 80)
-                reinterpret_cast<uint32_t*>(buf + (pos - T0) * 320)[tid] = reinterpret_cast<const uint32_t*>(S.cur)[tid];
-            tok_bar();
-        }
-        {   // scores (emulator:633-655): 16 warps x 4 tokens, 8 lanes per token
-            const int tl = cw * 4 + (lane >> 3);
-            long long hv = 0;
-            if (tl < cnt) {
-                const uint8_t* rec = buf + tl * 320;
-                const uint4 kw = *reinterpret_cast<const uint4*>(rec + 64 + hg * 16);
-                const unsigned long long meta = *reinterpret_cast<const unsigned long long*>(rec);
-                const uint32_t sh = static_cast<uint32_t>((meta >> (5 * (hg >> 1))) & 31u);
-                int sh16 = 0, sl16 = 0;
-                sh16 = dp2a_lo_ss(qh2[0], kw.x, sh16);
-                sh16 = dp2a_hi_ss(qh2[1], kw.x, sh16);
-                sh16 = dp2a_lo_ss(qh2[2], kw.y, sh16);
-                sh16 = dp2a_hi_ss(qh2[3], kw.y, sh16);
-                sh16 = dp2a_lo_ss(qh2[4], kw.z, sh16);
-                sh16 = dp2a_hi_ss(qh2[5], kw.z, sh16);
-                sh16 = dp2a_lo_ss(qh2[6], kw.w, sh16);
-                sh16 = dp2a_hi_ss(qh2[7], kw.w, sh16);
-                sl16 = dp2a_lo_us(ql2[0], kw.x, sl16);
-                sl16 = dp2a_hi_us(ql2[1], kw.x, sl16);
-                sl16 = dp2a_lo_us(ql2[2], kw.y, sl16);
-                sl16 = dp2a_hi_us(ql2[3], kw.y, sl16);
-                sl16 = dp2a_lo_us(ql2[4], kw.z, sl16);
-                sl16 = dp2a_hi_us(ql2[5], kw.z, sl16);
-                sl16 = dp2a_lo_us(ql2[6], kw.w, sl16);
-                sl16 = dp2a_hi_us(ql2[7], kw.w, sl16);
-                const long long half = static_cast<long long>(sh16) * 65536 + sl16;
-                hv = wrap_bits(sh >= 10 ? static_cast<long long>(static_cast<unsigned long long>(half) << (sh - 10))
-                                        : (half >> (10 - sh)), 44);
-            }
-            hv += __shfl_xor_sync(FULL, hv, 1);
-            hv += __shfl_xor_sync(FULL, hv, 2);
-            hv += __shfl_xor_sync(FULL, hv, 4);
-            if ((lane & 7) == 0 && tl < cnt) S.score[tl] = sat32(rshift_even(wrap_bits(hv, 44) * a.score_scale, 24));
-        }
-        tok_bar();
-        // Coefficients from the running maximum before each token (emulator:656-672).
-        const int carry = misc[0];
-        int32_t m_incl = INT32_MIN, m_excl = INT32_MIN, sc = INT32_MIN;
-        if (tid < kTile) {
-            sc = tid < cnt ? S.score[tid] : INT32_MIN;
-            m_incl = sc;
+    // Pipeline over the KV tiles: in iteration k the 16 worker warps (2..17)
+    // build tile k -- scores, running maximum, coefficients and state terms
+    // into buffer k & 1 -- while warp 0 (state) and thread 32 (normaliser)
+    // run the recurrences of tile k - 1 from buffer (k - 1) & 1.  One CTA
+    // barrier ends each iteration.
+    const int wtid = tid - 64, wcw = cw - 2;
+    for (int k = 0; k <= ntiles; ++k) {
+        if (cw >= 2) {
+            if (k < ntiles) {
+                const int T0 = k * kTile, cnt = min(kTile, n - T0);
+                uint8_t* buf = S.tile[k & 1];
+                uint32_t* coef = S.coef + (k & 1) * kTile;
+                int32_t* tbuf = S.tbuf + (k & 1) * kTile * 32;
+                if (wtid == 0 && k + 1 < ntiles) {  // buffer (k + 1) & 1 was last read in iteration k - 1
+                    fence_proxy_async_smem();
+                    const int c2 = min(kTile, n - T0 - kTile);
+                    mbar_arrive_expect_tx(&s.abar[(k + 1) & 1], c2 * 320);
+                    bulk_g2s(S.tile[(k + 1) & 1], head_base + static_cast<size_t>(T0 + kTile) * 320, c2 * 320,
+                             &s.abar[(k + 1) & 1]);
+                }
+                tok_mbar_wait(ta, &s.abar[k & 1], static_cast<uint32_t>((k >> 1) & 1), kErrWaitFull | kErrWaitTile);
+                if (pos < T0 + cnt) {  // the tile holds the current token: use the fresh record
+                    if (wtid < 80)
+                        reinterpret_cast<uint32_t*>(buf + (pos - T0) * 320)[wtid] =
+                            reinterpret_cast<const uint32_t*>(S.cur)[wtid];
+                    tok_wbar();
+                }
+                {   // scores (emulator:633-655): 16 warps x 4 tokens, 8 lanes per token
+                    const int tl = wcw * 4 + (lane >> 3);
+                    long long hv = 0;
+                    if (tl < cnt) {
+                        const uint8_t* rec = buf + tl * 320;
+                        const uint4 kw = *reinterpret_cast<const uint4*>(rec + 64 + hg * 16);
+                        const unsigned long long meta = *reinterpret_cast<const unsigned long long*>(rec);
+                        const uint32_t sh = static_cast<uint32_t>((meta >> (5 * (hg >> 1))) & 31u);
+                        int sh16 = 0, sl16 = 0;
+                        sh16 = dp2a_lo_ss(qh2[0], kw.x, sh16);
+                        sh16 = dp2a_hi_ss(qh2[1], kw.x, sh16);
+                        sh16 = dp2a_lo_ss(qh2[2], kw.y, sh16);
+                        sh16 = dp2a_hi_ss(qh2[3], kw.y, sh16);
+                        sh16 = dp2a_lo_ss(qh2[4], kw.z, sh16);
+                        sh16 = dp2a_hi_ss(qh2[5], kw.z, sh16);
+                        sh16 = dp2a_lo_ss(qh2[6], kw.w, sh16);
+                        sh16 = dp2a_hi_ss(qh2[7], kw.w, sh16);
+                        sl16 = dp2a_lo_us(ql2[0], kw.x, sl16);
+                        sl16 = dp2a_hi_us(ql2[1], kw.x, sl16);
+                        sl16 = dp2a_lo_us(ql2[2], kw.y, sl16);
+                        sl16 = dp2a_hi_us(ql2[3], kw.y, sl16);
+                        sl16 = dp2a_lo_us(ql2[4], kw.z, sl16);
+                        sl16 = dp2a_hi_us(ql2[5], kw.z, sl16);
+                        sl16 = dp2a_lo_us(ql2[6], kw.w, sl16);
+                        sl16 = dp2a_hi_us(ql2[7], kw.w, sl16);
+                        const long long half = static_cast<long long>(sh16) * 65536 + sl16;
+                        hv = wrap_bits(sh >= 10 ? static_cast<long long>(static_cast<unsigned long long>(half) << (sh - 10))
+                                                : (half >> (10 - sh)), 44);
+                    }
+                    hv += __shfl_xor_sync(FULL, hv, 1);
+                    hv += __shfl_xor_sync(FULL, hv, 2);
+                    hv += __shfl_xor_sync(FULL, hv, 4);
+                    if ((lane & 7) == 0 && tl < cnt) S.score[tl] = sat32(rshift_even(wrap_bits(hv, 44) * a.score_scale, 24));
+                }
+                tok_wbar();
+                // Coefficients from the running maximum before each token (emulator:656-672).
+                const int carry = misc[0];
+                int32_t m_incl = INT32_MIN, m_excl = INT32_MIN, sc = INT32_MIN;
+                if (wtid < kTile) {
+                    sc = wtid < cnt ? S.score[wtid] : INT32_MIN;
+                    m_incl = sc;
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int32_t y = __shfl_up_sync(FULL, m_incl, o);
-                if (lane >= o) m_incl = max(m_incl, y);
-            }
-            m_excl = __shfl_up_sync(FULL, m_incl, 1);
-            if (lane == 0) m_excl = INT32_MIN;
-            if (tid == 31) misc[2] = m_incl;
-        }
-        tok_bar();
-        if (tid < kTile) {
-            const int32_t prev = max(max(carry, m_excl), cw == 1 ? misc[2] : INT32_MIN);
-            const int t = T0 + tid;
-            uint32_t c = 0;
-            bool ev = false;
-            if (tid < cnt) {
-                if (t == 0) {
-                    c = 1u << 17;
-                    ev = true;
-                } else if (sc <= prev) {
-                    c = exp_negative_q17(sat32(static_cast<long long>(sc) - prev), S.lut, a.log2e_q21);
-                } else {
-                    c = exp_negative_q17(sat32(static_cast<long long>(prev) - sc), S.lut, a.log2e_q21);
-                    ev = true;
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const int32_t y = __shfl_up_sync(FULL, m_incl, o);
+                        if (lane >= o) m_incl = max(m_incl, y);
+                    }
+                    m_excl = __shfl_up_sync(FULL, m_incl, 1);
+                    if (lane == 0) m_excl = INT32_MIN;
+                    if (wtid == 31) misc[2] = m_incl;
+                }
+                tok_wbar();
+                if (wtid < kTile) {
+                    const int32_t prev = max(max(carry, m_excl), wcw == 1 ? misc[2] : INT32_MIN);
+                    const int t = T0 + wtid;
+                    uint32_t c = 0;
+                    bool ev = false;
+                    if (wtid < cnt) {
+                        if (t == 0) {
+                            c = 1u << 17;
+                            ev = true;
+                        } else if (sc <= prev) {
+                            c = exp_negative_q17(sat32(static_cast<long long>(sc) - prev), S.lut, a.log2e_q21);
+                        } else {
+                            c = exp_negative_q17(sat32(static_cast<long long>(prev) - sc), S.lut, a.log2e_q21);
+                            ev = true;
+                        }
+                    }
+                    coef[wtid] = c | (ev ? 0x80000000u : 0u);
+                    if (wtid == kTile - 1) misc[0] = max(carry, max(m_incl, misc[2]));
+                }
+                tok_wbar();
+                // State terms in parallel: thread = (dimension, slice of 4 tokens).
+                const int t_lo = wcw * 4, t_hi = min(cnt, t_lo + 4);
+                for (int tl = t_lo; tl < t_hi; ++tl) {
+                    const int32_t v = rec_v(buf + tl * 320, dim);
+                    const uint32_t cf = coef[tl];
+                    tbuf[tl * 32 + dl] = (cf >> 31) ? v : mulq17(v, cf);
                 }
             }
-            S.coef[tid] = c | (ev ? 0x80000000u : 0u);
-            if (tid == kTile - 1) misc[0] = max(carry, max(m_incl, misc[2]));
-        }
-        tok_bar();
-        // State terms in parallel: thread = (dimension, slice of 4 tokens).
-        {
-            const int t_lo = cw * 4, t_hi = min(cnt, t_lo + 4);
-            for (int tl = t_lo; tl < t_hi; ++tl) {
-                const int32_t v = rec_v(buf + tl * 320, dim);
-                const uint32_t cf = S.coef[tl];
-                S.tbuf[tl * 32 + dl] = (cf >> 31) ? v : mulq17(v, cf);
-            }
-        }
-        tok_bar();
-        if (tid < 32) {  // the saturating state recurrence, in token order
-            for (int tl = 0; tl < cnt; ++tl) {
-                const uint32_t cf = S.coef[tl];
-                const int32_t tv = S.tbuf[tl * 32 + dl];
-                if (T0 + tl == 0) st = tv;
-                else if (cf >> 31) st = sat32(static_cast<long long>(mulq17(st, cf & 0x7fffffffu)) + tv);
-                else st = sat32(static_cast<long long>(st) + tv);
-            }
-        } else if (tid == 32) {  // the normaliser recurrence
-            for (int tl = 0; tl < cnt; ++tl) {
-                const uint32_t cf = S.coef[tl];
-                const uint32_t cc = cf & 0x7fffffffu;
-                if (T0 + tl == 0) z = 1u << 17;
-                else if (cf >> 31)
-                    z = ((static_cast<uint32_t>(rshift_even(static_cast<long long>(z) * cc, 17)) & M30) + (1u << 17)) & M30;
-                else z = (z + cc) & M30;
+        } else if (k >= 1) {  // the recurrences of tile k - 1, in token order
+            const int kp = k - 1, T0 = kp * kTile, cnt = min(kTile, n - T0);
+            const uint32_t* coef = S.coef + (kp & 1) * kTile;
+            const int32_t* tbuf = S.tbuf + (kp & 1) * kTile * 32;
+            if (tid < 32) {  // the saturating state recurrence
+                for (int tl = 0; tl < cnt; ++tl) {
+                    const uint32_t cf = coef[tl];
+                    const int32_t tv = tbuf[tl * 32 + dl];
+                    if (T0 + tl == 0) st = tv;
+                    else if (cf >> 31) st = sat32(static_cast<long long>(mulq17(st, cf & 0x7fffffffu)) + tv);
+                    else st = sat32(static_cast<long long>(st) + tv);
+                }
+            } else if (tid == 32) {  // the normaliser recurrence
+                for (int tl = 0; tl < cnt; ++tl) {
+                    const uint32_t cf = coef[tl];
+                    const uint32_t cc = cf & 0x7fffffffu;
+                    if (T0 + tl == 0) z = 1u << 17;
+                    else if (cf >> 31)
+                        z = ((static_cast<uint32_t>(rshift_even(static_cast<long long>(z) * cc, 17)) & M30) + (1u << 17)) &
+                            M30;
+                    else z = (z + cc) & M30;
+                }
             }
         }
         tok_bar();
