@@ -258,6 +258,26 @@ __device__ __forceinline__ int32_t mulq17(int32_t a, uint32_t b) {
         wrap_bits(rshift_even(static_cast<long long>(a) * static_cast<long long>(b), 17), 32));
 }
 
+// mulq17 for b < 2^31 in 32-bit steps: one wide multiply, a funnel shift for
+// floor(p / 2^17) mod 2^32, and the round-half-even increment from the 17
+// dropped bits and the quotient's parity.  Equal to mulq17 (checked on 2e8
+// random and edge operands); shorter on a serial chain.
+__device__ __forceinline__ int32_t mulq17_w(int32_t a, uint32_t b) {
+    const long long p = static_cast<long long>(a) * static_cast<int32_t>(b);
+    const uint32_t lo = static_cast<uint32_t>(p), hi = static_cast<uint32_t>(static_cast<unsigned long long>(p) >> 32);
+    const uint32_t q = __funnelshift_r(lo, hi, 17);
+    const uint32_t r = lo & 0x1FFFFu;
+    const uint32_t inc = static_cast<uint32_t>(r > 0x10000u) | (static_cast<uint32_t>(r == 0x10000u) & q);
+    return static_cast<int32_t>(q + (inc & 1u));
+}
+
+// sat32(x + y) of two int32 values.
+__device__ __forceinline__ int32_t add_sat32(int32_t x, int32_t y) {
+    int32_t d;
+    asm("add.sat.s32 %0, %1, %2;" : "=r"(d) : "r"(x), "r"(y));
+    return d;
+}
+
 // One lane's share of the G32 E8M0/INT14 quantizer (emulator:167-210,
 // int4_decoder_blocks.cpp:22-73); all 32 lanes of the warp hold one group.
 // Returns the INT14 value; *e8m0 receives max_exp + 127.

@@ -1108,17 +1108,16 @@ __device__ __forceinline__ void tok_attention(const TokenArgs& ta, const TokSmem
                     const uint32_t cf = coef[tl];
                     const int32_t tv = tbuf[tl * 32 + dl];
                     if (T0 + tl == 0) st = tv;
-                    else if (cf >> 31) st = sat32(static_cast<long long>(mulq17(st, cf & 0x7fffffffu)) + tv);
-                    else st = sat32(static_cast<long long>(st) + tv);
+                    else if (cf >> 31) st = add_sat32(mulq17_w(st, cf & 0x7fffffffu), tv);
+                    else st = add_sat32(st, tv);
                 }
             } else if (tid == 32) {  // the normaliser recurrence
                 for (int tl = 0; tl < cnt; ++tl) {
                     const uint32_t cf = coef[tl];
                     const uint32_t cc = cf & 0x7fffffffu;
                     if (T0 + tl == 0) z = 1u << 17;
-                    else if (cf >> 31)
-                        z = ((static_cast<uint32_t>(rshift_even(static_cast<long long>(z) * cc, 17)) & M30) + (1u << 17)) &
-                            M30;
+                    else if (cf >> 31)  // z < 2^30 and cc <= 2^17: mulq17_w's steps on the unsigned product
+                        z = ((static_cast<uint32_t>(mulq17_w(static_cast<int32_t>(z), cc)) & M30) + (1u << 17)) & M30;
                     else z = (z + cc) & M30;
                 }
             }
