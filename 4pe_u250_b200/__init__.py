@@ -34,7 +34,7 @@ EXPORTS = [
     "i4d_profile_token", "i4d_token_breakdown", "i4d_linear_bank_noalloc",
     "i4d_token_timeline", "i4d_create_shard", "i4d_shard_export", "i4d_shard_attach",
     "i4d_decode_greedy", "i4d_argmax", "i4d_sampler_init", "i4d_sample", "i4d_decode_sample",
-    "i4d_pack_autoround_matrix", "i4d_pack_fp32_head",
+    "i4d_pack_autoround_matrix", "i4d_pack_fp32_head", "i4d_prefill", "i4d_prefill_tokens",
 ]
 
 SAMPLER_HOST = 0      # decode_host.cpp:724-868
@@ -122,6 +122,8 @@ def load_library():
         "i4d_shard_export": [P, P, ctypes.c_size_t],
         "i4d_shard_attach": [P, P, ctypes.c_size_t],
         "i4d_decode_greedy": [P, ctypes.c_uint32, ctypes.c_int32, P, P],
+        "i4d_prefill": [P, ctypes.c_uint32, P, ctypes.c_uint32, P],
+        "i4d_prefill_tokens": [P, ctypes.c_uint32, P, ctypes.c_uint32, P, P],
         "i4d_argmax": [P, P, ctypes.c_size_t, P],
         "i4d_sample": [P, P, P, ctypes.c_uint32, P, P],
         "i4d_decode_sample": [P, ctypes.c_uint32, ctypes.c_int32, P, ctypes.c_uint32, P, P],
@@ -260,6 +262,23 @@ class Context:
         nxt = ctypes.c_int32(0)
         logits = np.empty(formats.PADDED_VOCAB, dtype=np.float32) if want_logits else None
         self._check(self._L.i4d_decode_greedy(self._h, position, int(token_id), ctypes.byref(nxt), _ptr(logits)))
+        return nxt.value, logits
+
+    def prefill(self, position0, residuals_in):
+        """A prompt from its embedding rows [n][4096] at positions position0..:
+        the last token's 32256 padded logits; KV records of every token."""
+        x = np.ascontiguousarray(residuals_in, dtype=np.float32).reshape(-1, formats.DIM)
+        logits = np.empty(formats.PADDED_VOCAB, dtype=np.float32)
+        self._check(self._L.i4d_prefill(self._h, position0, x.ctypes.data, x.shape[0], logits.ctypes.data))
+        return logits
+
+    def prefill_tokens(self, position0, token_ids, want_logits=False):
+        """A prompt from token ids (embeddings loaded): (greedy next id, logits or None)."""
+        ids = np.ascontiguousarray(token_ids, dtype=np.int32)
+        nxt = ctypes.c_int32(0)
+        logits = np.empty(formats.PADDED_VOCAB, dtype=np.float32) if want_logits else None
+        self._check(self._L.i4d_prefill_tokens(self._h, position0, ids.ctypes.data, ids.size, ctypes.byref(nxt),
+                                               _ptr(logits)))
         return nxt.value, logits
 
     def sample(self, logits_dev_ptr, history, sampler):

@@ -24,6 +24,7 @@
 #include "i4d_token.cuh"
 #include "i4d_sample.cuh"
 #include "i4d_pack.cuh"
+#include "i4d_prefill.cuh"
 
 extern "C" {
 extern const unsigned int i4d_expf_fix_count;
@@ -148,6 +149,21 @@ struct i4d_ctx {
     unsigned long long* h_sample_state = nullptr;
     int* h_sample_out = nullptr;
     unsigned* h_err = nullptr;
+    // Prompt batches (i4d_prefill): per-token residuals, RMS reciprocals,
+    // quantised activations, stage partials, rotated q, attention
+    // coefficients and positions of up to kPrefillMax tokens.
+    float* d_pf_resid = nullptr;
+    float* d_pf_recip = nullptr;
+    int16_t* d_pf_q = nullptr;
+    uint8_t* d_pf_e = nullptr;
+    float* d_pf_part = nullptr;
+    int32_t* d_pf_qrot = nullptr;
+    uint32_t* d_pf_coef = nullptr;
+    int* d_pf_pos = nullptr;
+    int* d_pf_ids = nullptr;
+    float* h_pf_resid = nullptr;
+    int* h_pf_pos = nullptr;
+    int* h_pf_ids = nullptr;
     bool bank_loaded[4] = {false, false, false, false};
     bool rope_loaded = false;
     cudaGraphExec_t graph = nullptr;       // H2D + token kernels + D2H
@@ -450,6 +466,85 @@ i4d_status finish(i4d_ctx* c) {
     return I4D_OK;
 }
 
+// One GEMV stage of a prompt batch (act: the batch's [T][kPfTok] activations).
+cudaError_t run_batch(i4d_ctx* c, int layer, int st, int T, int act_bank_stride) {
+    BatchArgs b = {};
+    b.w = c->d_w + stage_offset(c, layer, st);
+    b.bank_stride = stage_bank_bytes(st);
+    b.cpb = c->cpb;
+    b.units = kStageUnits[st];
+    b.chunks = kStageChunks[st];
+    b.T = T;
+    b.act_q = c->d_pf_q;
+    b.act_e = c->d_pf_e;
+    b.act_bank_stride = act_bank_stride;
+    b.partials = c->d_pf_part;
+    b.err = c->d_err;
+    k_linear_batch<<<4 * c->cpb, kBatchThreads, batch_smem_bytes(b.chunks, T), c->stream>>>(b);
+    return cudaGetLastError();
+}
+
+cudaError_t run_pf_norm(i4d_ctx* c, int T, int partial_stage, const float* gamma) {
+    PfNormArgs n = {};
+    n.resid = c->d_pf_resid;
+    n.partials = partial_stage < 0 ? nullptr : c->d_pf_part;
+    n.rows = partial_stage < 0 ? 0 : kStageUnits[partial_stage] * 32;
+    n.gamma = gamma;
+    n.recip = c->d_pf_recip;
+    n.q = c->d_pf_q;
+    n.e = c->d_pf_e;
+    k_pf_norm<<<T, 1024, 0, c->stream>>>(n);
+    return cudaGetLastError();
+}
+
+// The layers of one prompt batch of T tokens (residuals in d_pf_resid,
+// positions in d_pf_pos), in the decode order of every token: norm, QKV,
+// attention (records of all T tokens, then the T queries), O + residual,
+// norm, GATE/UP, SwiGLU, DOWN + residual.  With `last`, the final norm and
+// the LM head of the batch's last token follow (logits in d_logits).
+i4d_status enqueue_prefill(i4d_ctx* c, int T, bool last) {
+    for (int l = 0; l < c->layers; ++l) {
+        CK(run_pf_norm(c, T, l == 0 ? -1 : ST_DOWN, c->d_gamma + static_cast<size_t>(2 * l) * kDim));
+        CK(run_batch(c, l, ST_QKV, T, 1024));
+        AttnArgs at = base_attn(c, l);
+        at.partials = c->d_pf_part;
+        at.part_tok_stride = static_cast<size_t>(4) * kStageUnits[ST_QKV] * 32;
+        at.pos_ptr = c->d_pf_pos;
+        at.q_rot = c->d_pf_qrot;
+        at.coef_scratch = c->d_pf_coef;
+        at.out_q = c->d_pf_q;
+        at.out_e = c->d_pf_e;
+        at.out_tok_stride = kPfTok;
+        at.phase = 1;
+        k_attention<<<dim3(kHeads, T), kAttnThreads, attn_smem_bytes(), c->stream>>>(at);
+        CK(cudaGetLastError());
+        at.phase = 2;
+        k_attention<<<dim3(kHeads, T), kAttnThreads, attn_smem_bytes(), c->stream>>>(at);
+        CK(cudaGetLastError());
+        CK(run_batch(c, l, ST_O, T, 1024));
+        CK(run_pf_norm(c, T, ST_O, c->d_gamma + static_cast<size_t>(2 * l + 1) * kDim));
+        CK(run_batch(c, l, ST_GU, T, 1024));
+        k_pf_swiglu<<<dim3(kStageUnits[ST_GU] / 2, T), 32, 0, c->stream>>>(c->d_pf_part, kStageUnits[ST_GU], c->expf,
+                                                                            c->d_pf_q, c->d_pf_e);
+        CK(cudaGetLastError());
+        CK(run_batch(c, l, ST_DOWN, T, 2816));
+    }
+    CK(run_pf_norm(c, T, ST_DOWN, nullptr));
+    if (!last) return I4D_OK;
+    CK(cudaMemcpyAsync(c->d_resid, c->d_pf_resid + static_cast<size_t>(T - 1) * kDim, kDim * sizeof(float),
+                       cudaMemcpyDeviceToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->d_recip, c->d_pf_recip + (T - 1), sizeof(float), cudaMemcpyDeviceToDevice, c->stream));
+    LinearArgs lg = base_linear(c, 0, ST_LOGITS);
+    lg.in_kind = IN_RMS;
+    lg.resid = c->d_resid;
+    lg.gamma = c->d_gamma + static_cast<size_t>(64) * kDim;
+    lg.recip = c->d_recip;
+    lg.epi = EPI_STORE;
+    lg.out = c->d_logits;
+    CK(run_linear(c, lg, false));
+    return I4D_OK;
+}
+
 bool all_loaded(const i4d_ctx* c) {
     for (int b = c->bank0; b < c->bank0 + c->nbanks; ++b)
         if (!c->bank_loaded[b]) return false;
@@ -478,11 +573,13 @@ void i4d_destroy(i4d_ctx* c) {
                    c->d_emb, c->d_resid, c->d_recip, c->d_shared, c->d_ao_q, c->d_ao_e, c->d_ad_q,
                    c->d_ad_e, c->d_logits, c->d_counters, c->d_err, c->d_pos, c->d_scratch, c->d_attn_coef, c->d_recips, c->d_trace,
                    c->d_tok, c->d_argmax, c->d_sample_hist, c->d_sample_keys, c->d_sample_idx,
-                   c->d_sample_state, c->d_sample_out, c->d_sample_v, c->d_sample_smax};
+                   c->d_sample_state, c->d_sample_out, c->d_sample_v, c->d_sample_smax, c->d_pf_resid,
+                   c->d_pf_recip, c->d_pf_q, c->d_pf_e, c->d_pf_part, c->d_pf_qrot, c->d_pf_coef, c->d_pf_pos,
+                   c->d_pf_ids};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* host[] = {c->h_resid_in, c->h_resid_out, c->h_logits, c->h_pos, c->h_err, c->h_tok, c->h_argmax,
-                    c->h_sample_state, c->h_sample_out};
+                    c->h_sample_state, c->h_sample_out, c->h_pf_resid, c->h_pf_pos, c->h_pf_ids};
     for (void* p : host)
         if (p) cudaFreeHost(p);
     if (c->stream) cudaStreamDestroy(c->stream);
@@ -527,6 +624,8 @@ static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ct
     CKC(cudaFuncSetAttribute(k_linear, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBudget)));
     CKC(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(attn_smem_bytes())));
+    CKC(cudaFuncSetAttribute(k_linear_batch, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(batch_smem_bytes(kStageChunks[ST_DOWN], kPrefillMax))));
     CKC(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(sample_smem_bytes())));
     CKC(cudaFuncSetAttribute(k_token<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -594,6 +693,18 @@ static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ct
     CKC(cudaMallocHost(&c->h_sample_state, sizeof(unsigned long long)));
     CKC(cudaMallocHost(&c->h_sample_out, sizeof(int)));
     CKC(cudaMallocHost(&c->h_err, sizeof(unsigned)));
+    CKC(cudaMalloc(&c->d_pf_resid, static_cast<size_t>(kPrefillMax) * kDim * sizeof(float)));
+    CKC(cudaMalloc(&c->d_pf_recip, kPrefillMax * sizeof(float)));
+    CKC(cudaMalloc(&c->d_pf_q, static_cast<size_t>(kPrefillMax) * kPfTok * sizeof(int16_t)));
+    CKC(cudaMalloc(&c->d_pf_e, static_cast<size_t>(kPrefillMax) * kPfTok / 32));
+    CKC(cudaMalloc(&c->d_pf_part, static_cast<size_t>(kPrefillMax) * 4 * kStageUnits[ST_GU] * 32 * sizeof(float)));
+    CKC(cudaMalloc(&c->d_pf_qrot, static_cast<size_t>(kPrefillMax) * kDim * sizeof(int32_t)));
+    CKC(cudaMalloc(&c->d_pf_coef, static_cast<size_t>(kPrefillMax) * kHeads * c->stride * sizeof(uint32_t)));
+    CKC(cudaMalloc(&c->d_pf_pos, kPrefillMax * sizeof(int)));
+    CKC(cudaMalloc(&c->d_pf_ids, kPrefillMax * sizeof(int)));
+    CKC(cudaMallocHost(&c->h_pf_resid, static_cast<size_t>(kPrefillMax) * kDim * sizeof(float)));
+    CKC(cudaMallocHost(&c->h_pf_pos, kPrefillMax * sizeof(int)));
+    CKC(cudaMallocHost(&c->h_pf_ids, kPrefillMax * sizeof(int)));
 
     // exp2 LUT of the online softmax: round(2^(30 + i/32)), and log2(e) in
     // Q21 (emulator:566-579 define the same quantities).
@@ -1056,6 +1167,66 @@ i4d_status i4d_decode_token(i4d_ctx* c, uint32_t position, const float* residual
     std::memcpy(logits_out, c->h_logits, kPVocab * sizeof(float));
     if (residual_out) std::memcpy(residual_out, c->h_resid_out, kDim * sizeof(float));
     return I4D_OK;
+}
+
+// Prompt of n tokens in batches of kPrefillMax; ids (device embeddings) or
+// residuals (host) give each token's input.
+static i4d_status prefill_impl(i4d_ctx* c, uint32_t position0, const float* residuals, const int32_t* ids,
+                               uint32_t n, int32_t* next_id, float* logits_out) {
+    if (!all_loaded(c)) return fail(c, I4D_ERR_STATE, "banks and rope LUT must be loaded before a prefill");
+    if (c->world != 1) return fail(c, I4D_ERR_STATE, "prefill needs all four banks in one context");
+    if (ids && !c->d_emb) return fail(c, I4D_ERR_STATE, "embeddings must be loaded before a token prefill");
+    if (n == 0) return fail(c, I4D_ERR_ARG, "empty prompt");
+    if (position0 >= static_cast<uint32_t>(c->stride) || n > static_cast<uint32_t>(c->stride) - position0)
+        return fail(c, I4D_ERR_ARG, "positions %u..%u out of range (KV capacity %d)", position0,
+                    position0 + n - 1, c->stride);
+    if (ids)
+        for (uint32_t i = 0; i < n; ++i)
+            if (ids[i] < 0 || ids[i] >= kVocab) return fail(c, I4D_ERR_ARG, "token id %d out of range", ids[i]);
+    CK(cudaSetDevice(c->device));
+    for (uint32_t b = 0; b < n; b += kPrefillMax) {
+        const int T = static_cast<int>(n - b < static_cast<uint32_t>(kPrefillMax) ? n - b : kPrefillMax);
+        const bool last = b + T == n;
+        for (int t = 0; t < T; ++t) c->h_pf_pos[t] = static_cast<int>(position0 + b + t);
+        CK(cudaMemcpyAsync(c->d_pf_pos, c->h_pf_pos, T * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+        if (ids) {
+            std::memcpy(c->h_pf_ids, ids + b, T * sizeof(int));
+            CK(cudaMemcpyAsync(c->d_pf_ids, c->h_pf_ids, T * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+            k_pf_embed<<<T, kDim / 4, 0, c->stream>>>(c->d_emb, c->d_pf_ids, c->d_pf_resid);
+            CK(cudaGetLastError());
+        } else {
+            std::memcpy(c->h_pf_resid, residuals + static_cast<size_t>(b) * kDim, static_cast<size_t>(T) * kDim * sizeof(float));
+            CK(cudaMemcpyAsync(c->d_pf_resid, c->h_pf_resid, static_cast<size_t>(T) * kDim * sizeof(float),
+                               cudaMemcpyHostToDevice, c->stream));
+        }
+        const i4d_status st = enqueue_prefill(c, T, last);
+        if (st != I4D_OK) return st;
+        if (last && next_id) {
+            k_argmax<<<1, 1024, 0, c->stream>>>(c->d_logits, kVocab, c->d_argmax);
+            CK(cudaGetLastError());
+        }
+        // The pinned staging is reused by the next batch.
+        const i4d_status fs = finish(c);
+        if (fs != I4D_OK) return fs;
+    }
+    if (next_id) {
+        unsigned long long k = 0;
+        CK(cudaMemcpy(&k, c->d_argmax, sizeof(k), cudaMemcpyDeviceToHost));
+        *next_id = k == 0ull ? -1 : static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(k & 0xffffffffu));
+    }
+    if (logits_out) CK(cudaMemcpy(logits_out, c->d_logits, kPVocab * sizeof(float), cudaMemcpyDeviceToHost));
+    return I4D_OK;
+}
+
+i4d_status i4d_prefill(i4d_ctx* c, uint32_t position0, const float* residuals_in, uint32_t n, float* logits_out) {
+    if (!c || !residuals_in) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    return prefill_impl(c, position0, residuals_in, nullptr, n, nullptr, logits_out);
+}
+
+i4d_status i4d_prefill_tokens(i4d_ctx* c, uint32_t position0, const int32_t* token_ids, uint32_t n,
+                              int32_t* next_id, float* logits_out) {
+    if (!c || !token_ids) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    return prefill_impl(c, position0, nullptr, token_ids, n, next_id, logits_out);
 }
 
 i4d_status i4d_kv_reset(i4d_ctx* c) {

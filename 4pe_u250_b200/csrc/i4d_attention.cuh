@@ -44,6 +44,13 @@ struct AttnArgs {
     int16_t* out_q;
     uint8_t* out_e;
     unsigned* err;
+    // Prompt batches (grid y = token of the batch; all zero for one token).
+    // phase 0: the whole head; 1: rotated q to q_rot and the KV record only;
+    // 2: attention over records already written (q from q_rot).
+    int phase;
+    int32_t* q_rot;            // [tokens][4096]
+    size_t part_tok_stride;    // floats from one token's partials to the next
+    int out_tok_stride;        // out_q values per token (out_e: / 32)
 };
 
 constexpr int kAttnThreads = 256;
@@ -196,6 +203,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constan
     extern __shared__ __align__(128) uint8_t attn_smem[];
     AttnSmem S = attn_carve(attn_smem);
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int y = blockIdx.y;
+    uint32_t* coef_scr = a.coef_scratch + static_cast<size_t>(y) * kHeads * a.stride;
     const unsigned FULL = 0xffffffffu;
     const uint32_t M30 = (1u << 30) - 1u;
     int* misc = S.misc;
@@ -217,12 +226,12 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constan
     // The position is written before the token's first kernel, and cached
     // records of earlier tokens never change during a token, so the first
     // tile streams in while the QKV projection is still finishing.
-    const int pos = *a.pos_ptr;
+    const int pos = a.pos_ptr[y];
     const bool bad = pos < 0 || pos >= a.stride;
     const int n = pos + 1;
     const int ntiles = (n + kTile - 1) / kTile;
     const uint8_t* head_base = kv_record(a, h, 0);
-    if (!bad && tid == 0) {
+    if (!bad && tid == 0 && a.phase != 1) {
         const int cnt = min(kTile, n);
         mbar_arrive_expect_tx(&S.bar[0], cnt * 320);
         bulk_g2s(S.tile[0], head_base, cnt * 320, &S.bar[0]);
@@ -239,56 +248,64 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constan
     int32_t* tk = S.ev_v;  // scratch until the tile loop
     int32_t qv = 0, kv = 0, vv = 0;
     const int row = h * kHeadDim + d;
-    if (tid < 128) {
-        if (a.direct) {
-            qv = a.direct[row];
-            kv = a.direct[kDim + row];
-            vv = a.direct[2 * kDim + row];
-        } else {
-            qv = float_to_q17(combine4(a.partials, 3 * kDim, row));
-            kv = float_to_q17(combine4(a.partials, 3 * kDim, kDim + row));
-            vv = float_to_q17(combine4(a.partials, 3 * kDim, 2 * kDim + row));
-        }
-        tq[d] = qv;
-        tk[d] = kv;
-    }
-    __syncthreads();
-    if (tid < 128) {  // adjacent-pair RoPE (emulator:526-541)
-        const int pr = d >> 1;
-        const long long c = a.rope_cos[pos * 64 + pr], sn = a.rope_sin[pos * 64 + pr];
-        const long long qa = tq[2 * pr], qb = tq[2 * pr + 1];
-        const long long ka = tk[2 * pr], kb = tk[2 * pr + 1];
-        qv = (d & 1) ? sat32((qa * sn + qb * c) >> 17) : sat32((qa * c - qb * sn) >> 17);
-        kv = (d & 1) ? sat32((ka * sn + kb * c) >> 17) : sat32((ka * c - kb * sn) >> 17);
-    }
-    __syncthreads();
     uint8_t* grec = kv_record(a, h, pos);
-    if (tid < 128) {  // warp = 32-value group of the record
-        tq[d] = qv;
-        const uint32_t kmag = static_cast<uint32_t>(kv < 0 ? -static_cast<long long>(kv) : kv);
-        const uint32_t vmag = static_cast<uint32_t>(vv < 0 ? -static_cast<long long>(vv) : vv);
-        const uint32_t ks = kv_shift_of(__reduce_max_sync(FULL, kmag));
-        const uint32_t vs = kv_shift_of(__reduce_max_sync(FULL, vmag));
-        const uint8_t k8 = static_cast<uint8_t>(kv_quant(kv, ks)), v8 = static_cast<uint8_t>(kv_quant(vv, vs));
-        S.cur[64 + d] = k8;
-        S.cur[192 + d] = v8;
-        grec[64 + d] = k8;
-        grec[192 + d] = v8;
-        if (lane == 0) {
-            misc[8 + warp] = static_cast<int>(ks);
-            misc[12 + warp] = static_cast<int>(vs);
-        }
-    }
-    __syncthreads();
-    if (tid < 8) {
-        unsigned long long meta = 0;
-        if (tid == 0)
-            for (int g = 0; g < 4; ++g) {
-                meta |= static_cast<unsigned long long>(misc[8 + g]) << (5 * g);
-                meta |= static_cast<unsigned long long>(misc[12 + g]) << (20 + 5 * g);
+    if (a.phase == 2) {  // record written by phase 1: q and the record from memory
+        if (tid < 128) tq[d] = a.q_rot[static_cast<size_t>(y) * kDim + row];
+        if (tid < 80) reinterpret_cast<uint32_t*>(S.cur)[tid] = reinterpret_cast<const uint32_t*>(grec)[tid];
+    } else {
+        if (tid < 128) {
+            if (a.direct) {
+                qv = a.direct[row];
+                kv = a.direct[kDim + row];
+                vv = a.direct[2 * kDim + row];
+            } else {
+                const float* P = a.partials + y * a.part_tok_stride;
+                qv = float_to_q17(combine4(P, 3 * kDim, row));
+                kv = float_to_q17(combine4(P, 3 * kDim, kDim + row));
+                vv = float_to_q17(combine4(P, 3 * kDim, 2 * kDim + row));
             }
-        reinterpret_cast<unsigned long long*>(S.cur)[tid] = meta;
-        reinterpret_cast<unsigned long long*>(grec)[tid] = meta;
+            tq[d] = qv;
+            tk[d] = kv;
+        }
+        __syncthreads();
+        if (tid < 128) {  // adjacent-pair RoPE (emulator:526-541)
+            const int pr = d >> 1;
+            const long long c = a.rope_cos[pos * 64 + pr], sn = a.rope_sin[pos * 64 + pr];
+            const long long qa = tq[2 * pr], qb = tq[2 * pr + 1];
+            const long long ka = tk[2 * pr], kb = tk[2 * pr + 1];
+            qv = (d & 1) ? sat32((qa * sn + qb * c) >> 17) : sat32((qa * c - qb * sn) >> 17);
+            kv = (d & 1) ? sat32((ka * sn + kb * c) >> 17) : sat32((ka * c - kb * sn) >> 17);
+        }
+        __syncthreads();
+        if (tid < 128) {  // warp = 32-value group of the record
+            tq[d] = qv;
+            if (a.phase == 1) a.q_rot[static_cast<size_t>(y) * kDim + row] = qv;
+            const uint32_t kmag = static_cast<uint32_t>(kv < 0 ? -static_cast<long long>(kv) : kv);
+            const uint32_t vmag = static_cast<uint32_t>(vv < 0 ? -static_cast<long long>(vv) : vv);
+            const uint32_t ks = kv_shift_of(__reduce_max_sync(FULL, kmag));
+            const uint32_t vs = kv_shift_of(__reduce_max_sync(FULL, vmag));
+            const uint8_t k8 = static_cast<uint8_t>(kv_quant(kv, ks)), v8 = static_cast<uint8_t>(kv_quant(vv, vs));
+            S.cur[64 + d] = k8;
+            S.cur[192 + d] = v8;
+            grec[64 + d] = k8;
+            grec[192 + d] = v8;
+            if (lane == 0) {
+                misc[8 + warp] = static_cast<int>(ks);
+                misc[12 + warp] = static_cast<int>(vs);
+            }
+        }
+        __syncthreads();
+        if (tid < 8) {
+            unsigned long long meta = 0;
+            if (tid == 0)
+                for (int g = 0; g < 4; ++g) {
+                    meta |= static_cast<unsigned long long>(misc[8 + g]) << (5 * g);
+                    meta |= static_cast<unsigned long long>(misc[12 + g]) << (20 + 5 * g);
+                }
+            reinterpret_cast<unsigned long long*>(S.cur)[tid] = meta;
+            reinterpret_cast<unsigned long long*>(grec)[tid] = meta;
+        }
+        if (a.phase == 1) return;
     }
     // Q of this lane's half-group (16 values) split into 16-bit halves for dp2a.
     const int hg = lane & 7;
@@ -400,7 +417,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constan
             const int t = T0 + tid;
             S.seg[tid] = sg;
             if (tid < cnt) {
-                a.coef_scratch[static_cast<size_t>(h) * a.stride + t] = S.coef[tid];
+                coef_scr[static_cast<size_t>(h) * a.stride + t] = S.coef[tid];
                 if (ev && sg < kMaxSeg) {
                     S.ev_c[sg] = c;
                     S.ev_tok[sg] = t;
@@ -470,7 +487,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constan
             }
         } else {
             for (int t = 1; t < n; ++t) {
-                const uint32_t cf = a.coef_scratch[static_cast<size_t>(h) * a.stride + t];
+                const uint32_t cf = coef_scr[static_cast<size_t>(h) * a.stride + t];
                 const uint32_t cc = cf & 0x7fffffffu;
                 if (cf >> 31) z = ((static_cast<uint32_t>(rshift_even(static_cast<long long>(z) * cc, 17)) & M30) + (1u << 17)) & M30;
                 else z = (z + cc) & M30;
@@ -483,7 +500,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constan
         auto vat = [&](int t) -> int32_t { return t == pos ? rec_v(S.cur, d) : rec_v(kv_record(a, h, t), d); };
         auto seq = [&](int t0, int t1) {  // sequential chain over non-event tokens [t0, t1)
             for (int t = t0; t < t1; ++t) {
-                const uint32_t cf = a.coef_scratch[static_cast<size_t>(h) * a.stride + t];
+                const uint32_t cf = coef_scr[static_cast<size_t>(h) * a.stride + t];
                 st = sat32(static_cast<long long>(st) + mulq17(vat(t), cf & 0x7fffffffu));
             }
         };
@@ -501,7 +518,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constan
         } else {
             st = vat(0);
             for (int t = 1; t < n; ++t) {
-                const uint32_t cf = a.coef_scratch[static_cast<size_t>(h) * a.stride + t];
+                const uint32_t cf = coef_scr[static_cast<size_t>(h) * a.stride + t];
                 const uint32_t cc = cf & 0x7fffffffu;
                 const int32_t v = vat(t);
                 if (cf >> 31) st = sat32(static_cast<long long>(mulq17(st, cc)) + v);
@@ -525,8 +542,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constan
     float r = __fmul_rn(__fmul_rn(__int2float_rn(o), 1.0f / 131072.0f), inv_scale);
     r = __fadd_rn(r, r >= 0.0f ? 0.5f : -0.5f);
     r = fmaxf(-8191.0f, fminf(8191.0f, r));
-    a.out_q[row] = static_cast<int16_t>(__float2int_rz(r));
-    if (lane == 0) a.out_e[h * 4 + warp] = maxf == 0.0f ? 0 : static_cast<uint8_t>(maxe + 127);
+    a.out_q[static_cast<size_t>(y) * a.out_tok_stride + row] = static_cast<int16_t>(__float2int_rz(r));
+    if (lane == 0)
+        a.out_e[static_cast<size_t>(y) * (a.out_tok_stride / 32) + h * 4 + warp] =
+            maxf == 0.0f ? 0 : static_cast<uint8_t>(maxe + 127);
 }
 
 

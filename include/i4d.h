@@ -140,6 +140,24 @@ i4d_status i4d_decode_token(i4d_ctx* ctx, uint32_t position, const float* residu
 i4d_status i4d_decode_greedy(i4d_ctx* ctx, uint32_t position, int32_t token_id, int32_t* next_id,
                              float* logits_out);
 
+/* Prompt prefill in batches (SURVEY-(f) row 3).  The reference feeds a
+ * prompt through run_one_token one position at a time
+ * (decode_host.cpp:1570-1580), streaming every weight once per token; here
+ * up to 16 prompt tokens share each pass over the weights.  The result is
+ * bit-identical to n calls of i4d_decode_token at positions position0 ..
+ * position0 + n - 1: the same KV records of every token, and logits_out (may
+ * be NULL) receives the last token's 32256 padded logits.  residuals_in:
+ * n x 4096 FP32 embedding rows (host).  Needs a context holding all four
+ * banks (not a shard); position0 + n must not exceed the KV capacity. */
+i4d_status i4d_prefill(i4d_ctx* ctx, uint32_t position0, const float* residuals_in, uint32_t n,
+                       float* logits_out);
+
+/* i4d_prefill from token ids (host, n ids in [0, 32000)) with the embeddings
+ * of i4d_load_embeddings; next_id (may be NULL) receives the greedy next
+ * token of the last position, as i4d_decode_greedy. */
+i4d_status i4d_prefill_tokens(i4d_ctx* ctx, uint32_t position0, const int32_t* token_ids, uint32_t n,
+                              int32_t* next_id, float* logits_out);
+
 /* Bank-image producer on the device (scripts/autoround_pack_llama2_u250.py).
  * bank_images_dev: four device buffers of I4D_BANK_BYTES, the images being
  * built (i4d_load_bank accepts them as they are).
