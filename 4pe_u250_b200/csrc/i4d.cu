@@ -480,8 +480,7 @@ cudaError_t run_batch(i4d_ctx* c, int layer, int st, int T, int act_bank_stride)
     b.act_bank_stride = act_bank_stride;
     b.partials = c->d_pf_part;
     b.err = c->d_err;
-    k_linear_batch<<<4 * c->cpb, kBatchThreads, batch_smem_bytes(b.chunks, T), c->stream>>>(b);
-    return cudaGetLastError();
+    return launch(c, true, k_linear_batch, dim3(4 * c->cpb), dim3(kBatchThreads), batch_smem_bytes(b.chunks), b);
 }
 
 cudaError_t run_pf_norm(i4d_ctx* c, int T, int partial_stage, const float* gamma) {
@@ -493,8 +492,7 @@ cudaError_t run_pf_norm(i4d_ctx* c, int T, int partial_stage, const float* gamma
     n.recip = c->d_pf_recip;
     n.q = c->d_pf_q;
     n.e = c->d_pf_e;
-    k_pf_norm<<<T, 1024, 0, c->stream>>>(n);
-    return cudaGetLastError();
+    return launch(c, true, k_pf_norm, dim3(T), dim3(1024), 0, n);
 }
 
 // The layers of one prompt batch of T tokens (residuals in d_pf_resid,
@@ -515,18 +513,14 @@ i4d_status enqueue_prefill(i4d_ctx* c, int T, bool last) {
         at.out_q = c->d_pf_q;
         at.out_e = c->d_pf_e;
         at.out_tok_stride = kPfTok;
-        at.phase = 1;
-        k_attention<<<dim3(kHeads, T), kAttnThreads, attn_smem_bytes(), c->stream>>>(at);
-        CK(cudaGetLastError());
+        CK(launch(c, true, k_pf_kv, dim3(kHeads, T), dim3(128), 0, at));
         at.phase = 2;
-        k_attention<<<dim3(kHeads, T), kAttnThreads, attn_smem_bytes(), c->stream>>>(at);
-        CK(cudaGetLastError());
+        CK(launch(c, true, k_attention, dim3(kHeads, T), dim3(kAttnThreads), attn_smem_bytes(), at));
         CK(run_batch(c, l, ST_O, T, 1024));
         CK(run_pf_norm(c, T, ST_O, c->d_gamma + static_cast<size_t>(2 * l + 1) * kDim));
         CK(run_batch(c, l, ST_GU, T, 1024));
-        k_pf_swiglu<<<dim3(kStageUnits[ST_GU] / 2, T), 32, 0, c->stream>>>(c->d_pf_part, kStageUnits[ST_GU], c->expf,
-                                                                            c->d_pf_q, c->d_pf_e);
-        CK(cudaGetLastError());
+        CK(launch(c, true, k_pf_swiglu, dim3(kStageUnits[ST_GU] / 2, T), dim3(32), 0, (const float*)c->d_pf_part,
+                  static_cast<int>(kStageUnits[ST_GU]), c->expf, c->d_pf_q, c->d_pf_e));
         CK(run_batch(c, l, ST_DOWN, T, 2816));
     }
     CK(run_pf_norm(c, T, ST_DOWN, nullptr));
@@ -625,7 +619,7 @@ static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ct
     CKC(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(attn_smem_bytes())));
     CKC(cudaFuncSetAttribute(k_linear_batch, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(batch_smem_bytes(kStageChunks[ST_DOWN], kPrefillMax))));
+                             static_cast<int>(batch_smem_bytes(kStageChunks[ST_DOWN]))));
     CKC(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(sample_smem_bytes())));
     CKC(cudaFuncSetAttribute(k_token<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -45,8 +45,8 @@ struct AttnArgs {
     uint8_t* out_e;
     unsigned* err;
     // Prompt batches (grid y = token of the batch; all zero for one token).
-    // phase 0: the whole head; 1: rotated q to q_rot and the KV record only;
-    // 2: attention over records already written (q from q_rot).
+    // phase 0: the whole head; 2: attention over records already written by
+    // k_pf_kv, with the rotated q from q_rot.
     int phase;
     int32_t* q_rot;            // [tokens][4096]
     size_t part_tok_stride;    // floats from one token's partials to the next
@@ -199,6 +199,59 @@ __device__ __forceinline__ int32_t rec_v(const uint8_t* rec, int d) {
     return static_cast<int32_t>(static_cast<int8_t>(rec[192 + d])) << ((meta >> (20 + 5 * (d >> 5))) & 31u);
 }
 
+// The current-token half of k_attention for every token of a prompt batch
+// (grid: head, token): q/k/v from the QKV partials, RoPE, the rotated q to
+// q_rot and the quantised KV record (same operations as k_attention's
+// current-token section; emulator:526-541, swiftkv_attention.hpp:21-36).
+// Thread = dimension d; warp = 32-value group; the RoPE pair (2i, 2i + 1)
+// is the lane pair (d, d ^ 1).
+__global__ void __launch_bounds__(128) k_pf_kv(const __grid_constant__ AttnArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    const int h = blockIdx.x, y = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
+    const unsigned FULL = 0xffffffffu;
+    const int pos = a.pos_ptr[y];
+    if (pos < 0 || pos >= a.stride) {
+        if (d == 0) atomicOr(a.err, kErrArg);
+        return;
+    }
+    const int row = h * kHeadDim + d;
+    const float* P = a.partials + y * a.part_tok_stride;
+    const int32_t q = float_to_q17(combine4(P, 3 * kDim, row));
+    const int32_t k = float_to_q17(combine4(P, 3 * kDim, kDim + row));
+    const int32_t vv = float_to_q17(combine4(P, 3 * kDim, 2 * kDim + row));
+    const int32_t qo = __shfl_xor_sync(FULL, q, 1), ko = __shfl_xor_sync(FULL, k, 1);
+    const long long qa = (d & 1) ? qo : q, qb = (d & 1) ? q : qo;
+    const long long ka = (d & 1) ? ko : k, kb = (d & 1) ? k : ko;
+    const int pr = d >> 1;
+    const long long c = a.rope_cos[pos * 64 + pr], sn = a.rope_sin[pos * 64 + pr];
+    const int32_t qv = (d & 1) ? sat32((qa * sn + qb * c) >> 17) : sat32((qa * c - qb * sn) >> 17);
+    const int32_t kv = (d & 1) ? sat32((ka * sn + kb * c) >> 17) : sat32((ka * c - kb * sn) >> 17);
+    a.q_rot[static_cast<size_t>(y) * kDim + row] = qv;
+    uint8_t* grec = kv_record(a, h, pos);
+    const uint32_t kmag = static_cast<uint32_t>(kv < 0 ? -static_cast<long long>(kv) : kv);
+    const uint32_t vmag = static_cast<uint32_t>(vv < 0 ? -static_cast<long long>(vv) : vv);
+    const uint32_t ks = kv_shift_of(__reduce_max_sync(FULL, kmag));
+    const uint32_t vs = kv_shift_of(__reduce_max_sync(FULL, vmag));
+    grec[64 + d] = static_cast<uint8_t>(kv_quant(kv, ks));
+    grec[192 + d] = static_cast<uint8_t>(kv_quant(vv, vs));
+    __shared__ uint32_t shifts[8];
+    if (lane == 0) {
+        shifts[warp] = ks;
+        shifts[4 + warp] = vs;
+    }
+    __syncthreads();
+    if (d < 8) {
+        unsigned long long meta = 0;
+        if (d == 0)
+            for (int g = 0; g < 4; ++g) {
+                meta |= static_cast<unsigned long long>(shifts[g]) << (5 * g);
+                meta |= static_cast<unsigned long long>(shifts[4 + g]) << (20 + 5 * g);
+            }
+        reinterpret_cast<unsigned long long*>(grec)[d] = meta;
+    }
+}
+
 __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constant__ AttnArgs a) {
     extern __shared__ __align__(128) uint8_t attn_smem[];
     AttnSmem S = attn_carve(attn_smem);
@@ -231,12 +284,18 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constan
     const int n = pos + 1;
     const int ntiles = (n + kTile - 1) / kTile;
     const uint8_t* head_base = kv_record(a, h, 0);
-    if (!bad && tid == 0 && a.phase != 1) {
+    // Phase 2 reads records that the previous kernel wrote: load after the wait.
+    if (!bad && tid == 0 && a.phase == 0) {
         const int cnt = min(kTile, n);
         mbar_arrive_expect_tx(&S.bar[0], cnt * 320);
         bulk_g2s(S.tile[0], head_base, cnt * 320, &S.bar[0]);
     }
     pdl_wait();
+    if (!bad && tid == 0 && a.phase == 2) {
+        const int cnt = min(kTile, n);
+        mbar_arrive_expect_tx(&S.bar[0], cnt * 320);
+        bulk_g2s(S.tile[0], head_base, cnt * 320, &S.bar[0]);
+    }
     if (bad) {
         if (tid == 0) atomicOr(a.err, kErrArg);
         return;
@@ -279,7 +338,6 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constan
         __syncthreads();
         if (tid < 128) {  // warp = 32-value group of the record
             tq[d] = qv;
-            if (a.phase == 1) a.q_rot[static_cast<size_t>(y) * kDim + row] = qv;
             const uint32_t kmag = static_cast<uint32_t>(kv < 0 ? -static_cast<long long>(kv) : kv);
             const uint32_t vmag = static_cast<uint32_t>(vv < 0 ? -static_cast<long long>(vv) : vv);
             const uint32_t ks = kv_shift_of(__reduce_max_sync(FULL, kmag));
@@ -305,7 +363,6 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constan
             reinterpret_cast<unsigned long long*>(S.cur)[tid] = meta;
             reinterpret_cast<unsigned long long*>(grec)[tid] = meta;
         }
-        if (a.phase == 1) return;
     }
     // Q of this lane's half-group (16 values) split into 16-bit halves for dp2a.
     const int hg = lane & 7;

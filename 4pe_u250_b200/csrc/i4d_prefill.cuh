@@ -5,14 +5,16 @@
 // (decode_host.cpp:1570-1580, run_one_token at :1340), so every prompt token
 // streams all 3.46 GB of weights.  Here the GEMV stages of a layer take a
 // batch of T prompt tokens: each weight chunk is streamed into shared memory
-// once and every consumer warp applies it to its own token.  Per (token, row)
+// once and applied to all T tokens with int8 tensor-core MMAs.  Per (token, row)
 // the arithmetic is the decode path's unchanged (exact G32 int32 dots on the
 // split activations, contrib = fl(float(dot) * fl(ws * as)), the FP32 chain
 // in local-group order from +0.0f, emulator:216-264), so each token's
 // partials, residual and KV record are bit-identical to decoding it alone.
-// Attention runs per (head, token) in two launches (i4d_attention.cuh phase
-// 1 writes all T records, phase 2 attends), which is the decode order: token
-// t reads records 0..t.
+// Attention runs per (head, token) in two launches (k_pf_kv writes all T
+// records, then k_attention phase 2 attends), which is the decode order:
+// token t reads records 0..t.  Every kernel of a batch is launched with
+// programmatic dependent launch: it waits for its predecessor before reading
+// any of its outputs, and the GEMV producer streams weights before that.
 #pragma once
 
 #include "i4d_device.cuh"
@@ -21,8 +23,10 @@
 
 namespace i4d {
 
-constexpr int kPrefillMax = 16;                      // tokens per batch = consumer warps
-constexpr int kBatchThreads = 32 * (1 + kPrefillMax);
+constexpr int kPrefillMax = 16;                      // tokens per batch (two MMA token tiles)
+constexpr int kBatchUnits = 4;                       // units in flight per CTA
+constexpr int kBatchWarps = 4 * kBatchUnits;         // per unit: 2 row tiles x 2 token tiles
+constexpr int kBatchThreads = 32 * (1 + kBatchWarps);
 constexpr int kBatchSlots = 24;                      // chunk ring slots
 constexpr int kPfTok = 11264;                        // activation columns per token (DOWN input)
 
@@ -40,113 +44,196 @@ struct BatchArgs {
     unsigned* err;
 };
 
-__host__ __device__ inline size_t batch_smem_bytes(int chunks, int T) {
-    return static_cast<size_t>(kBatchSlots) * kChunkBytes + 2 * kBatchSlots * 8 +
-           static_cast<size_t>(T) * chunks * 8 * 72;
+// Per-token activation block in shared memory: ah [groups][32] (int8),
+// al [groups][32] (0..127), the group scales [groups] (FP32) and 16 bytes of
+// padding.  The stride, groups * 17 + 4 words, is 4 x an odd number, so the 8
+// tokens that one MMA B fragment reads start in 8 distinct 4-bank groups.
+__host__ __device__ constexpr int batch_tok_stride(int groups) { return groups * 68 + 16; }
+
+__host__ __device__ inline size_t batch_smem_bytes(int chunks) {
+    return static_cast<size_t>(kBatchSlots) * kChunkBytes + 2 * kBatchSlots * 8 + align16(kBatchSlots * 4) +
+           static_cast<size_t>(kPrefillMax) * batch_tok_stride(chunks * 8);
 }
 
-// One CTA per SM: a producer thread streams the CTA's units chunk by chunk;
-// consumer warp t (token t) reads every chunk, lane = row, and chains the
-// unit's 8 x chunks group contributions in order in a register.
+// Four INT4 weights of one packed word as int8 MMA operands, both scaled by
+// 16: the low nibbles hold w + 8 (offset binary) and the high nibbles w
+// (two's complement), so 16w is (x << 4) ^ 0x80 and (x & 0xF0) per byte.
+__device__ __forceinline__ uint32_t w16_lo(uint32_t x) { return ((x << 4) & 0xF0F0F0F0u) ^ 0x80808080u; }
+__device__ __forceinline__ uint32_t w16_hi(uint32_t x) { return x & 0xF0F0F0F0u; }
+
+// D = A (16 x 32 int8, row-major) x B (32 x 8 int8), int32.
+__device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// One CTA per SM.  A producer thread streams the CTA's units in rounds of
+// kBatchUnits, chunk j of every unit of the round before chunk j + 1, into a
+// ring.  Warp (s, rt, tt) takes unit s of each round, rows 16 rt .. 16 rt +
+// 15 of it and tokens 8 tt .. 8 tt + 7: per chunk and G32 group two int8
+// MMAs (the activation's high and low parts, a = 128 ah + al) give the exact
+// int32 dot of every (row, token), and each (row, token) chains its group
+// contributions in order in a register, as the decode path.
 __global__ void __launch_bounds__(kBatchThreads, 1) k_linear_batch(const __grid_constant__ BatchArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int groups = a.chunks * 8;
+    const int tstride = batch_tok_stride(groups);
     uint8_t* ring = smem_raw;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + static_cast<size_t>(kBatchSlots) * kChunkBytes);
     uint64_t* empty = full + kBatchSlots;
-    uint8_t* act_base = reinterpret_cast<uint8_t*>(empty + kBatchSlots);
+    int* issued = reinterpret_cast<int*>(empty + kBatchSlots);
+    uint8_t* act = reinterpret_cast<uint8_t*>(issued) + align16(kBatchSlots * 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bank = blockIdx.x / a.cpb, c = blockIdx.x % a.cpb;
     const int u0 = static_cast<int>((static_cast<long long>(c) * a.units) / a.cpb);
     const int u1 = static_cast<int>((static_cast<long long>(c + 1) * a.units) / a.cpb);
-    const int nchunks = (u1 - u0) * a.chunks;
-    const int nt = a.T < kPrefillMax ? a.T : kPrefillMax;
+    const int nunits = u1 - u0;
+    const int T = a.T < kPrefillMax ? a.T : kPrefillMax;
+    const int ntt = (T + 7) >> 3;  // token tiles in use
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kBatchSlots; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], nt);
+            mbar_init(&empty[i], 2 * ntt);
         }
         mbar_fence_init();
     }
+    if (threadIdx.x < kBatchSlots) issued[threadIdx.x] = -1;
     __syncthreads();
+    pdl_trigger();
 
-    if (warp == 0) {
+    if (warp == 0) {  // weights never depend on earlier kernels: no wait
         if (lane == 0) {
             const uint8_t* src = a.w + static_cast<size_t>(bank) * a.bank_stride +
                                  static_cast<size_t>(u0) * a.chunks * kChunkBytes;
-            int slot = 0;
+            int idx = 0, slot = 0;
             uint32_t phase = 0;
-            for (int i = 0; i < nchunks; ++i) {
-                if (i >= kBatchSlots) mbar_wait(&empty[slot], phase ^ 1u, a.err, kErrWaitEmpty);
-                mbar_arrive_expect_tx(&full[slot], kChunkBytes);
-                bulk_g2s(ring + static_cast<size_t>(slot) * kChunkBytes, src + static_cast<size_t>(i) * kChunkBytes,
-                         kChunkBytes, &full[slot]);
-                if (++slot == kBatchSlots) {
-                    slot = 0;
-                    phase ^= 1u;
-                }
+            for (int rb = 0; rb < nunits; rb += kBatchUnits) {
+                const int nu = min(kBatchUnits, nunits - rb);
+                for (int j = 0; j < a.chunks; ++j)
+                    for (int su = 0; su < nu; ++su, ++idx) {
+                        if (idx >= kBatchSlots) mbar_wait(&empty[slot], phase ^ 1u, a.err, kErrWaitEmpty);
+                        publish_issued(&issued[slot], idx);
+                        mbar_arrive_expect_tx(&full[slot], kChunkBytes);
+                        bulk_g2s(ring + static_cast<size_t>(slot) * kChunkBytes,
+                                 src + (static_cast<size_t>(rb + su) * a.chunks + j) * kChunkBytes, kChunkBytes,
+                                 &full[slot]);
+                        if (++slot == kBatchSlots) {
+                            slot = 0;
+                            phase ^= 1u;
+                        }
+                    }
             }
         }
         return;
     }
-    const int t = warp - 1;
-    if (t >= nt) return;
 
-    // This token's split activations (layout of put_act, per token).
-    int8_t* hi = reinterpret_cast<int8_t*>(act_base + static_cast<size_t>(t) * groups * 72);
-    uint8_t* lo = reinterpret_cast<uint8_t*>(hi + groups * 32);
-    int* corr = reinterpret_cast<int*>(lo + groups * 32);
-    float* ascale = reinterpret_cast<float*>(corr + groups);
+    // Activations of tokens 0 .. 8 ntt - 1 (zero past T): 8 values per
+    // thread and step, split into ah / al bytes; then the group scales.
+    const int cw = warp - 1, ct = threadIdx.x - 32;
+    pdl_wait();
     {
-        const size_t base = static_cast<size_t>(t) * kPfTok + static_cast<size_t>(bank) * a.act_bank_stride;
-        const int16_t* q = a.act_q + base;
-        const uint8_t* e = a.act_e + base / 32;
-        for (int lg = 0; lg < groups; ++lg) {
-            const int v = q[lg * 32 + lane];
-            hi[lg * 32 + lane] = static_cast<int8_t>(v >> 7);
-            lo[lg * 32 + lane] = static_cast<uint8_t>(v & 127);
-            const int lo16 = __reduce_add_sync(0xffffffffu, lane < 16 ? v : 0);
-            if (lane == 0) {
-                corr[lg] = 8 * lo16;
-                ascale[lg] = e8m0_scale(e[lg]);
+        const int per_tok = groups * 4;  // 8-value pieces per token
+        for (int i = ct; i < 8 * ntt * per_tok; i += 32 * kBatchWarps) {
+            const int n = i / per_tok, col = (i - n * per_tok) * 8;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (n < T)
+                v = *reinterpret_cast<const uint4*>(a.act_q + static_cast<size_t>(n) * kPfTok +
+                                                    static_cast<size_t>(bank) * a.act_bank_stride + col);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            uint32_t hv[2] = {0u, 0u}, lv[2] = {0u, 0u};
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int q = static_cast<int16_t>((w[k >> 1] >> (16 * (k & 1))) & 0xffffu);
+                hv[k >> 2] |= (static_cast<uint32_t>(q >> 7) & 0xffu) << (8 * (k & 3));
+                lv[k >> 2] |= static_cast<uint32_t>(q & 127) << (8 * (k & 3));
             }
+            uint8_t* tb = act + static_cast<size_t>(n) * tstride;
+            *reinterpret_cast<uint2*>(tb + col) = make_uint2(hv[0], hv[1]);
+            *reinterpret_cast<uint2*>(tb + groups * 32 + col) = make_uint2(lv[0], lv[1]);
+        }
+        for (int i = ct; i < 8 * ntt * groups; i += 32 * kBatchWarps) {
+            const int n = i / groups, lg = i - n * groups;
+            float* asc = reinterpret_cast<float*>(act + static_cast<size_t>(n) * tstride + groups * 64);
+            asc[lg] = n < T ? e8m0_scale(a.act_e[(static_cast<size_t>(n) * kPfTok +
+                                                  static_cast<size_t>(bank) * a.act_bank_stride) / 32 + lg])
+                            : 0.0f;
         }
     }
-    __syncwarp();
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * kBatchWarps) : "memory");
+    const int su = cw >> 2, rt = (cw >> 1) & 1, tt = cw & 1;
+    if (tt >= ntt) return;
 
+    const int gid = lane >> 2, tig = lane & 3;
+    const int r0 = rt * 16 + gid, r1 = r0 + 8;           // rows of c0/c1 and c2/c3
+    const int n0 = tt * 8 + 2 * tig;                      // tokens of c0/c2 and c1/c3
+    const uint8_t* tb = act + static_cast<size_t>(tt * 8 + gid) * tstride;  // B operand: token tt*8 + gid
+    const uint8_t* bh = tb + 4 * tig;
+    const uint8_t* bl = tb + groups * 32 + 4 * tig;
+    const float* as0 = reinterpret_cast<const float*>(act + static_cast<size_t>(n0) * tstride + groups * 64);
+    const float* as1 = reinterpret_cast<const float*>(act + static_cast<size_t>(n0 + 1) * tstride + groups * 64);
     const int rows_total = a.units * 32;
-    float* out = a.partials + (static_cast<size_t>(t) * 4 + bank) * rows_total + lane;
-    float acc = 0.0f;
-    int j = 0, u = u0, slot = 0;
-    uint32_t phase = 0;
-    for (int i = 0; i < nchunks; ++i) {
-        mbar_wait(&full[slot], phase, a.err, kErrWaitFull);
-        const uint8_t* ch = ring + static_cast<size_t>(slot) * kChunkBytes;
-        uint4 wv[8];
+    const size_t tok_stride = static_cast<size_t>(4) * rows_total;
+    float* out = a.partials + static_cast<size_t>(bank) * rows_total;
+    // chunk_piece(r, g) for the two rows (r & 7 == gid; r >> 3 == 2 rt, 2 rt + 1)
+    const int p0 = kChunkScaleBytes + ((gid * 4 + 2 * rt) * 8) * 16 + 4 * tig;
+    const int p1 = p0 + 8 * 16;
+
+    for (int rb = 0; rb + su < nunits; rb += kBatchUnits) {
+        const int nu = min(kBatchUnits, nunits - rb);
+        float c00 = 0.0f, c01 = 0.0f, c10 = 0.0f, c11 = 0.0f;  // [row r0/r1][token n0/n0+1]
+        for (int j = 0; j < a.chunks; ++j) {
+            const int idx = rb * a.chunks + j * nu + su;
+            const int slot = idx % kBatchSlots;
+            wait_issued(&issued[slot], idx, a.err);
+            mbar_wait(&full[slot], static_cast<uint32_t>((idx / kBatchSlots) & 1), a.err, kErrWaitFull);
+            const uint8_t* ch = ring + static_cast<size_t>(slot) * kChunkBytes;
+            uint32_t w0[8], w1[8];
 #pragma unroll
-        for (int g = 0; g < 8; ++g) wv[g] = *reinterpret_cast<const uint4*>(ch + chunk_piece(lane, g));
-        const int16_t raw0 = reinterpret_cast<const int16_t*>(ch)[lane * 2];
-        const int16_t raw1 = reinterpret_cast<const int16_t*>(ch)[lane * 2 + 1];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        if (++slot == kBatchSlots) {
-            slot = 0;
-            phase ^= 1u;
-        }
-        const float ws0 = __fmul_rn(static_cast<float>(raw0), 1.0f / 32768.0f);
-        const float ws1 = __fmul_rn(static_cast<float>(raw1), 1.0f / 32768.0f);
+            for (int g = 0; g < 8; ++g) {
+                w0[g] = *reinterpret_cast<const uint32_t*>(ch + p0 + ((g ^ gid) << 4));
+                w1[g] = *reinterpret_cast<const uint32_t*>(ch + p1 + ((g ^ gid) << 4));
+            }
+            const int16_t* sc = reinterpret_cast<const int16_t*>(ch);
+            const float ws00 = __fmul_rn(static_cast<float>(sc[r0 * 2]), 1.0f / 32768.0f);
+            const float ws01 = __fmul_rn(static_cast<float>(sc[r0 * 2 + 1]), 1.0f / 32768.0f);
+            const float ws10 = __fmul_rn(static_cast<float>(sc[r1 * 2]), 1.0f / 32768.0f);
+            const float ws11 = __fmul_rn(static_cast<float>(sc[r1 * 2 + 1]), 1.0f / 32768.0f);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-            const int lg = j * 8 + g;
-            const int dot = group_dot(wv[g], hi + lg * 32, lo + lg * 32, corr[lg]);
-            acc = __fadd_rn(acc, __fmul_rn(static_cast<float>(dot), __fmul_rn(g < 4 ? ws0 : ws1, ascale[lg])));
+            for (int g = 0; g < 8; ++g) {
+                const int lg = j * 8 + g;
+                const uint32_t a0 = w16_lo(w0[g]), a1 = w16_lo(w1[g]), a2 = w16_hi(w0[g]), a3 = w16_hi(w1[g]);
+                const uint32_t h0 = *reinterpret_cast<const uint32_t*>(bh + lg * 32);
+                const uint32_t h1 = *reinterpret_cast<const uint32_t*>(bh + lg * 32 + 16);
+                const uint32_t l0 = *reinterpret_cast<const uint32_t*>(bl + lg * 32);
+                const uint32_t l1 = *reinterpret_cast<const uint32_t*>(bl + lg * 32 + 16);
+                int dh[4], dl[4];
+                mma_s8(dh, a0, a1, a2, a3, h0, h1);
+                mma_s8(dl, a0, a1, a2, a3, l0, l1);
+                // 16 * dot = 16 * (128 * sum(w ah) + sum(w al)); exact in int32
+                const int d0 = (dh[0] * 128 + dl[0]) >> 4, d1 = (dh[1] * 128 + dl[1]) >> 4;
+                const int d2 = (dh[2] * 128 + dl[2]) >> 4, d3 = (dh[3] * 128 + dl[3]) >> 4;
+                const float s0 = as0[lg], s1 = as1[lg];
+                const float wa = g < 4 ? ws00 : ws01, wb = g < 4 ? ws10 : ws11;
+                c00 = __fadd_rn(c00, __fmul_rn(static_cast<float>(d0), __fmul_rn(wa, s0)));
+                c01 = __fadd_rn(c01, __fmul_rn(static_cast<float>(d1), __fmul_rn(wa, s1)));
+                c10 = __fadd_rn(c10, __fmul_rn(static_cast<float>(d2), __fmul_rn(wb, s0)));
+                c11 = __fadd_rn(c11, __fmul_rn(static_cast<float>(d3), __fmul_rn(wb, s1)));
+            }
         }
-        if (++j == a.chunks) {
-            out[static_cast<size_t>(u) * 32] = acc;
-            acc = 0.0f;
-            j = 0;
-            ++u;
+        const size_t row0 = static_cast<size_t>(u0 + rb + su) * 32 + r0;
+        if (n0 < T) {
+            out[n0 * tok_stride + row0] = c00;
+            out[n0 * tok_stride + row0 + 8] = c10;
+        }
+        if (n0 + 1 < T) {
+            out[(n0 + 1) * tok_stride + row0] = c01;
+            out[(n0 + 1) * tok_stride + row0 + 8] = c11;
         }
     }
 }
@@ -167,6 +254,8 @@ struct PfNormArgs {
 };
 
 __global__ void __launch_bounds__(1024) k_pf_norm(const __grid_constant__ PfNormArgs a) {
+    pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.x, i = threadIdx.x;
     float* r = a.resid + static_cast<size_t>(t) * kDim;
     float x[4];
@@ -180,9 +269,12 @@ __global__ void __launch_bounds__(1024) k_pf_norm(const __grid_constant__ PfNorm
         }
     }
     __shared__ float inv_s;
+    __shared__ float xs[kDim];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) xs[i + k * 1024] = x[k];
     __syncthreads();
     if (i < 32) {
-        const float inv = rms_recip_warp(r);
+        const float inv = rms_recip_warp(xs);
         if (i == 0) {
             inv_s = inv;
             a.recip[t] = inv;
@@ -205,6 +297,8 @@ __global__ void __launch_bounds__(1024) k_pf_norm(const __grid_constant__ PfNorm
 // linear_finalize's EPI_SWIGLU; emulator:716-722, 769-770).  Grid (stripes, T).
 __global__ void __launch_bounds__(32) k_pf_swiglu(const float* partials, int units, ExpfFix fx, int16_t* q,
                                                    uint8_t* e) {
+    pdl_trigger();
+    pdl_wait();
     const int stripe = blockIdx.x, t = blockIdx.y, lane = threadIdx.x;
     const int rows = units * 32, stripes = units / 2;
     const float* P = partials + static_cast<size_t>(t) * 4 * rows;
