@@ -36,6 +36,7 @@ sys.path.insert(0, ROOT)
 METRIC = "batch-1 INT4 Llama-2-7B decode tokens/s"
 UNIT = "tokens/s"
 PROMPT = 16
+PREFILL_TOKENS = 128  # prompt length of the prefill measurement
 
 
 def parse():
@@ -355,6 +356,26 @@ def main():
         "replay_matches_e2e": replay_ok,
         "clocks": clk,
     }
+    # ---- batched prompt prefill (i4d_prefill_tokens) of the same token
+    # sequence: it rewrites the same KV records bit for bit, and its greedy
+    # next id must be the decoded continuation ----
+    if not shard:
+        n_pf = min(PREFILL_TOKENS, total - 1)
+        ids = np.asarray(tokens[:n_pf], np.int32)
+        ctx.prefill_tokens(0, ids)  # warm-up
+        barrier()
+        reps = 3
+        ev0.record(stream)
+        for _ in range(reps):
+            nxt_pf, _ = ctx.prefill_tokens(0, ids)
+        ev1.record(stream)
+        barrier()
+        pf_ms = max_over_ranks(ev0.elapsed_time(ev1)) / reps
+        batches = -(-n_pf // 16)
+        line["prefill"] = {"value": streams * n_pf / (pf_ms * 1e-3), "unit": "prompt tokens/s", "tokens": n_pf,
+                           "ms": pf_ms, "api": "i4d_prefill_tokens (token ids in, greedy next id out)",
+                           "h2d_bytes": 8 * n_pf, "d2h_bytes": 8 + 4 * batches,
+                           "matches_decode": bool(nxt_pf == tokens[n_pf]) if n_pf >= PROMPT else None}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_sample(banks, emb, lut, tokens, args.cpu_layers, args.cpu_steps)
     ctx.close()
