@@ -11,6 +11,7 @@ Errors raise I4DError carrying the C status and message; there is no CPU
 fallback: without the CUDA library every call fails.
 """
 import ctypes
+import math
 import os
 
 import numpy as np
@@ -34,7 +35,7 @@ EXPORTS = [
     "i4d_profile_token", "i4d_token_breakdown", "i4d_linear_bank_noalloc",
     "i4d_token_timeline", "i4d_create_shard", "i4d_shard_export", "i4d_shard_attach",
     "i4d_decode_greedy", "i4d_argmax", "i4d_sampler_init", "i4d_sample", "i4d_decode_sample",
-    "i4d_pack_autoround_matrix", "i4d_pack_fp32_head", "i4d_prefill", "i4d_prefill_tokens",
+    "i4d_pack_autoround_matrix", "i4d_pack_fp32_head", "i4d_prefill", "i4d_prefill_tokens", "i4d_eval_nll",
 ]
 
 SAMPLER_HOST = 0      # decode_host.cpp:724-868
@@ -124,6 +125,7 @@ def load_library():
         "i4d_decode_greedy": [P, ctypes.c_uint32, ctypes.c_int32, P, P],
         "i4d_prefill": [P, ctypes.c_uint32, P, ctypes.c_uint32, P],
         "i4d_prefill_tokens": [P, ctypes.c_uint32, P, ctypes.c_uint32, P, P],
+        "i4d_eval_nll": [P, P, ctypes.c_uint32, P],
         "i4d_argmax": [P, P, ctypes.c_size_t, P],
         "i4d_sample": [P, P, P, ctypes.c_uint32, P, P],
         "i4d_decode_sample": [P, ctypes.c_uint32, ctypes.c_int32, P, ctypes.c_uint32, P, P],
@@ -280,6 +282,33 @@ class Context:
         self._check(self._L.i4d_prefill_tokens(self._h, position0, ids.ctypes.data, ids.size, ctypes.byref(nxt),
                                                _ptr(logits)))
         return nxt.value, logits
+
+    def eval_nll(self, token_ids):
+        """Per-position negative log-likelihoods of one chunk (n - 1 doubles)."""
+        ids = np.ascontiguousarray(token_ids, dtype=np.int32)
+        out = np.empty(max(ids.size - 1, 0), dtype=np.float64)
+        self._check(self._L.i4d_eval_nll(self._h, ids.ctypes.data, ids.size, out.ctypes.data if out.size else None))
+        return out
+
+    def perplexity(self, token_ids, chunk=None):
+        """The emulator's PPL loop (calculate_perplexity, emulator:1852-1944):
+        chunks of `chunk` tokens (default: the KV capacity), each evaluated
+        from position 0; returns (average loss, perplexity, tokens evaluated),
+        the NLLs summed in order in double."""
+        ids = np.ascontiguousarray(token_ids, dtype=np.int32)
+        chunk = chunk or self.kv_capacity or 4096
+        total, count = 0.0, 0
+        for start in range(0, ids.size, chunk):
+            part = ids[start:start + chunk]
+            if part.size < 2:
+                break
+            for v in self.eval_nll(part):
+                total += float(v)
+                count += 1
+        if count == 0:
+            raise ValueError("needs at least 2 tokens")
+        loss = total / count
+        return loss, math.exp(loss), count
 
     def sample(self, logits_dev_ptr, history, sampler):
         """One device draw over 32000 logits at a device pointer; advances sampler.rng_state."""

@@ -161,6 +161,10 @@ struct i4d_ctx {
     uint32_t* d_pf_coef = nullptr;
     int* d_pf_pos = nullptr;
     int* d_pf_ids = nullptr;
+    int* d_pf_tgt = nullptr;      // perplexity: target id of every token of the batch
+    float* d_pf_lg = nullptr;     // perplexity: [16][32000] logits / expf terms
+    float* d_pf_terms = nullptr;  // perplexity: [16][4] max, sum, target logit
+    float* h_pf_terms = nullptr;
     float* h_pf_resid = nullptr;
     int* h_pf_pos = nullptr;
     int* h_pf_ids = nullptr;
@@ -499,8 +503,10 @@ cudaError_t run_pf_norm(i4d_ctx* c, int T, int partial_stage, const float* gamma
 // positions in d_pf_pos), in the decode order of every token: norm, QKV,
 // attention (records of all T tokens, then the T queries), O + residual,
 // norm, GATE/UP, SwiGLU, DOWN + residual.  With `last`, the final norm and
-// the LM head of the batch's last token follow (logits in d_logits).
-i4d_status enqueue_prefill(i4d_ctx* c, int T, bool last) {
+// the LM head of the batch's last token follow (logits in d_logits); with
+// `nll`, the final norm and LM head of every token and its perplexity terms
+// (targets in d_pf_tgt, terms in d_pf_terms).
+i4d_status enqueue_prefill(i4d_ctx* c, int T, bool last, bool nll) {
     for (int l = 0; l < c->layers; ++l) {
         CK(run_pf_norm(c, T, l == 0 ? -1 : ST_DOWN, c->d_gamma + static_cast<size_t>(2 * l) * kDim));
         CK(run_batch(c, l, ST_QKV, T, 1024));
@@ -522,6 +528,20 @@ i4d_status enqueue_prefill(i4d_ctx* c, int T, bool last) {
         CK(launch(c, true, k_pf_swiglu, dim3(kStageUnits[ST_GU] / 2, T), dim3(32), 0, (const float*)c->d_pf_part,
                   static_cast<int>(kStageUnits[ST_GU]), c->expf, c->d_pf_q, c->d_pf_e));
         CK(run_batch(c, l, ST_DOWN, T, 2816));
+    }
+    if (nll) {
+        CK(run_pf_norm(c, T, ST_DOWN, c->d_gamma + static_cast<size_t>(64) * kDim));
+        CK(run_batch(c, 0, ST_LOGITS, T, 1024));
+        PfNllArgs na = {};
+        na.partials = c->d_pf_part;
+        na.lg = c->d_pf_lg;
+        na.target = c->d_pf_tgt;
+        na.terms = c->d_pf_terms;
+        na.expf = c->expf;
+        CK(launch(c, true, k_pf_logits, dim3(T), dim3(1024), 0, na));
+        CK(launch(c, true, k_pf_exp, dim3((kVocab + 1023) / 1024, T), dim3(1024), 0, na));
+        CK(launch(c, true, k_pf_sum, dim3(T), dim3(32), 0, na));
+        return I4D_OK;
     }
     CK(run_pf_norm(c, T, ST_DOWN, nullptr));
     if (!last) return I4D_OK;
@@ -569,11 +589,11 @@ void i4d_destroy(i4d_ctx* c) {
                    c->d_tok, c->d_argmax, c->d_sample_hist, c->d_sample_keys, c->d_sample_idx,
                    c->d_sample_state, c->d_sample_out, c->d_sample_v, c->d_sample_smax, c->d_pf_resid,
                    c->d_pf_recip, c->d_pf_q, c->d_pf_e, c->d_pf_part, c->d_pf_qrot, c->d_pf_coef, c->d_pf_pos,
-                   c->d_pf_ids};
+                   c->d_pf_ids, c->d_pf_tgt, c->d_pf_lg, c->d_pf_terms};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* host[] = {c->h_resid_in, c->h_resid_out, c->h_logits, c->h_pos, c->h_err, c->h_tok, c->h_argmax,
-                    c->h_sample_state, c->h_sample_out, c->h_pf_resid, c->h_pf_pos, c->h_pf_ids};
+                    c->h_sample_state, c->h_sample_out, c->h_pf_resid, c->h_pf_pos, c->h_pf_ids, c->h_pf_terms};
     for (void* p : host)
         if (p) cudaFreeHost(p);
     if (c->stream) cudaStreamDestroy(c->stream);
@@ -691,14 +711,18 @@ static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ct
     CKC(cudaMalloc(&c->d_pf_recip, kPrefillMax * sizeof(float)));
     CKC(cudaMalloc(&c->d_pf_q, static_cast<size_t>(kPrefillMax) * kPfTok * sizeof(int16_t)));
     CKC(cudaMalloc(&c->d_pf_e, static_cast<size_t>(kPrefillMax) * kPfTok / 32));
-    CKC(cudaMalloc(&c->d_pf_part, static_cast<size_t>(kPrefillMax) * 4 * kStageUnits[ST_GU] * 32 * sizeof(float)));
+    CKC(cudaMalloc(&c->d_pf_part, static_cast<size_t>(kPrefillMax) * 4 * kPVocab * sizeof(float)));
     CKC(cudaMalloc(&c->d_pf_qrot, static_cast<size_t>(kPrefillMax) * kDim * sizeof(int32_t)));
     CKC(cudaMalloc(&c->d_pf_coef, static_cast<size_t>(kPrefillMax) * kHeads * c->stride * sizeof(uint32_t)));
     CKC(cudaMalloc(&c->d_pf_pos, kPrefillMax * sizeof(int)));
     CKC(cudaMalloc(&c->d_pf_ids, kPrefillMax * sizeof(int)));
     CKC(cudaMallocHost(&c->h_pf_resid, static_cast<size_t>(kPrefillMax) * kDim * sizeof(float)));
     CKC(cudaMallocHost(&c->h_pf_pos, kPrefillMax * sizeof(int)));
-    CKC(cudaMallocHost(&c->h_pf_ids, kPrefillMax * sizeof(int)));
+    CKC(cudaMallocHost(&c->h_pf_ids, 2 * kPrefillMax * sizeof(int)));
+    CKC(cudaMalloc(&c->d_pf_tgt, kPrefillMax * sizeof(int)));
+    CKC(cudaMalloc(&c->d_pf_lg, static_cast<size_t>(kPrefillMax) * kVocab * sizeof(float)));
+    CKC(cudaMalloc(&c->d_pf_terms, kPrefillMax * 4 * sizeof(float)));
+    CKC(cudaMallocHost(&c->h_pf_terms, kPrefillMax * 4 * sizeof(float)));
 
     // exp2 LUT of the online softmax: round(2^(30 + i/32)), and log2(e) in
     // Q21 (emulator:566-579 define the same quantities).
@@ -1166,7 +1190,8 @@ i4d_status i4d_decode_token(i4d_ctx* c, uint32_t position, const float* residual
 // Prompt of n tokens in batches of kPrefillMax; ids (device embeddings) or
 // residuals (host) give each token's input.
 static i4d_status prefill_impl(i4d_ctx* c, uint32_t position0, const float* residuals, const int32_t* ids,
-                               uint32_t n, int32_t* next_id, float* logits_out) {
+                               uint32_t n, int32_t* next_id, float* logits_out, const int32_t* targets = nullptr,
+                               double* nll_out = nullptr) {
     if (!all_loaded(c)) return fail(c, I4D_ERR_STATE, "banks and rope LUT must be loaded before a prefill");
     if (c->world != 1) return fail(c, I4D_ERR_STATE, "prefill needs all four banks in one context");
     if (ids && !c->d_emb) return fail(c, I4D_ERR_STATE, "embeddings must be loaded before a token prefill");
@@ -1193,8 +1218,15 @@ static i4d_status prefill_impl(i4d_ctx* c, uint32_t position0, const float* resi
             CK(cudaMemcpyAsync(c->d_pf_resid, c->h_pf_resid, static_cast<size_t>(T) * kDim * sizeof(float),
                                cudaMemcpyHostToDevice, c->stream));
         }
-        const i4d_status st = enqueue_prefill(c, T, last);
+        if (targets) {  // staged in the second half of h_pf_ids
+            std::memcpy(c->h_pf_ids + kPrefillMax, targets + b, T * sizeof(int));
+            CK(cudaMemcpyAsync(c->d_pf_tgt, c->h_pf_ids + kPrefillMax, T * sizeof(int), cudaMemcpyHostToDevice,
+                               c->stream));
+        }
+        const i4d_status st = enqueue_prefill(c, T, last && !targets, targets != nullptr);
         if (st != I4D_OK) return st;
+        if (targets)
+            CK(cudaMemcpyAsync(c->h_pf_terms, c->d_pf_terms, T * 4 * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
         if (last && next_id) {
             k_argmax<<<1, 1024, 0, c->stream>>>(c->d_logits, kVocab, c->d_argmax);
             CK(cudaGetLastError());
@@ -1202,6 +1234,12 @@ static i4d_status prefill_impl(i4d_ctx* c, uint32_t position0, const float* resi
         // The pinned staging is reused by the next batch.
         const i4d_status fs = finish(c);
         if (fs != I4D_OK) return fs;
+        for (int t = 0; nll_out && t < T; ++t) {  // emulator:1922-1926, in its types
+            const float* tm = c->h_pf_terms + 4 * t;
+            const double log_sum_exp = tm[0] + std::log(tm[1]);
+            const double log_prob = tm[2] - log_sum_exp;
+            nll_out[b + t] = -log_prob;
+        }
     }
     if (next_id) {
         unsigned long long k = 0;
@@ -1221,6 +1259,15 @@ i4d_status i4d_prefill_tokens(i4d_ctx* c, uint32_t position0, const int32_t* tok
                               int32_t* next_id, float* logits_out) {
     if (!c || !token_ids) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
     return prefill_impl(c, position0, nullptr, token_ids, n, next_id, logits_out);
+}
+
+i4d_status i4d_eval_nll(i4d_ctx* c, const int32_t* token_ids, uint32_t n, double* nll_out) {
+    if (!c || !token_ids || !nll_out) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
+    if (n < 2) return fail(c, I4D_ERR_ARG, "perplexity needs at least 2 tokens");
+    for (uint32_t i = 0; i < n; ++i)
+        if (token_ids[i] < 0 || token_ids[i] >= kVocab)
+            return fail(c, I4D_ERR_ARG, "token id %d out of range", token_ids[i]);
+    return prefill_impl(c, 0, nullptr, token_ids, n - 1, nullptr, nullptr, token_ids + 1, nll_out);
 }
 
 i4d_status i4d_kv_reset(i4d_ctx* c) {

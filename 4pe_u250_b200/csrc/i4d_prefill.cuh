@@ -20,6 +20,8 @@
 #include "i4d_device.cuh"
 #include "i4d_expf.cuh"
 #include "i4d_linear.cuh"
+#include "i4d_sample.cuh"
+#include "i4d_token.cuh"
 
 namespace i4d {
 
@@ -308,6 +310,69 @@ __global__ void __launch_bounds__(32) k_pf_swiglu(const float* partials, int uni
     const int v = quantize_g32_lane(swiglu1(g, u, fx), &e8);
     q[static_cast<size_t>(t) * kPfTok + stripe * 32 + lane] = static_cast<int16_t>(v);
     if (lane == 0) e[static_cast<size_t>(t) * (kPfTok / 32) + stripe] = static_cast<uint8_t>(e8);
+}
+
+// Perplexity terms of every token of a batch (emulator calculate_perplexity,
+// :1902-1926), from the LM-head partials [T][4][32256]:
+//   k_pf_logits  logits l_i = (p0+p1)+(p2+p3), i < 32000; max_l as the serial
+//                scan `if (l[i] > max_l)` from l[0] finds it (the value of the
+//                first maximum, NaN skipped; NaN when l[0] is NaN); the
+//                target's logit.  One CTA per token.
+//   k_pf_exp     expf(l_i - max_l) in place (glibc-equal expf).
+//   k_pf_sum     the serial FP32 sum from +0.0f in index order.
+// The host finishes each term as the emulator: (double)(max_l +
+// logf(sum_exp)) and -(logit - that) in double.
+struct PfNllArgs {
+    const float* partials;  // [T][4][kPVocab]
+    float* lg;              // [T][kVocab]: logits, then the expf terms
+    const int* target;      // [T]
+    float* terms;           // [T][4]: max_l, sum_exp, target logit, 0
+    ExpfFix expf;
+};
+
+__global__ void __launch_bounds__(1024) k_pf_logits(const __grid_constant__ PfNllArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x;
+    const float* P = a.partials + static_cast<size_t>(t) * 4 * kPVocab;
+    float* lg = a.lg + static_cast<size_t>(t) * kVocab;
+    const int tgt = a.target[t];
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < kVocab; i += 1024) {
+        const float v = combine4(P, kPVocab, i);
+        lg[i] = v;
+        const unsigned long long k = argmax_key(v, i);
+        best = k > best ? k : best;
+        if (i == tgt) a.terms[t * 4 + 2] = v;
+    }
+    __shared__ unsigned long long w[32];
+    best = warp_max_u64(best);
+    if ((threadIdx.x & 31) == 0) w[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const unsigned long long k = warp_max_u64(w[threadIdx.x]);
+        if (threadIdx.x == 0) {
+            const float l0 = lg[0];
+            a.terms[t * 4] = (l0 != l0 || k == 0ull) ? l0 : lg[0xffffffffu - static_cast<uint32_t>(k & 0xffffffffu)];
+            a.terms[t * 4 + 3] = 0.0f;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(1024) k_pf_exp(const __grid_constant__ PfNllArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.y, i = blockIdx.x * 1024 + threadIdx.x;
+    if (i >= kVocab) return;
+    float* lg = a.lg + static_cast<size_t>(t) * kVocab;
+    lg[i] = expf_libc(__fsub_rn(lg[i], a.terms[t * 4]), a.expf);
+}
+
+__global__ void __launch_bounds__(32) k_pf_sum(const __grid_constant__ PfNllArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x;
+    if (threadIdx.x == 0) a.terms[t * 4 + 1] = sample_serial_sum(a.lg + static_cast<size_t>(t) * kVocab, kVocab);
 }
 
 // Prompt embeddings: resid[t] = emb[ids[t]] (ids checked on the host).

@@ -158,6 +158,17 @@ i4d_status i4d_prefill(i4d_ctx* ctx, uint32_t position0, const float* residuals_
 i4d_status i4d_prefill_tokens(i4d_ctx* ctx, uint32_t position0, const int32_t* token_ids, uint32_t n,
                               int32_t* next_id, float* logits_out);
 
+/* Perplexity terms of one evaluation chunk (SURVEY-(f) row 4; the chunk
+ * loop body of calculate_perplexity, emulator:1857-1927): token_ids[0..n),
+ * 2 <= n, n - 1 <= KV capacity; positions 0 .. n-2 run as prompt batches
+ * from position 0 (the chunk's cache restart), and nll_out[p] (n - 1
+ * doubles) receives -(logits[ids[p+1]] - (double)(max_l + logf(sum_exp)))
+ * with max_l the first maximum of the 32000 logits and sum_exp the serial
+ * FP32 sum of expf(logit - max_l), in the emulator's types and order.  The
+ * caller sums nll_out over chunks as the emulator does (total_nll / count,
+ * exp of that).  Overwrites the context's KV records from position 0. */
+i4d_status i4d_eval_nll(i4d_ctx* ctx, const int32_t* token_ids, uint32_t n, double* nll_out);
+
 /* Bank-image producer on the device (scripts/autoround_pack_llama2_u250.py).
  * bank_images_dev: four device buffers of I4D_BANK_BYTES, the images being
  * built (i4d_load_bank accepts them as they are).

@@ -45,11 +45,13 @@ class Oracle:
             "i4o_exp_negative_q17": [ctypes.c_int32],
             "i4o_sample": [ctypes.c_int, P, ctypes.c_int, P, ctypes.c_int, ctypes.c_float, ctypes.c_float,
                            ctypes.c_float, P],
+            "i4o_nll": [P, ctypes.c_int, ctypes.c_int, P, P],
         }
         for k, v in sigs.items():
             getattr(L, k).argtypes = v
         L.i4o_argmax.restype = ctypes.c_int
         L.i4o_sample.restype = ctypes.c_int
+        L.i4o_nll.restype = ctypes.c_double
         L.i4o_exp_negative_q17.restype = ctypes.c_uint32
         self.L = L
         self._rope = None
@@ -162,6 +164,14 @@ class Oracle:
         x = np.ascontiguousarray(logits, dtype=np.float32)
         return self.L.i4o_argmax(x.ctypes.data, n)
 
+    def nll(self, logits, target):
+        """The perplexity loop's term for one position (emulator:1902-1926):
+        (nll, max_l, sum_exp)."""
+        x = np.ascontiguousarray(logits, dtype=np.float32)
+        m, s = ctypes.c_float(0.0), ctypes.c_float(0.0)
+        v = self.L.i4o_nll(x.ctypes.data, x.size, int(target), ctypes.byref(m), ctypes.byref(s))
+        return v, m.value, s.value
+
     def sample(self, mode, logits, history, temperature, top_p, repeat_penalty, state):
         """One sampler draw (mode 0: decode_host.cpp:724-868, 1: emulator:1411-1569);
         returns (token, advanced state)."""
@@ -242,6 +252,7 @@ class RefEmulator:
             "ref_kv_get": [ctypes.c_int] * 4 + [P, P, P, P],
             "ref_argmax": [P, ctypes.c_int],
             "ref_sample": [P, ctypes.c_int, P, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_float, P],
+            "ref_perplexity": [ctypes.c_char_p, ctypes.c_int],
         }
         for k, v in sigs.items():
             getattr(L, k).argtypes = v
@@ -256,6 +267,11 @@ class RefEmulator:
         t = self.L.ref_sample(x.ctypes.data, x.size, h.ctypes.data if h.size else None, h.size, temperature, top_p,
                               repeat_penalty, ctypes.addressof(st))
         return t, int(st[0])
+
+    def perplexity(self, token_file, max_tokens=0):
+        """The emulator's own calculate_perplexity (emulator:1775-1958) on an
+        int32 token file ending in .bin; its report goes to stdout."""
+        self.L.ref_perplexity(token_file.encode(), max_tokens)
 
     def load(self, directory, layers, stride):
         if self.L.ref_load(directory.encode(), layers, stride) != 0:

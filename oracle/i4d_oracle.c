@@ -578,6 +578,22 @@ int i4o_argmax(const float* logits, int n) {
     return best;
 }
 
+/* ---- perplexity term (emulator:1902-1926) ---- */
+
+double i4o_nll(const float* logits, int n, int target, float* max_out, float* sum_out) {
+    float max_l = logits[0];
+    for (int i = 1; i < n; ++i)
+        if (logits[i] > max_l) max_l = logits[i];
+    float sum_exp = 0.0f;
+    for (int i = 0; i < n; ++i) sum_exp += expf(logits[i] - max_l);
+    const float lse_f = max_l + logf(sum_exp);
+    const double log_sum_exp = (double)lse_f;
+    const double log_prob = (double)logits[target] - log_sum_exp;
+    if (max_out) *max_out = max_l;
+    if (sum_out) *sum_out = sum_exp;
+    return -log_prob;
+}
+
 /* ---- sampler (decode_host.cpp:724-868, emulator:1411-1569) ---- */
 
 /* decode_host.cpp:703-717: first strict maximum, NaN skipped; -1 if none. */

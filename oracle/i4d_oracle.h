@@ -137,6 +137,14 @@ void i4o_expf_array(const float* x, float* y, size_t n); /* host C library expf 
 /* emulator:1428-1438: index of the first strict maximum over n. */
 int i4o_argmax(const float* logits, int n);
 
+/* Negative log-likelihood of `target` as the emulator's perplexity loop
+ * computes it (emulator:1902-1926): max_l = serial maximum from logits[0]
+ * (strictly greater replaces), sum_exp = serial FP32 sum of expf(l - max_l)
+ * from 0.0f, log_sum_exp = (double)(max_l + logf(sum_exp)) (float
+ * arithmetic, then widened), nll = -((double)logits[target] - log_sum_exp).
+ * max_out / sum_out (may be NULL) receive max_l and sum_exp. */
+double i4o_nll(const float* logits, int n, int target, float* max_out, float* sum_out);
+
 /* One sampler draw over logits[0, n), the state advanced in place.
  * mode 0: decode_host.cpp:724-868 (the hardware host's Sampler); mode 1:
  * emulator:1411-1569 (llama2.c's).  Top-p candidates are ordered by

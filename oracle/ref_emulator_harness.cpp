@@ -152,4 +152,12 @@ int ref_sample(float* logits, int n, const int32_t* history, int n_history, floa
     return t;
 }
 
+// The emulator's perplexity loop (calculate_perplexity, emulator:1775-1958)
+// over a pre-tokenized int32 file whose name ends in .bin (no tokenizer is
+// read on that path); the report goes to stdout.
+void ref_perplexity(const char* token_file, int max_tokens) {
+    calculate_perplexity(g_model, nullptr, token_file, max_tokens);
+    std::cout.flush();
+}
+
 }  // extern "C"
