@@ -376,6 +376,18 @@ def main():
                            "ms": pf_ms, "api": "i4d_prefill_tokens (token ids in, greedy next id out)",
                            "h2d_bytes": 8 * n_pf, "d2h_bytes": 8 + 4 * batches,
                            "matches_decode": bool(nxt_pf == tokens[n_pf]) if n_pf >= PROMPT else None}
+        # ---- perplexity terms of the same tokens (i4d_eval_nll: n - 1 positions) ----
+        ctx.eval_nll(ids)
+        barrier()
+        ev0.record(stream)
+        for _ in range(reps):
+            ctx.eval_nll(ids)
+        ev1.record(stream)
+        barrier()
+        ev_ms = max_over_ranks(ev0.elapsed_time(ev1)) / reps
+        line["perplexity_eval"] = {"value": streams * (n_pf - 1) / (ev_ms * 1e-3), "unit": "positions/s",
+                                   "positions": n_pf - 1, "ms": ev_ms,
+                                   "api": "i4d_eval_nll (token ids in, one NLL per position out)"}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_sample(banks, emb, lut, tokens, args.cpu_layers, args.cpu_steps)
     ctx.close()
