@@ -3,15 +3,16 @@
 // Loads model_bank{0..3}.bin, rope_lut.bin and embeddings.bin exactly as
 // decode_host does (host/decode_host.cpp:1236-1296, same size checks), then
 // runs the per-token contract through libi4d: residual = embedding row in,
-// 32256 padded logits out (decode_host.cpp:1340-1556).  Prefill is one token
-// per step as in the reference (decode_host.cpp:1570-1580); generation is
-// greedy (argmax of the first 32000 logits, NaN skipped, decode_host.cpp:703-717).
-// The tokenizer and stochastic sampler are outside this path: prompts are
-// token ids.
+// 32256 padded logits out (decode_host.cpp:1340-1556).  The prompt runs one
+// token per step as in the reference (decode_host.cpp:1570-1580), or with
+// --prefill as one i4d_prefill call (batches of 16 prompt tokens, the same KV
+// records and last logits); generation is greedy (argmax of the first 32000
+// logits, NaN skipped, decode_host.cpp:703-717).  The tokenizer and
+// stochastic sampler are outside this path: prompts are token ids.
 //
 //   i4d_decode --banks DIR [--rope FILE] [--embeddings FILE] --prompt-ids 1,2,3
 //              [--max-tokens N] [--layers L] [--kv-capacity S] [--device D]
-//              [--dump-logits DIR] [--no-eos] [--verbose]
+//              [--dump-logits DIR] [--no-eos] [--prefill] [--verbose]
 #include <chrono>
 #include <cmath>
 #include <cstdio>
@@ -31,7 +32,7 @@ struct Config {
     std::string banks_dir, rope, embeddings, dump_logits;
     std::vector<int> prompt;
     int max_tokens = 128, layers = 32, kv_capacity = 4096, device = 0;
-    bool stop_on_eos = true, verbose = false;
+    bool stop_on_eos = true, verbose = false, prefill = false;
 };
 
 std::vector<char> read_file(const std::string& path, size_t expect) {
@@ -79,6 +80,7 @@ Config parse(int argc, char** argv) {
         else if (a == "--device") c.device = std::stoi(next());
         else if (a == "--no-eos") c.stop_on_eos = false;
         else if (a == "--verbose") c.verbose = true;
+        else if (a == "--prefill") c.prefill = true;
         else if (a == "--prompt-ids") {
             std::stringstream ss(next());
             std::string tok;
@@ -128,7 +130,22 @@ int main(int argc, char** argv) {
             ++pos;
             next = argmax_logits(logits.data());
         };
-        for (int t : cfg.prompt) step(t);
+        if (cfg.prefill) {  // the whole prompt in batches; logits of its last token
+            std::vector<float> rows(cfg.prompt.size() * I4D_DIM);
+            for (size_t i = 0; i < cfg.prompt.size(); ++i) {
+                const int token = cfg.prompt[i];
+                if (token < 0 || token >= I4D_VOCAB) throw std::runtime_error("token id out of range");
+                std::memcpy(rows.data() + i * I4D_DIM, emb + static_cast<size_t>(token) * I4D_DIM, I4D_DIM * 4);
+            }
+            const auto t0 = std::chrono::steady_clock::now();
+            check(ctx, i4d_prefill(ctx, 0, rows.data(), static_cast<uint32_t>(cfg.prompt.size()), logits.data()),
+                  "prefill");
+            total_ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+            pos = static_cast<int>(cfg.prompt.size());
+            next = argmax_logits(logits.data());
+        } else {
+            for (int t : cfg.prompt) step(t);
+        }
         while (static_cast<int>(generated.size()) < cfg.max_tokens && pos < cfg.kv_capacity) {
             if (cfg.stop_on_eos && (next == 1 || next == 2)) break;
             generated.push_back(next);
