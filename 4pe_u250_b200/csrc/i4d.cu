@@ -484,7 +484,10 @@ cudaError_t run_batch(i4d_ctx* c, int layer, int st, int T, int act_bank_stride)
     b.act_bank_stride = act_bank_stride;
     b.partials = c->d_pf_part;
     b.err = c->d_err;
-    return launch(c, true, k_linear_batch, dim3(4 * c->cpb), dim3(kBatchThreads), batch_smem_bytes(b.chunks), b);
+    b.ns = batch_slots(b.chunks, T);
+    if (b.ns < 2) return cudaErrorInvalidValue;
+    return launch(c, true, k_linear_batch, dim3(4 * c->cpb), dim3(kBatchThreads),
+                  batch_smem_bytes(b.chunks, T, b.ns), b);
 }
 
 cudaError_t run_pf_norm(i4d_ctx* c, int T, int partial_stage, const float* gamma) {
@@ -639,7 +642,7 @@ static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ct
     CKC(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(attn_smem_bytes())));
     CKC(cudaFuncSetAttribute(k_linear_batch, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(batch_smem_bytes(kStageChunks[ST_DOWN]))));
+                             kBatchSmemMax));
     CKC(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(sample_smem_bytes())));
     CKC(cudaFuncSetAttribute(k_token<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,

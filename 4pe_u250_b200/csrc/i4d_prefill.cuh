@@ -25,11 +25,11 @@
 
 namespace i4d {
 
-constexpr int kPrefillMax = 16;                      // tokens per batch (two MMA token tiles)
-constexpr int kBatchUnits = 4;                       // units in flight per CTA
-constexpr int kBatchWarps = 4 * kBatchUnits;         // per unit: 2 row tiles x 2 token tiles
+constexpr int kPrefillMax = 32;                      // tokens per batch (four MMA token tiles)
+constexpr int kBatchWarps = 16;                      // MMA warps: units in flight x 2 row tiles x token tiles
 constexpr int kBatchThreads = 32 * (1 + kBatchWarps);
-constexpr int kBatchSlots = 24;                      // chunk ring slots
+constexpr int kBatchSlots = 24;                      // most chunk ring slots
+constexpr int kBatchSmemMax = 232448;                // dynamic shared memory of one CTA (227 KB)
 constexpr int kPfTok = 11264;                        // activation columns per token (DOWN input)
 
 struct BatchArgs {
@@ -39,6 +39,7 @@ struct BatchArgs {
     int units;              // units per bank
     int chunks;             // chunks per unit
     int T;                  // tokens in the batch, 1..kPrefillMax
+    int ns;                 // ring slots (batch_slots), 2..kBatchSlots
     const int16_t* act_q;   // [T][kPfTok]; bank b at b * act_bank_stride
     const uint8_t* act_e;   // [T][kPfTok / 32]
     int act_bank_stride;
@@ -52,9 +53,24 @@ struct BatchArgs {
 // tokens that one MMA B fragment reads start in 8 distinct 4-bank groups.
 __host__ __device__ constexpr int batch_tok_stride(int groups) { return groups * 68 + 16; }
 
-__host__ __device__ inline size_t batch_smem_bytes(int chunks) {
-    return static_cast<size_t>(kBatchSlots) * kChunkBytes + 2 * kBatchSlots * 8 + align16(kBatchSlots * 4) +
-           static_cast<size_t>(kPrefillMax) * batch_tok_stride(chunks * 8);
+// Token tiles of 8 in use for T tokens, and the units a CTA works on at a
+// time: 4 (two token tiles or fewer) or 2 (four token tiles).
+__host__ __device__ constexpr int batch_tiles(int T) { return (T + 7) >> 3; }
+__host__ __device__ constexpr int batch_units(int T) { return batch_tiles(T) <= 2 ? 4 : 2; }
+
+__host__ __device__ inline size_t batch_fixed_bytes(int chunks, int T) {
+    return 2 * kBatchSlots * 8 + align16(kBatchSlots * 4) +
+           static_cast<size_t>(8 * batch_tiles(T)) * batch_tok_stride(chunks * 8);
+}
+
+// Ring slots that fit beside the activations (DOWN at 32 tokens: 9).
+__host__ __device__ inline int batch_slots(int chunks, int T) {
+    const long long n = (kBatchSmemMax - static_cast<long long>(batch_fixed_bytes(chunks, T))) / kChunkBytes;
+    return static_cast<int>(n < kBatchSlots ? n : kBatchSlots);
+}
+
+__host__ __device__ inline size_t batch_smem_bytes(int chunks, int T, int ns) {
+    return static_cast<size_t>(ns) * kChunkBytes + batch_fixed_bytes(chunks, T);
 }
 
 // Four INT4 weights of one packed word as int8 MMA operands, both scaled by
@@ -73,8 +89,8 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, ui
 }
 
 // One CTA per SM.  A producer thread streams the CTA's units in rounds of
-// kBatchUnits, chunk j of every unit of the round before chunk j + 1, into a
-// ring.  Warp (s, rt, tt) takes unit s of each round, rows 16 rt .. 16 rt +
+// batch_units(T), chunk j of every unit of the round before chunk j + 1, into
+// a ring.  Warp (s, rt, tt) takes unit s of each round, rows 16 rt .. 16 rt +
 // 15 of it and tokens 8 tt .. 8 tt + 7: per chunk and G32 group two int8
 // MMAs (the activation's high and low parts, a = 128 ah + al) give the exact
 // int32 dot of every (row, token), and each (row, token) chains its group
@@ -83,8 +99,9 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_linear_batch(const __grid_
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int groups = a.chunks * 8;
     const int tstride = batch_tok_stride(groups);
+    const int ns = a.ns;
     uint8_t* ring = smem_raw;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + static_cast<size_t>(kBatchSlots) * kChunkBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + static_cast<size_t>(ns) * kChunkBytes);
     uint64_t* empty = full + kBatchSlots;
     int* issued = reinterpret_cast<int*>(empty + kBatchSlots);
     uint8_t* act = reinterpret_cast<uint8_t*>(issued) + align16(kBatchSlots * 4);
@@ -94,16 +111,18 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_linear_batch(const __grid_
     const int u1 = static_cast<int>((static_cast<long long>(c + 1) * a.units) / a.cpb);
     const int nunits = u1 - u0;
     const int T = a.T < kPrefillMax ? a.T : kPrefillMax;
-    const int ntt = (T + 7) >> 3;  // token tiles in use
+    const int ntt = batch_tiles(T);   // token tiles in use
+    const int upr = batch_units(T);   // units per round
+    const int wpu = kBatchWarps / upr;  // warps per unit: 2 row tiles x (wpu / 2) token tiles
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kBatchSlots; ++i) {
+        for (int i = 0; i < ns; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 2 * ntt);
         }
         mbar_fence_init();
     }
-    if (threadIdx.x < kBatchSlots) issued[threadIdx.x] = -1;
+    if (threadIdx.x < ns) issued[threadIdx.x] = -1;
     __syncthreads();
     pdl_trigger();
 
@@ -113,17 +132,17 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_linear_batch(const __grid_
                                  static_cast<size_t>(u0) * a.chunks * kChunkBytes;
             int idx = 0, slot = 0;
             uint32_t phase = 0;
-            for (int rb = 0; rb < nunits; rb += kBatchUnits) {
-                const int nu = min(kBatchUnits, nunits - rb);
+            for (int rb = 0; rb < nunits; rb += upr) {
+                const int nu = min(upr, nunits - rb);
                 for (int j = 0; j < a.chunks; ++j)
                     for (int su = 0; su < nu; ++su, ++idx) {
-                        if (idx >= kBatchSlots) mbar_wait(&empty[slot], phase ^ 1u, a.err, kErrWaitEmpty);
+                        if (idx >= ns) mbar_wait(&empty[slot], phase ^ 1u, a.err, kErrWaitEmpty);
                         publish_issued(&issued[slot], idx);
                         mbar_arrive_expect_tx(&full[slot], kChunkBytes);
                         bulk_g2s(ring + static_cast<size_t>(slot) * kChunkBytes,
                                  src + (static_cast<size_t>(rb + su) * a.chunks + j) * kChunkBytes, kChunkBytes,
                                  &full[slot]);
-                        if (++slot == kBatchSlots) {
+                        if (++slot == ns) {
                             slot = 0;
                             phase ^= 1u;
                         }
@@ -166,7 +185,7 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_linear_batch(const __grid_
         }
     }
     asm volatile("bar.sync 1, %0;" ::"r"(32 * kBatchWarps) : "memory");
-    const int su = cw >> 2, rt = (cw >> 1) & 1, tt = cw & 1;
+    const int su = cw / wpu, rt = cw & 1, tt = (cw % wpu) >> 1;
     if (tt >= ntt) return;
 
     const int gid = lane >> 2, tig = lane & 3;
@@ -184,14 +203,14 @@ __global__ void __launch_bounds__(kBatchThreads, 1) k_linear_batch(const __grid_
     const int p0 = kChunkScaleBytes + ((gid * 4 + 2 * rt) * 8) * 16 + 4 * tig;
     const int p1 = p0 + 8 * 16;
 
-    for (int rb = 0; rb + su < nunits; rb += kBatchUnits) {
-        const int nu = min(kBatchUnits, nunits - rb);
+    for (int rb = 0; rb + su < nunits; rb += upr) {
+        const int nu = min(upr, nunits - rb);
         float c00 = 0.0f, c01 = 0.0f, c10 = 0.0f, c11 = 0.0f;  // [row r0/r1][token n0/n0+1]
         for (int j = 0; j < a.chunks; ++j) {
             const int idx = rb * a.chunks + j * nu + su;
-            const int slot = idx % kBatchSlots;
+            const int slot = idx % ns;
             wait_issued(&issued[slot], idx, a.err);
-            mbar_wait(&full[slot], static_cast<uint32_t>((idx / kBatchSlots) & 1), a.err, kErrWaitFull);
+            mbar_wait(&full[slot], static_cast<uint32_t>((idx / ns) & 1), a.err, kErrWaitFull);
             const uint8_t* ch = ring + static_cast<size_t>(slot) * kChunkBytes;
             uint32_t w0[8], w1[8];
 #pragma unroll

@@ -371,7 +371,7 @@ def main():
         ev1.record(stream)
         barrier()
         pf_ms = max_over_ranks(ev0.elapsed_time(ev1)) / reps
-        batches = -(-n_pf // 16)
+        batches = -(-n_pf // 32)  # prompt tokens per batch
         line["prefill"] = {"value": streams * n_pf / (pf_ms * 1e-3), "unit": "prompt tokens/s", "tokens": n_pf,
                            "ms": pf_ms, "api": "i4d_prefill_tokens (token ids in, greedy next id out)",
                            "h2d_bytes": 8 * n_pf, "d2h_bytes": 8 + 4 * batches,

@@ -143,7 +143,7 @@ i4d_status i4d_decode_greedy(i4d_ctx* ctx, uint32_t position, int32_t token_id, 
 /* Prompt prefill in batches (SURVEY-(f) row 3).  The reference feeds a
  * prompt through run_one_token one position at a time
  * (decode_host.cpp:1570-1580), streaming every weight once per token; here
- * up to 16 prompt tokens share each pass over the weights.  The result is
+ * up to 32 prompt tokens share each pass over the weights.  The result is
  * bit-identical to n calls of i4d_decode_token at positions position0 ..
  * position0 + n - 1: the same KV records of every token, and logits_out (may
  * be NULL) receives the last token's 32256 padded logits.  residuals_in:

@@ -40,12 +40,12 @@ def _u32(x):
     return x.view(np.uint32)
 
 
-@pytest.mark.parametrize("p0,n", [(0, 37), (5, 16), (3, 1)])
+@pytest.mark.parametrize("p0,n", [(0, 37), (5, 16), (3, 1), (0, 70), (2, 24)])
 def test_prefill_matches_decode_steps(pkg, rope_lut, model, p0, n):
     banks, _ = model
     rng = np.random.default_rng(SEED + p0 + n)
     x = rng.normal(0.0, 0.02, (p0 + n + 1, 4096)).astype(np.float32)
-    pf, dec = _pair(pkg, banks, rope_lut, 64)
+    pf, dec = _pair(pkg, banks, rope_lut, 128)
     with pf, dec:
         for pos in range(p0):  # an earlier part of the sequence, decoded on both
             assert np.array_equal(_u32(pf.decode_token(pos, x[pos])), _u32(dec.decode_token(pos, x[pos])))
