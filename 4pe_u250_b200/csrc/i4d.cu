@@ -528,7 +528,7 @@ i4d_status enqueue_prefill(i4d_ctx* c, int T, bool last, bool nll) {
         CK(run_batch(c, l, ST_O, T, 1024));
         CK(run_pf_norm(c, T, ST_O, c->d_gamma + static_cast<size_t>(2 * l + 1) * kDim));
         CK(run_batch(c, l, ST_GU, T, 1024));
-        CK(launch(c, true, k_pf_swiglu, dim3(kStageUnits[ST_GU] / 2, T), dim3(32), 0, (const float*)c->d_pf_part,
+        CK(launch(c, true, k_pf_swiglu, dim3(kStageUnits[ST_GU] / 16, T), dim3(256), 0, (const float*)c->d_pf_part,
                   static_cast<int>(kStageUnits[ST_GU]), c->expf, c->d_pf_q, c->d_pf_e));
         CK(run_batch(c, l, ST_DOWN, T, 2816));
     }

@@ -55,7 +55,7 @@ struct AttnArgs {
 
 constexpr int kAttnThreads = 256;
 constexpr int kTile = 64;       // tokens per shared-memory tile
-constexpr int kMaxSeg = 16;     // rescale events handled by the segmented path
+constexpr int kMaxSeg = 12;     // rescale events handled by the segmented path (74 KB: 3 CTAs per SM)
 
 // Fixed-point exp of a non-positive Q15.17 value (emulator:575-595,
 // swiftkv_attention.cpp:199-260).

@@ -289,21 +289,31 @@ __global__ void __launch_bounds__(1024) k_pf_norm(const __grid_constant__ PfNorm
             r[col] = x[k];
         }
     }
-    __shared__ float inv_s;
+    // RMS as rms_recip_warp, one bank per warp: lane s < 8 of warp b sums
+    // slot s of bank b (8 lanes, 8 distinct shared-memory banks).
     __shared__ float xs[kDim];
+    __shared__ float bank_total[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) xs[i + k * 1024] = x[k];
     __syncthreads();
-    if (i < 32) {
-        const float inv = rms_recip_warp(xs);
-        if (i == 0) {
-            inv_s = inv;
-            a.recip[t] = inv;
+    const int w = i >> 5, lane = i & 31;
+    if (w < 4 && lane < 8) {
+        const float* base = xs + w * 1024 + lane;
+        float acc = 0.0f;
+#pragma unroll 32
+        for (int k = 0; k < 128; ++k) {
+            const float v = base[k * 8];
+            acc = __fadd_rn(acc, __fmul_rn(v, v));
         }
+        float total = 0.0f;
+        for (int sl = 0; sl < 8; ++sl) total = __fadd_rn(total, __shfl_sync(0xffu, acc, sl));
+        if (lane == 0) bank_total[w] = total;
     }
     __syncthreads();
+    const float sum = __fadd_rn(__fadd_rn(bank_total[0], bank_total[1]), __fadd_rn(bank_total[2], bank_total[3]));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(sum, 1.0f / 4096.0f), 1.0e-5f)));
+    if (i == 0) a.recip[t] = inv;
     if (!a.gamma) return;
-    const float inv = inv_s;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int col = i + k * 1024;
@@ -315,12 +325,13 @@ __global__ void __launch_bounds__(1024) k_pf_norm(const __grid_constant__ PfNorm
 }
 
 // SwiGLU of the GATE/UP partials then the G32 quantiser, per token (as
-// linear_finalize's EPI_SWIGLU; emulator:716-722, 769-770).  Grid (stripes, T).
-__global__ void __launch_bounds__(32) k_pf_swiglu(const float* partials, int units, ExpfFix fx, int16_t* q,
-                                                   uint8_t* e) {
+// linear_finalize's EPI_SWIGLU; emulator:716-722, 769-770).  Grid (stripes /
+// 8, T), one warp per stripe.
+__global__ void __launch_bounds__(256) k_pf_swiglu(const float* partials, int units, ExpfFix fx, int16_t* q,
+                                                    uint8_t* e) {
     pdl_trigger();
     pdl_wait();
-    const int stripe = blockIdx.x, t = blockIdx.y, lane = threadIdx.x;
+    const int stripe = blockIdx.x * 8 + (threadIdx.x >> 5), t = blockIdx.y, lane = threadIdx.x & 31;
     const int rows = units * 32, stripes = units / 2;
     const float* P = partials + static_cast<size_t>(t) * 4 * rows;
     const float g = combine4(P, rows, stripe * 32 + lane);
