@@ -130,9 +130,8 @@ i4d_status i4d_load_embeddings(i4d_ctx* ctx, const float* emb, size_t n_floats);
 i4d_status i4d_decode_token(i4d_ctx* ctx, uint32_t position, const float* residual_in,
                             float* logits_out, float* residual_out);
 
-/* Greedy step on the device (SURVEY-(f): the embedding lookup and the
- * sampler of decode_host.cpp:666-676 and 703-717 moved onto the GPU): the
- * input is row token_id of the embeddings loaded by i4d_load_embeddings, and
+/* Greedy step on the device (the embedding lookup and the argmax of
+ * decode_host.cpp:666-676 and 703-717 moved onto the GPU): the input is row token_id of the embeddings loaded by i4d_load_embeddings, and
  * next_id receives the first index of the maximum of logits[0, 32000), NaN
  * skipped (-1 if every logit is NaN), as argmax_logits.  logits_out (may be
  * NULL) receives the 32256 padded logits.  Per step only the position and id
@@ -140,15 +139,17 @@ i4d_status i4d_decode_token(i4d_ctx* ctx, uint32_t position, const float* residu
 i4d_status i4d_decode_greedy(i4d_ctx* ctx, uint32_t position, int32_t token_id, int32_t* next_id,
                              float* logits_out);
 
-/* Prompt prefill in batches (SURVEY-(f) row 3).  The reference feeds a
- * prompt through run_one_token one position at a time
- * (decode_host.cpp:1570-1580), streaming every weight once per token; here
+/* Prompt prefill in batches.  The reference feeds a prompt through
+ * run_one_token one position at a time (decode_host.cpp:1570-1580),
+ * streaming every weight once per token; here
  * up to 32 prompt tokens share each pass over the weights.  The result is
  * bit-identical to n calls of i4d_decode_token at positions position0 ..
  * position0 + n - 1: the same KV records of every token, and logits_out (may
  * be NULL) receives the last token's 32256 padded logits.  residuals_in:
  * n x 4096 FP32 embedding rows (host).  Needs a context holding all four
- * banks (not a shard); position0 + n must not exceed the KV capacity. */
+ * banks (not a shard); position0 + n must not exceed the KV capacity.  After
+ * an error status the records of the prompt's positions are unspecified;
+ * records before position0 are untouched. */
 i4d_status i4d_prefill(i4d_ctx* ctx, uint32_t position0, const float* residuals_in, uint32_t n,
                        float* logits_out);
 
@@ -158,8 +159,8 @@ i4d_status i4d_prefill(i4d_ctx* ctx, uint32_t position0, const float* residuals_
 i4d_status i4d_prefill_tokens(i4d_ctx* ctx, uint32_t position0, const int32_t* token_ids, uint32_t n,
                               int32_t* next_id, float* logits_out);
 
-/* Perplexity terms of one evaluation chunk (SURVEY-(f) row 4; the chunk
- * loop body of calculate_perplexity, emulator:1857-1927): token_ids[0..n),
+/* Perplexity terms of one evaluation chunk (the chunk loop body of
+ * calculate_perplexity, emulator:1857-1927): token_ids[0..n),
  * 2 <= n, n - 1 <= KV capacity; positions 0 .. n-2 run as prompt batches
  * from position 0 (the chunk's cache restart), and nll_out[p] (n - 1
  * doubles) receives -(logits[ids[p+1]] - (double)(max_l + logf(sum_exp)))

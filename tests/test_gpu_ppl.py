@@ -1,4 +1,4 @@
-"""Perplexity on the device (SURVEY-(f) row 4): per-position negative
+"""Perplexity on the device: per-position negative
 log-likelihoods from prompt batches (i4d_eval_nll) bit-equal, as doubles, to
 the oracle's term (i4o_nll, pinned to the reference's calculate_perplexity in
 test_ppl_oracle.py) over the decode path's logits, and the chunked loop of
