@@ -36,6 +36,7 @@ EXPORTS = [
     "i4d_token_timeline", "i4d_create_shard", "i4d_shard_export", "i4d_shard_attach",
     "i4d_decode_greedy", "i4d_argmax", "i4d_sampler_init", "i4d_sample", "i4d_decode_sample",
     "i4d_pack_autoround_matrix", "i4d_pack_fp32_head", "i4d_prefill", "i4d_prefill_tokens", "i4d_eval_nll",
+    "i4d_device_arch", "i4d_profile_gemv", "i4d_profile_attention",
 ]
 
 SAMPLER_HOST = 0      # decode_host.cpp:724-868
@@ -113,6 +114,9 @@ def load_library():
         "i4d_attention": [P, ctypes.c_int, ctypes.c_uint32, P, P, P, P, P],
         "i4d_swiglu_quant": [P, P, P, P, P],
         "i4d_expf": [P, P, P, ctypes.c_size_t],
+        "i4d_device_arch": [ctypes.c_int, P, P],
+        "i4d_profile_gemv": [P, ctypes.c_int, ctypes.c_int, P],
+        "i4d_profile_attention": [P, ctypes.c_int, ctypes.c_uint32, P, ctypes.c_int, ctypes.c_int, P],
         "i4d_decode_token_async": [P, ctypes.c_uint32, P, P],
         "i4d_stream": [P],
         "i4d_profile_token": [P, ctypes.c_uint32, P, P, P],
@@ -157,6 +161,17 @@ def shard_banks(rank, world):
     n = 4 // world
     return list(range(rank * n, rank * n + n))
 
+
+
+def device_arch(device=0):
+    """(binary architecture of the loaded token kernel, device compute
+    capability), both as 10 * major + minor, queried through the C ABI."""
+    L = load_library()
+    b, cc = ctypes.c_int(0), ctypes.c_int(0)
+    st = L.i4d_device_arch(device, ctypes.byref(b), ctypes.byref(cc))
+    if st != OK:
+        raise I4DError(st, "i4d_device_arch failed")
+    return b.value, cc.value
 
 class Context:
     """One decode context on one GPU (i4d_ctx).  With world > 1 it is rank
@@ -345,6 +360,19 @@ class Context:
         n = np.zeros(8, np.uint32)
         self._check(self._L.i4d_profile_token(self._h, position, residual_in_dev_ptr, ms.ctypes.data, n.ctypes.data))
         return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(KERNEL_CLASSES)}
+
+    def profile_gemv(self, mode, reps):
+        """Milliseconds per GEMV of `mode`, `reps` launches over the layers' matrices in turn."""
+        ms = ctypes.c_float(0.0)
+        self._check(self._L.i4d_profile_gemv(self._h, mode, reps, ctypes.byref(ms)))
+        return ms.value
+
+    def profile_attention(self, layer, position, qkv_dev_ptr, fill, reps):
+        """Milliseconds per attention step of `layer` at `position` (see i4d_profile_attention)."""
+        ms = ctypes.c_float(0.0)
+        self._check(self._L.i4d_profile_attention(self._h, layer, position, qkv_dev_ptr, fill, reps,
+                                                  ctypes.byref(ms)))
+        return ms.value
 
     def token_breakdown(self, position, residual_in_dev_ptr):
         """CTA-averaged microseconds per category of the persistent kernel."""

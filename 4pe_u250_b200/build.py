@@ -101,10 +101,12 @@ def build_host():
 
 
 def build_oracle():
+    """The C restatement always; the reference emulator (oracle/_ref) only
+    where I4D_REF_ROOT names a reference tree."""
     _run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "oracle"])
-    if os.path.isdir(os.environ.get("I4D_REF_ROOT", "/root/reference")):
-        _run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref",
-              "REF_ROOT=" + os.environ.get("I4D_REF_ROOT", "/root/reference")])
+    ref_root = os.environ.get("I4D_REF_ROOT")
+    if ref_root and os.path.isdir(ref_root):
+        _run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref", "REF_ROOT=" + ref_root])
 
 
 def main():

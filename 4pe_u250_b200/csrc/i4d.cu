@@ -1691,6 +1691,20 @@ i4d_status i4d_argmax(i4d_ctx* c, const float* logits, size_t n, int32_t* index)
     return I4D_OK;
 }
 
+i4d_status i4d_device_arch(int device, int* binary_version, int* device_cc) {
+    if (!binary_version || !device_cc) return I4D_ERR_ARG;
+    if (cudaSetDevice(device) != cudaSuccess) return I4D_ERR_CUDA;
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, k_token<false>) != cudaSuccess) return I4D_ERR_CUDA;
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess)
+        return I4D_ERR_CUDA;
+    *binary_version = fa.binaryVersion;
+    *device_cc = major * 10 + minor;
+    return I4D_OK;
+}
+
 i4d_status i4d_expf(i4d_ctx* c, const float* x, float* y, size_t n) {
     if (!c || !x || !y) return c ? fail(c, I4D_ERR_ARG, "null buffer") : I4D_ERR_ARG;
     if (n == 0) return I4D_OK;
@@ -1772,5 +1786,85 @@ extern "C" i4d_status i4d_token_timeline(i4d_ctx* c, uint32_t position, const fl
     c->tl_detail = false;
     if (st != I4D_OK) return st;
     if (e != cudaSuccess) return fail(c, I4D_ERR_CUDA, "%s", cudaGetErrorString(e));
+    return I4D_OK;
+}
+
+// ------------------------------------------------------ op-level measurement
+
+extern "C" i4d_status i4d_profile_gemv(i4d_ctx* c, int mode, int reps, float* ms_per_gemv) {
+    if (c && c->world > 1) return fail(c, I4D_ERR_STATE, "not available on a bank shard");
+    if (!c || !ms_per_gemv || reps <= 0 || mode < 0 || mode > 7) return c ? fail(c, I4D_ERR_ARG, "bad arguments") : I4D_ERR_ARG;
+    if (!c->bank_loaded[0] || !c->bank_loaded[1] || !c->bank_loaded[2] || !c->bank_loaded[3])
+        return fail(c, I4D_ERR_STATE, "all four banks must be loaded");
+    CK(cudaSetDevice(c->device));
+    for (cudaEvent_t& ev : c->prof_ev)
+        if (!ev) CK(cudaEventCreate(&ev));
+    const int rows = mode_rows(mode), cols = mode == 6 ? kFfn : kDim;
+    const int st = mode_stage(mode);
+    DEVBUF(aq, cols * sizeof(int16_t));
+    DEVBUF(ae, cols / 32);
+    DEVBUF(y, rows * sizeof(float));
+    // The arithmetic does not depend on the values: a fixed activation.
+    CK(cudaMemsetAsync(aq.p, 0x15, cols * sizeof(int16_t), c->stream));
+    CK(cudaMemsetAsync(ae.p, 127, cols / 32, c->stream));
+    auto one = [&](int r) {
+        const int layer = mode == 7 ? 0 : r % c->layers;  // a different matrix each launch
+        LinearArgs a = base_linear(c, layer, st);
+        a.w += static_cast<size_t>(mode_unit_offset(mode)) * a.chunks * kChunkBytes;
+        a.units = rows / 32;
+        a.in_kind = IN_ACT;
+        a.act_q = aq.as<int16_t>();
+        a.act_e = ae.as<uint8_t>();
+        a.act_bank_stride = cols / 4;
+        a.epi = EPI_STORE;
+        a.out = y.as<float>();
+        return run_linear(c, a, true);
+    };
+    for (int r = 0; r < 3; ++r) CK(one(r));  // warm-up
+    CK(cudaEventRecord(c->prof_ev[0], c->stream));
+    for (int r = 0; r < reps; ++r) CK(one(r));
+    CK(cudaEventRecord(c->prof_ev[1], c->stream));
+    const i4d_status s = finish(c);
+    if (s != I4D_OK) return s;
+    float ms = 0.0f;
+    CK(cudaEventElapsedTime(&ms, c->prof_ev[0], c->prof_ev[1]));
+    *ms_per_gemv = ms / reps;
+    return I4D_OK;
+}
+
+// Attention of one layer at `position` over the records already in the KV
+// cache.  fill > 0: first writes the records of positions [0, position) by
+// running the attention step at each of them with q/k/v row (p % fill) of
+// qkv_dev ([fill][3][4096] Q15.17); then times `reps` steps at `position`
+// (each rewrites that position's record) with row 0.
+extern "C" i4d_status i4d_profile_attention(i4d_ctx* c, int layer, uint32_t position, const int32_t* qkv_dev,
+                                            int fill, int reps, float* ms_per_step) {
+    if (c && c->world > 1) return fail(c, I4D_ERR_STATE, "not available on a bank shard");
+    if (!c || !qkv_dev || !ms_per_step || reps <= 0 || fill < 0) return c ? fail(c, I4D_ERR_ARG, "bad arguments") : I4D_ERR_ARG;
+    if (!c->rope_loaded) return fail(c, I4D_ERR_STATE, "rope LUT not loaded");
+    if (layer < 0 || layer >= c->layers || position >= static_cast<uint32_t>(c->stride))
+        return fail(c, I4D_ERR_ARG, "layer %d / position %u out of range", layer, position);
+    CK(cudaSetDevice(c->device));
+    for (cudaEvent_t& ev : c->prof_ev)
+        if (!ev) CK(cudaEventCreate(&ev));
+    AttnArgs a = base_attn(c, layer);
+    a.partials = nullptr;
+    auto step = [&](int p, int row) {
+        k_set_pos<<<1, 1, 0, c->stream>>>(c->d_pos, p);
+        a.direct = qkv_dev + static_cast<size_t>(row) * 3 * kDim;
+        k_attention<<<kHeads, kAttnThreads, attn_smem_bytes(), c->stream>>>(a);
+        return cudaGetLastError();
+    };
+    if (fill > 0)
+        for (uint32_t p = 0; p < position; ++p) CK(step(static_cast<int>(p), static_cast<int>(p % fill)));
+    CK(step(static_cast<int>(position), 0));  // warm-up
+    CK(cudaEventRecord(c->prof_ev[0], c->stream));
+    for (int r = 0; r < reps; ++r) CK(step(static_cast<int>(position), 0));
+    CK(cudaEventRecord(c->prof_ev[1], c->stream));
+    const i4d_status s = finish(c);
+    if (s != I4D_OK) return s;
+    float ms = 0.0f;
+    CK(cudaEventElapsedTime(&ms, c->prof_ev[0], c->prof_ev[1]));
+    *ms_per_step = ms / reps;
     return I4D_OK;
 }

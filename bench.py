@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark: batch-1 INT4 Llama-2-7B decode.
+"""Benchmark: batch-1 INT4 Llama-2-7B decode (the full-model greedy workload).
 
 One step = one decode token through all 32 layers and the LM head
 (int4_decoder_controller.cpp:138-234) on seeded synthetic weights in the
@@ -37,6 +37,7 @@ METRIC = "batch-1 INT4 Llama-2-7B decode tokens/s"
 UNIT = "tokens/s"
 PROMPT = 16
 PREFILL_TOKENS = 128  # prompt length of the prefill measurement
+SHARD_WORLDS = (2, 4)  # group sizes of the bank-sharded decode
 
 
 def parse():
@@ -47,12 +48,11 @@ def parse():
     ap.add_argument("--impl", default="i4d", choices=["i4d", "reference"])
     ap.add_argument("--seed", type=int, default=2)
     ap.add_argument("--kv-capacity", type=int, default=2048)
-    ap.add_argument("--cpu-layers", type=int, default=4, help="layers in the CPU baseline sample")
-    ap.add_argument("--cpu-steps", type=int, default=6)
+    ap.add_argument("--cpu-steps", type=int, default=24, help="timed steps of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--soak", type=int, default=400, help="untimed steps before timing (clock steady state)")
-    ap.add_argument("--shard", action="store_true",
-                    help="N GPUs (2 or 4) decode one stream as one bank-sharded group instead of N replicas")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N GPUs decode N independent streams (default for N > 1: one bank-sharded stream)")
     return ap.parse_args()
 
 
@@ -135,41 +135,34 @@ def write_model_dir(d, banks, emb, lut):
         f.write(lut)
 
 
-def cpu_sample(banks, emb, lut, tokens, layers, steps):
-    """Times the reference emulator (or, without it, the oracle port) on a
-    bounded sample: `layers` decoder layers + LM head per token, `steps`
-    tokens; the per-token time is scaled to 32 layers by MAC count."""
-    from oracle import RefEmulator, Oracle, ref_available
-    macs_layer = 4 * 4096 * 4096 + 3 * 11264 * 4096
-    macs_head = 32256 * 4096
-    scale = (32 * macs_layer + macs_head) / (layers * macs_layer + macs_head)
-    if ref_available():
-        tmp = "/dev/shm" if os.path.isdir("/dev/shm") else None
-        with tempfile.TemporaryDirectory(prefix="i4d_ref_", dir=tmp) as d:
-            write_model_dir(d, banks, emb, lut)
-            ref = RefEmulator()
-            ref.load(d, layers, 2048)
-            ref.forward(tokens[0], 0)
-            t0 = time.perf_counter()
-            for i in range(steps):
-                ref.forward(tokens[i + 1], i + 1)
-            dt = (time.perf_counter() - t0) / steps
-            cores = ref.threads()
-        kind = "reference"
-    else:
-        orc = Oracle()
-        tables = orc.rope_tables(lut)
-        kv = orc.kv_store(layers, 2048)
+def cpu_decode(banks, emb, lut, prompt, warmup, steps):
+    """The reference's own CPU implementation of the step: the emulator
+    compiled from its source (oracle/_ref), all 32 layers and the LM head,
+    OpenMP over the host cores.  It runs forward() at positions 0..warmup-1
+    untimed, then `steps` timed forwards at positions warmup..warmup+steps-1
+    (the GPU arm's positions), feeding the prompt and then its own greedy ids
+    (emulator:1608-1682 without the EOS stop).  Returns the measured rate."""
+    from oracle import RefEmulator, ref_available
+    if not ref_available():
+        return None
+    tmp = "/dev/shm" if os.path.isdir("/dev/shm") else None
+    with tempfile.TemporaryDirectory(prefix="i4d_ref_", dir=tmp) as d:
+        write_model_dir(d, banks, emb, lut)
+        ref = RefEmulator()
+        ref.load(d, 32, 2048)
+    tok = prompt[0]
+    dt = 0.0
+    for pos in range(warmup + steps):
         t0 = time.perf_counter()
-        for i in range(steps):
-            orc.forward(banks, tables, kv, layers, 2048, i, emb[tokens[i] * 4096:(tokens[i] + 1) * 4096])
-        dt = (time.perf_counter() - t0) / steps
-        cores = os.cpu_count()
-        kind = "port"
-    per_token = dt * scale
-    return {"value": 1.0 / per_token, "unit": UNIT, "cores": cores, "kind": kind,
-            "sample": f"{steps} decode steps of {layers} layers + LM head on the same synthetic model, "
-                      f"per-token time scaled x{scale:.2f} to 32 layers by MAC count"}
+        logits, _ = ref.forward(tok, pos)
+        if pos >= warmup:
+            dt += time.perf_counter() - t0
+        tok = prompt[pos + 1] if pos + 1 < len(prompt) else ref.argmax(logits)
+    return {"value": steps / dt, "unit": UNIT, "cores": ref.threads(), "kind": "reference",
+            "ms_per_step": dt / steps * 1e3, "steps_run": steps, "positions": [warmup, warmup + steps - 1],
+            "sample": f"{steps} timed decode steps of the full 32-layer model + LM head at positions "
+                      f"{warmup}..{warmup + steps - 1} after {warmup} untimed ones, the same synthetic model "
+                      f"and greedy sequence as the GPU arm"}
 
 
 def run_reference(args, world, rank):
@@ -177,15 +170,16 @@ def run_reference(args, world, rank):
         return
     syn = importlib.import_module("4pe_u250_b200.synth")
     F = importlib.import_module("4pe_u250_b200.formats")
-    banks = syn.model_banks(args.cpu_layers, args.seed)
-    syn.fill_matrix(banks, 0, F.MODE_LOGITS, args.seed)
+    banks = syn.model_banks(32, args.seed)
     emb = syn.embeddings(args.seed)
     lut = F.generate_rope_lut()
     prompt = np.random.default_rng(args.seed).integers(3, 32000, size=PROMPT).tolist()
-    tokens = (prompt * ((args.steps + args.warmup) // PROMPT + 2))[: args.steps + args.warmup + 1]
-    r = cpu_sample(banks, emb, lut, tokens, args.cpu_layers, min(args.steps, args.cpu_steps))
+    r = cpu_decode(banks, emb, lut, prompt, args.warmup, args.steps)
+    if r is None:
+        print(json.dumps({"impl": "reference", "unavailable": "the reference emulator (oracle/_ref) was not built"}))
+        return
     line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / r["value"],
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4xint14/fp32",
             "data": "synthetic", "config": workload_config(args, world),
             "cpu_baseline": r, "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -193,8 +187,51 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def gemv_line(ctx, F, peak, peak_kind, streams, max_over_ranks):
+    """The single INT4 GEMV of the Q-projection shape (4096 x 4096 in four
+    input-column bank shards, 8,650,752 B of nibbles and Q1.15 scales): the
+    op of sharded_gemv_4pe (emulator:216-264) through the library's GEMV
+    kernel, one launch per GEMV, each on the next layer's Q matrix (32
+    matrices, 277 MB > the 126 MB L2, so every launch streams from HBM)."""
+    reps = 320
+    ctx.profile_gemv(F.MODE_Q, 32)  # warm-up
+    ms = max_over_ranks(ctx.profile_gemv(F.MODE_Q, reps))
+    nbytes = 4096 * 4096 // 2 + 4096 * 32 * 2
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"workload": "config1: one Q-shape INT4 GEMV y = Wx, W 4096 x 4096 in the packer's 4-bank tile layout",
+            "value": streams * gbs, "unit": "GB/s", "us_per_gemv": ms * 1e3, "bytes_per_gemv": nbytes,
+            "launches": reps, "frac_of_peak": gbs / peak, "peak": peak, "peak_kind": peak_kind,
+            "l2": "32 distinct matrices in rotation (277 MB > 126 MB L2)"}
+
+
+def attention_line(pkg, F, syn, lut, device, peak, peak_kind):
+    """The attention-only sweep: RoPE + INT8-KV fixed-point online softmax for
+    32 heads x 128 (swiftkv_attention_4pe, emulator:602-714) at context
+    lengths 512..4096 (position L-1).  The cache is filled by the attention
+    step itself over 16 seeded N(0,1) q/k/v rows taken to Q15.17; each timed
+    step reads 32 * L records (261 algorithmic bytes each)."""
+    import torch
+    from oracle import Oracle
+    orc = Oracle()
+    rng = np.random.default_rng(3)
+    rows = np.stack([orc.float_to_q17(rng.standard_normal(3 * 4096).astype(np.float32)) for _ in range(16)])
+    qkv = torch.from_numpy(rows.astype(np.int32)).to(f"cuda:{device}")
+    out = {"workload": "config4: attention of one layer, 32 heads x 128, INT8 KV, L = 512/1024/2048/4096",
+           "unit": "GB/s", "peak": peak, "peak_kind": peak_kind, "L": {}}
+    with pkg.Context(device=device, num_layers=1, kv_capacity=4096) as actx:
+        actx.load_rope(lut)
+        actx.profile_attention(0, 4095, qkv.data_ptr(), 16, 1)  # writes the records of positions 0..4094
+        for L in (512, 1024, 2048, 4096):
+            ms = actx.profile_attention(0, L - 1, qkv.data_ptr(), 0, 50)
+            nbytes = 32 * L * 261
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            out["L"][str(L)] = {"us": ms * 1e3, "bytes": nbytes, "gbs": gbs, "frac_of_peak": gbs / peak}
+    out["value"] = out["L"]["4096"]["gbs"]
+    return out
+
+
 def workload_config(args, world):
-    par = (f"bank-shard{world}" if args.shard else f"replicas{world}") if world > 1 else "1gpu"
+    par = (f"replicas{world}" if args.replicas else f"bank-shard{world}") if world > 1 else "1gpu"
     return {"workload": "config3: full 32-layer INT4 Llama-2-7B decode, 16-token prompt then greedy, "
                         "KV capacity 2048, seed 2",
             "layers": 32, "kv_capacity": args.kv_capacity, "positions": [args.warmup, args.warmup + args.steps - 1],
@@ -224,9 +261,9 @@ def main():
     total = args.warmup + args.steps
     assert total <= args.kv_capacity
 
-    shard = args.shard and world > 1
-    if shard and world not in (2, 4):
-        raise SystemExit("--shard needs 2 or 4 GPUs")
+    shard = world > 1 and not args.replicas
+    if shard and world not in SHARD_WORLDS:
+        raise SystemExit(f"bank sharding runs on {SHARD_WORLDS} GPUs; use --replicas for {world}")
     banks = syn.model_banks(32, args.seed)
     emb = syn.embeddings(args.seed)
     lut = F.generate_rope_lut()
@@ -388,8 +425,13 @@ def main():
         line["perplexity_eval"] = {"value": streams * (n_pf - 1) / (ev_ms * 1e-3), "unit": "positions/s",
                                    "positions": n_pf - 1, "ms": ev_ms,
                                    "api": "i4d_eval_nll (token ids in, one NLL per position out)"}
+    if not shard:
+        line["gemv"] = gemv_line(ctx, F, peak, peak_kind, streams, max_over_ranks)
+        line["attention"] = attention_line(pkg, F, syn, lut, local, peak, peak_kind)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_sample(banks, emb, lut, tokens, args.cpu_layers, args.cpu_steps)
+        r = cpu_decode(banks, emb, lut, prompt, args.warmup, min(args.steps, args.cpu_steps))
+        if r is not None:
+            line["cpu_baseline"] = r
     ctx.close()
     if world > 1:
         dist.destroy_process_group()

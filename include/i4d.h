@@ -316,9 +316,13 @@ i4d_status i4d_linear_bank(i4d_ctx* ctx, const void* superblocks, size_t n_bytes
  * decoder-layer matrix); a larger stream, such as the LM head's, is rejected
  * with I4D_ERR_SIZE.  The array's device error word is cleared at the start
  * of each call; nothing else needs to start at zero.  The first call on a
- * device looks up the array's address (cudaGetSymbolAddress), so make one
- * call before any stream capture.  The call runs on the context's stream and
- * returns once it has finished.  The array is shared by every context of a
+ * device looks up the array's address (cudaGetSymbolAddress), so make that
+ * first call before any stream capture.  The call is synchronous: it reads
+ * the caller's device buffers on the context's stream without waiting for
+ * any other stream, so superblocks_dev, act_q_dev and act_e8m0_dev must be
+ * fully written before the call (e.g. synchronise the stream that wrote
+ * them), and it returns once its own work has finished.  The array is
+ * shared by every context of a
  * device: calls that overlap on one device, from any thread or context,
  * race on it and must be serialised by the caller. */
 i4d_status i4d_linear_bank_noalloc(i4d_ctx* ctx, const void* superblocks_dev, size_t n_bytes,
@@ -359,6 +363,31 @@ i4d_status i4d_argmax(i4d_ctx* ctx, const float* logits, size_t n, int32_t* inde
 /* The device expf used by SwiGLU, element-wise (test hook: its results must
  * equal the host C library's expf, which the reference emulator calls). */
 i4d_status i4d_expf(i4d_ctx* ctx, const float* x, float* y, size_t n);
+
+/* Build target of the loaded device code and the GPU it runs on, queried at
+ * run time: *binary_version = the token kernel's binary architecture (100
+ * for an sm_100a build), *device_cc = the device's compute capability as
+ * 10 * major + minor.  No counterpart in the reference (an FPGA build checks
+ * its xclbin at load, decode_host.cpp:1189). */
+i4d_status i4d_device_arch(int device, int* binary_version, int* device_cc);
+
+/* Measurement hooks of the op-level kernels, on the context's stream, timed
+ * with CUDA events (no counterpart in the reference; the FPGA design reports
+ * only per-token latency, docs/thesis/main.tex:410-414).
+ * i4d_profile_gemv: `reps` back-to-back GEMVs of `mode`, layer r mod
+ * num_layers for the r-th (a different matrix each time, so a model of more
+ * than 126 MB of such matrices streams each from HBM), fixed activations;
+ * *ms_per_gemv = elapsed / reps.  The GEMV of sharded_gemv_4pe,
+ * emulator:216-264.
+ * i4d_profile_attention: the attention step of one layer at `position` over
+ * the records in the KV cache (swiftkv_attention_4pe, emulator:602-714).
+ * With fill > 0 it first runs the step at every position below `position`
+ * with q/k/v row p % fill of qkv_dev ([fill][3][4096] Q15.17, device), so
+ * the cache holds records of those rows; then times `reps` steps at
+ * `position` with row 0. */
+i4d_status i4d_profile_gemv(i4d_ctx* ctx, int mode, int reps, float* ms_per_gemv);
+i4d_status i4d_profile_attention(i4d_ctx* ctx, int layer, uint32_t position, const int32_t* qkv_dev, int fill,
+                                 int reps, float* ms_per_step);
 
 #ifdef __cplusplus
 }

@@ -223,6 +223,28 @@ def pack_autoround_banks(mode, raw=None, scales=None, head=None):
     return [synth.pack_arrays(w, s, p, rows // 128, cols // 1024) for p in range(4)]
 
 
+def split_to_record(ks, vs, k8, v8):
+    """Emulator split arrays (4 K shifts, 4 V shifts, K int8[128], V int8[128])
+    -> the 320-byte record of swiftkv_attention.hpp:21-36."""
+    rec = np.zeros(320, np.uint8)
+    meta = 0
+    for g in range(4):
+        meta |= int(ks[g]) << (5 * g)
+        meta |= int(vs[g]) << (20 + 5 * g)
+    rec[0:8] = np.frombuffer(np.uint64(meta).tobytes(), np.uint8)
+    rec[64:192] = np.asarray(k8, np.int8).view(np.uint8)
+    rec[192:320] = np.asarray(v8, np.int8).view(np.uint8)
+    return rec
+
+
+def record_to_split(rec):
+    rec = np.asarray(rec, np.uint8)
+    meta = int(np.frombuffer(rec[0:8].tobytes(), np.uint64)[0])
+    ks = np.array([(meta >> (5 * g)) & 31 for g in range(4)], np.uint8)
+    vs = np.array([(meta >> (20 + 5 * g)) & 31 for g in range(4)], np.uint8)
+    return ks, vs, rec[64:192].view(np.int8).copy(), rec[192:320].view(np.int8).copy()
+
+
 def ref_available():
     return os.path.exists(REF_SO)
 
@@ -250,6 +272,7 @@ class RefEmulator:
             "ref_attention": [P, P, P, ctypes.c_int, ctypes.c_int, P, P],
             "ref_swiglu": [P, P, ctypes.c_int, P],
             "ref_kv_get": [ctypes.c_int] * 4 + [P, P, P, P],
+            "ref_kv_set": [ctypes.c_int] * 4 + [P, P, P, P],
             "ref_argmax": [P, ctypes.c_int],
             "ref_sample": [P, ctypes.c_int, P, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_float, P],
             "ref_perplexity": [ctypes.c_char_p, ctypes.c_int],
@@ -328,6 +351,20 @@ class RefEmulator:
         vs = np.empty(4, np.uint8)
         self.L.ref_kv_get(bank, layer, lh, token, k8.ctypes.data, ks.ctypes.data, v8.ctypes.data, vs.ctypes.data)
         return ks, vs, k8, v8
+
+    def kv_set(self, bank, layer, lh, token, ks, vs, k8, v8):
+        """Writes one cached entry in the emulator's split arrays."""
+        arrs = [np.ascontiguousarray(k8, np.int8), np.ascontiguousarray(ks, np.uint8),
+                np.ascontiguousarray(v8, np.int8), np.ascontiguousarray(vs, np.uint8)]
+        self.L.ref_kv_set(bank, layer, lh, token, *[a.ctypes.data for a in arrs])
+
+    def kv_record(self, bank, layer, lh, token):
+        """The cached entry as the 320-byte HLS record (metadata word: K shift
+        of group g at bit 5g, V shift at 20 + 5g; K int8 at 64, V at 192)."""
+        return split_to_record(*self.kv_get(bank, layer, lh, token))
+
+    def kv_set_record(self, bank, layer, lh, token, rec):
+        self.kv_set(bank, layer, lh, token, *record_to_split(rec))
 
     def argmax(self, logits):
         """The emulator's sample_argmax over 32000 logits (emulator:1428-1438)."""

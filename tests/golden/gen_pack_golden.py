@@ -1,7 +1,7 @@
 """Generates tests/golden/pack_golden.json: SHA-256 digests of the bank
 superblocks the REFERENCE packer (scripts/autoround_pack_llama2_u250.py)
 writes for seeded AutoRound inputs.  Run in a container that has the
-reference tree (it is imported from REF_SCRIPTS); the digests travel, the
+reference tree (I4D_REF_ROOT; the packer is imported from its scripts/); the digests travel, the
 reference does not.
 
 Inputs (reproduced by tests from the seeds, see pack_inputs below):
@@ -21,7 +21,6 @@ import sys
 
 import numpy as np
 
-REF_SCRIPTS = os.environ.get("REF_SCRIPTS", "/root/reference/scripts")
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 CASES = [  # (name, mode, seed)
@@ -52,7 +51,8 @@ def pack_inputs(mode, seed):
 
 
 def main():
-    sys.path.insert(0, REF_SCRIPTS)
+    # Needs the reference tree: I4D_REF_ROOT names it.
+    sys.path.insert(0, os.path.join(os.environ["I4D_REF_ROOT"], "scripts"))
     import autoround_pack_llama2_u250 as ref
 
     out = {"source": "scripts/autoround_pack_llama2_u250.py (pack_matrix_to_super_blocks, permute_qk_rows, "

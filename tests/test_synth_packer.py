@@ -8,7 +8,8 @@ import numpy as np
 import pytest
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "packer_golden.json")
-REF_PACKER = "/root/reference/scripts/autoround_pack_llama2_u250.py"
+REF_ROOT = os.environ.get("I4D_REF_ROOT")
+REF_PACKER = os.path.join(REF_ROOT, "scripts", "autoround_pack_llama2_u250.py") if REF_ROOT else ""
 
 
 def _small_case():
@@ -19,7 +20,7 @@ def _small_case():
     return w, s, M, K
 
 
-@pytest.mark.skipif(not os.path.exists(REF_PACKER), reason="reference tree not mounted")
+@pytest.mark.skipif(not os.path.exists(REF_PACKER), reason="I4D_REF_ROOT does not name a reference tree")
 def test_c_packer_matches_reference_python_packer(synth):
     spec = importlib.util.spec_from_file_location("ref_packer", REF_PACKER)
     mod = importlib.util.module_from_spec(spec)

@@ -73,6 +73,28 @@ def test_noalloc_matches_linear_bank_decoder_slices(nctx, lit, out_tiles):
     assert _bits(second).tolist() == _bits(ref).tolist()
 
 
+def test_noalloc_allocates_no_device_memory(nctx):
+    # The entry point's defining property: after a first call (which looks up
+    # the static array's address), further calls leave the device's free
+    # memory exactly where it was.  Every buffer is made before the baseline.
+    import torch
+    lit, out_tiles = 11, 32
+    sb, q, e = _random_case(77, lit, out_tiles)
+    dev = torch.device("cuda", 0)
+    sb_d, q_d, e_d = (torch.from_numpy(a).to(dev) for a in (sb, q, e))
+    out_d = torch.zeros(out_tiles * 128, dtype=torch.float32, device=dev)
+    args = (sb_d.data_ptr(), sb.nbytes, lit, out_tiles, q_d.data_ptr(), e_d.data_ptr(), out_d.data_ptr())
+    torch.cuda.synchronize()
+    nctx.linear_bank_noalloc(*args)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info(0)
+    for _ in range(5):
+        nctx.linear_bank_noalloc(*args)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info(0)
+    assert free1 == free0, (free0, free1)
+
+
 @pytest.mark.parametrize("lit,out_tiles", [(4, 92), (4, 252)])
 def test_noalloc_rejects_streams_beyond_the_scratch(pkg, nctx, lit, out_tiles):
     import torch
