@@ -28,17 +28,22 @@
 
 namespace i4d {
 
-constexpr int kTokColWarps = 16;             // consumer warps that compute chunks
-constexpr int kTokRedWarps = 2;              // consumer warps that chain finished units
-constexpr int kTokWarps = kTokColWarps + kTokRedWarps;
+constexpr int kTokWarps = 18;                // consumer warps (GEMV units, attention item)
 constexpr int kTokThreads = 32 * (1 + kTokWarps);
 constexpr int kTokRing = 40;               // ring capacity in chunks of kChunkBytes
 constexpr int kTokCpc = 4;                 // chunks per bulk copy (16,896 B: streams near the HBM peak)
 constexpr int kTokSlots = kTokRing / kTokCpc;  // ring slots, one copy each
 constexpr int kTokSlotBytes = kTokCpc * kChunkBytes;
-constexpr int kTokUnion = 59904;           // GEMV activations + contributions, or attention scratch
-constexpr int kTokContribBytes = 50688;     // contribution slots: 12 units of 4 chunks, 4 of DOWN
-constexpr int kTokMaxSlots = 16;
+constexpr int kTokUnion = 59904;           // GEMV activations + transpose tiles, or attention scratch
+// Activation record of one local G32 group (80 B): hi int8[32], lo
+// uint8[32], correction int32, scale float, 8 pad bytes.  The 80-byte stride
+// puts the 8 groups a warp reads at once on distinct shared-memory banks.
+constexpr int kActRec = 80;
+constexpr int kTokActBytes = kMaxLocalGroups * kActRec;  // 7,040
+constexpr int kTileFloats = 8 * 36;                      // one warp's transpose tile
+constexpr int kTokTileBytes = kTokWarps * 2 * kTileFloats * 4;
+constexpr int kTokQaccBytes = 4 * 32 * 4;                 // running row sums of each quad's unit
+static_assert(kTokActBytes + kTokTileBytes + kTokQaccBytes + 16 <= kTokUnion, "union region");
 constexpr int kAttnParts = 4;              // 32-dimension parts per head
 constexpr int kAttnItems = kHeads * kAttnParts;
 
@@ -149,18 +154,14 @@ struct TokSmem {
     uint64_t* empty;
     uint64_t* abar;      // [2] attention tile barriers
     uint8_t* uni;        // union region
-    int* next;           // dynamic chunk counter
-    int* unit_cnt;       // [kTokMaxSlots]: chunk arrivals per contribution slot in this stage
-    int* slot_ok;        // [kTokMaxSlots]: first unit index the slot may take
-    int* fin;            // [kFinMax + 2]
     int* flag;           // [4] misc
     int* issued;         // [kTokSlots]: copy sequence number last issued into each slot
     double* expf_tab;    // [64]: the expf core's 2^(j/64) table
 };
 
 __host__ __device__ inline size_t tok_smem_bytes() {
-    return static_cast<size_t>(kTokRing) * kChunkBytes + 2 * kTokSlots * 8 + 16 + kTokUnion + 16 + 2 * kTokMaxSlots * 4 +
-           align16((kFinMax + 2) * 4) + 16 + align16(kTokSlots * 4) + 64 * 8;
+    return static_cast<size_t>(kTokRing) * kChunkBytes + 2 * kTokSlots * 8 + 16 + kTokUnion + 16 +
+           align16(kTokSlots * 4) + 64 * 8;
 }
 
 __device__ __forceinline__ TokSmem tok_carve(uint8_t* p) {
@@ -173,13 +174,6 @@ __device__ __forceinline__ TokSmem tok_carve(uint8_t* p) {
     p += 2 * kTokSlots * 8 + 16;
     s.uni = p;
     p += kTokUnion;
-    s.next = reinterpret_cast<int*>(p);
-    p += 16;
-    s.unit_cnt = reinterpret_cast<int*>(p);
-    s.slot_ok = s.unit_cnt + kTokMaxSlots;
-    p += 2 * kTokMaxSlots * 4;
-    s.fin = reinterpret_cast<int*>(p);
-    p += align16((kFinMax + 2) * 4);
     s.flag = reinterpret_cast<int*>(p);
     p += 16;
     s.issued = reinterpret_cast<int*>(p);
@@ -262,8 +256,21 @@ __device__ __forceinline__ float* stage_partials(const TokenArgs& a, int ordinal
 // Every CTA computes the same residual; CTA 0 stores it for the next update.
 // All loads (gammas, residual_{n-1}, the four partials) are issued as one
 // batch after the stage wait; loading before the wait was measured slower.
+// Stores one lane's INT14 activation (value q of local group lg, column
+// `lane`) in split form (q = 128 * hi + lo, lo in [0, 128)), plus the group's
+// offset correction (8 * the sum of its first 16 values, for the offset-binary
+// low nibbles) and scale.
+__device__ __forceinline__ void put_act_rec(uint8_t* acts, int lg, int lane, int q, uint32_t e8m0) {
+    uint8_t* r = acts + lg * kActRec;
+    reinterpret_cast<int8_t*>(r)[lane] = static_cast<int8_t>(q >> 7);
+    r[32 + lane] = static_cast<uint8_t>(q & 127);
+    int lo16 = lane < 16 ? q : 0;
+    lo16 = __reduce_add_sync(0xffffffffu, lo16);
+    if (lane == 0) *reinterpret_cast<int2*>(r + 64) = make_int2(8 * lo16, __float_as_int(e8m0_scale(e8m0)));
+}
+
 template <int G>
-__device__ __forceinline__ void tok_input_rms(const TokenArgs& a, const TokSmem& s, const LinearSmem& ls, int bank,
+__device__ __forceinline__ void tok_input_rms(const TokenArgs& a, const TokSmem& s, uint8_t* acts, int bank,
                                               int norm, int prev_ordinal, float* xs, int cw, int lane) {
     constexpr int kPer = (G + kTokWarps - 1) / kTokWarps;
     constexpr int kQ = kDim / 4;                                      // float4 per vector
@@ -338,7 +345,7 @@ __device__ __forceinline__ void tok_input_rms(const TokenArgs& a, const TokSmem&
             uint32_t e8;
             const float v = __fmul_rn(__fmul_rn(xs[bank * G * 32 + lg * 32 + lane], r), g[k]);
             const int q = quantize_g32_lane(v, &e8);
-            put_act(ls, lg, lane, q, e8);
+            put_act_rec(acts, lg, lane, q, e8);
         }
     }
 }
@@ -346,7 +353,7 @@ __device__ __forceinline__ void tok_input_rms(const TokenArgs& a, const TokSmem&
 // Input of DOWN: SwiGLU of this bank's 2816 FFN columns from the GATE/UP
 // partials (gate rows [0, 11264), up rows [11264, 22528)), then the G32
 // quantizer (emulator:716-722, 769-770).
-__device__ __forceinline__ void tok_input_swiglu(const TokenArgs& a, const TokSmem& s, const LinearSmem& ls, int bank,
+__device__ __forceinline__ void tok_input_swiglu(const TokenArgs& a, const TokSmem& s, uint8_t* acts, int bank,
                                                  int layer, int cw, int lane) {
     constexpr int G = 88;
     constexpr int kPer = (G + kTokWarps - 1) / kTokWarps;
@@ -396,13 +403,13 @@ __device__ __forceinline__ void tok_input_swiglu(const TokenArgs& a, const TokSm
         if (lg < G) {
             uint32_t e8;
             const int q = quantize_g32_lane(sw[k], &e8);
-            put_act(ls, lg, lane, q, e8);
+            put_act_rec(acts, lg, lane, q, e8);
         }
     }
 }
 
 // Input of O: the attention output of this bank's 8 heads.
-__device__ __forceinline__ void tok_input_attention(const TokenArgs& a, const LinearSmem& ls, int bank, int cw, int lane) {
+__device__ __forceinline__ void tok_input_attention(const TokenArgs& a, uint8_t* acts, int bank, int cw, int lane) {
     constexpr int G = 32;
     constexpr int kPer = (G + kTokWarps - 1) / kTokWarps;
 #pragma unroll
@@ -411,7 +418,7 @@ __device__ __forceinline__ void tok_input_attention(const TokenArgs& a, const Li
         if (lg >= G) break;
         const int q = __ldcg(a.ao_q + bank * 1024 + lg * 32 + lane);
         const uint32_t e8 = __ldcg(a.ao_e + bank * 32 + lg);
-        put_act(ls, lg, lane, q, e8);
+        put_act_rec(acts, lg, lane, q, e8);
     }
 }
 
@@ -428,235 +435,140 @@ __device__ __forceinline__ void tok_wait_copy(const TokenArgs& a, const TokSmem&
     tok_mbar_wait(a, &s.full[slot], static_cast<uint32_t>((cp / kTokSlots) & 1), kErrWaitFull | kErrWaitCopy);
 }
 
-// Waits until contribution slot `us` may take unit `uidx`.  On a timeout
-// with a timeline attached, records the slot's state in events 24..29.
-__device__ __forceinline__ void tok_wait_slot(const TokenArgs& a, const TokSmem& s, int us, int uidx) {
-    if (*reinterpret_cast<volatile int*>(&s.slot_ok[us]) >= uidx) return;
-    for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.slot_ok[us]) < uidx; ++it) {
-        if (it >= 256) __nanosleep(32);
-        if ((it & 63) == 0 && aborted(a)) break;
-        if (it > (1u << 24)) {
-            raise_abort(a, kErrWaitFull | kErrWaitSlot);
-            if (a.timeline) {
-                unsigned long long* t = a.timeline + blockIdx.x * kTlEvents;
-                t[24] = static_cast<unsigned long long>(us);
-                t[25] = static_cast<unsigned long long>(uidx);
-                t[26] = static_cast<unsigned long long>(*reinterpret_cast<volatile int*>(&s.slot_ok[us]));
-                t[27] = static_cast<unsigned long long>(*reinterpret_cast<volatile int*>(&s.unit_cnt[us])) + 1;
-                t[28] = static_cast<unsigned long long>(*reinterpret_cast<volatile int*>(&s.flag[2]));
-                t[29] = static_cast<unsigned long long>(*reinterpret_cast<volatile int*>(&s.flag[3]));
-            }
-            break;
-        }
-    }
-}
-
-template <int C>
-constexpr int kRowNU = (kTokContribBytes / (C * 8 * 128) > kTokMaxSlots ? kTokMaxSlots : kTokContribBytes / (C * 8 * 128)) /
-                       kTokRedWarps * kTokRedWarps;
-
 struct WarpTimes {
-    long long data = 0, slot = 0, comp = 0, chain = 0;
+    long long data = 0, comp = 0;
 };
 
-// Chunk loop, one row per lane (any chunks per unit; used for DOWN): a warp
-// takes whole chunks in order, activations come from shared memory.
+// Chain hand-off words of a quad (shared memory): acquire / release at CTA scope.
+__device__ __forceinline__ int ld_acquire_cta_s(const int* p) {
+    int v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_cta_s(int* p, int v) {
+    asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+
+constexpr int kQuads = 4;                 // GEMV warps: kQuads x 4 (warps 16, 17 take no units)
+
+// Unit loop of a GEMV stage.  A unit is 32 output rows x this bank's local
+// columns (C chunks of 256 columns).  Quad q (warps 4q .. 4q+3) takes units
+// q, q + 4, ... of the CTA's range; over the quad's stream of chunks
+// s = 0, 1, ... (unit s / C, chunk s % C), warp j takes s = j, j + 4, ...,
+// so the four chunks of a ring copy are worked on at once and a slot is held
+// for about one chunk's time.
+//
+// Per chunk, lane (g = lane % 8, rb = lane / 8) computes the exact G32 dots
+// of group g for rows 8rb .. 8rb+7 and their contributions
+// fl(float(dot) * fl(ws * as)); an 8 x 8 transpose through the warp's
+// shared-memory tile gives lane (g, rb) row 8rb+g's contributions of the
+// chunk's 8 groups in column order.  The row's serial FP32 chain over the
+// bank's groups (emulator:216-264) then passes through the quad in chunk
+// order: the warp of chunk s waits until the quad's chain word reads s,
+// adds its 8 values to the running sums of the unit's 32 rows (or starts
+// them from +0.0f at chunk 0), and stores them back -- or, at the unit's
+// last chunk, stores the bank partials -- before releasing s + 1.  Only the
+// 8 additions wait; the dots of the next chunk do not.
 template <int C, bool TR>
-__device__ __forceinline__ void tok_chunks_rows(const TokenArgs& a, const TokSmem& s, const StageDesc& d,
-                                                const LinearSmem& ls, float* contrib, int lane, WarpTimes& wt) {
-    constexpr int G = C * 8;
-    constexpr int NU = kRowNU<C>;
-    const unsigned FULL = 0xffffffffu;
-    const int nchunks = (d.u1 - d.u0) * C;
+__device__ __forceinline__ void tok_units(const TokenArgs& a, const TokSmem& s, const StageDesc& d,
+                                          const uint8_t* acts, float* tile, float* qacc, int* qflag,
+                                          float* partials, int cw, int lane, WarpTimes& wt) {
+    const int quad = cw >> 2, j = cw & 3;
+    const int g = lane & 7, rb = lane >> 3, g128 = g >> 2;
+    const int row = 8 * rb + g;  // the row this lane chains
+    const int nunits = d.u1 - d.u0;
+    const int nchunks = nunits * C;
+    const int nq = nunits > quad ? (nunits - quad + kQuads - 1) / kQuads : 0;  // this quad's units
+    const int rows_total = stage_units(d.st) * 32;
+    const int ord = stage_ordinal(d.st, d.layer);
     const bool tr = TR && a.trace != nullptr;
-    for (;;) {
+    int par = 0;
+    // With 4 chunks per unit a warp always takes chunk j: its group's
+    // activations stay in registers for the whole stage.
+    uint4 h0, h1, l0, l1;
+    int2 cs;
+    auto load_acts = [&](int c) {
+        const uint8_t* ar = acts + (c * 8 + g) * kActRec;
+        h0 = *reinterpret_cast<const uint4*>(ar);
+        h1 = *reinterpret_cast<const uint4*>(ar + 16);
+        l0 = *reinterpret_cast<const uint4*>(ar + 32);
+        l1 = *reinterpret_cast<const uint4*>(ar + 48);
+        cs = *reinterpret_cast<const int2*>(ar + 64);
+    };
+    if (C == 4) load_acts(j);
+#pragma unroll 1
+    for (int sq = j; sq < nq * C; sq += 4) {
         const long long c0 = tr ? clock64() : 0;
-        int i = 0;
-        if (lane == 0) i = atomicAdd(s.next, 1);
-        i = __shfl_sync(FULL, i, 0);
-        if (i >= nchunks) break;
+        const int us = sq / C, c = sq - us * C;
+        const int k = quad + kQuads * us;  // unit index in the CTA's range
+        const int i = k * C + c;           // chunk index in the CTA's stage stream
         const int cp = d.cbase + i / kTokCpc;
         const int slot = cp % kTokSlots;
+        if (C != 4) load_acts(c);
         tok_wait_copy(a, s, cp, slot);
+        const long long c1 = tr ? clock64() : 0;
         const uint8_t* ch = s.ring + static_cast<size_t>(slot) * kTokSlotBytes + (i % kTokCpc) * kChunkBytes;
         uint4 wv[8];
 #pragma unroll
-        for (int g = 0; g < 8; ++g) wv[g] = *reinterpret_cast<const uint4*>(ch + chunk_piece(lane, g));
-        const int16_t raw0 = reinterpret_cast<const int16_t*>(ch)[lane * 2];
-        const int16_t raw1 = reinterpret_cast<const int16_t*>(ch)[lane * 2 + 1];
-        __syncwarp();
-        if (lane == 0) {
-            // The empty barrier counts kTokCpc chunk releases; the last chunk of
-            // a short final copy also releases the chunks the copy lacks.
-            uint32_t rel = 1;
-            if (i == nchunks - 1 && nchunks % kTokCpc != 0) rel = kTokCpc - nchunks % kTokCpc + 1;
-            mbar_arrive_cnt(&s.empty[slot], rel);
-        }
-        const long long c1 = tr ? clock64() : 0;
-        const int uidx = i / C, j = i - uidx * C;
-        const int us = uidx % NU;
-        tok_wait_slot(a, s, us, uidx);
-        const long long c2 = tr ? clock64() : 0;
-        float* cb = contrib + us * G * 32;
-        const float ws0 = __fmul_rn(static_cast<float>(raw0), 1.0f / 32768.0f);
-        const float ws1 = __fmul_rn(static_cast<float>(raw1), 1.0f / 32768.0f);
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-            const int lg = j * 8 + g;
-            const int dot = group_dot(wv[g], ls.act_hi + lg * 32, ls.act_lo + lg * 32, ls.corr[lg]);
-            cb[lg * 32 + lane] = __fmul_rn(static_cast<float>(dot), __fmul_rn(g < 4 ? ws0 : ws1, ls.act_scale[lg]));
-        }
-        __threadfence_block();
-        __syncwarp();
-        if (lane == 0) atomicAdd(&s.unit_cnt[us], 1);  // the reducer chains the unit
-        const long long c3 = tr ? clock64() : 0;
-        if (tr) {
-            const long long c4 = clock64();
-            wt.data += c1 - c0;
-            wt.slot += c2 - c1;
-            wt.comp += c3 - c2;
-            wt.chain += c4 - c3;
-        }
-    }
-}
-
-// Chunk loop of the 4-chunk stages, one column chunk per warp: warp cw
-// takes chunk j = cw % 4 of units in order; lane (g = lane % 8, rb = lane / 8)
-// computes the G32 dots of group g for rows 8rb .. 8rb+7, with its group's
-// split activations held in registers for the whole stage.  Per chunk a lane
-// reads only its 128 weight bytes and 32 scale bytes from shared memory.
-// Contributions are stored at [group][row] with a stride of 33 floats (no
-// bank conflicts for either writer or chain).
-constexpr int kColContribStride = 33;
-// Contribution slots: a multiple of the reducer count, so that every slot is
-// owned by one reducer, which waits on its barrier phases strictly in order
-// (a parity wait cannot tell phases two apart).
-constexpr int kColNU = kTokContribBytes / (32 * kColContribStride * 4) / kTokRedWarps * kTokRedWarps;  // 12
-static_assert(kColNU <= kTokMaxSlots, "contribution slots");
-
-template <bool TR>
-__device__ __forceinline__ void tok_chunks_cols(const TokenArgs& a, const TokSmem& s, const StageDesc& d,
-                                                const LinearSmem& ls, float* contrib, int cw, int lane,
-                                                WarpTimes& wt) {
-    constexpr int G = 32;
-    constexpr int NU = kColNU;
-    const unsigned FULL = 0xffffffffu;
-    const int j = cw & 3, g = lane & 7, rb = lane >> 3, g128 = g >> 2;
-    const int lg = j * 8 + g;
-    const uint4 h0 = *reinterpret_cast<const uint4*>(ls.act_hi + lg * 32);
-    const uint4 h1 = *reinterpret_cast<const uint4*>(ls.act_hi + lg * 32 + 16);
-    const uint4 l0 = *reinterpret_cast<const uint4*>(ls.act_lo + lg * 32);
-    const uint4 l1 = *reinterpret_cast<const uint4*>(ls.act_lo + lg * 32 + 16);
-    const int corr = ls.corr[lg];
-    const float as = ls.act_scale[lg];
-    const int nunits = d.u1 - d.u0;
-    const bool tr = TR && a.trace != nullptr;
-    const bool tl = TR && a.timeline && d.st == TS_QKV && d.layer == a.tl_layer;
-    int ngrab = 0;
-    for (;;) {
-        const long long c0 = tr ? clock64() : 0;
-        int u = 0;
-        if (lane == 0) u = atomicAdd(&s.next[j], 1);
-        u = __shfl_sync(FULL, u, 0);
-        if (tl && lane == 0) {
-            if (ngrab < 6) a.timeline[blockIdx.x * kTlEvents + 34 + 8 * cw + ngrab] = global_ns();
-            ++ngrab;
-        }
-        if (u >= nunits) break;
-        const int cp = d.cbase + u;  // one copy per unit
-        const int slot = cp % kTokSlots;
-        tok_wait_copy(a, s, cp, slot);
-        if (TR && lane == 0 && a.timeline && d.st == TS_GU && d.layer == a.tl_layer && u < 24)
-            atomicCAS(&a.timeline[blockIdx.x * kTlEvents + 186 + u], 0ull, global_ns());
-        const uint8_t* ch = s.ring + static_cast<size_t>(slot) * kTokSlotBytes + j * kChunkBytes;
-        uint4 wv[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) wv[k] = *reinterpret_cast<const uint4*>(ch + chunk_piece(rb * 8 + k, g));
+        for (int q = 0; q < 8; ++q) wv[q] = *reinterpret_cast<const uint4*>(ch + chunk_piece(rb * 8 + q, g));
         // Scales of rows 8rb .. 8rb+7: int16 at (row * 2 + g128) * 2.
         const uint4 sa = *reinterpret_cast<const uint4*>(ch + rb * 32);
         const uint4 sb = *reinterpret_cast<const uint4*>(ch + rb * 32 + 16);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s.empty[slot]);
-        const long long c1 = tr ? clock64() : 0;
-        const int us = u % NU;
-        tok_wait_slot(a, s, us, u);
-        const long long c2 = tr ? clock64() : 0;
-        float* cb = contrib + us * G * kColContribStride;
+        if (lane == 0) {
+            // The empty barrier counts kTokCpc chunk releases; the last chunk
+            // of a short final copy also releases the chunks the copy lacks.
+            uint32_t rel = 1;
+            if (i == nchunks - 1 && nchunks % kTokCpc != 0) rel = kTokCpc - nchunks % kTokCpc + 1;
+            mbar_arrive_cnt(&s.empty[slot], rel);
+        }
+        const float as = __int_as_float(cs.y);
         const uint32_t sw[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+        float cv[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const int16_t raw = static_cast<int16_t>(g128 ? (sw[k] >> 16) : (sw[k] & 0xffffu));
+        for (int q = 0; q < 8; ++q) {
+            const int16_t raw = static_cast<int16_t>(g128 ? (sw[q] >> 16) : (sw[q] & 0xffffu));
             const float ws = __fmul_rn(static_cast<float>(raw), 1.0f / 32768.0f);
-            const int dot = group_dot_r(wv[k], h0, h1, l0, l1, corr);
-            cb[lg * kColContribStride + rb * 8 + k] = __fmul_rn(static_cast<float>(dot), __fmul_rn(ws, as));
+            const int dot = group_dot_r(wv[q], h0, h1, l0, l1, cs.x);
+            cv[q] = __fmul_rn(static_cast<float>(dot), __fmul_rn(ws, as));
         }
-        __threadfence_block();
+        // Transpose: tile[group][row] with a 36-float group stride (both the
+        // 16-byte stores and the column reads hit every bank once per phase).
+        float* T = tile + par * kTileFloats;
+        *reinterpret_cast<float4*>(T + 36 * g + 8 * rb) = make_float4(cv[0], cv[1], cv[2], cv[3]);
+        *reinterpret_cast<float4*>(T + 36 * g + 8 * rb + 4) = make_float4(cv[4], cv[5], cv[6], cv[7]);
         __syncwarp();
-        if (lane == 0) atomicAdd(&s.unit_cnt[us], 1);  // the reducer chains the unit
-        const long long c3 = tr ? clock64() : 0;
-        if (tr) {
-            const long long c4 = clock64();
-            wt.data += c1 - c0;
-            wt.slot += c2 - c1;
-            wt.comp += c3 - c2;
-            wt.chain += c4 - c3;
-        }
-    }
-    if (tl && lane == 0) {
-        a.timeline[blockIdx.x * kTlEvents + 34 + 8 * cw + 6] = global_ns();
-        a.timeline[blockIdx.x * kTlEvents + 34 + 8 * cw + 7] = static_cast<unsigned long long>(ngrab);
-    }
-}
-
-// Reducer warps: reducer r chains units r, r + kTokRedWarps, ... in order
-// once all their chunks have stored contributions (lane = row):
-// acc = fl(acc + contrib[g]) over the unit's groups from +0.0f
-// (emulator:216-264), stores the bank partial and frees the slot.
-template <int G, int STRIDE, int NU>
-__device__ __forceinline__ void tok_reduce_units(const TokenArgs& a, const TokSmem& s, const StageDesc& d,
-                                                 const float* contrib, float* partials, int r, int lane) {
-    static_assert(NU % kTokRedWarps == 0, "each contribution slot must belong to one reducer");
-    const int nunits = d.u1 - d.u0;
-    const int rows_total = stage_units(d.st) * 32;
-    for (int u = r; u < nunits; u += kTokRedWarps) {
-        const int us = u % NU;
-        if (lane == 0) *reinterpret_cast<volatile int*>(&s.flag[2 + r]) = u;  // progress, for diagnostics
-        // The slot's arrival count only grows within a stage: its k-th unit is
-        // complete at (k + 1) * chunks arrivals.
-        const int target = (u / NU + 1) * (G / 8);
-        for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.unit_cnt[us]) < target; ++it) {
-            if (it >= 64) __nanosleep(32);
-            if ((it & 63) == 0 && aborted(a)) return;
+        float t[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t[q] = T[36 * q + row];
+        par ^= 1;  // the other tile: its reads finished before this chunk's __syncwarp
+        // The chain: wait for chunk sq - 1 of the quad's stream.
+        for (uint32_t it = 0; ld_acquire_cta_s(qflag) != sq; ++it) {
+            if ((it & 63) == 0 && aborted(a)) break;
             if (it > (1u << 24)) {
                 raise_abort(a, kErrWaitFull | kErrWaitUnit);
-                return;
+                break;
             }
+            if (it >= 64) __nanosleep(32);
         }
-        __threadfence_block();
-        const float* cb = contrib + us * G * STRIDE;
-        // All of a batch's loads are in flight before the dependent adds.
-        constexpr int kBatch = G <= 32 ? G : (G + 1) / 2;
-        float acc = 0.0f;
+        float acc = c == 0 ? 0.0f : qacc[row];
 #pragma unroll
-        for (int q0 = 0; q0 < G; q0 += kBatch) {
-            float v[kBatch];
-#pragma unroll
-            for (int q = 0; q < kBatch; ++q) v[q] = q0 + q < G ? cb[(q0 + q) * STRIDE + lane] : 0.0f;
-#pragma unroll
-            for (int q = 0; q < kBatch; ++q)
-                if (q0 + q < G) acc = __fadd_rn(acc, v[q]);
+        for (int q = 0; q < 8; ++q) acc = __fadd_rn(acc, t[q]);
+        if (c == C - 1) {
+            const size_t off = static_cast<size_t>(d.bank) * rows_total + static_cast<size_t>(d.u0 + k) * 32 + row;
+            partials[off] = acc;
+            // Bank sharding: every rank receives every bank's partials.
+            for (int p = 0; p < a.world; ++p)
+                if (a.peer_partials[p] != a.partials) a.peer_partials[p][(ord & 1) * kPartialBuf + off] = acc;
+        } else {
+            qacc[row] = acc;
         }
-        const size_t off = static_cast<size_t>(d.bank) * rows_total + static_cast<size_t>(d.u0 + u) * 32 + lane;
-        partials[off] = acc;
-        // Bank sharding: every rank receives every bank's partials.
-        for (int p = 0; p < a.world; ++p)
-            if (a.peer_partials[p] != a.partials) a.peer_partials[p][(stage_ordinal(d.st, d.layer) & 1) * kPartialBuf + off] = acc;
-        // Every lane has consumed its contribution loads (acc depends on
-        // them), so the slot may be reused.  No fence here: one would also
-        // wait for the partial store above to reach L2; the stage-end CTA
-        // barrier and thread 0's fence publish the partials.
         __syncwarp();
-        if (lane == 0) *reinterpret_cast<volatile int*>(&s.slot_ok[us]) = u + NU;
+        if (lane == 0) st_release_cta_s(qflag, sq + 1);
+        if (tr) {
+            wt.data += c1 - c0;
+            wt.comp += clock64() - c1;
+        }
     }
 }
 
@@ -672,16 +584,11 @@ template <int C, bool TR>
 __device__ __forceinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem& s, const StageDesc& d, int cw,
                                             int lane) {
     constexpr int G = C * 8;
-    static_assert(kRowNU<C> >= 2 && kColNU >= 2, "contribution slots");
-    static_assert((G * 72 + 15) / 16 * 16 +
-                      (C == 4 ? kColNU * 32 * kColContribStride * 4 : kRowNU<C> * G * 128) <= kTokUnion,
-                  "union region");
-    LinearSmem ls;
-    ls.act_hi = reinterpret_cast<int8_t*>(s.uni);
-    ls.act_lo = s.uni + G * 32;
-    ls.corr = reinterpret_cast<int*>(s.uni + G * 64);
-    ls.act_scale = reinterpret_cast<float*>(s.uni + G * 68);
-    float* contrib = reinterpret_cast<float*>(s.uni + align16(G * 72));
+    static_assert(G * kActRec <= kTokActBytes, "activation records");
+    uint8_t* acts = s.uni;
+    float* tiles = reinterpret_cast<float*>(s.uni + kTokActBytes);
+    float* qacc = reinterpret_cast<float*>(s.uni + kTokActBytes + kTokTileBytes);
+    int* qflag = reinterpret_cast<int*>(s.uni + kTokActBytes + kTokTileBytes + kTokQaccBytes);
     const int tid = cw * 32 + lane;
     const int ord = stage_ordinal(d.st, d.layer);
     const int tl_layer = d.st == TS_LOGITS ? a.tl_layer : d.layer;  // the LM head is recorded with any layer
@@ -693,22 +600,18 @@ __device__ __forceinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem
     if (tid == 0) {
         if (d.st == TS_O) wait_counter(a, &a.sync[kSyncAtt + d.layer], d.tgt_att);
         else if (ord > 0) wait_counter(a, &a.sync[kSyncStage + ord - 1], d.tgt_stage);
-        s.next[0] = s.next[1] = s.next[2] = s.next[3] = 0;
     }
-    if (tid < kTokMaxSlots) {
-        s.unit_cnt[tid] = 0;  // chunk arrivals per contribution slot, this stage
-        s.slot_ok[tid] = tid;
-    }
+    if (tid < kQuads) qflag[tid] = 0;  // chunks chained by each quad in this stage
     tok_bar();
     const long long t_ready = clock64();
     if (tid == 0) tl_mark<TR>(a, tl_layer, 4 * d.st + 1);
     if (d.st == TS_O) {
-        tok_input_attention(a, ls, d.bank, cw, lane);
+        tok_input_attention(a, acts, d.bank, cw, lane);
     } else if (d.st == TS_DOWN) {
-        tok_input_swiglu(a, s, ls, d.bank, d.layer, cw, lane);
+        tok_input_swiglu(a, s, acts, d.bank, d.layer, cw, lane);
     } else {
         const int norm = d.st == TS_QKV ? 2 * d.layer : d.st == TS_GU ? 2 * d.layer + 1 : 2 * d.layer;
-        if constexpr (G == 32) tok_input_rms<32>(a, s, ls, d.bank, norm, ord - 1, contrib, cw, lane);
+        if constexpr (G == 32) tok_input_rms<32>(a, s, acts, d.bank, norm, ord - 1, tiles, cw, lane);
     }
     tok_bar();
     const long long t_loop = clock64();
@@ -731,16 +634,9 @@ __device__ __forceinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem
     float* partials = stage_partials(a, ord);
     const bool tr = TR && a.trace != nullptr;
     WarpTimes wt;
-    if (cw >= kTokColWarps) {
-        if constexpr (C == 4)
-            tok_reduce_units<32, kColContribStride, kColNU>(a, s, d, contrib, partials, cw - kTokColWarps, lane);
-        else
-            tok_reduce_units<C * 8, 32, kRowNU<C>>(a, s, d, contrib, partials, cw - kTokColWarps, lane);
-    } else if constexpr (C == 4) {
-        tok_chunks_cols<TR>(a, s, d, ls, contrib, cw, lane, wt);
-    } else {
-        tok_chunks_rows<C, TR>(a, s, d, ls, contrib, lane, wt);
-    }
+    if (cw < 4 * kQuads)
+        tok_units<C, TR>(a, s, d, acts, tiles + cw * 2 * kTileFloats, qacc + (cw >> 2) * 32, qflag + (cw >> 2),
+                         partials, cw, lane, wt);
     // Release: the CTA barrier orders every warp's partial stores before
     // thread 0's release arrival (the grid-sync pattern).
     tok_bar();
@@ -764,12 +660,9 @@ __device__ __forceinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem
     if (tr && lane == 0) {
         unsigned long long* t = a.trace + blockIdx.x * kTraceSlots;
         atomicAdd(t + TR_W_DATA + 4 * d.st, static_cast<unsigned long long>(wt.data));
-        atomicAdd(t + TR_W_SLOT + 4 * d.st, static_cast<unsigned long long>(wt.slot));
         atomicAdd(t + TR_W_COMPUTE + 4 * d.st, static_cast<unsigned long long>(wt.comp));
-        atomicAdd(t + TR_W_CHAIN + 4 * d.st, static_cast<unsigned long long>(wt.chain));
     }
 }
-
 // Key of a logit for the greedy argmax: larger keys win; equal values favour
 // the smaller index (the first maximum, as emulator:1428-1438 and
 // decode_host.cpp:703-717 scan); -0.0 counts as +0.0; NaN never wins (key 0).
@@ -1234,6 +1127,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
             // partials, residual and counters of the stage handoffs stay in L2.
             const uint64_t pol_first = l2_policy_evict_first();
             cursor_begin(a, lbank, c, cur);
+
             while (cursor_valid(a, cur)) {
                 const int cnt = min(kTokCpc, cur.n - cur.i);
                 if (issued >= kTokSlots) {
