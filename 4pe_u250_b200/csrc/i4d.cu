@@ -639,6 +639,8 @@ static i4d_status create_impl(const i4d_config* cfg, int rank, int world, i4d_ct
     c->cpb = c->num_sms / c->nbanks > 0 ? c->num_sms / c->nbanks : 1;
     CKC(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     CKC(cudaFuncSetAttribute(k_linear, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBudget)));
+    CKC(cudaFuncSetAttribute(k_attn_items, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(attn_items_smem_bytes())));
     CKC(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(attn_smem_bytes())));
     CKC(cudaFuncSetAttribute(k_linear_batch, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1647,7 +1649,7 @@ i4d_status i4d_attention(i4d_ctx* c, int layer, uint32_t position, const int32_t
     a.direct = dqkv.as<int32_t>();
     a.out_q = dq.as<int16_t>();
     a.out_e = de.as<uint8_t>();
-    k_attention<<<kHeads, kAttnThreads, attn_smem_bytes(), c->stream>>>(a);
+    k_attn_items<<<kAttnItems, kItemThreads, attn_items_smem_bytes(), c->stream>>>(a);
     CK(cudaGetLastError());
     const i4d_status st = finish(c);
     if (st != I4D_OK) return st;
@@ -1747,7 +1749,7 @@ extern "C" i4d_status i4d_token_breakdown(i4d_ctx* c, uint32_t position, const f
     for (int k = 0; k < kTraceSlots; ++k) {
         double sum = 0.0;
         for (int b = 0; b < 4 * c->cpb; ++b) sum += static_cast<double>(h[static_cast<size_t>(b) * kTraceSlots + k]);
-        const double per = k >= TR_W_DATA ? 4.0 * c->cpb * kTokWarps : 4.0 * c->cpb;  // warp slots: per warp
+        const double per = k >= TR_W_DATA ? 4.0 * c->cpb * 4 * kQuads : 4.0 * c->cpb;  // warp slots: per GEMV warp
         us_out[k] = static_cast<float>(sum / per / (khz * 1e-3));
     }
     return I4D_OK;
@@ -1852,7 +1854,7 @@ extern "C" i4d_status i4d_profile_attention(i4d_ctx* c, int layer, uint32_t posi
     auto step = [&](int p, int row) {
         k_set_pos<<<1, 1, 0, c->stream>>>(c->d_pos, p);
         a.direct = qkv_dev + static_cast<size_t>(row) * 3 * kDim;
-        k_attention<<<kHeads, kAttnThreads, attn_smem_bytes(), c->stream>>>(a);
+        k_attn_items<<<kAttnItems, kItemThreads, attn_items_smem_bytes(), c->stream>>>(a);
         return cudaGetLastError();
     };
     if (fill > 0)

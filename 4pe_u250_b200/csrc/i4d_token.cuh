@@ -22,6 +22,7 @@
 #pragma once
 
 #include "i4d_attention.cuh"
+#include "i4d_attn_item.cuh"
 #include "i4d_device.cuh"
 #include "i4d_expf.cuh"
 #include "i4d_linear.cuh"
@@ -44,8 +45,8 @@ constexpr int kTileFloats = 8 * 36;                      // one warp's transpose
 constexpr int kTokTileBytes = kTokWarps * 2 * kTileFloats * 4;
 constexpr int kTokQaccBytes = 4 * 32 * 4;                 // running row sums of each quad's unit
 static_assert(kTokActBytes + kTokTileBytes + kTokQaccBytes + 16 <= kTokUnion, "union region");
-constexpr int kAttnParts = 4;              // 32-dimension parts per head
-constexpr int kAttnItems = kHeads * kAttnParts;
+static_assert(kAttnItemBytes <= kTokUnion, "attention item scratch exceeds the union region");
+static_assert(kTokWarps == kItemWarps, "the attention item runs on the token kernel's consumer warps");
 
 // Global synchronisation words.  They only grow, token after token; the
 // epoch word (tokens completed) sets each token's targets.  The host clears
@@ -106,9 +107,9 @@ enum TraceSlot : int {
     TR_TOTAL,         // consumer: whole kernel
     TR_ARRIVE,        // + stage: thread 0's release fence and counter arrival after the stage
     TR_W_DATA = TR_ARRIVE + 5,        // + 4 * stage, per consumer warp (summed over warps): waiting for ring data
-    TR_W_SLOT,        // + 4 * stage, per warp: waiting for a contribution slot
+    TR_W_SLOT,        // + 4 * stage, per warp: waiting for the quad's row chains
     TR_W_COMPUTE,     // + 4 * stage, per warp: chunk arithmetic
-    TR_W_CHAIN,       // + 4 * stage, per warp: row chains of finished units
+    TR_W_CHAIN,       // + 4 * stage, per warp: adding to the row chains and storing them
     kTraceSlots = TR_W_DATA + 20
 };
 
@@ -436,7 +437,7 @@ __device__ __forceinline__ void tok_wait_copy(const TokenArgs& a, const TokSmem&
 }
 
 struct WarpTimes {
-    long long data = 0, comp = 0;
+    long long data = 0, comp = 0, chain_wait = 0, chain = 0;
 };
 
 // Chain hand-off words of a quad (shared memory): acquire / release at CTA scope.
@@ -542,6 +543,7 @@ __device__ __forceinline__ void tok_units(const TokenArgs& a, const TokSmem& s, 
 #pragma unroll
         for (int q = 0; q < 8; ++q) t[q] = T[36 * q + row];
         par ^= 1;  // the other tile: its reads finished before this chunk's __syncwarp
+        const long long c2 = tr ? clock64() : 0;
         // The chain: wait for chunk sq - 1 of the quad's stream.
         for (uint32_t it = 0; ld_acquire_cta_s(qflag) != sq; ++it) {
             if ((it & 63) == 0 && aborted(a)) break;
@@ -551,6 +553,7 @@ __device__ __forceinline__ void tok_units(const TokenArgs& a, const TokSmem& s, 
             }
             if (it >= 64) __nanosleep(32);
         }
+        const long long c3 = tr ? clock64() : 0;
         float acc = c == 0 ? 0.0f : qacc[row];
 #pragma unroll
         for (int q = 0; q < 8; ++q) acc = __fadd_rn(acc, t[q]);
@@ -567,7 +570,9 @@ __device__ __forceinline__ void tok_units(const TokenArgs& a, const TokSmem& s, 
         if (lane == 0) st_release_cta_s(qflag, sq + 1);
         if (tr) {
             wt.data += c1 - c0;
-            wt.comp += clock64() - c1;
+            wt.comp += c2 - c1;
+            wt.chain_wait += c3 - c2;
+            wt.chain += clock64() - c3;
         }
     }
 }
@@ -661,6 +666,8 @@ __device__ __forceinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem
         unsigned long long* t = a.trace + blockIdx.x * kTraceSlots;
         atomicAdd(t + TR_W_DATA + 4 * d.st, static_cast<unsigned long long>(wt.data));
         atomicAdd(t + TR_W_COMPUTE + 4 * d.st, static_cast<unsigned long long>(wt.comp));
+        atomicAdd(t + TR_W_SLOT + 4 * d.st, static_cast<unsigned long long>(wt.chain_wait));
+        atomicAdd(t + TR_W_CHAIN + 4 * d.st, static_cast<unsigned long long>(wt.chain));
     }
 }
 // Key of a logit for the greedy argmax: larger keys win; equal values favour
@@ -728,314 +735,30 @@ __device__ __forceinline__ void tok_logits(const TokenArgs& a, unsigned tgt_stag
 
 // ------------------------------------------------------------ attention item
 
-// Scratch of one attention item inside the union region.
-struct TokAttnSmem {
-    uint8_t* tile[2];     // kTile records each
-    uint8_t* cur;         // current token's record
-    int32_t* score;       // [kTile]
-    uint32_t* coef;       // [2][kTile]: c | rescale << 31, by tile parity
-    uint32_t* lut;        // [33] exp2 table
-    int32_t* tbuf;        // [2][kTile][32]: per-token state terms of this part, by tile parity
-    int32_t* qrot;        // [128]
-    int32_t* krot;        // [128]
-    int* misc;            // [16]
-};
-
-__device__ __forceinline__ TokAttnSmem tok_attn_carve(uint8_t* p) {
-    TokAttnSmem s;
-    s.tile[0] = p;
-    s.tile[1] = p + kTile * 320;
-    s.cur = p + 2 * kTile * 320;
-    p += 2 * kTile * 320 + 320;
-    s.score = reinterpret_cast<int32_t*>(p);
-    s.coef = reinterpret_cast<uint32_t*>(p + kTile * 4);
-    p += kTile * 12;
-    s.lut = reinterpret_cast<uint32_t*>(p);
-    p += 144;
-    s.tbuf = reinterpret_cast<int32_t*>(p);
-    p += 2 * kTile * 32 * 4;
-    s.qrot = reinterpret_cast<int32_t*>(p);
-    p += 128 * 4;
-    s.krot = reinterpret_cast<int32_t*>(p);
-    p += 128 * 4;
-    s.misc = reinterpret_cast<int*>(p);
-    return s;
-}
-static_assert(2 * kTile * 320 + 320 + kTile * 12 + 144 + 2 * kTile * 32 * 4 + 2 * 128 * 4 + 16 * 4 <= kTokUnion,
-              "attention scratch exceeds the union region");
-
-// Barrier of the attention item's 16 worker warps (warps 2..17).
-__device__ __forceinline__ void tok_wbar() { asm volatile("bar.sync 2, %0;" ::"n"(32 * (kTokWarps - 2)) : "memory"); }
-
-// Attention of one (head, 32-dimension part) item.  Scores, the running
-// maximum and the coefficients are computed in parallel as in k_attention;
-// the per-token state terms mulq17(v_t, c_t) are computed in parallel into
-// shared memory, and the reference's saturating recurrence (emulator:656-685)
-// then runs exactly, one lane per dimension, over those terms.
+// Attention of one (head, 32-dimension part) item after the QKV stage
+// (i4d_attn_item.cuh); thread 0 then publishes the item's outputs to the O
+// stage with a release arrival on the layer's attention counter.
 template <bool TR>
 __device__ __forceinline__ void tok_attention(const TokenArgs& ta, const TokSmem& s, int layer, int item, int cw,
-                                           int lane,
-                                           unsigned tgt_qkv) {
-    const unsigned FULL = 0xffffffffu;
-    const uint32_t M30 = (1u << 30) - 1u;
+                                              int lane, unsigned tgt_qkv) {
     AttnArgs a = ta.attn;
     a.layer = layer;
     a.partials = stage_partials(ta, stage_ordinal(TS_QKV, layer));
-    const int h = item / kAttnParts, part = item % kAttnParts;
+    a.out_q = ta.ao_q;
+    a.out_e = ta.ao_e;
     const int tid = cw * 32 + lane;
-    TokAttnSmem S = tok_attn_carve(s.uni);
-    int* misc = S.misc;
-
-    const int pos = *a.pos_ptr;
-    const int n = pos + 1;
-    const int ntiles = (n + kTile - 1) / kTile;
-    const uint8_t* head_base = kv_record(a, h, 0);
-    if (tid == 0) {
-        mbar_init(&s.abar[0], 1);
-        mbar_init(&s.abar[1], 1);
-        mbar_fence_init();
-        misc[0] = INT32_MIN;
-    }
-    if (tid < 33) S.lut[tid] = a.exp2_q30[tid];
-    // RoPE factors of this position: independent of the QKV projection, so
-    // loaded before waiting for it.
-    long long rope_c = 0, rope_s = 0;
-    if (tid < 128) {
-        rope_c = a.rope_cos[pos * 64 + ((tid & 127) >> 1)];
-        rope_s = a.rope_sin[pos * 64 + ((tid & 127) >> 1)];
-    }
-    tok_bar();
+    const AttnItemSmem S = attn_item_carve(s.uni);
     const long long t_a0 = clock64();
+    long long t_a1 = t_a0;
     if (tid == 0) tl_mark<TR>(ta, layer, 20);
-    if (tid == 0) {
-        // Cached records of earlier tokens are final: stream the first tile
-        // while the other CTAs finish the QKV projection.
-        const int cnt = min(kTile, n);
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&s.abar[0], cnt * 320);
-        bulk_g2s(S.tile[0], head_base, cnt * 320, &s.abar[0]);
-        wait_counter(ta, &ta.sync[kSyncStage + stage_ordinal(TS_QKV, layer)], tgt_qkv);
-    }
-    tok_bar();
-    const long long t_a1 = clock64();
-    if (tid == 0) tl_mark<TR>(ta, layer, 21);
-
-    // Current token: Q/K/V rows of the head, RoPE, KV record.
-    const int d = tid & 127;
-    int32_t qv = 0, kv = 0, vv = 0;
-    if (tid < 128) {
-        const int row = h * kHeadDim + d;
-        qv = float_to_q17(combine4(a.partials, 3 * kDim, row));
-        kv = float_to_q17(combine4(a.partials, 3 * kDim, kDim + row));
-        vv = float_to_q17(combine4(a.partials, 3 * kDim, 2 * kDim + row));
-        S.qrot[d] = qv;
-        S.krot[d] = kv;
-    }
-    tok_bar();
-    if (tid < 128) {
-        const int pr = d >> 1;
-        const long long c = rope_c, sn = rope_s;
-        const long long qa = S.qrot[2 * pr], qb = S.qrot[2 * pr + 1];
-        const long long ka = S.krot[2 * pr], kb = S.krot[2 * pr + 1];
-        qv = (d & 1) ? sat32((qa * sn + qb * c) >> 17) : sat32((qa * c - qb * sn) >> 17);
-        kv = (d & 1) ? sat32((ka * sn + kb * c) >> 17) : sat32((ka * c - kb * sn) >> 17);
-    }
-    tok_bar();
-    uint8_t* grec = kv_record(a, h, pos);
-    if (tid < 128) {
-        S.qrot[d] = qv;
-        const uint32_t kmag = static_cast<uint32_t>(kv < 0 ? -static_cast<long long>(kv) : kv);
-        const uint32_t vmag = static_cast<uint32_t>(vv < 0 ? -static_cast<long long>(vv) : vv);
-        const uint32_t ks = kv_shift_of(__reduce_max_sync(FULL, kmag));
-        const uint32_t vs = kv_shift_of(__reduce_max_sync(FULL, vmag));
-        const uint8_t k8 = static_cast<uint8_t>(kv_quant(kv, ks)), v8 = static_cast<uint8_t>(kv_quant(vv, vs));
-        S.cur[64 + d] = k8;
-        S.cur[192 + d] = v8;
-        if (part == 0) {
-            grec[64 + d] = k8;
-            grec[192 + d] = v8;
-        }
-        if (lane == 0) {
-            misc[8 + cw] = static_cast<int>(ks);
-            misc[12 + cw] = static_cast<int>(vs);
-        }
-    }
-    tok_bar();
-    if (tid < 8) {
-        unsigned long long meta = 0;
-        if (tid == 0)
-            for (int g = 0; g < 4; ++g) {
-                meta |= static_cast<unsigned long long>(misc[8 + g]) << (5 * g);
-                meta |= static_cast<unsigned long long>(misc[12 + g]) << (20 + 5 * g);
-            }
-        reinterpret_cast<unsigned long long*>(S.cur)[tid] = meta;
-        if (part == 0) reinterpret_cast<unsigned long long*>(grec)[tid] = meta;
-    }
-    const int hg = lane & 7;
-    uint32_t qh2[8], ql2[8];
-    tok_bar();
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int32_t x0 = S.qrot[hg * 16 + 2 * i], x1 = S.qrot[hg * 16 + 2 * i + 1];
-        qh2[i] = (static_cast<uint32_t>(x0 >> 16) & 0xffffu) | (static_cast<uint32_t>(x1 >> 16) << 16);
-        ql2[i] = (static_cast<uint32_t>(x0) & 0xffffu) | (static_cast<uint32_t>(x1) << 16);
-    }
-
-
-    const int dl = tid & 31;                 // dimension inside this part
-    const int dim = part * 32 + dl;
-    int32_t st = 0;                          // state of dimension `dim` (lanes of warp 0)
-    uint32_t z = 1u << 17;                   // normaliser (thread 32)
-    // Pipeline over the KV tiles: in iteration k the 16 worker warps (2..17)
-    // build tile k -- scores, running maximum, coefficients and state terms
-    // into buffer k & 1 -- while warp 0 (state) and thread 32 (normaliser)
-    // run the recurrences of tile k - 1 from buffer (k - 1) & 1.  One CTA
-    // barrier ends each iteration.
-    const int wtid = tid - 64, wcw = cw - 2;
-    for (int k = 0; k <= ntiles; ++k) {
-        if (cw >= 2) {
-            if (k < ntiles) {
-                const int T0 = k * kTile, cnt = min(kTile, n - T0);
-                uint8_t* buf = S.tile[k & 1];
-                uint32_t* coef = S.coef + (k & 1) * kTile;
-                int32_t* tbuf = S.tbuf + (k & 1) * kTile * 32;
-                if (wtid == 0 && k + 1 < ntiles) {  // buffer (k + 1) & 1 was last read in iteration k - 1
-                    fence_proxy_async_smem();
-                    const int c2 = min(kTile, n - T0 - kTile);
-                    mbar_arrive_expect_tx(&s.abar[(k + 1) & 1], c2 * 320);
-                    bulk_g2s(S.tile[(k + 1) & 1], head_base + static_cast<size_t>(T0 + kTile) * 320, c2 * 320,
-                             &s.abar[(k + 1) & 1]);
-                }
-                tok_mbar_wait(ta, &s.abar[k & 1], static_cast<uint32_t>((k >> 1) & 1), kErrWaitFull | kErrWaitTile);
-                if (pos < T0 + cnt) {  // the tile holds the current token: use the fresh record
-                    if (wtid < 80)
-                        reinterpret_cast<uint32_t*>(buf + (pos - T0) * 320)[wtid] =
-                            reinterpret_cast<const uint32_t*>(S.cur)[wtid];
-                    tok_wbar();
-                }
-                {   // scores (emulator:633-655): 16 warps x 4 tokens, 8 lanes per token
-                    const int tl = wcw * 4 + (lane >> 3);
-                    long long hv = 0;
-                    if (tl < cnt) {
-                        const uint8_t* rec = buf + tl * 320;
-                        const uint4 kw = *reinterpret_cast<const uint4*>(rec + 64 + hg * 16);
-                        const unsigned long long meta = *reinterpret_cast<const unsigned long long*>(rec);
-                        const uint32_t sh = static_cast<uint32_t>((meta >> (5 * (hg >> 1))) & 31u);
-                        int sh16 = 0, sl16 = 0;
-                        sh16 = dp2a_lo_ss(qh2[0], kw.x, sh16);
-                        sh16 = dp2a_hi_ss(qh2[1], kw.x, sh16);
-                        sh16 = dp2a_lo_ss(qh2[2], kw.y, sh16);
-                        sh16 = dp2a_hi_ss(qh2[3], kw.y, sh16);
-                        sh16 = dp2a_lo_ss(qh2[4], kw.z, sh16);
-                        sh16 = dp2a_hi_ss(qh2[5], kw.z, sh16);
-                        sh16 = dp2a_lo_ss(qh2[6], kw.w, sh16);
-                        sh16 = dp2a_hi_ss(qh2[7], kw.w, sh16);
-                        sl16 = dp2a_lo_us(ql2[0], kw.x, sl16);
-                        sl16 = dp2a_hi_us(ql2[1], kw.x, sl16);
-                        sl16 = dp2a_lo_us(ql2[2], kw.y, sl16);
-                        sl16 = dp2a_hi_us(ql2[3], kw.y, sl16);
-                        sl16 = dp2a_lo_us(ql2[4], kw.z, sl16);
-                        sl16 = dp2a_hi_us(ql2[5], kw.z, sl16);
-                        sl16 = dp2a_lo_us(ql2[6], kw.w, sl16);
-                        sl16 = dp2a_hi_us(ql2[7], kw.w, sl16);
-                        const long long half = static_cast<long long>(sh16) * 65536 + sl16;
-                        hv = wrap_bits(sh >= 10 ? static_cast<long long>(static_cast<unsigned long long>(half) << (sh - 10))
-                                                : (half >> (10 - sh)), 44);
-                    }
-                    hv += __shfl_xor_sync(FULL, hv, 1);
-                    hv += __shfl_xor_sync(FULL, hv, 2);
-                    hv += __shfl_xor_sync(FULL, hv, 4);
-                    if ((lane & 7) == 0 && tl < cnt) S.score[tl] = sat32(rshift_even(wrap_bits(hv, 44) * a.score_scale, 24));
-                }
-                tok_wbar();
-                // Coefficients from the running maximum before each token (emulator:656-672).
-                const int carry = misc[0];
-                int32_t m_incl = INT32_MIN, m_excl = INT32_MIN, sc = INT32_MIN;
-                if (wtid < kTile) {
-                    sc = wtid < cnt ? S.score[wtid] : INT32_MIN;
-                    m_incl = sc;
-#pragma unroll
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const int32_t y = __shfl_up_sync(FULL, m_incl, o);
-                        if (lane >= o) m_incl = max(m_incl, y);
-                    }
-                    m_excl = __shfl_up_sync(FULL, m_incl, 1);
-                    if (lane == 0) m_excl = INT32_MIN;
-                    if (wtid == 31) misc[2] = m_incl;
-                }
-                tok_wbar();
-                if (wtid < kTile) {
-                    const int32_t prev = max(max(carry, m_excl), wcw == 1 ? misc[2] : INT32_MIN);
-                    const int t = T0 + wtid;
-                    uint32_t c = 0;
-                    bool ev = false;
-                    if (wtid < cnt) {
-                        if (t == 0) {
-                            c = 1u << 17;
-                            ev = true;
-                        } else if (sc <= prev) {
-                            c = exp_negative_q17(sat32(static_cast<long long>(sc) - prev), S.lut, a.log2e_q21);
-                        } else {
-                            c = exp_negative_q17(sat32(static_cast<long long>(prev) - sc), S.lut, a.log2e_q21);
-                            ev = true;
-                        }
-                    }
-                    coef[wtid] = c | (ev ? 0x80000000u : 0u);
-                    if (wtid == kTile - 1) misc[0] = max(carry, max(m_incl, misc[2]));
-                }
-                tok_wbar();
-                // State terms in parallel: thread = (dimension, slice of 4 tokens).
-                const int t_lo = wcw * 4, t_hi = min(cnt, t_lo + 4);
-                for (int tl = t_lo; tl < t_hi; ++tl) {
-                    const int32_t v = rec_v(buf + tl * 320, dim);
-                    const uint32_t cf = coef[tl];
-                    tbuf[tl * 32 + dl] = (cf >> 31) ? v : mulq17(v, cf);
-                }
-            }
-        } else if (k >= 1) {  // the recurrences of tile k - 1, in token order
-            const int kp = k - 1, T0 = kp * kTile, cnt = min(kTile, n - T0);
-            const uint32_t* coef = S.coef + (kp & 1) * kTile;
-            const int32_t* tbuf = S.tbuf + (kp & 1) * kTile * 32;
-            if (tid < 32) {  // the saturating state recurrence
-                for (int tl = 0; tl < cnt; ++tl) {
-                    const uint32_t cf = coef[tl];
-                    const int32_t tv = tbuf[tl * 32 + dl];
-                    if (T0 + tl == 0) st = tv;
-                    else if (cf >> 31) st = add_sat32(mulq17_w(st, cf & 0x7fffffffu), tv);
-                    else st = add_sat32(st, tv);
-                }
-            } else if (tid == 32) {  // the normaliser recurrence
-                for (int tl = 0; tl < cnt; ++tl) {
-                    const uint32_t cf = coef[tl];
-                    const uint32_t cc = cf & 0x7fffffffu;
-                    if (T0 + tl == 0) z = 1u << 17;
-                    else if (cf >> 31)  // z < 2^30 and cc <= 2^17: mulq17_w's steps on the unsigned product
-                        z = ((static_cast<uint32_t>(mulq17_w(static_cast<int32_t>(z), cc)) & M30) + (1u << 17)) & M30;
-                    else z = (z + cc) & M30;
-                }
-            }
-        }
-        tok_bar();
-    }
-    if (tid == 32) misc[3] = static_cast<int>(z);
-    tok_bar();
-    if (tid < 32) {  // normalise and quantise this part's 32-value group (emulator:686-711)
-        const uint32_t zz = static_cast<uint32_t>(misc[3]);
-        const uint32_t inv = zz == 0 ? 0u : static_cast<uint32_t>(((1ull << 34) + (zz >> 1)) / zz);
-        const int32_t o = mulq17(st, inv);
-        const int32_t mag = o == INT32_MIN ? INT32_MAX : abs(o);
-        const int32_t mx = __reduce_max_sync(FULL, mag);
-        const float maxf = __fmul_rn(__int2float_rn(mx), 1.0f / 131072.0f);
-        int maxe = -127;
-        if (maxf != 0.0f) frexpf(maxf, &maxe);
-        const float inv_scale = maxf == 0.0f ? 0.0f : pow2f(13 - maxe);
-        float r = __fmul_rn(__fmul_rn(__int2float_rn(o), 1.0f / 131072.0f), inv_scale);
-        r = __fadd_rn(r, r >= 0.0f ? 0.5f : -0.5f);
-        r = fmaxf(-8191.0f, fminf(8191.0f, r));
-        ta.ao_q[h * kHeadDim + dim] = static_cast<int16_t>(__float2int_rz(r));
-        if (lane == 0) ta.ao_e[h * 4 + part] = maxf == 0.0f ? 0 : static_cast<uint8_t>(maxe + 127);
-    }
-    tok_bar();
+    attn_item(a, S, s.abar, item / kAttnParts, item % kAttnParts, tid, &ta.sync[kSyncAbort],
+              [&] {
+                  wait_counter(ta, &ta.sync[kSyncStage + stage_ordinal(TS_QKV, layer)], tgt_qkv);
+                  t_a1 = clock64();
+                  tl_mark<TR>(ta, layer, 21);
+              },
+              [&](unsigned code) { raise_abort(ta, code); });
+    __syncwarp();
     if (tid == 0) {
         red_release_gpu(&ta.sync[kSyncAtt + layer], 1u);
         trace_add<TR>(ta, TR_ATTN_WAIT, t_a1 - t_a0);

@@ -187,6 +187,33 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def long_context_line(ctx, F, args, stream, ev0, ev1, row, d_logits, peak):
+    """Decode steps deep into the context (the sharded workload decodes to
+    2048): the cache is filled by one prompt prefill of seeded ids, then R
+    steps are timed at each position (each rewrites that position's record
+    and attends over every earlier one)."""
+    out = {"unit": "tokens/s", "positions": {}}
+    last = args.kv_capacity - 1
+    ids = np.random.default_rng(args.seed + 100).integers(3, 32000, size=last).astype(np.int32)
+    ctx.prefill_tokens(0, ids)
+    reps = 10
+    for p in sorted({143, 1023, last}):
+        if p > last:
+            continue
+        ctx.decode_token_async(p, row(int(ids[p % last])), d_logits.data_ptr())
+        ctx.sync()
+        ev0.record(stream)
+        for _ in range(reps):
+            ctx.decode_token_async(p, row(int(ids[p % last])), d_logits.data_ptr())
+        ev1.record(stream)
+        ctx.sync()
+        ms = ev0.elapsed_time(ev1) / reps
+        nbytes = F.token_bytes(p)
+        out["positions"][str(p)] = {"tok_s": 1000.0 / ms, "ms_per_step": ms, "bytes_per_token": nbytes,
+                                    "frac_of_peak": nbytes / (ms * 1e-3) / 1e9 / peak}
+    return out
+
+
 def gemv_line(ctx, F, peak, peak_kind, streams, max_over_ranks):
     """The single INT4 GEMV of the Q-projection shape (4096 x 4096 in four
     input-column bank shards, 8,650,752 B of nibbles and Q1.15 scales): the
@@ -426,6 +453,7 @@ def main():
                                    "positions": n_pf - 1, "ms": ev_ms,
                                    "api": "i4d_eval_nll (token ids in, one NLL per position out)"}
     if not shard:
+        line["long_context"] = long_context_line(ctx, F, args, stream, ev0, ev1, row, d_logits, peak)
         line["gemv"] = gemv_line(ctx, F, peak, peak_kind, streams, max_over_ranks)
         line["attention"] = attention_line(pkg, F, syn, lut, local, peak, peak_kind)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
