@@ -162,6 +162,15 @@ def shard_banks(rank, world):
     return list(range(rank * n, rank * n + n))
 
 
+def combine_bank_partials(partials):
+    """The pair reducers and finalizer of the four bank partials of a GEMV
+    (int4_linear_controller.cpp:1384-1439): y = (p0 + p1) + (p2 + p3) in
+    FP32, the order the token kernel applies to the partials that a sharded
+    group exchanges.  partials: [4][rows] float32, bank order."""
+    p = np.asarray(partials, dtype=np.float32)
+    return (p[0] + p[1]) + (p[2] + p[3])
+
+
 
 def device_arch(device=0):
     """(binary architecture of the loaded token kernel, device compute

@@ -128,6 +128,12 @@ __device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32
         : "memory");
 }
 
+// Bulk prefetch of global memory into L2 (no destination, no completion to
+// wait for); address and size multiples of 16 bytes.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Release/acquire counter operations of the grid hand-offs.  A release
 // reduction after a CTA barrier orders every thread's earlier stores of the
 // CTA before the counter update (the barrier makes them causally precede it).
@@ -136,6 +142,11 @@ __device__ __forceinline__ void red_release_gpu(unsigned* p, unsigned v) {
 }
 __device__ __forceinline__ void red_release_sys(unsigned* p, unsigned v) {
     asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned atom_add_acq_rel_sys(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
 }
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
     unsigned v;

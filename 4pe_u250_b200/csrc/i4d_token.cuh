@@ -58,7 +58,8 @@ constexpr int kSyncExit = 1;
 constexpr int kSyncStage = 2;                   // + ordinal: CTAs whose partials of that stage are stored
 constexpr int kSyncAtt = kSyncStage + 4 * 32 + 1;  // + layer: attention items finished
 constexpr int kSyncEpoch = kSyncAtt + 32;
-constexpr int kSyncWords = kSyncEpoch + 1;
+constexpr int kSyncLocal = kSyncEpoch + 1;      // + ordinal: this rank's CTAs arrived (bank-sharded groups)
+constexpr int kSyncWords = kSyncLocal + 4 * 32 + 1;
 constexpr int kPartialBuf = 4 * 32256;          // floats of one partial buffer [4 banks][rows]
 
 enum TokStage : int { TS_QKV = 0, TS_O, TS_GU, TS_DOWN, TS_LOGITS };
@@ -237,7 +238,8 @@ struct StageDesc {
     int u0, u1;           // this CTA's units in its bank
     int bank;
     int cbase;            // global copy sequence number of the stage's first copy
-    unsigned tgt_stage;   // stage counter value once every CTA of every rank arrived (this token)
+    unsigned tgt_stage;   // stage counter value once every CTA (one rank) or every rank (sharded) arrived
+    unsigned tgt_local;   // sharded: local counter value once every CTA of this rank arrived
     unsigned tgt_att;     // attention counter value once this rank's items finished (this token)
 };
 
@@ -648,11 +650,16 @@ __device__ __forceinline__ void tok_gemv_stage(const TokenArgs& a, const TokSmem
     const long long t_epi = clock64();
     if (tid == 0) {
         tl_mark<TR>(a, tl_layer, 4 * d.st + 3);
-        // Arrive on every rank's counter (one rank: just this one) with a
-        // release reduction; at system scope it also covers the partials
-        // stored to peer memory.
+        // Arrive with a release reduction.  One rank: on the stage counter.
+        // Bank-sharded: on this rank's local counter at system scope (which
+        // also covers the partials this CTA stored in peer memory); the
+        // rank's last CTA, having acquired every local arrival, then makes
+        // the rank's single arrival on every rank's stage counter -- G remote
+        // reductions per stage instead of one per CTA and rank.
         if (a.world > 1) {
-            for (int p = 0; p < a.world; ++p) red_release_sys(&a.peer_sync[p][kSyncStage + ord], 1u);
+            const unsigned old = atom_add_acq_rel_sys(&a.sync[kSyncLocal + ord], 1u);
+            if (old + 1u == d.tgt_local)
+                for (int p = 0; p < a.world; ++p) red_release_sys(&a.peer_sync[p][kSyncStage + ord], 1u);
         } else {
             red_release_gpu(&a.sync[kSyncStage + ord], 1u);
         }
@@ -895,11 +902,14 @@ __global__ void __launch_bounds__(kTokThreads, 1) k_token(const __grid_constant_
     if (a.emb && blockIdx.x == 0 && tid == 0) *a.argmax = 0ull;  // read by the host after the step
     StageDesc d;
     d.bank = a.bank0 + lbank;
-    // Counter targets of this token: counters only grow, by world * grid
-    // arrivals per stage and by this rank's attention items per layer.
+    // Counter targets of this token: counters only grow -- a stage counter by
+    // grid arrivals per token (one rank) or by world rank arrivals (sharded,
+    // with the local counter growing by grid), the attention counter by this
+    // rank's items per layer.
     const unsigned epoch = *reinterpret_cast<const volatile unsigned*>(a.epoch);
     const int att_items = kAttnItems / a.world;
-    d.tgt_stage = (epoch + 1u) * static_cast<unsigned>(a.world) * gridDim.x;
+    d.tgt_stage = (epoch + 1u) * (a.world > 1 ? static_cast<unsigned>(a.world) : gridDim.x);
+    d.tgt_local = (epoch + 1u) * gridDim.x;
     d.tgt_att = (epoch + 1u) * static_cast<unsigned>(att_items);
     d.cbase = 0;
     for (int l = 0; l <= a.layers; ++l) {

@@ -37,7 +37,7 @@ METRIC = "batch-1 INT4 Llama-2-7B decode tokens/s"
 UNIT = "tokens/s"
 PROMPT = 16
 PREFILL_TOKENS = 128  # prompt length of the prefill measurement
-SHARD_WORLDS = (2, 4)  # group sizes of the bank-sharded decode
+SHARD_GROUP_MAX = 4  # ranks of one bank-sharded group (one bank or more per rank)
 
 
 def parse():
@@ -257,8 +257,16 @@ def attention_line(pkg, F, syn, lut, device, peak, peak_kind):
     return out
 
 
+def shard_group_size(world):
+    """Ranks per bank-sharded group: all of them up to 4 (the banks), else
+    groups of 4, each decoding its own stream."""
+    return world if world <= SHARD_GROUP_MAX else SHARD_GROUP_MAX
+
+
 def workload_config(args, world):
-    par = (f"replicas{world}" if args.replicas else f"bank-shard{world}") if world > 1 else "1gpu"
+    g = shard_group_size(world)
+    par = ("1gpu" if world == 1 else f"replicas{world}" if args.replicas else
+           f"bank-shard{g}" if g == world else f"bank-shard{g}x{world // g}")
     return {"workload": "config3: full 32-layer INT4 Llama-2-7B decode, 16-token prompt then greedy, "
                         "KV capacity 2048, seed 2",
             "layers": 32, "kv_capacity": args.kv_capacity, "positions": [args.warmup, args.warmup + args.steps - 1],
@@ -289,20 +297,25 @@ def main():
     assert total <= args.kv_capacity
 
     shard = world > 1 and not args.replicas
-    if shard and world not in SHARD_WORLDS:
-        raise SystemExit(f"bank sharding runs on {SHARD_WORLDS} GPUs; use --replicas for {world}")
+    gsize = shard_group_size(world) if shard else 1
+    if shard and (world % gsize or gsize not in (2, 4)):
+        raise SystemExit(f"bank sharding needs 2, 4 or a multiple of 4 GPUs; use --replicas for {world}")
+    group = None
+    if shard and gsize < world:  # every rank creates every group, in the same order
+        groups = [dist.new_group(list(range(g0, g0 + gsize))) for g0 in range(0, world, gsize)]
+        group = groups[rank // gsize]
     banks = syn.model_banks(32, args.seed)
     emb = syn.embeddings(args.seed)
     lut = F.generate_rope_lut()
     if shard:
-        ctx = pkg.Context(device=local, num_layers=32, kv_capacity=args.kv_capacity, rank=rank, world=world)
+        ctx = pkg.Context(device=local, num_layers=32, kv_capacity=args.kv_capacity, rank=rank % gsize, world=gsize)
     else:
         ctx = pkg.Context(device=local, num_layers=32, kv_capacity=args.kv_capacity)
     ctx.load_banks(banks)
     ctx.load_rope(lut)
     ctx.load_embeddings(emb)
     if shard:
-        ctx.attach_peers()
+        ctx.attach_peers(group)
     stream = torch.cuda.ExternalStream(ctx.stream_handle())
     prompt = np.random.default_rng(args.seed).integers(3, 32000, size=PROMPT).tolist()
 
@@ -384,10 +397,10 @@ def main():
         breakdown = ctx.token_breakdown(mid, row(tokens[mid]))
     peak, peak_kind = measured_peak()
     # A shard streams its banks' share of the bytes: per-GPU bandwidth.
-    achieved = F.token_bytes(mid) / (world if shard else 1) / (tok_ms * 1e-3) / 1e9
+    achieved = F.token_bytes(mid) / gsize / (tok_ms * 1e-3) / 1e9
     traffic = committed_traffic()
 
-    streams = 1 if shard else world  # a sharded group decodes one stream
+    streams = world // gsize  # a sharded group decodes one stream
     value = streams * args.steps / (dev_ms * 1e-3)
     e2e = streams * args.steps / (e2e_ms * 1e-3)
     e2e_logits = streams * args.steps / (e2e_logits_ms * 1e-3)
@@ -395,7 +408,7 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
-        "scaling": "strong" if shard else "weak", "vs_baseline": None, "dtype": "int4xint14/fp32",
+        "scaling": "strong" if shard and gsize == world else "weak", "vs_baseline": None, "dtype": "int4xint14/fp32",
         "data": "synthetic", "config": workload_config(args, world),
         "e2e": {"value": e2e, "unit": UNIT, "api": "i4d_decode_greedy (token id in, next token id out)",
                 "h2d_bytes_per_step": 4 + 4, "d2h_bytes_per_step": 8 + 4, "ms_per_step": e2e_ms / args.steps},
@@ -404,13 +417,13 @@ def main():
                        "h2d_bytes_per_step": 4096 * 4 + 4, "d2h_bytes_per_step": F.PADDED_VOCAB * 4 + 4096 * 4 + 4,
                        "ms_per_step": e2e_logits_ms / args.steps},
         "roofline": {"bound": "hbm", "kernel": "k_token (persistent decode step, 1 launch per token" +
-                               (f" on each of {world} bank shards; achieved = per-GPU share of the bytes)" if shard
+                               (f" on each of {gsize} bank shards; achieved = per-GPU share of the bytes)" if shard
                                 else ")"),
                      "achieved": achieved, "peak": peak,
                      "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback", "unit": "GB/s", "frac": achieved / peak,
                      "traffic": (traffic["bytes_per_launch"] if traffic and not shard else None),
-                     "algorithmic_bytes_per_launch": F.token_bytes(mid) // (world if shard else 1),
+                     "algorithmic_bytes_per_launch": F.token_bytes(mid) // gsize,
                      "kernel_ms": tok_ms},
         "token_roofline": {"bytes_per_token": F.token_bytes(mid), "achieved_gbs":
                            F.token_bytes(mid) / (dev_ms / args.steps * 1e-3) / 1e9,
