@@ -36,7 +36,7 @@ EXPORTS = [
     "i4d_token_timeline", "i4d_create_shard", "i4d_shard_export", "i4d_shard_attach",
     "i4d_decode_greedy", "i4d_argmax", "i4d_sampler_init", "i4d_sample", "i4d_decode_sample",
     "i4d_pack_autoround_matrix", "i4d_pack_fp32_head", "i4d_prefill", "i4d_prefill_tokens", "i4d_eval_nll",
-    "i4d_device_arch", "i4d_profile_gemv", "i4d_profile_attention",
+    "i4d_device_arch", "i4d_profile_gemv", "i4d_profile_attention", "i4d_kv_write_tokens",
 ]
 
 SAMPLER_HOST = 0      # decode_host.cpp:724-868
@@ -115,6 +115,7 @@ def load_library():
         "i4d_swiglu_quant": [P, P, P, P, P],
         "i4d_expf": [P, P, P, ctypes.c_size_t],
         "i4d_device_arch": [ctypes.c_int, P, P],
+        "i4d_kv_write_tokens": [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P],
         "i4d_profile_gemv": [P, ctypes.c_int, ctypes.c_int, P],
         "i4d_profile_attention": [P, ctypes.c_int, ctypes.c_uint32, P, ctypes.c_int, ctypes.c_int, P],
         "i4d_decode_token_async": [P, ctypes.c_uint32, P, P],
@@ -409,6 +410,12 @@ class Context:
         rec = np.ascontiguousarray(record, dtype=np.uint8)
         assert rec.size == formats.KV_RECORD_BYTES
         self._check(self._L.i4d_kv_write(self._h, bank, layer, local_head, token, rec.ctypes.data))
+
+    def kv_write_tokens(self, bank, layer, local_head, token0, records):
+        """Records of tokens token0 .. token0 + n - 1 of one head ([n][320] bytes)."""
+        rec = np.ascontiguousarray(records, dtype=np.uint8).reshape(-1, formats.KV_RECORD_BYTES)
+        self._check(self._L.i4d_kv_write_tokens(self._h, bank, layer, local_head, token0, rec.shape[0],
+                                                rec.ctypes.data))
 
     def sync(self):
         self._check(self._L.i4d_sync(self._h))

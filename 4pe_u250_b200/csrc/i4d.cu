@@ -1313,6 +1313,18 @@ i4d_status i4d_kv_write(i4d_ctx* c, int bank, int layer, int lh, int token, cons
     return I4D_OK;
 }
 
+i4d_status i4d_kv_write_tokens(i4d_ctx* c, int bank, int layer, int lh, int token0, int n, const void* records) {
+    if (!c || !records || n <= 0) return c ? fail(c, I4D_ERR_ARG, "bad records") : I4D_ERR_ARG;
+    size_t off, last;
+    i4d_status st = kv_addr(c, bank, layer, lh, token0, &off);
+    if (st == I4D_OK) st = kv_addr(c, bank, layer, lh, token0 + n - 1, &last);
+    if (st != I4D_OK) return st;
+    CK(cudaSetDevice(c->device));
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaMemcpy(c->d_kv + off, records, static_cast<size_t>(n) * 320, cudaMemcpyHostToDevice));
+    return I4D_OK;
+}
+
 i4d_status i4d_sync(i4d_ctx* c) {
     if (!c) return I4D_ERR_ARG;
     CK(cudaSetDevice(c->device));

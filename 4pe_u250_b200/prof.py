@@ -4,6 +4,9 @@
   python -m 4pe_u250_b200.prof decode --layers 2         a few decode steps
   python -m 4pe_u250_b200.prof prefill --layers 32 --tokens 16
                                                          two prompt batches
+  python -m 4pe_u250_b200.prof attention --context 4096 --reps 3
+                                                         attention steps of one
+                                                         layer over a filled cache
 
 Each builds a seeded synthetic model with only the layers it needs, so the
 device footprint stays at a few hundred MB.
@@ -14,17 +17,52 @@ import importlib
 import numpy as np
 
 
+def kv_records(n, seed):
+    """n synthetic KV records of one head: N(0, 1) K and V taken to Q15.17 and
+    quantised by the reference's shift quantiser (the layout of
+    swiftkv_attention.hpp:21-36), built in numpy."""
+    rng = np.random.default_rng(seed)
+    out = np.zeros((n, 320), np.uint8)
+    for part, base in ((0, 64), (1, 192)):
+        raw = np.clip(np.round(rng.standard_normal((n, 128)) * 131072.0), -2**31, 2**31 - 1).astype(np.int64)
+        g = raw.reshape(n, 4, 32)
+        mx = np.abs(g).max(axis=2)
+        msb = np.floor(np.log2(np.maximum(mx, 1))).astype(np.int64)
+        shift = np.where(mx == 0, 0, np.maximum(msb - 6, 0))
+        mag = np.abs(g)
+        half = np.where(shift > 0, 1 << np.maximum(shift - 1, 0), 0)[:, :, None]
+        q = np.minimum((mag + half) >> shift[:, :, None], 127) * np.sign(g)
+        out[:, base:base + 128] = q.reshape(n, 128).astype(np.int8).view(np.uint8)
+        meta = np.zeros(n, np.uint64)
+        for k in range(4):
+            meta |= shift[:, k].astype(np.uint64) << np.uint64(5 * k + 20 * part)
+        out[:, 0:8] |= meta.view(np.uint8).reshape(n, 8)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemv", "decode", "prefill"])
+    ap.add_argument("what", choices=["gemv", "decode", "prefill", "attention"])
     ap.add_argument("--mode", type=int, default=4)
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--tokens", type=int, default=4)
+    ap.add_argument("--context", type=int, default=4096)
     a = ap.parse_args()
     pkg = importlib.import_module("4pe_u250_b200")
     synth = importlib.import_module("4pe_u250_b200.synth")
     F = pkg.formats
+    if a.what == "attention":
+        import torch
+        with pkg.Context(num_layers=1, kv_capacity=a.context) as ctx:
+            ctx.load_rope()
+            for head in range(32):
+                ctx.kv_write_tokens(head // 8, 0, head % 8, 0, kv_records(a.context - 1, 7 + head))
+            rng = np.random.default_rng(3)
+            qkv = torch.from_numpy(np.round(rng.standard_normal(3 * 4096) * 131072.0).astype(np.int32)).cuda()
+            print(ctx.profile_attention(0, a.context - 1, qkv.data_ptr(), 0, a.reps))
+        print("ok")
+        return
     banks = synth.model_banks(a.layers, 5)
     with pkg.Context(num_layers=a.layers, kv_capacity=64) as ctx:
         ctx.load_banks(banks)

@@ -288,6 +288,13 @@ i4d_status i4d_kv_reset(i4d_ctx* ctx);
  * (swiftkv_attention.hpp:21-36): bank, layer, local head 0..7, token. */
 i4d_status i4d_kv_read(i4d_ctx* ctx, int bank, int layer, int local_head, int token, void* record);
 i4d_status i4d_kv_write(i4d_ctx* ctx, int bank, int layer, int local_head, int token, const void* record);
+/* Writes the records of tokens [token0, token0 + n) of one (bank, layer,
+ * local head) from n x 320 contiguous host bytes, in one copy: restoring a
+ * saved cache, or a synthetic context for the attention measurements.  The
+ * HLS host fills the cache through its KV buffer object the same way
+ * (decode_host.cpp:1291-1294). */
+i4d_status i4d_kv_write_tokens(i4d_ctx* ctx, int bank, int layer, int local_head, int token0, int n,
+                               const void* records);
 /* Waits for all work on the context. */
 i4d_status i4d_sync(i4d_ctx* ctx);
 
