@@ -29,7 +29,6 @@ namespace i4d {
 constexpr int kItemWarps = 18;
 constexpr int kItemThreads = 32 * kItemWarps;
 constexpr int kAttnParts = 4;              // 32-dimension parts per head
-constexpr int kKvPrefetch = 4;             // KV tiles pulled into L2 ahead of the shared-memory copies
 constexpr int kAttnItems = kHeads * kAttnParts;
 
 struct TileInfo {
@@ -163,10 +162,6 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, const AttnItemSmem&
         fence_proxy_async_smem();
         mbar_arrive_expect_tx(&abar[0], cnt * 320);
         bulk_g2s(S.tile[0], head_base, cnt * 320, &abar[0]);
-        // The copies of later tiles then find their records in L2: only one
-        // tile can be in flight into shared memory.
-        for (int t = 1; t <= kKvPrefetch && t < ntiles; ++t)
-            bulk_prefetch_l2(head_base + static_cast<size_t>(t) * kTile * 320, min(kTile, n - t * kTile) * 320);
         wait_input();
     }
     item_bar();
@@ -245,9 +240,6 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, const AttnItemSmem&
                     mbar_arrive_expect_tx(&abar[p ^ 1], c2 * 320);
                     bulk_g2s(S.tile[p ^ 1], head_base + static_cast<size_t>(T0 + kTile) * 320, c2 * 320,
                              &abar[p ^ 1]);
-                    const int tp = k + 1 + kKvPrefetch;
-                    if (tp < ntiles)
-                        bulk_prefetch_l2(head_base + static_cast<size_t>(tp) * kTile * 320, min(kTile, n - tp * kTile) * 320);
                 }
                 if (wtid < 32) psum[wtid] = 0;
                 item_mbar_wait(&abar[p], static_cast<uint32_t>((k >> 1) & 1), abort_word, fail);

@@ -128,12 +128,6 @@ __device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32
         : "memory");
 }
 
-// Bulk prefetch of global memory into L2 (no destination, no completion to
-// wait for); address and size multiples of 16 bytes.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 // Release/acquire counter operations of the grid hand-offs.  A release
 // reduction after a CTA barrier orders every thread's earlier stores of the
 // CTA before the counter update (the barrier makes them causally precede it).

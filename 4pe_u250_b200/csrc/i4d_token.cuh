@@ -486,7 +486,6 @@ __device__ __forceinline__ void tok_units(const TokenArgs& a, const TokSmem& s, 
     const int ord = stage_ordinal(d.st, d.layer);
     const bool tr = TR && a.trace != nullptr;
     int par = 0;
-    bool stored = false;
     // With 4 chunks per unit a warp always takes chunk j: its group's
     // activations stay in registers for the whole stage.
     uint4 h0, h1, l0, l1;
@@ -566,7 +565,6 @@ __device__ __forceinline__ void tok_units(const TokenArgs& a, const TokSmem& s, 
             // Bank sharding: every rank receives every bank's partials.
             for (int p = 0; p < a.world; ++p)
                 if (a.peer_partials[p] != a.partials) a.peer_partials[p][(ord & 1) * kPartialBuf + off] = acc;
-            stored = true;
         } else {
             qacc[row] = acc;
         }
@@ -578,13 +576,6 @@ __device__ __forceinline__ void tok_units(const TokenArgs& a, const TokSmem& s, 
             wt.chain_wait += c3 - c2;
             wt.chain += clock64() - c3;
         }
-    }
-    // A warp that stored partials waits here for them to be performed, while
-    // other warps of the CTA are still computing; the stage's release
-    // arrival after the CTA barrier then finds them done.
-    if (stored) {
-        if (a.world > 1) __threadfence_system();
-        else __threadfence();
     }
 }
 
