@@ -392,7 +392,7 @@ class Context:
 
     def token_timeline(self, position, residual_in_dev_ptr, layer, detail=False):
         """[CTAs, 162] global-timer stamps (ns) and counts of one layer (see i4d_token_timeline)."""
-        out = np.zeros((1024, 210), np.uint64)
+        out = np.zeros((1024, 218), np.uint64)
         n = ctypes.c_int(0)
         self._check(self._L.i4d_token_timeline(self._h, position, residual_in_dev_ptr, layer, int(bool(detail)),
                                                out.ctypes.data, out.shape[0], ctypes.byref(n)))

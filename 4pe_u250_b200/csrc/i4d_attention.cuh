@@ -58,25 +58,30 @@ constexpr int kTile = 64;       // tokens per shared-memory tile
 constexpr int kMaxSeg = 12;     // rescale events handled by the segmented path (74 KB: 3 CTAs per SM)
 
 // Fixed-point exp of a non-positive Q15.17 value (emulator:575-595,
-// swiftkv_attention.cpp:199-260).
+// swiftkv_attention.cpp:199-260), in 32-bit steps: for -2^22 < x <= 0 the
+// product x * log2e_q21 has at most 44 bits, its round-half-even shift by 21
+// fits in 24 bits (so the reference's 24-bit wrap changes nothing), the
+// interpolation product delta * rem has at most 38 bits and the final
+// rounding add stays below 2^32.  Equal to the 64-bit statement of the
+// reference on every x in (-2^22, 0] (checked exhaustively on the host).
 __device__ __forceinline__ uint32_t exp_negative_q17(int32_t x, const uint32_t* lut, int log2e_q21) {
     if (x >= 0) return 1u << 17;
     if (x <= -(32 << 17)) return 0;
-    long long l2 = rshift_even(static_cast<long long>(x) * log2e_q21, 21);
-    l2 = wrap_bits(l2, 24);
-    const int ex = static_cast<int>(l2 >> 17);
-    const int32_t fr = static_cast<int32_t>(l2 - (static_cast<long long>(ex) << 17));
-    const unsigned idx = static_cast<unsigned>(fr) >> 12;
-    const unsigned rem = static_cast<unsigned>(fr) & 0xfffu;
+    const long long p = static_cast<long long>(x) * log2e_q21;
+    const uint32_t lo = static_cast<uint32_t>(p), hi = static_cast<uint32_t>(static_cast<unsigned long long>(p) >> 32);
+    int32_t l2 = static_cast<int32_t>(__funnelshift_r(lo, hi, 21));
+    const uint32_t r = lo & 0x1FFFFFu;
+    l2 += static_cast<int32_t>((r > 0x100000u) | ((r == 0x100000u) & static_cast<uint32_t>(l2)));
+    const int ex = l2 >> 17;  // <= 0
+    const uint32_t fr = static_cast<uint32_t>(l2) & 0x1FFFFu;
+    const uint32_t idx = fr >> 12, rem = fr & 0xFFFu;
     const uint32_t base = lut[idx];
     const uint32_t delta = lut[idx + 1] - base;
-    const uint32_t interp =
-        base + static_cast<uint32_t>((static_cast<unsigned long long>(delta) * rem + (1u << 11)) >> 12);
-    const int sh = 13 - ex;
-    unsigned long long out = 0;
-    if (sh <= 0) out = static_cast<unsigned long long>(interp) << (-sh);
-    else if (sh < 32) out = (static_cast<unsigned long long>(interp) + (1ull << (sh - 1))) >> sh;
-    return static_cast<uint32_t>(out) & ((1u << 18) - 1u);
+    const unsigned long long w = static_cast<unsigned long long>(delta) * rem + (1u << 11);
+    const uint32_t interp = base + static_cast<uint32_t>(w >> 12);
+    const int sh = 13 - ex;  // >= 13
+    if (sh >= 32) return 0;
+    return ((interp + (1u << (sh - 1))) >> sh) & ((1u << 18) - 1u);
 }
 
 // KV group shift: max(0, msb(max |v|) - 6) (swiftkv_attention.cpp:358-389).
@@ -125,7 +130,7 @@ __device__ __forceinline__ uint8_t* kv_record(const AttnArgs& a, int head, int t
 }
 
 struct AttnSmem {
-    uint8_t* tile[2];
+    uint8_t* tiles;      // two adjacent tiles of kTile records (a pointer array indexed by parity would live in local memory)
     uint8_t* cur;        // current token's record
     uint64_t* bar;       // [2]
     uint32_t* lut;       // [33]
@@ -157,8 +162,7 @@ __host__ __device__ inline size_t attn_smem_bytes() {
 
 __device__ __forceinline__ AttnSmem attn_carve(uint8_t* p) {
     AttnSmem s;
-    s.tile[0] = p;
-    s.tile[1] = p + kTile * 320;
+    s.tiles = p;
     s.cur = p + 2 * kTile * 320;
     p += attn_align16(2 * kTile * 320 + 320);
     s.bar = reinterpret_cast<uint64_t*>(p);
@@ -288,13 +292,13 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constan
     if (!bad && tid == 0 && a.phase == 0) {
         const int cnt = min(kTile, n);
         mbar_arrive_expect_tx(&S.bar[0], cnt * 320);
-        bulk_g2s(S.tile[0], head_base, cnt * 320, &S.bar[0]);
+        bulk_g2s(S.tiles, head_base, cnt * 320, &S.bar[0]);
     }
     pdl_wait();
     if (!bad && tid == 0 && a.phase == 2) {
         const int cnt = min(kTile, n);
         mbar_arrive_expect_tx(&S.bar[0], cnt * 320);
-        bulk_g2s(S.tile[0], head_base, cnt * 320, &S.bar[0]);
+        bulk_g2s(S.tiles, head_base, cnt * 320, &S.bar[0]);
     }
     if (bad) {
         if (tid == 0) atomicOr(a.err, kErrArg);
@@ -378,12 +382,12 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constan
     // ---- tiles of kTile cached records ----
     for (int k = 0; k < ntiles; ++k) {
         const int T0 = k * kTile, cnt = min(kTile, n - T0);
-        uint8_t* buf = S.tile[k & 1];
+        uint8_t* buf = S.tiles + (k & 1) * (kTile * 320);
         if (tid == 0 && k + 1 < ntiles) {
             fence_proxy_async_smem();
             const int c2 = min(kTile, n - T0 - kTile);
             mbar_arrive_expect_tx(&S.bar[(k + 1) & 1], c2 * 320);
-            bulk_g2s(S.tile[(k + 1) & 1], head_base + static_cast<size_t>(T0 + kTile) * 320, c2 * 320,
+            bulk_g2s(S.tiles + ((k + 1) & 1) * (kTile * 320), head_base + static_cast<size_t>(T0 + kTile) * 320, c2 * 320,
                      &S.bar[(k + 1) & 1]);
         }
         mbar_wait(&S.bar[k & 1], static_cast<uint32_t>((k >> 1) & 1), a.err, kErrWaitFull);

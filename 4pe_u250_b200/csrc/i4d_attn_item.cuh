@@ -6,20 +6,24 @@
 // The current token: q/k/v of the head (from the QKV bank partials or given
 // directly), Q15.17, adjacent-pair RoPE, the KV shift quantiser and the
 // 320-byte record (part 0 writes it to the cache).  Then the cache is
-// scanned in tiles of kTile records, double-buffered by bulk copies:
+// scanned in tiles of kTile records, double-buffered by bulk copies; per
+// tile the 16 worker warps compute
 //  * scores: exact integer dot products (16 warps x 4 tokens, 8 lanes each);
-//  * one warp: running maximum before each token (a prefix maximum carried
-//    across tiles), the softmax coefficients c_t, the tokens where the
-//    maximum grows ("events"), the tile's sum of c_t over the other tokens
-//    and a bound on the magnitudes of their state terms;
-//  * state terms mulq17(v_t, c_t) per (token, dimension) in 32-bit form, and
-//    per dimension the tile's sum over the non-event tokens.
+//  * coefficients (two warps, one token per lane): the running maximum before
+//    each token is a prefix maximum carried across tiles, so every softmax
+//    coefficient c_t is known at once, with the tokens where the maximum
+//    grows ("events", and token 0), the tile's sum of c_t over its other
+//    tokens and a bound on the magnitudes of their state terms;
+//  * state terms mulq17(v_t, c_t) per (token, dimension) in 32-bit form (v_t
+//    itself at events).
 // Warp 0 (lane = dimension) then applies the tile, one tile behind the
-// workers: a tile with no event whose bound shows that no step of the
-// saturating chain can saturate adds its sum in one step (integer addition
-// is associative; the normaliser adds modulo 2^30); any other tile runs the
-// reference's token-order recurrence over the tile's precomputed terms.
-// Either way the state is bit-exact with the sequential scan.
+// workers.  When the tile's bound shows that no step of the reference's
+// saturating chain can saturate, the runs of non-event tokens are added as
+// plain sums (integer addition is associative; the normaliser adds modulo
+// 2^30) and only the events (rescale, then add v) are applied one by one;
+// otherwise the reference's token-order recurrence runs over the
+// precomputed terms.  Either way the state is bit-exact with the sequential
+// scan.
 #pragma once
 
 #include "i4d_attention.cuh"
@@ -31,34 +35,39 @@ constexpr int kItemThreads = 32 * kItemWarps;
 constexpr int kAttnParts = 4;              // 32-dimension parts per head
 constexpr int kAttnItems = kHeads * kAttnParts;
 
+constexpr int kTileBytes = kTile * 320;
+
 struct TileInfo {
-    unsigned long long ev;     // nonzero: the tile holds an event (or token 0)
-    unsigned long long zsum;   // sum of c_t over the tile's non-event tokens
-    unsigned long long bound;  // sum of the bounds on |term| over the same tokens
-    unsigned long long pad;
+    unsigned evm[4];            // bit t of word w: token 32w + t of the window is an event (token 0 included)
+    unsigned long long bound;   // bound on sum |term_t| + sum |v_e| over the window (>= 2^40: unbounded)
+    unsigned zsum;              // sum of c_t over the window's non-event tokens
+    unsigned runs;              // nonzero: each run's sums are in place (the workers' run pass ran)
 };
 
 struct AttnItemSmem {
-    uint8_t* tile[2];     // kTile records each
+    // Two tile buffers of kTile records, adjacent: buffer b at tiles + b * kTileBytes.
+    // (A pointer array indexed by the runtime parity would put the whole
+    // carve in local memory.)
+    uint8_t* tiles;
     uint8_t* cur;         // current token's record
     int32_t* score;       // [kTile]
     uint32_t* coef;       // [2][kTile]: c | event << 31, by tile parity
     int32_t* tbuf;        // [2][kTile][32]: state terms of this part (v_t itself at events)
-    int32_t* psum;        // [2][32]: per dimension, the tile's sum of the non-event terms
     TileInfo* tinfo;      // [2]
+    uint32_t* zseg;       // [kZseg]: per run of non-event tokens (in token order), the sum of its c_t
     uint32_t* lut;        // [33] exp2 table
     int32_t* qrot;        // [128]
     unsigned long long* meta;  // current record's shift word
     int* misc;            // [16]
 };
 
-constexpr size_t kAttnItemBytes = 2 * kTile * 320 + 320 + kTile * 4 + 2 * kTile * 4 + 2 * kTile * 32 * 4 + 2 * 32 * 4 +
-                                  2 * sizeof(TileInfo) + 144 + 128 * 4 + 16 + 16 * 4;
+constexpr int kZseg = 2 * kTile + 4;       // runs of a window: one more than its events (by parity: 2 x (kTile + 2))
+constexpr size_t kAttnItemBytes = 2 * kTile * 320 + 320 + kTile * 4 + 2 * kTile * 4 + 2 * kTile * 32 * 4 +
+                                  2 * sizeof(TileInfo) + kZseg * 4 + 144 + 128 * 4 + 16 + 16 * 4;
 
 __device__ __forceinline__ AttnItemSmem attn_item_carve(uint8_t* p) {
     AttnItemSmem s;
-    s.tile[0] = p;
-    s.tile[1] = p + kTile * 320;
+    s.tiles = p;
     p += 2 * kTile * 320;
     s.cur = p;
     p += 320;
@@ -68,10 +77,10 @@ __device__ __forceinline__ AttnItemSmem attn_item_carve(uint8_t* p) {
     p += 2 * kTile * 4;
     s.tbuf = reinterpret_cast<int32_t*>(p);
     p += 2 * kTile * 32 * 4;
-    s.psum = reinterpret_cast<int32_t*>(p);
-    p += 2 * 32 * 4;
     s.tinfo = reinterpret_cast<TileInfo*>(p);
     p += 2 * sizeof(TileInfo);
+    s.zseg = reinterpret_cast<uint32_t*>(p);
+    p += kZseg * 4;
     s.lut = reinterpret_cast<uint32_t*>(p);
     p += 144;
     s.qrot = reinterpret_cast<int32_t*>(p);
@@ -101,10 +110,13 @@ __device__ __forceinline__ int32_t term_q17(int v8, uint32_t shift, uint32_t c) 
     return (p + ((1 << (s - 1)) - 1) + ((p >> s) & 1)) >> s;
 }
 
-// Upper bound on |term_q17(v8, shift, c)| over every |v8| <= 127.
-__device__ __forceinline__ unsigned long long term_bound(uint32_t shift, uint32_t c) {
-    if (shift > 24) return 1ull << 40;
-    return ((static_cast<unsigned long long>(127u * c) << shift) >> 17) + 1ull;
+// Upper bound on |term_q17(v8, shift, c)| over every int8 v8, and on |v8 <<
+// shift| (an event's value, c = 2^17), at most 2^25 each; anything larger
+// reads as 2^40 (no bound).
+__device__ __forceinline__ uint32_t term_bound(uint32_t shift, uint32_t c) {
+    if (shift > 24) return 1u << 31;
+    const unsigned long long b = ((static_cast<unsigned long long>(128u * c) << shift) >> 17) + 1ull;
+    return b > (1ull << 25) ? (1u << 31) : static_cast<uint32_t>(b);
 }
 
 // Bounded mbarrier wait of an item; `fail(code)` records a timeout, and a
@@ -128,9 +140,13 @@ __device__ __forceinline__ bool item_mbar_wait(uint64_t* bar, uint32_t parity, c
 // copy is issued (the token kernel waits there for the QKV stage).  Warp 0
 // ends with the item's 32 outputs stored (a.out_q, a.out_e); the caller
 // publishes them.
-template <class WaitInput, class Fail>
-__device__ __forceinline__ void attn_item(const AttnArgs& a, const AttnItemSmem& S, uint64_t* abar, int h, int part,
-                                          int tid, const unsigned* abort_word, WaitInput wait_input, Fail fail) {
+// `mark(k)` runs on thread 0 at the item's internal milestones (k = 0: the
+// current token done; 1 + i: tile loop iteration i done, i < 3; 4: all tiles
+// applied; 5: outputs stored).
+template <class WaitInput, class Fail, class Mark>
+__device__ __forceinline__ void attn_item(const AttnArgs a, const AttnItemSmem S, uint64_t* abar, int h, int part,
+                                          int tid, const unsigned* abort_word, WaitInput wait_input, Fail fail,
+                                          Mark mark) {
     const unsigned FULL = 0xffffffffu;
     const uint32_t M30 = (1u << 30) - 1u;
     const int warp = tid >> 5, lane = tid & 31;
@@ -143,7 +159,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, const AttnItemSmem&
         mbar_init(&abar[0], 1);
         mbar_init(&abar[1], 1);
         mbar_fence_init();
-        misc[0] = INT32_MIN;  // running maximum of the tiles scanned so far
+        misc[2] = INT32_MIN;  // running maximum before tile k: misc[2 + (k & 1)]
         *S.meta = 0ull;
     }
     if (tid < 33) S.lut[tid] = a.exp2_q30[tid];
@@ -155,13 +171,21 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, const AttnItemSmem&
         rope_s = a.rope_sin[pos * 64 + (tid >> 1)];
     }
     item_bar();
+    // A context of up to 2 * kTile tokens is one window over both (adjacent)
+    // tile buffers, scanned in one pass; a longer one goes tile by tile.
+    const bool one = n <= 2 * kTile;
     if (tid == 0) {
         // Cached records of earlier tokens are final: stream the first tile
-        // while the projections are still being produced.
+        // (both, for a single window) while the projections are still being
+        // produced.
         const int cnt = min(kTile, n);
         fence_proxy_async_smem();
         mbar_arrive_expect_tx(&abar[0], cnt * 320);
-        bulk_g2s(S.tile[0], head_base, cnt * 320, &abar[0]);
+        bulk_g2s(S.tiles, head_base, cnt * 320, &abar[0]);
+        if (one && n > kTile) {
+            mbar_arrive_expect_tx(&abar[1], (n - kTile) * 320);
+            bulk_g2s(S.tiles + kTileBytes, head_base + static_cast<size_t>(kTile) * 320, (n - kTile) * 320, &abar[1]);
+        }
         wait_input();
     }
     item_bar();
@@ -209,16 +233,27 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, const AttnItemSmem&
         reinterpret_cast<unsigned long long*>(S.cur)[tid] = m;
         if (part == 0) reinterpret_cast<unsigned long long*>(grec)[tid] = m;
     }
-    // q of this lane's 16-value half-group, split into 16-bit halves for dp2a.
+    // q split into 16-bit halves for dp2a, per 16-value half-group hg and
+    // pair i: qs[8 hg + i] (high halves) and qs[64 + 8 hg + i] (low halves),
+    // in place of qrot.  It stays in shared memory: held in registers
+    // through the scan it would be demoted to local memory, whose lines the
+    // token kernel's small L1 does not keep.
     const int hg = lane & 7;
-    uint32_t qh2[8], ql2[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int32_t x0 = S.qrot[hg * 16 + 2 * i], x1 = S.qrot[hg * 16 + 2 * i + 1];
-        qh2[i] = (static_cast<uint32_t>(x0 >> 16) & 0xffffu) | (static_cast<uint32_t>(x1 >> 16) << 16);
-        ql2[i] = (static_cast<uint32_t>(x0) & 0xffffu) | (static_cast<uint32_t>(x1) << 16);
+    {
+        uint32_t qh = 0, ql = 0;
+        if (tid < 64) {
+            const int32_t x0 = S.qrot[2 * tid], x1 = S.qrot[2 * tid + 1];
+            qh = (static_cast<uint32_t>(x0 >> 16) & 0xffffu) | (static_cast<uint32_t>(x1 >> 16) << 16);
+            ql = (static_cast<uint32_t>(x0) & 0xffffu) | (static_cast<uint32_t>(x1) << 16);
+        }
+        item_bar();
+        if (tid < 64) {
+            reinterpret_cast<uint32_t*>(S.qrot)[tid] = qh;
+            reinterpret_cast<uint32_t*>(S.qrot)[64 + tid] = ql;
+        }
     }
     item_bar();
+    if (tid == 0) mark(0);
 
     const int dl = lane;                     // dimension inside this part
     const int dim = part * 32 + dl;
@@ -226,177 +261,292 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, const AttnItemSmem&
     int32_t st = 0;                          // warp 0: the state of dimension `dim`
     uint32_t z = 1u << 17;                   // warp 0: the normaliser (every lane)
     const int wtid = tid - 64, wcw = warp - 2;
-    for (int k = 0; k <= ntiles; ++k) {
+    const int nwin = one ? 1 : ntiles;       // windows: W tokens each
+    const int W = one ? 2 * kTile : kTile;
+    static_assert(kTile == 64, "a window's event masks are 32-token words, at most four");
+    // Window k onto the state (warp 0, lane = dimension), in token order.
+    auto apply = [&](int k) {
+        const int p = one ? 0 : k & 1, T0 = k * W, cnt = min(W, n - T0);
+        const TileInfo& ti = S.tinfo[p];
+        const uint32_t* coef = S.coef + p * kTile;
+        const int32_t* tbuf = S.tbuf + p * kTile * 32 + dl;
+        const uint32_t* zseg = S.zseg + (one ? 0 : p * (kTile + 2));
+        const long long mag = st < 0 ? -static_cast<long long>(st) : st;
+        if (ti.runs && static_cast<unsigned long long>(mag) + ti.bound <= static_cast<unsigned long long>(INT32_MAX)) {
+            // |state| stays below |st| + bound <= 2^31 - 1 at every step, so
+            // no step saturates: each run of non-event tokens adds as one
+            // exact sum (left by the workers in the run's last term slot,
+            // its c_t sum in zseg), and only the events are applied one by
+            // one, their operands loaded one event ahead.
+            // Event masks in two 64-bit registers (an array indexed in the
+            // loop would live in local memory).
+            unsigned long long mlo = static_cast<unsigned long long>(ti.evm[0]) |
+                                     (static_cast<unsigned long long>(ti.evm[1]) << 32);
+            unsigned long long mhi = static_cast<unsigned long long>(ti.evm[2]) |
+                                     (static_cast<unsigned long long>(ti.evm[3]) << 32);
+            auto next_event = [&]() -> int {  // position of the next event, or cnt
+                if (mlo) {
+                    const int e = __ffsll(static_cast<long long>(mlo)) - 1;
+                    mlo &= mlo - 1ull;
+                    return e;
+                }
+                if (mhi) {
+                    const int e = 64 + __ffsll(static_cast<long long>(mhi)) - 1;
+                    mhi &= mhi - 1ull;
+                    return e;
+                }
+                return cnt;
+            };
+            int prev = -1, e = next_event(), i = 0;
+            int32_t sv = e > prev + 1 ? tbuf[(e - 1) * 32] : 0;
+            int32_t vv = e < cnt ? tbuf[e * 32] : 0;
+            uint32_t cv = e < cnt ? coef[e] & 0x7fffffffu : 0u;
+            uint32_t zv = zseg[0];
+            for (;;) {
+                const int e2 = e < cnt ? next_event() : cnt;
+                // The next event's operands (independent of the state chain).
+                const int32_t sv2 = e2 < cnt || e2 > e + 1 ? (e2 > e + 1 ? tbuf[(e2 - 1) * 32] : 0) : 0;
+                const int32_t vv2 = e2 < cnt ? tbuf[e2 * 32] : 0;
+                const uint32_t cv2 = e2 < cnt ? coef[e2] & 0x7fffffffu : 0u;
+                const uint32_t zv2 = zseg[min(i + 1, kZseg - 1)];
+                st += sv;
+                z = (z + zv) & M30;
+                if (e >= cnt) break;
+                if (T0 + e == 0) {
+                    st = vv;
+                    z = 1u << 17;
+                } else {  // new maximum: rescale, then add v (emulator:674-685)
+                    st = mulq17_w(st, cv) + vv;
+                    z = ((static_cast<uint32_t>(mulq17_w(static_cast<int32_t>(z), cv)) & M30) + (1u << 17)) & M30;
+                }
+                prev = e;
+                e = e2;
+                sv = sv2;
+                vv = vv2;
+                cv = cv2;
+                zv = zv2;
+                ++i;
+            }
+        } else {
+            // The reference's recurrence (emulator:656-685), saturating at
+            // every step, with each term recomputed from the cached record
+            // (the window's buffers may already hold later records).
+            for (int tl = 0; tl < cnt; ++tl) {
+                const uint32_t cf = coef[tl];
+                const uint32_t cc = cf & 0x7fffffffu;
+                const uint8_t* rec = T0 + tl == pos ? S.cur : kv_record(a, h, T0 + tl);
+                const unsigned long long meta = *reinterpret_cast<const volatile unsigned long long*>(rec);
+                const uint32_t sh = static_cast<uint32_t>((meta >> vbit) & 31u);
+                const int v8 = static_cast<int8_t>(*reinterpret_cast<const volatile uint8_t*>(rec + 192 + dim));
+                const int32_t vfull = static_cast<int32_t>(static_cast<uint32_t>(v8) << sh);
+                if (cf >> 31) {
+                    if (T0 + tl == 0) {
+                        st = vfull;
+                        z = 1u << 17;
+                    } else {  // new maximum: rescale, then add v (emulator:674-685)
+                        st = add_sat32(mulq17_w(st, cc), vfull);
+                        z = ((static_cast<uint32_t>(mulq17_w(static_cast<int32_t>(z), cc)) & M30) + (1u << 17)) & M30;
+                    }
+                } else {
+                    st = add_sat32(st, term_q17(v8, sh, cc));
+                    z = (z + cc) & M30;
+                }
+            }
+        }
+    };
+    for (int k = 0; k <= nwin; ++k) {
         if (warp >= 2) {
-            if (k < ntiles) {
-                const int T0 = k * kTile, cnt = min(kTile, n - T0), p = k & 1;
-                uint8_t* buf = S.tile[p];
+            if (k < nwin) {
+                const int T0 = k * W, cnt = min(W, n - T0), p = one ? 0 : k & 1;
+                const int rounds = (cnt + 63) >> 6;  // 64-token rounds of the worker warps
+                uint8_t* buf = S.tiles + p * kTileBytes;
                 uint32_t* coef = S.coef + p * kTile;
                 int32_t* tbuf = S.tbuf + p * kTile * 32;
-                int32_t* psum = S.psum + p * 32;
-                if (wtid == 0 && k + 1 < ntiles) {  // buffer p ^ 1 was last read in iteration k - 1
+                TileInfo& ti = S.tinfo[p];
+                if (!one && wtid == 0 && k + 1 < ntiles) {  // buffer p ^ 1 was last read in iteration k - 1
                     fence_proxy_async_smem();
                     const int c2 = min(kTile, n - T0 - kTile);
                     mbar_arrive_expect_tx(&abar[p ^ 1], c2 * 320);
-                    bulk_g2s(S.tile[p ^ 1], head_base + static_cast<size_t>(T0 + kTile) * 320, c2 * 320,
+                    bulk_g2s(S.tiles + (p ^ 1) * kTileBytes, head_base + static_cast<size_t>(T0 + kTile) * 320, c2 * 320,
                              &abar[p ^ 1]);
                 }
-                if (wtid < 32) psum[wtid] = 0;
+                if (wtid == 0) {  // this parity's summary was last read by warp 0 in iteration k - 1
+                    ti.zsum = 0u;
+                    ti.bound = 0ull;
+                }
+                if (wtid < 4) ti.evm[wtid] = 0u;  // words past the window's last token stay empty
                 item_mbar_wait(&abar[p], static_cast<uint32_t>((k >> 1) & 1), abort_word, fail);
-                if (pos < T0 + cnt) {  // the tile holds the current token: use the fresh record
+                if (one && cnt > kTile) item_mbar_wait(&abar[1], 0u, abort_word, fail);
+                if (pos < T0 + cnt) {  // the window holds the current token: use the fresh record
                     if (wtid < 80)
                         reinterpret_cast<uint32_t*>(buf + (pos - T0) * 320)[wtid] =
                             reinterpret_cast<const uint32_t*>(S.cur)[wtid];
                     item_wbar();
                 }
-                {   // scores (emulator:633-655): 16 warps x 4 tokens, 8 lanes per token
-                    const int tl = wcw * 4 + (lane >> 3);
-                    long long hv = 0;
-                    if (tl < cnt) {
-                        const uint8_t* rec = buf + tl * 320;
-                        const uint4 kw = *reinterpret_cast<const uint4*>(rec + 64 + hg * 16);
-                        const unsigned long long meta = *reinterpret_cast<const unsigned long long*>(rec);
-                        const uint32_t sh = static_cast<uint32_t>((meta >> (5 * (hg >> 1))) & 31u);
-                        int sh16 = 0, sl16 = 0;
-                        sh16 = dp2a_lo_ss(qh2[0], kw.x, sh16);
-                        sh16 = dp2a_hi_ss(qh2[1], kw.x, sh16);
-                        sh16 = dp2a_lo_ss(qh2[2], kw.y, sh16);
-                        sh16 = dp2a_hi_ss(qh2[3], kw.y, sh16);
-                        sh16 = dp2a_lo_ss(qh2[4], kw.z, sh16);
-                        sh16 = dp2a_hi_ss(qh2[5], kw.z, sh16);
-                        sh16 = dp2a_lo_ss(qh2[6], kw.w, sh16);
-                        sh16 = dp2a_hi_ss(qh2[7], kw.w, sh16);
-                        sl16 = dp2a_lo_us(ql2[0], kw.x, sl16);
-                        sl16 = dp2a_hi_us(ql2[1], kw.x, sl16);
-                        sl16 = dp2a_lo_us(ql2[2], kw.y, sl16);
-                        sl16 = dp2a_hi_us(ql2[3], kw.y, sl16);
-                        sl16 = dp2a_lo_us(ql2[4], kw.z, sl16);
-                        sl16 = dp2a_hi_us(ql2[5], kw.z, sl16);
-                        sl16 = dp2a_lo_us(ql2[6], kw.w, sl16);
-                        sl16 = dp2a_hi_us(ql2[7], kw.w, sl16);
-                        const long long half = static_cast<long long>(sh16) * 65536 + sl16;
-                        hv = wrap_bits(sh >= 10 ? static_cast<long long>(static_cast<unsigned long long>(half) << (sh - 10))
-                                                : (half >> (10 - sh)), 44);
+                {   // scores (emulator:633-655): 16 warps x 4 tokens per round, 8 lanes per token
+                    const uint32_t* qs = reinterpret_cast<const uint32_t*>(S.qrot);
+                    const uint4 qa = *reinterpret_cast<const uint4*>(qs + 8 * hg);
+                    const uint4 qb = *reinterpret_cast<const uint4*>(qs + 8 * hg + 4);
+                    const uint4 la = *reinterpret_cast<const uint4*>(qs + 64 + 8 * hg);
+                    const uint4 lb = *reinterpret_cast<const uint4*>(qs + 64 + 8 * hg + 4);
+                    const uint32_t qh2[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                    const uint32_t ql2[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+                    long long hv[2] = {0, 0};
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        const int tl = r * 64 + wcw * 4 + (lane >> 3);
+                        if (r < rounds && tl < cnt) {
+                            const uint8_t* rec = buf + tl * 320;
+                            const uint4 kw = *reinterpret_cast<const uint4*>(rec + 64 + hg * 16);
+                            const unsigned long long meta = *reinterpret_cast<const unsigned long long*>(rec);
+                            const uint32_t sh = static_cast<uint32_t>((meta >> (5 * (hg >> 1))) & 31u);
+                            int sh16 = 0, sl16 = 0;
+                            sh16 = dp2a_lo_ss(qh2[0], kw.x, sh16);
+                            sh16 = dp2a_hi_ss(qh2[1], kw.x, sh16);
+                            sh16 = dp2a_lo_ss(qh2[2], kw.y, sh16);
+                            sh16 = dp2a_hi_ss(qh2[3], kw.y, sh16);
+                            sh16 = dp2a_lo_ss(qh2[4], kw.z, sh16);
+                            sh16 = dp2a_hi_ss(qh2[5], kw.z, sh16);
+                            sh16 = dp2a_lo_ss(qh2[6], kw.w, sh16);
+                            sh16 = dp2a_hi_ss(qh2[7], kw.w, sh16);
+                            sl16 = dp2a_lo_us(ql2[0], kw.x, sl16);
+                            sl16 = dp2a_hi_us(ql2[1], kw.x, sl16);
+                            sl16 = dp2a_lo_us(ql2[2], kw.y, sl16);
+                            sl16 = dp2a_hi_us(ql2[3], kw.y, sl16);
+                            sl16 = dp2a_lo_us(ql2[4], kw.z, sl16);
+                            sl16 = dp2a_hi_us(ql2[5], kw.z, sl16);
+                            sl16 = dp2a_lo_us(ql2[6], kw.w, sl16);
+                            sl16 = dp2a_hi_us(ql2[7], kw.w, sl16);
+                            const long long half = static_cast<long long>(sh16) * 65536 + sl16;
+                            hv[r] = wrap_bits(sh >= 10 ? static_cast<long long>(static_cast<unsigned long long>(half) << (sh - 10))
+                                                       : (half >> (10 - sh)), 44);
+                        }
                     }
-                    hv += __shfl_xor_sync(FULL, hv, 1);
-                    hv += __shfl_xor_sync(FULL, hv, 2);
-                    hv += __shfl_xor_sync(FULL, hv, 4);
-                    if ((lane & 7) == 0 && tl < cnt) S.score[tl] = sat32(rshift_even(wrap_bits(hv, 44) * a.score_scale, 24));
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        hv[r] += __shfl_xor_sync(FULL, hv[r], 1);
+                        hv[r] += __shfl_xor_sync(FULL, hv[r], 2);
+                        hv[r] += __shfl_xor_sync(FULL, hv[r], 4);
+                        const int tl = r * 64 + wcw * 4 + (lane >> 3);
+                        if ((lane & 7) == 0 && r < rounds && tl < cnt)
+                            S.score[tl] = sat32(rshift_even(wrap_bits(hv[r], 44) * a.score_scale, 24));
+                    }
                 }
                 item_wbar();
-                if (wcw == 0) {
-                    // Coefficients from the running maximum before each token
-                    // (emulator:656-672): lane l takes tokens 2l and 2l + 1.
-                    const int32_t carry = misc[0];
-                    const int t0 = 2 * lane;
-                    const int32_t s0 = t0 < cnt ? S.score[t0] : INT32_MIN;
-                    const int32_t s1 = t0 + 1 < cnt ? S.score[t0 + 1] : INT32_MIN;
-                    int32_t mx = max(s0, s1);
+                if (wcw * 32 < cnt) {
+                    // Coefficients (emulator:656-672), lane = token wcw * 32 + lane:
+                    // the running maximum before it is the largest of the
+                    // carry, the window's earlier 32-token words and the
+                    // prefix of its own word.
+                    const int tl = wcw * 32 + lane;
+                    int32_t carry = misc[2 + p];
+                    for (int j = 0; j < wcw; ++j) carry = max(carry, __reduce_max_sync(FULL, S.score[j * 32 + lane]));
+                    const int32_t sc = tl < cnt ? S.score[tl] : INT32_MIN;
+                    int32_t pm = sc;
 #pragma unroll
                     for (int o = 1; o < 32; o <<= 1) {
-                        const int32_t y = __shfl_up_sync(FULL, mx, o);
-                        if (lane >= o) mx = max(mx, y);
+                        const int32_t y = __shfl_up_sync(FULL, pm, o);
+                        if (lane >= o) pm = max(pm, y);
                     }
-                    int32_t ex = __shfl_up_sync(FULL, mx, 1);
+                    int32_t ex = __shfl_up_sync(FULL, pm, 1);
                     if (lane == 0) ex = INT32_MIN;
-                    const int32_t prev0 = max(carry, ex);
-                    const int32_t prev1 = max(prev0, s0);
-                    bool any_ev = false;
-                    uint32_t zs = 0;
-                    unsigned long long bs = 0;
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        const int tl = t0 + j;
-                        if (tl < cnt) {
-                            const int32_t sc = j ? s1 : s0, prev = j ? prev1 : prev0;
-                            uint32_t c;
-                            bool ev;
-                            if (T0 + tl == 0) {
-                                c = 1u << 17;
-                                ev = true;
-                            } else if (sc <= prev) {
-                                c = exp_negative_q17(sat32(static_cast<long long>(sc) - prev), S.lut, a.log2e_q21);
-                                ev = false;
-                            } else {
-                                c = exp_negative_q17(sat32(static_cast<long long>(prev) - sc), S.lut, a.log2e_q21);
-                                ev = true;
-                            }
-                            coef[tl] = c | (ev ? 0x80000000u : 0u);
-                            if (ev) {
-                                any_ev = true;
-                            } else {
-                                const unsigned long long meta =
-                                    *reinterpret_cast<const unsigned long long*>(buf + tl * 320);
-                                zs += c;
-                                bs += term_bound(static_cast<uint32_t>((meta >> vbit) & 31u), c);
-                            }
-                        }
+                    const int32_t prev = max(carry, ex);
+                    const bool ev = tl < cnt && (T0 + tl == 0 || sc > prev);
+                    const unsigned evm = __ballot_sync(FULL, ev);
+                    if (lane == 0) ti.evm[wcw] = evm;
+                    if (lane == 31 && (wcw + 1) * 32 >= cnt) misc[2 + (p ^ 1)] = max(carry, pm);  // the next window's carry
+                    uint32_t c = 0, zs = 0, bs = 0;
+                    if (tl < cnt) {
+                        if (T0 + tl == 0) c = 1u << 17;
+                        else if (!ev) c = exp_negative_q17(sat32(static_cast<long long>(sc) - prev), S.lut, a.log2e_q21);
+                        else c = exp_negative_q17(sat32(static_cast<long long>(prev) - sc), S.lut, a.log2e_q21);
+                        coef[tl] = c | (ev ? 0x80000000u : 0u);
+                        const uint32_t vsh = static_cast<uint32_t>(
+                            (*reinterpret_cast<const unsigned long long*>(buf + tl * 320) >> vbit) & 31u);
+                        zs = ev ? 0u : c;
+                        bs = term_bound(vsh, ev ? (1u << 17) : c);
                     }
-                    const unsigned evb = __ballot_sync(FULL, any_ev);
                     zs = __reduce_add_sync(FULL, zs);
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) bs += __shfl_xor_sync(FULL, bs, o);
-                    if (lane == 31) misc[0] = max(carry, mx);
+                    const bool big = __any_sync(FULL, bs > (1u << 25));
+                    bs = __reduce_add_sync(FULL, big ? 0u : bs);  // at most 32 * 2^25
                     if (lane == 0) {
-                        S.tinfo[p].ev = evb;
-                        S.tinfo[p].zsum = zs;
-                        S.tinfo[p].bound = bs;
+                        atomicAdd(&ti.zsum, zs);
+                        atomicAdd(&ti.bound, big ? (1ull << 40) : static_cast<unsigned long long>(bs));
                     }
                 }
                 item_wbar();
-                {   // state terms: warp = 4 tokens, lane = dimension
-                    int32_t ps = 0;
+                for (int r = 0; r < rounds; ++r) {  // state terms: warp = 4 tokens per round, lane = dimension
+                    unsigned long long mt[4];
+                    int v8[4];
+                    uint32_t cf[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {  // operands first, then the arithmetic
+                        const int tl = min(r * 64 + wcw * 4 + i, cnt - 1);
+                        const uint8_t* rec = buf + tl * 320;
+                        mt[i] = *reinterpret_cast<const unsigned long long*>(rec);
+                        v8[i] = static_cast<int8_t>(rec[192 + dim]);
+                        cf[i] = coef[tl];
+                    }
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        const int tl = wcw * 4 + i;
-                        if (tl < cnt) {
-                            const uint8_t* rec = buf + tl * 320;
-                            const unsigned long long meta = *reinterpret_cast<const unsigned long long*>(rec);
-                            const uint32_t sh = static_cast<uint32_t>((meta >> vbit) & 31u);
-                            const int v8 = static_cast<int8_t>(rec[192 + dim]);
-                            const uint32_t cf = coef[tl];
-                            int32_t term;
-                            if (cf >> 31) {
-                                term = static_cast<int32_t>(static_cast<uint32_t>(v8) << sh);  // v itself
-                            } else {
-                                term = term_q17(v8, sh, cf);
-                                ps += term;
-                            }
-                            tbuf[tl * 32 + dl] = term;
+                        const int tl = r * 64 + wcw * 4 + i;
+                        const uint32_t sh = static_cast<uint32_t>((mt[i] >> vbit) & 31u);
+                        const int32_t t = (cf[i] >> 31) ? static_cast<int32_t>(static_cast<uint32_t>(v8[i]) << sh)  // v itself
+                                                        : term_q17(v8[i], sh, cf[i]);
+                        if (tl < cnt) tbuf[tl * 32 + dl] = t;
+                    }
+                }
+                // Run pass: warp w sums runs w, w + 16, ... of non-event
+                // tokens (run r ends before event r, the last run at the
+                // window's end) per dimension into the run's last term slot,
+                // and their c_t into zseg[r].  It is done only when the
+                // window's bound allows the summed form at all; warp 0 still
+                // checks it against its state before using the sums.
+                item_wbar();
+                const bool runs = ti.bound <= static_cast<unsigned long long>(INT32_MAX);
+                if (runs) {
+                    const unsigned e0 = ti.evm[0], e1 = ti.evm[1], e2 = ti.evm[2], e3 = ti.evm[3];
+                    const int n0 = __popc(e0), n1 = __popc(e1), n2 = __popc(e2), n3 = __popc(e3);
+                    const int nev = n0 + n1 + n2 + n3;
+                    // Position of event r (0-based, in token order); nev -> cnt.
+                    auto ev_pos = [&](int r) -> int {
+                        if (r < 0) return -1;
+                        if (r >= nev) return cnt;
+                        if (r < n0) return __fns(e0, 0, r + 1);
+                        r -= n0;
+                        if (r < n1) return 32 + __fns(e1, 0, r + 1);
+                        r -= n1;
+                        if (r < n2) return 64 + __fns(e2, 0, r + 1);
+                        return 96 + __fns(e3, 0, r - n2 + 1);
+                    };
+                    uint32_t* zseg = S.zseg + (one ? 0 : p * (kTile + 2));
+                    for (int r = wcw; r <= nev; r += 16) {
+                        const int t0 = ev_pos(r - 1) + 1, t1 = ev_pos(r);
+                        int32_t s0 = 0, s1 = 0;
+                        uint32_t zs = 0;
+                        int t = t0;
+                        for (; t + 2 <= t1; t += 2) {
+                            s0 += tbuf[t * 32 + dl];
+                            s1 += tbuf[(t + 1) * 32 + dl];
+                            zs += coef[t] + coef[t + 1];
                         }
-                    }
-                    atomicAdd(&psum[dl], ps);
-                }
-            }
-        } else if (warp == 0 && k >= 1) {  // tile k - 1 onto the state, in token order
-            const int kp = k - 1, p = kp & 1, T0 = kp * kTile, cnt = min(kTile, n - T0);
-            const TileInfo ti = S.tinfo[p];
-            const long long mag = st < 0 ? -static_cast<long long>(st) : st;
-            if (ti.ev == 0 && static_cast<unsigned long long>(mag) + ti.bound <= static_cast<unsigned long long>(INT32_MAX)) {
-                st += S.psum[p * 32 + dl];  // no step of the chain can saturate: the sum is exact
-                z = (z + static_cast<uint32_t>(ti.zsum)) & M30;
-            } else {
-                const uint32_t* coef = S.coef + p * kTile;
-                const int32_t* tbuf = S.tbuf + p * kTile * 32;
-                for (int tl = 0; tl < cnt; ++tl) {
-                    const uint32_t cf = coef[tl];
-                    const uint32_t cc = cf & 0x7fffffffu;
-                    const int32_t tv = tbuf[tl * 32 + dl];
-                    if (T0 + tl == 0) {
-                        st = tv;
-                        z = 1u << 17;
-                    } else if (cf >> 31) {  // new maximum: rescale, then add v (emulator:674-685)
-                        st = add_sat32(mulq17_w(st, cc), tv);
-                        z = ((static_cast<uint32_t>(mulq17_w(static_cast<int32_t>(z), cc)) & M30) + (1u << 17)) & M30;
-                    } else {
-                        st = add_sat32(st, tv);
-                        z = (z + cc) & M30;
+                        if (t < t1) {
+                            s0 += tbuf[t * 32 + dl];
+                            zs += coef[t];
+                        }
+                        if (t1 > t0) tbuf[(t1 - 1) * 32 + dl] = s0 + s1;
+                        if (lane == 0) zseg[r] = zs;
                     }
                 }
+                if (wtid == 0) ti.runs = runs ? 1u : 0u;
             }
+        } else if (warp == 0 && k >= 1) {
+            apply(k - 1);  // window k - 1, one window behind the workers
         }
         item_bar();
+        if (tid == 0 && k < 3) mark(1 + k);
     }
+    if (tid == 0) mark(4);
     if (warp == 0) {  // normalise and quantise this part's 32-value group (emulator:686-711)
         const uint32_t inv = z == 0 ? 0u : static_cast<uint32_t>(((1ull << 34) + (z >> 1)) / z);
         const int32_t o = mulq17(st, inv);
@@ -411,6 +561,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, const AttnItemSmem&
         r = fmaxf(-8191.0f, fminf(8191.0f, r));
         a.out_q[h * kHeadDim + dim] = static_cast<int16_t>(__float2int_rz(r));
         if (lane == 0) a.out_e[h * 4 + part] = maxf == 0.0f ? 0 : static_cast<uint8_t>(maxe + 127);
+        if (tid == 0) mark(5);
     }
 }
 
@@ -428,7 +579,7 @@ __global__ void __launch_bounds__(kItemThreads, 1) k_attn_items(const __grid_con
         return;
     }
     attn_item(a, S, abar, h, part, static_cast<int>(threadIdx.x), nullptr, [] {},
-              [&](unsigned code) { atomicOr(a.err, code); });
+              [&](unsigned code) { atomicOr(a.err, code); }, [](int) {});
 }
 
 __host__ __device__ constexpr size_t attn_items_smem_bytes() { return 128 + kAttnItemBytes; }

@@ -122,8 +122,8 @@ enum TraceSlot : int {
 // consumer warp w in the QKV stage: k < 6 time of its k-th unit grab, 6 loop
 // exit, 7 number of grabs; 162 + q: GATE/UP stage, time the producer issued
 // copy q of the stage (q < 24); 186 + q: time the first compute warp found
-// copy q landed.
-constexpr int kTlEvents = 34 + 8 * 16 + 48;
+// copy q landed; 210 + k: attention item milestone k (attn_item's mark).
+constexpr int kTlEvents = 34 + 8 * 16 + 48 + 8;
 
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
@@ -764,7 +764,7 @@ __device__ __forceinline__ void tok_attention(const TokenArgs& ta, const TokSmem
                   t_a1 = clock64();
                   tl_mark<TR>(ta, layer, 21);
               },
-              [&](unsigned code) { raise_abort(ta, code); });
+              [&](unsigned code) { raise_abort(ta, code); }, [&](int k) { tl_mark<TR>(ta, layer, 210 + k); });
     __syncwarp();
     if (tid == 0) {
         red_release_gpu(&ta.sync[kSyncAtt + layer], 1u);

@@ -224,3 +224,45 @@ def test_attention_saturating_state(ctx, oracle, rope_tables):
     oq, oe = oracle.attention(kv, 2, 4096, 0, pos, oracle.rope(q, rope_tables, pos),
                               oracle.rope(k, rope_tables, pos), v)
     assert np.array_equal(gq, oq) and np.array_equal(ge, oe)
+
+
+@pytest.mark.parametrize("pos", [100, 127, 128, 200])
+def test_attention_rising_scores(ctx, oracle, rope_tables, pos):
+    """Scores that rise on most tokens (a new maximum nearly every step, as a
+    recency-biased head gives) across one 128-token window (pos < 128) and
+    across 64-token tiles beyond it."""
+    rng = np.random.default_rng(11 + pos)
+    ctx.kv_reset()
+    q = rng.integers(-1024, 1024, 4096).astype(np.int32)
+    qr = oracle.rope(q, rope_tables, pos)
+    kv = oracle.kv_store(2, 4096)
+    recs = {}
+    for head in (2, 13, 30):
+        k8 = np.where(qr[head * 128:(head + 1) * 128] >= 0, 60, -60)
+        recs[head] = [_record(k8, [4 + (t * 20) // pos + (t % 3 == 0)] * 4, rng.integers(-127, 128, 128),
+                              [int(rng.integers(0, 14))] * 4) for t in range(pos)]
+    _write_records(ctx, kv, 1, recs)
+    k, v = (_rand_q17(rng, 4096, 0.5) for _ in range(2))
+    gq, ge = ctx.attention(1, pos, q, k, v)
+    oq, oe = oracle.attention(kv, 2, 4096, 1, pos, qr, oracle.rope(k, rope_tables, pos), v)
+    assert np.array_equal(gq, oq) and np.array_equal(ge, oe)
+
+
+def test_attention_saturation_in_a_later_tile(ctx, oracle, rope_tables):
+    """Small values in the first tile, then values near the int32 limit from
+    token 150 on: the windows after the first take the saturating path."""
+    rng = np.random.default_rng(12)
+    ctx.kv_reset()
+    pos = 230
+    kv = oracle.kv_store(2, 4096)
+    recs = {}
+    for head in (4, 21):
+        k8 = rng.integers(-5, 6, 128)
+        recs[head] = [_record(k8, [2] * 4, rng.integers(-127, 128, 128), [24 if t >= 150 else 6] * 4)
+                      for t in range(pos)]
+    _write_records(ctx, kv, 0, recs)
+    q, k, v = (_rand_q17(rng, 4096, 0.01) for _ in range(3))
+    gq, ge = ctx.attention(0, pos, q, k, v)
+    oq, oe = oracle.attention(kv, 2, 4096, 0, pos, oracle.rope(q, rope_tables, pos),
+                              oracle.rope(k, rope_tables, pos), v)
+    assert np.array_equal(gq, oq) and np.array_equal(ge, oe)
