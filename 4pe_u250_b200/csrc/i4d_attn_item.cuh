@@ -42,6 +42,8 @@ struct TileInfo {
     unsigned long long bound;   // bound on sum |term_t| + sum |v_e| over the window (>= 2^40: unbounded)
     unsigned zsum;              // sum of c_t over the window's non-event tokens
     unsigned runs;              // nonzero: each run's sums are in place (the workers' run pass ran)
+    unsigned nev;               // events in the window (set by the run pass)
+    unsigned pad[3];
 };
 
 struct AttnItemSmem {
@@ -272,7 +274,33 @@ __device__ __forceinline__ void attn_item(const AttnArgs a, const AttnItemSmem S
         const int32_t* tbuf = S.tbuf + p * kTile * 32 + dl;
         const uint32_t* zseg = S.zseg + (one ? 0 : p * (kTile + 2));
         const long long mag = st < 0 ? -static_cast<long long>(st) : st;
-        if (ti.runs && static_cast<unsigned long long>(mag) + ti.bound <= static_cast<unsigned long long>(INT32_MAX)) {
+        if (one && ti.runs) {
+            // A single window starts from the empty state, so its bound alone
+            // decides (the run pass ran only if it holds): the chain over
+            // the compact arrays the run pass left in the record buffers.
+            const int32_t* RS = reinterpret_cast<const int32_t*>(S.tiles) + dl;
+            const int32_t* EV = RS + (2 * kTile + 1) * 32;
+            const uint32_t* EC = reinterpret_cast<const uint32_t*>(EV - dl + 2 * kTile * 32);
+            const int nev = static_cast<int>(ti.nev);
+            // Event 0 is token 0, which resets the state (run 0 is empty).
+            st = EV[0];
+            z = 1u << 17;
+            int32_t rs = RS[32], ev = EV[32];
+            uint32_t c = EC[1], zr = zseg[1];
+            for (int i = 1; i < nev; ++i) {
+                const int j = i + 1 < nev ? i + 1 : i;  // operands of the next event, loaded ahead
+                const int32_t rs2 = RS[j * 32], ev2 = EV[j * 32];
+                const uint32_t c2 = EC[j], zr2 = zseg[j];
+                st = mulq17_w(st + rs, c) + ev;
+                z = ((static_cast<uint32_t>(mulq17_w(static_cast<int32_t>((z + zr) & M30), c)) & M30) + (1u << 17)) & M30;
+                rs = rs2;
+                ev = ev2;
+                c = c2;
+                zr = zr2;
+            }
+            st += RS[nev * 32];
+            z = (z + zseg[nev]) & M30;
+        } else if (ti.runs && static_cast<unsigned long long>(mag) + ti.bound <= static_cast<unsigned long long>(INT32_MAX)) {
             // |state| stays below |st| + bound <= 2^31 - 1 at every step, so
             // no step saturates: each run of non-event tokens adds as one
             // exact sum (left by the workers in the run's last term slot,
@@ -520,6 +548,19 @@ __device__ __forceinline__ void attn_item(const AttnArgs a, const AttnItemSmem S
                         return 96 + __fns(e3, 0, r - n2 + 1);
                     };
                     uint32_t* zseg = S.zseg + (one ? 0 : p * (kTile + 2));
+                    // A single window has no further copies, so its record
+                    // buffers are free now: the runs and events go there as
+                    // compact arrays in event order (RS[r][32], EV[i][32],
+                    // EC[i]) for warp 0's chain.
+                    int32_t* RS = reinterpret_cast<int32_t*>(S.tiles);
+                    int32_t* EV = RS + (2 * kTile + 1) * 32;
+                    uint32_t* EC = reinterpret_cast<uint32_t*>(EV + 2 * kTile * 32);
+                    if (one)
+                        for (int i = wcw; i < nev; i += 16) {
+                            const int e = ev_pos(i);
+                            EV[i * 32 + dl] = tbuf[e * 32 + dl];
+                            if (lane == 0) EC[i] = coef[e] & 0x7fffffffu;
+                        }
                     for (int r = wcw; r <= nev; r += 16) {
                         const int t0 = ev_pos(r - 1) + 1, t1 = ev_pos(r);
                         int32_t s0 = 0, s1 = 0;
@@ -534,9 +575,11 @@ __device__ __forceinline__ void attn_item(const AttnArgs a, const AttnItemSmem S
                             s0 += tbuf[t * 32 + dl];
                             zs += coef[t];
                         }
-                        if (t1 > t0) tbuf[(t1 - 1) * 32 + dl] = s0 + s1;
+                        if (one) RS[r * 32 + dl] = s0 + s1;
+                        else if (t1 > t0) tbuf[(t1 - 1) * 32 + dl] = s0 + s1;
                         if (lane == 0) zseg[r] = zs;
                     }
+                    if (wtid == 0) ti.nev = static_cast<unsigned>(nev);
                 }
                 if (wtid == 0) ti.runs = runs ? 1u : 0u;
             }
