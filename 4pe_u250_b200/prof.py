@@ -7,6 +7,12 @@
   python -m 4pe_u250_b200.prof attention --context 4096 --reps 3
                                                          attention steps of one
                                                          layer over a filled cache
+  python -m 4pe_u250_b200.prof sample --reps 3           device draws (top-p 0.9
+                                                         and multinomial) over
+                                                         32000 seeded logits
+  python -m 4pe_u250_b200.prof pack --reps 1             one GATE projection and
+                                                         the FP32 LM head packed
+                                                         into bank images
 
 Each builds a seeded synthetic model with only the layers it needs, so the
 device footprint stays at a few hundred MB.
@@ -42,7 +48,7 @@ def kv_records(n, seed):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemv", "decode", "prefill", "attention"])
+    ap.add_argument("what", choices=["gemv", "decode", "prefill", "attention", "sample", "pack"])
     ap.add_argument("--mode", type=int, default=4)
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--reps", type=int, default=3)
@@ -61,6 +67,33 @@ def main():
             rng = np.random.default_rng(3)
             qkv = torch.from_numpy(np.round(rng.standard_normal(3 * 4096) * 131072.0).astype(np.int32)).cuda()
             print(ctx.profile_attention(0, a.context - 1, qkv.data_ptr(), 0, a.reps))
+        print("ok")
+        return
+    if a.what == "sample":
+        import torch
+        with pkg.Context(num_layers=1, kv_capacity=8) as ctx:
+            logits = torch.from_numpy(np.random.default_rng(4).normal(0.0, 2.0, F.PADDED_VOCAB).astype(np.float32)).cuda()
+            hist = np.random.default_rng(5).integers(0, F.VOCAB, 64).astype(np.int32)
+            for top_p in (0.9, 0.0):
+                smp = pkg.Sampler.make(0.8, top_p=top_p, repeat_penalty=1.1, seed=7)
+                for _ in range(a.reps):
+                    print(ctx.sample(logits.data_ptr(), hist, smp))
+        print("ok")
+        return
+    if a.what == "pack":
+        import torch
+        with pkg.Context(num_layers=1, kv_capacity=8) as ctx:
+            g = torch.Generator(device="cuda").manual_seed(6)
+            imgs = [torch.zeros(F.BANK_BYTES, dtype=torch.uint8, device="cuda") for _ in range(4)]
+            ptrs = [t.data_ptr() for t in imgs]
+            rows, cols = 11008, 4096  # GATE, unpadded
+            nib = torch.randint(0, 256, (rows * cols // 2,), dtype=torch.uint8, device="cuda", generator=g)
+            sc = torch.rand(rows * cols // 128, device="cuda", generator=g) * 0.018 + 0.002
+            head = torch.randn(32000 * 4096, device="cuda", generator=g) * 0.02
+            for _ in range(a.reps):
+                ctx.pack_autoround_matrix(0, F.MODE_GATE, nib.data_ptr(), sc.data_ptr(), ptrs)
+                ctx.pack_fp32_head(head.data_ptr(), ptrs)
+            torch.cuda.synchronize()
         print("ok")
         return
     banks = synth.model_banks(a.layers, 5)
