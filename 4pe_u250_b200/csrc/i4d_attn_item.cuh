@@ -128,7 +128,7 @@ __device__ __forceinline__ bool item_mbar_wait(uint64_t* bar, uint32_t parity, c
                                                Fail fail) {
     for (uint32_t it = 0;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 15) == 0 && abort_word && *reinterpret_cast<const volatile unsigned*>(abort_word)) return false;
+        if ((it & 255u) == 255u && abort_word && *reinterpret_cast<const volatile unsigned*>(abort_word)) return false;
         if (it > (1u << 22)) {
             fail(kErrWaitFull | kErrWaitTile);
             return false;

@@ -202,12 +202,14 @@ __device__ __forceinline__ void raise_abort(const TokenArgs& a, unsigned code) {
 // abort or timeout.  Counters only grow (mod 2^32), so the comparison is
 // taken on the signed difference.  The poll is an acquire load (paired with
 // the release reductions of the arrivals); a relaxed poll followed by a
-// full fence was measured about 10 us per token slower.
+// full fence was measured about 10 us per token slower.  Every spin loop of
+// the kernel reads the abort word only once per 256 polls, never on the
+// first miss: it is another global round trip in the poll's path.
 __device__ bool wait_counter(const TokenArgs& a, const unsigned* word, unsigned target) {
     for (uint32_t it = 0;; ++it) {
         const unsigned v = a.world > 1 ? ld_acquire_sys(word) : ld_acquire_gpu(word);
         if (static_cast<int>(v - target) >= 0) return true;
-        if (aborted(a)) return false;
+        if ((it & 255u) == 255u && aborted(a)) return false;
         if (it > (1u << 24)) {
             raise_abort(a, kErrWaitFull | kErrWaitCounter);
             return false;
@@ -221,7 +223,7 @@ __device__ __forceinline__ bool tok_mbar_wait(const TokenArgs& a, uint64_t* bar,
     if (mbar_try_wait(bar, parity)) return true;
     for (uint32_t it = 0;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 15) == 0 && aborted(a)) return false;
+        if ((it & 255u) == 255u && aborted(a)) return false;
         if (it > (1u << 22)) {
             raise_abort(a, code);
             return false;
@@ -428,7 +430,7 @@ __device__ __forceinline__ void tok_input_attention(const TokenArgs& a, uint8_t*
 // Waits until copy `cp` is issued into `slot` and has landed.
 __device__ __forceinline__ void tok_wait_copy(const TokenArgs& a, const TokSmem& s, int cp, int slot) {
     for (uint32_t it = 0; *reinterpret_cast<volatile int*>(&s.issued[slot]) != cp; ++it) {
-        if ((it & 63) == 0 && aborted(a)) break;
+        if ((it & 255u) == 255u && aborted(a)) break;
         if (it > (1u << 24)) {
             raise_abort(a, kErrWaitFull | kErrWaitCopy);
             break;
@@ -548,7 +550,7 @@ __device__ __forceinline__ void tok_units(const TokenArgs& a, const TokSmem& s, 
         const long long c2 = tr ? clock64() : 0;
         // The chain: wait for chunk sq - 1 of the quad's stream.
         for (uint32_t it = 0; ld_acquire_cta_s(qflag) != sq; ++it) {
-            if ((it & 63) == 0 && aborted(a)) break;
+            if ((it & 255u) == 255u && aborted(a)) break;
             if (it > (1u << 24)) {
                 raise_abort(a, kErrWaitFull | kErrWaitUnit);
                 break;
