@@ -214,6 +214,45 @@ def long_context_line(ctx, F, args, stream, ev0, ev1, row, d_logits, peak):
     return out
 
 
+def layer_line(pkg, F, syn, lut, emb, device, peak):
+    """Config 2: one decoder layer at position 511 over 511 prior KV records
+    (the layer of forward(), emulator:727-783).  The step of a 2-layer model
+    minus that of a 1-layer model at the same position is one layer's time
+    (the final norm and LM head cancel); the caches are filled by a prefill of
+    511 seeded ids.  Algorithmic bytes: the layer's weights and gammas plus
+    512 records per head."""
+    import torch
+    ids = np.random.default_rng(1).integers(3, 32000, size=512).astype(np.int32)
+    d_emb = torch.from_numpy(emb).to(f"cuda:{device}")
+    out = {}
+    for layers in (1, 2):
+        with pkg.Context(device=device, num_layers=layers, kv_capacity=512) as c:
+            c.load_banks(syn.model_banks(layers, 1))
+            c.load_rope(lut)
+            c.load_embeddings(emb)
+            c.prefill_tokens(0, ids[:511])
+            d_logits = torch.empty(F.PADDED_VOCAB, dtype=torch.float32, device=f"cuda:{device}")
+            row = d_emb.data_ptr() + int(ids[511]) * 4096 * 4
+            s = torch.cuda.ExternalStream(c.stream_handle())
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            for _ in range(10):
+                c.decode_token_async(511, row, d_logits.data_ptr())
+            c.sync()
+            reps = 50
+            e0.record(s)
+            for _ in range(reps):
+                c.decode_token_async(511, row, d_logits.data_ptr())
+            e1.record(s)
+            c.sync()
+            out[layers] = e0.elapsed_time(e1) / reps
+    us = (out[2] - out[1]) * 1e3
+    nbytes = 105971712 + 2 * 4096 * 4 + 512 * 32 * 261
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"workload": "config2: one decoder layer at position 511 over 511 prior KV records (2-layer step minus 1-layer step)",
+            "us_per_layer": us, "bytes": nbytes, "gbs": gbs, "frac_of_peak": gbs / peak,
+            "step_ms": {"1_layer": out[1], "2_layers": out[2]}}
+
+
 def gemv_line(ctx, F, peak, peak_kind, streams, max_over_ranks):
     """The single INT4 GEMV of the Q-projection shape (4096 x 4096 in four
     input-column bank shards, 8,650,752 B of nibbles and Q1.15 scales): the
@@ -468,6 +507,7 @@ def main():
     if not shard:
         line["long_context"] = long_context_line(ctx, F, args, stream, ev0, ev1, row, d_logits, peak)
         line["gemv"] = gemv_line(ctx, F, peak, peak_kind, streams, max_over_ranks)
+        line["layer"] = layer_line(pkg, F, syn, lut, emb, local, peak)
         line["attention"] = attention_line(pkg, F, syn, lut, local, peak, peak_kind)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r = cpu_decode(banks, emb, lut, prompt, args.warmup, min(args.steps, args.cpu_steps))
