@@ -300,60 +300,51 @@ __device__ __forceinline__ void attn_item(const AttnArgs a, const AttnItemSmem S
             }
             st += RS[nev * 32];
             z = (z + zseg[nev]) & M30;
-        } else if (ti.runs && static_cast<unsigned long long>(mag) + ti.bound <= static_cast<unsigned long long>(INT32_MAX)) {
-            // |state| stays below |st| + bound <= 2^31 - 1 at every step, so
-            // no step saturates: each run of non-event tokens adds as one
-            // exact sum (left by the workers in the run's last term slot,
-            // its c_t sum in zseg), and only the events are applied one by
-            // one, their operands loaded one event ahead.
-            // Event masks in two 64-bit registers (an array indexed in the
-            // loop would live in local memory).
-            unsigned long long mlo = static_cast<unsigned long long>(ti.evm[0]) |
-                                     (static_cast<unsigned long long>(ti.evm[1]) << 32);
-            unsigned long long mhi = static_cast<unsigned long long>(ti.evm[2]) |
-                                     (static_cast<unsigned long long>(ti.evm[3]) << 32);
-            auto next_event = [&]() -> int {  // position of the next event, or cnt
-                if (mlo) {
-                    const int e = __ffsll(static_cast<long long>(mlo)) - 1;
-                    mlo &= mlo - 1ull;
-                    return e;
-                }
-                if (mhi) {
-                    const int e = 64 + __ffsll(static_cast<long long>(mhi)) - 1;
-                    mhi &= mhi - 1ull;
-                    return e;
-                }
-                return cnt;
-            };
-            int prev = -1, e = next_event(), i = 0;
-            int32_t sv = e > prev + 1 ? tbuf[(e - 1) * 32] : 0;
-            int32_t vv = e < cnt ? tbuf[e * 32] : 0;
-            uint32_t cv = e < cnt ? coef[e] & 0x7fffffffu : 0u;
-            uint32_t zv = zseg[0];
+        } else if (ti.bound <= static_cast<unsigned long long>(INT32_MAX) &&
+                   static_cast<unsigned long long>(mag) + ti.bound <= static_cast<unsigned long long>(INT32_MAX)) {
+            // A 64-token tile of a longer context: |state| stays below |st| +
+            // bound <= 2^31 - 1 at every step, so no step saturates; each run
+            // of non-event tokens is summed here from the terms (eight
+            // independent accumulators; integer addition is associative), and
+            // only the events are applied one by one.  This runs one tile
+            // behind the workers, in parallel with their next tile.
+            unsigned long long m = static_cast<unsigned long long>(ti.evm[0]) |
+                                   (static_cast<unsigned long long>(ti.evm[1]) << 32);
+            int t = 0;
             for (;;) {
-                const int e2 = e < cnt ? next_event() : cnt;
-                // The next event's operands (independent of the state chain).
-                const int32_t sv2 = e2 < cnt || e2 > e + 1 ? (e2 > e + 1 ? tbuf[(e2 - 1) * 32] : 0) : 0;
-                const int32_t vv2 = e2 < cnt ? tbuf[e2 * 32] : 0;
-                const uint32_t cv2 = e2 < cnt ? coef[e2] & 0x7fffffffu : 0u;
-                const uint32_t zv2 = zseg[min(i + 1, kZseg - 1)];
-                st += sv;
-                z = (z + zv) & M30;
+                const int e = m ? __ffsll(static_cast<long long>(m)) - 1 : cnt;
+                int32_t s0 = 0, s1 = 0, s2 = 0, s3 = 0, s4 = 0, s5 = 0, s6 = 0, s7 = 0;
+                uint32_t z0 = 0, z1 = 0;
+                for (; t + 8 <= e; t += 8) {
+                    s0 += tbuf[t * 32];
+                    s1 += tbuf[(t + 1) * 32];
+                    s2 += tbuf[(t + 2) * 32];
+                    s3 += tbuf[(t + 3) * 32];
+                    s4 += tbuf[(t + 4) * 32];
+                    s5 += tbuf[(t + 5) * 32];
+                    s6 += tbuf[(t + 6) * 32];
+                    s7 += tbuf[(t + 7) * 32];
+                    z0 += (coef[t] + coef[t + 1]) + (coef[t + 2] + coef[t + 3]);
+                    z1 += (coef[t + 4] + coef[t + 5]) + (coef[t + 6] + coef[t + 7]);
+                }
+                for (; t < e; ++t) {
+                    s0 += tbuf[t * 32];
+                    z0 += coef[t];
+                }
+                st += ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7));
+                z = (z + z0 + z1) & M30;
                 if (e >= cnt) break;
+                const uint32_t c = coef[e] & 0x7fffffffu;
+                const int32_t v = tbuf[e * 32];
                 if (T0 + e == 0) {
-                    st = vv;
+                    st = v;
                     z = 1u << 17;
                 } else {  // new maximum: rescale, then add v (emulator:674-685)
-                    st = mulq17_w(st, cv) + vv;
-                    z = ((static_cast<uint32_t>(mulq17_w(static_cast<int32_t>(z), cv)) & M30) + (1u << 17)) & M30;
+                    st = mulq17_w(st, c) + v;
+                    z = ((static_cast<uint32_t>(mulq17_w(static_cast<int32_t>(z), c)) & M30) + (1u << 17)) & M30;
                 }
-                prev = e;
-                e = e2;
-                sv = sv2;
-                vv = vv2;
-                cv = cv2;
-                zv = zv2;
-                ++i;
+                t = e + 1;
+                m &= m - 1ull;
             }
         } else {
             // The reference's recurrence (emulator:656-685), saturating at
@@ -530,6 +521,9 @@ __device__ __forceinline__ void attn_item(const AttnArgs a, const AttnItemSmem S
                 // and their c_t into zseg[r].  It is done only when the
                 // window's bound allows the summed form at all; warp 0 still
                 // checks it against its state before using the sums.
+                // (Tiles of a longer context go without: warp 0 sums their
+                // runs from the terms, one tile behind.)
+                if (one) {
                 item_wbar();
                 const bool runs = ti.bound <= static_cast<unsigned long long>(INT32_MAX);
                 if (runs) {
@@ -582,6 +576,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs a, const AttnItemSmem S
                     if (wtid == 0) ti.nev = static_cast<unsigned>(nev);
                 }
                 if (wtid == 0) ti.runs = runs ? 1u : 0u;
+                }  // single window
             }
         } else if (warp == 0 && k >= 1) {
             apply(k - 1);  // window k - 1, one window behind the workers
