@@ -52,7 +52,7 @@ struct AttnItemSmem {
     // carve in local memory.)
     uint8_t* tiles;
     uint8_t* cur;         // current token's record
-    int32_t* score;       // [kTile]
+    int32_t* score;       // [2 * kTile]: a single window scores up to 128 tokens
     uint32_t* coef;       // [2][kTile]: c | event << 31, by tile parity
     int32_t* tbuf;        // [2][kTile][32]: state terms of this part (v_t itself at events)
     TileInfo* tinfo;      // [2]
@@ -64,7 +64,7 @@ struct AttnItemSmem {
 };
 
 constexpr int kZseg = 2 * kTile + 4;       // runs of a window: one more than its events (by parity: 2 x (kTile + 2))
-constexpr size_t kAttnItemBytes = 2 * kTile * 320 + 320 + kTile * 4 + 2 * kTile * 4 + 2 * kTile * 32 * 4 +
+constexpr size_t kAttnItemBytes = 2 * kTile * 320 + 320 + 2 * kTile * 4 + 2 * kTile * 4 + 2 * kTile * 32 * 4 +
                                   2 * sizeof(TileInfo) + kZseg * 4 + 144 + 128 * 4 + 16 + 16 * 4;
 
 __device__ __forceinline__ AttnItemSmem attn_item_carve(uint8_t* p) {
@@ -74,7 +74,7 @@ __device__ __forceinline__ AttnItemSmem attn_item_carve(uint8_t* p) {
     s.cur = p;
     p += 320;
     s.score = reinterpret_cast<int32_t*>(p);
-    p += kTile * 4;
+    p += 2 * kTile * 4;
     s.coef = reinterpret_cast<uint32_t*>(p);
     p += 2 * kTile * 4;
     s.tbuf = reinterpret_cast<int32_t*>(p);

@@ -35,7 +35,7 @@ constexpr int kTokRing = 40;               // ring capacity in chunks of kChunkB
 constexpr int kTokCpc = 4;                 // chunks per bulk copy (16,896 B: streams near the HBM peak)
 constexpr int kTokSlots = kTokRing / kTokCpc;  // ring slots, one copy each
 constexpr int kTokSlotBytes = kTokCpc * kChunkBytes;
-constexpr int kTokUnion = 59904;           // GEMV activations + transpose tiles, or attention scratch
+constexpr int kTokUnion = 60160;           // GEMV activations + transpose tiles, or attention scratch
 // Activation record of one local G32 group (80 B): hi int8[32], lo
 // uint8[32], correction int32, scale float, 8 pad bytes.  The 80-byte stride
 // puts the 8 groups a warp reads at once on distinct shared-memory banks.
