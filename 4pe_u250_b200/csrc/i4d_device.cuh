@@ -114,6 +114,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Bulk prefetch of global memory into L2 (no destination and no completion
+// to wait for); address and size multiples of 16 bytes.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// 16-byte asynchronous copy global -> shared (no registers on the way);
+// both addresses 16-byte aligned.  Completion: cp_async_commit, then
+// cp_async_wait_all in the issuing thread, then a barrier for the others.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // L2 policy for data read once (weights): evict before anything else.
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t p;

@@ -154,7 +154,6 @@ struct TokSmem {
     uint8_t* ring;
     uint64_t* full;
     uint64_t* empty;
-    uint64_t* abar;      // [2] attention tile barriers
     uint8_t* uni;        // union region
     int* flag;           // [4] misc
     int* issued;         // [kTokSlots]: copy sequence number last issued into each slot
@@ -162,7 +161,7 @@ struct TokSmem {
 };
 
 __host__ __device__ inline size_t tok_smem_bytes() {
-    return static_cast<size_t>(kTokRing) * kChunkBytes + 2 * kTokSlots * 8 + 16 + kTokUnion + 16 +
+    return static_cast<size_t>(kTokRing) * kChunkBytes + 2 * kTokSlots * 8 + kTokUnion + 16 +
            align16(kTokSlots * 4) + 64 * 8;
 }
 
@@ -172,8 +171,7 @@ __device__ __forceinline__ TokSmem tok_carve(uint8_t* p) {
     p += static_cast<size_t>(kTokRing) * kChunkBytes;
     s.full = reinterpret_cast<uint64_t*>(p);
     s.empty = s.full + kTokSlots;
-    s.abar = s.empty + kTokSlots;
-    p += 2 * kTokSlots * 8 + 16;
+    p += 2 * kTokSlots * 8;
     s.uni = p;
     p += kTokUnion;
     s.flag = reinterpret_cast<int*>(p);
@@ -760,13 +758,13 @@ __device__ __forceinline__ void tok_attention(const TokenArgs& ta, const TokSmem
     const long long t_a0 = clock64();
     long long t_a1 = t_a0;
     if (tid == 0) tl_mark<TR>(ta, layer, 20);
-    attn_item(a, S, s.abar, item / kAttnParts, item % kAttnParts, tid, &ta.sync[kSyncAbort],
+    attn_item(a, S, item / kAttnParts, item % kAttnParts, tid,
               [&] {
                   wait_counter(ta, &ta.sync[kSyncStage + stage_ordinal(TS_QKV, layer)], tgt_qkv);
                   t_a1 = clock64();
                   tl_mark<TR>(ta, layer, 21);
               },
-              [&](unsigned code) { raise_abort(ta, code); }, [&](int k) { tl_mark<TR>(ta, layer, 210 + k); });
+              [&](int k) { tl_mark<TR>(ta, layer, 210 + k); });
     __syncwarp();
     if (tid == 0) {
         red_release_gpu(&ta.sync[kSyncAtt + layer], 1u);
