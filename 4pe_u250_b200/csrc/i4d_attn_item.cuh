@@ -54,7 +54,6 @@ struct WinInfo {
     int32_t post[kRunWarps][32];
     uint32_t mag[kRunWarps][32];     // per warp and dimension: sum of |value|, clamped to 2^31
     uint32_t zpre[kRunWarps], zpost[kRunWarps];
-    uint32_t nevw[kRunWarps];        // events in the warp's tokens
     uint32_t pad[4];
 };
 static_assert(sizeof(WinInfo) % 16 == 0, "the carve keeps 16-byte alignment after the window summary");
@@ -366,95 +365,124 @@ __device__ __forceinline__ void attn_item(const AttnArgs a, const AttnItemSmem S
             item_wbar();
             // ---- runs: tokens [16 wcw, 16 wcw + 16), lane = dimension ----
             int nev = 0, before = 0;
+            uint32_t wmask = 0u;  // bit u: worker warp u's tokens hold an event
             const int t0 = wcw * 16;
 #pragma unroll
             for (int j = 0; j < kWin / 32; ++j) {
                 const unsigned m = wi.evm[j];
                 nev += __popc(m);
                 if (j < (t0 >> 5)) before += __popc(m);
+                wmask |= ((m & 0xffffu) ? 1u : 0u) << (2 * j);
+                wmask |= ((m >> 16) ? 1u : 0u) << (2 * j + 1);
             }
             const unsigned mine = (wi.evm[t0 >> 5] >> (t0 & 31)) & 0xffffu;  // this warp's events
             before += __popc(wi.evm[t0 >> 5] & ((1u << (t0 & 31)) - 1u));
-            const int nmine = __popc(mine);
             if (nev <= kMaxEv) {
+                // The warp's 16 coefficients and shifts as four and one
+                // 16-byte shared loads (entries past the window are stale
+                // and masked below), its dimension's V bytes one by one.
                 int8_t v8[16];
                 uint32_t cf[16], sh[16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int tl = min(t0 + i, cnt - 1);
-                    v8[i] = S.vbuf[tl * 32 + dl];
-                    cf[i] = S.coef[tl];
-                    sh[i] = S.vsh[tl];
+                for (int q = 0; q < 4; ++q) {
+                    const uint4 c4 = *reinterpret_cast<const uint4*>(S.coef + t0 + 4 * q);
+                    cf[4 * q] = c4.x;
+                    cf[4 * q + 1] = c4.y;
+                    cf[4 * q + 2] = c4.z;
+                    cf[4 * q + 3] = c4.w;
                 }
-                // Each token's value first: the state term, or v itself at an
-                // event (emulator:674-685); tokens past the window add 0.
+                const uint4 s4 = *reinterpret_cast<const uint4*>(S.vsh + t0);
+                const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                for (int i = 0; i < 16; ++i) sh[i] = (sw[i >> 2] >> (8 * (i & 3))) & 0xffu;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v8[i] = S.vbuf[min(t0 + i, cnt - 1) * 32 + dl];
+                // Each token's value: v = v8 << shift itself at an event,
+                // else the state term mulq17(v, c) (emulator:674-685, on the
+                // value of emulator:677); tokens past the window add 0.  The
+                // magnitude sum saturates at 2^31 (each |value| taken below
+                // 2^31, so two never overflow 32 bits).
                 int32_t x[16];
-                unsigned long long mag = 0ull;
+                uint32_t mag = 0u, zsum = 0u;
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    x[i] = t0 + i >= cnt ? 0
-                           : (cf[i] >> 31) ? static_cast<int32_t>(static_cast<uint32_t>(v8[i]) << sh[i])
-                                           : term_q17(v8[i], sh[i], cf[i]);
-                    mag += static_cast<unsigned long long>(x[i] < 0 ? -static_cast<long long>(x[i]) : x[i]);
+                    const int32_t vfull = static_cast<int32_t>(static_cast<uint32_t>(v8[i]) << sh[i]);
+                    const bool in = t0 + i < cnt;
+                    x[i] = !in ? 0 : (cf[i] >> 31) ? vfull : mulq17_w(vfull, cf[i]);
+                    const uint32_t ux = static_cast<uint32_t>(x[i]);
+                    const uint32_t ax = min(x[i] < 0 ? 0u - ux : ux, 0x7fffffffu);
+                    mag = min(mag + ax, 1u << 31);
+                    zsum += (in && !(cf[i] >> 31)) ? cf[i] : 0u;
                 }
-                wi.mag[wcw][dl] = static_cast<uint32_t>(min(mag, 1ull << 31));
-                // In token order: the part before the first event, each run
-                // between two of this warp's events (complete here: stored),
-                // the part after the last one.
-                int r = before;
-                int32_t acc = 0;
-                uint32_t zacc = 0;
+                wi.mag[wcw][dl] = mag;
+                if (mine == 0u) {  // one part of one run: a plain sum
+                    int32_t acc = 0;
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    if ((mine >> i) & 1u) {  // event r ends run r
-                        if (r == before) {
-                            wi.pre[wcw][dl] = acc;
-                            if (lane == 0) wi.zpre[wcw] = zacc;
-                        } else {
-                            S.rs[r * 32 + dl] = acc;
-                            if (lane == 0) S.zs[r] = zacc;
-                        }
-                        S.ev[r * 32 + dl] = x[i];
-                        if (lane == 0) S.ec[r] = cf[i] & 0x7fffffffu;
-                        ++r;
-                        acc = 0;
-                        zacc = 0;
-                    } else if (t0 + i < cnt) {
-                        acc += x[i];
-                        zacc += cf[i];
-                    }
-                }
-                if (nmine == 0) {
+                    for (int i = 0; i < 16; ++i) acc += x[i];
                     wi.pre[wcw][dl] = acc;
-                    if (lane == 0) wi.zpre[wcw] = zacc;
+                    if (lane == 0) wi.zpre[wcw] = zsum;
                 } else {
+                    // In token order: the part before the first event, each
+                    // run between two of this warp's events (complete here:
+                    // stored), the part after the last one.
+                    int r = before;
+                    int32_t acc = 0;
+                    uint32_t zacc = 0;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        if ((mine >> i) & 1u) {  // event r ends run r
+                            if (r == before) {
+                                wi.pre[wcw][dl] = acc;
+                                if (lane == 0) wi.zpre[wcw] = zacc;
+                            } else {
+                                S.rs[r * 32 + dl] = acc;
+                                if (lane == 0) S.zs[r] = zacc;
+                            }
+                            S.ev[r * 32 + dl] = x[i];
+                            if (lane == 0) S.ec[r] = cf[i] & 0x7fffffffu;
+                            ++r;
+                            acc = 0;
+                            zacc = 0;
+                        } else if (t0 + i < cnt) {
+                            acc += x[i];
+                            zacc += cf[i];
+                        }
+                    }
                     wi.post[wcw][dl] = acc;
                     if (lane == 0) wi.zpost[wcw] = zacc;
                 }
-                if (lane == 0) wi.nevw[wcw] = static_cast<uint32_t>(nmine);
             }
             item_wbar();
             // A run that crosses warps: the warp holding its closing event
             // (run `before`, closed by this warp's first event), or the last
-            // warp for the window's final run, adds the partial sums back to
-            // where the run opened -- the last event of an earlier warp, or
-            // the window start.
+            // warp for the window's final run, adds the partial sums of the
+            // warps back to where the run opened -- after the last event of
+            // an earlier warp (its post part), or at the window start.  The
+            // opening warp comes from the event mask, the sums are
+            // independent loads.
             if (nev <= kMaxEv) {
 #pragma unroll 1
                 for (int pass = 0; pass < 2; ++pass) {
-                    if (pass == 0 && nmine == 0) continue;
+                    if (pass == 0 && mine == 0u) continue;
                     if (pass == 1 && wcw != kRunWarps - 1) break;
-                    const bool own_post = pass == 1 && nmine > 0;  // the final run opened in this warp
+                    const bool own_post = pass == 1 && mine != 0u;  // the final run opened in this warp
                     int32_t tot = own_post ? wi.post[wcw][dl] : wi.pre[wcw][dl];
                     uint32_t zt = own_post ? wi.zpost[wcw] : wi.zpre[wcw];
-                    for (int u = own_post ? -1 : wcw - 1; u >= 0; --u) {
-                        if (wi.nevw[u] != 0u) {
-                            tot += wi.post[u][dl];
-                            zt += wi.zpost[u];
-                            break;
+                    if (!own_post) {
+                        const uint32_t m = wmask & ((1u << wcw) - 1u);
+                        const int open = m ? 31 - __clz(m) : -1;  // warp whose post part opens the run
+                        if (open >= 0) {
+                            tot += wi.post[open][dl];
+                            zt += wi.zpost[open];
                         }
-                        tot += wi.pre[u][dl];
-                        zt += wi.zpre[u];
+#pragma unroll
+                        for (int u = 0; u < kRunWarps - 1; ++u) {
+                            const bool take = u > open && u < wcw;
+                            const int32_t pv = wi.pre[u][dl];
+                            const uint32_t zv = wi.zpre[u];
+                            tot += take ? pv : 0;
+                            zt += take ? zv : 0u;
+                        }
                     }
                     const int run = pass == 0 ? before : nev;
                     S.rs[run * 32 + dl] = tot;
