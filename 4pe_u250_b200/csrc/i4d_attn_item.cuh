@@ -71,14 +71,12 @@ struct AttnItemSmem {
     WinInfo* info;
     uint32_t* lut;        // [33] exp2 table
     int32_t* qrot;        // [128]
-    unsigned long long* meta;  // current record's shift word
     int* misc;            // [16]
 };
 
 constexpr size_t kZsBytes = ((kMaxEv + 1) * 4 + 15) / 16 * 16;
 constexpr size_t kAttnItemBytes = 320 + kWin * 4 + kWin * 4 + kWin * 32 + kWin + (kMaxEv + 1) * 128 +
-                                  kMaxEv * 128 + kMaxEv * 4 + kZsBytes + sizeof(WinInfo) + 144 + 128 * 4 + 16 +
-                                  16 * 4;
+                                  kMaxEv * 128 + kMaxEv * 4 + kZsBytes + sizeof(WinInfo) + 144 + 128 * 4 + 16 * 4;
 
 __device__ __forceinline__ AttnItemSmem attn_item_carve(uint8_t* p) {
     AttnItemSmem s;
@@ -106,8 +104,6 @@ __device__ __forceinline__ AttnItemSmem attn_item_carve(uint8_t* p) {
     p += 144;
     s.qrot = reinterpret_cast<int32_t*>(p);
     p += 128 * 4;
-    s.meta = reinterpret_cast<unsigned long long*>(p);
-    p += 16;
     s.misc = reinterpret_cast<int*>(p);
     return s;
 }
@@ -150,10 +146,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs a, const AttnItemSmem S
     const int n = pos + 1;
     const int nwin = (n + kWin - 1) / kWin;
     const uint8_t* head_base = kv_record(a, h, 0);
-    if (tid == 0) {
-        misc[2] = INT32_MIN;  // running maximum before window k: misc[2 + (k & 1)]
-        *S.meta = 0ull;
-    }
+    if (tid == 0) misc[2] = INT32_MIN;  // running maximum before window k: misc[2 + (k & 1)]
     if (tid < 33) S.lut[tid] = a.exp2_q30[tid];
     if (tid < 16) reinterpret_cast<uint32_t*>(S.cur)[tid] = 0u;  // record word 0
     // RoPE factors of this position: independent of the projections.
@@ -193,7 +186,18 @@ __device__ __forceinline__ void attn_item(const AttnArgs a, const AttnItemSmem S
         const long long ka = (d & 1) ? ko : kv, kb = (d & 1) ? kv : ko;
         const int32_t qr = (d & 1) ? sat32((qa * rope_s + qb * rope_c) >> 17) : sat32((qa * rope_c - qb * rope_s) >> 17);
         const int32_t kr = (d & 1) ? sat32((ka * rope_s + kb * rope_c) >> 17) : sat32((ka * rope_c - kb * rope_s) >> 17);
-        S.qrot[d] = qr;
+        // q split into 16-bit halves for dp2a, per pair i = d / 2: qs[i] the
+        // high halves, qs[64 + i] the low halves (per 16-value half-group hg:
+        // qs[8 hg ..]).  It stays in shared memory: held in registers
+        // through the scan it would be demoted to local memory, whose lines
+        // the token kernel's small L1 does not keep.
+        const int32_t qn = __shfl_xor_sync(FULL, qr, 1);
+        if (!(d & 1)) {
+            reinterpret_cast<uint32_t*>(S.qrot)[d >> 1] =
+                (static_cast<uint32_t>(qr >> 16) & 0xffffu) | (static_cast<uint32_t>(qn >> 16) << 16);
+            reinterpret_cast<uint32_t*>(S.qrot)[64 + (d >> 1)] =
+                (static_cast<uint32_t>(qr) & 0xffffu) | (static_cast<uint32_t>(qn) << 16);
+        }
         // KV shift quantiser per 32-value group (warp), emulator:543-564.
         const uint32_t kmag = static_cast<uint32_t>(kr < 0 ? -static_cast<long long>(kr) : kr);
         const uint32_t vmag = static_cast<uint32_t>(vv < 0 ? -static_cast<long long>(vv) : vv);
@@ -206,36 +210,16 @@ __device__ __forceinline__ void attn_item(const AttnArgs a, const AttnItemSmem S
             grec[64 + d] = k8;
             grec[192 + d] = v8;
         }
+        // The record's shift word (word 0, zeroed above): this group's fields.
         if (lane == 0)
-            atomicOr(S.meta, (static_cast<unsigned long long>(ks) << (5 * warp)) |
-                                 (static_cast<unsigned long long>(vs) << (20 + 5 * warp)));
+            atomicOr(reinterpret_cast<unsigned long long*>(S.cur),
+                     (static_cast<unsigned long long>(ks) << (5 * warp)) |
+                         (static_cast<unsigned long long>(vs) << (20 + 5 * warp)));
     }
     item_bar();
-    if (tid < 8) {
-        const unsigned long long m = tid == 0 ? *S.meta : 0ull;
-        reinterpret_cast<unsigned long long*>(S.cur)[tid] = m;
-        if (part == 0) reinterpret_cast<unsigned long long*>(grec)[tid] = m;
-    }
-    // q split into 16-bit halves for dp2a, per 16-value half-group hg and
-    // pair i: qs[8 hg + i] (high halves) and qs[64 + 8 hg + i] (low halves),
-    // in place of qrot.  It stays in shared memory: held in registers
-    // through the scan it would be demoted to local memory, whose lines the
-    // token kernel's small L1 does not keep.
+    if (part == 0 && tid < 8)  // bytes 0..63 of the record: the shift word, then zeros
+        reinterpret_cast<unsigned long long*>(grec)[tid] = reinterpret_cast<const unsigned long long*>(S.cur)[tid];
     const int hg = lane & 7;
-    {
-        uint32_t qh = 0, ql = 0;
-        if (tid < 64) {
-            const int32_t x0 = S.qrot[2 * tid], x1 = S.qrot[2 * tid + 1];
-            qh = (static_cast<uint32_t>(x0 >> 16) & 0xffffu) | (static_cast<uint32_t>(x1 >> 16) << 16);
-            ql = (static_cast<uint32_t>(x0) & 0xffffu) | (static_cast<uint32_t>(x1) << 16);
-        }
-        item_bar();
-        if (tid < 64) {
-            reinterpret_cast<uint32_t*>(S.qrot)[tid] = qh;
-            reinterpret_cast<uint32_t*>(S.qrot)[64 + tid] = ql;
-        }
-    }
-    item_bar();
     if (tid == 0) mark(0);
 
     const int dl = lane;                     // dimension inside this part
