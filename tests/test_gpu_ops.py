@@ -226,11 +226,12 @@ def test_attention_saturating_state(ctx, oracle, rope_tables):
     assert np.array_equal(gq, oq) and np.array_equal(ge, oe)
 
 
-@pytest.mark.parametrize("pos", [100, 127, 128, 200])
+@pytest.mark.parametrize("pos", [100, 127, 128, 200, 255, 256, 257, 520])
 def test_attention_rising_scores(ctx, oracle, rope_tables, pos):
     """Scores that rise on most tokens (a new maximum nearly every step, as a
-    recency-biased head gives) across one 128-token window (pos < 128) and
-    across 64-token tiles beyond it."""
+    recency-biased head gives): more events than a 256-token window applies as
+    a chain, so those windows go token by token; positions on both sides of
+    a window boundary (the current token first or last in its window)."""
     rng = np.random.default_rng(11 + pos)
     ctx.kv_reset()
     q = rng.integers(-1024, 1024, 4096).astype(np.int32)
@@ -259,6 +260,51 @@ def test_attention_saturation_in_a_later_tile(ctx, oracle, rope_tables):
     for head in (4, 21):
         k8 = rng.integers(-5, 6, 128)
         recs[head] = [_record(k8, [2] * 4, rng.integers(-127, 128, 128), [24 if t >= 150 else 6] * 4)
+                      for t in range(pos)]
+    _write_records(ctx, kv, 0, recs)
+    q, k, v = (_rand_q17(rng, 4096, 0.01) for _ in range(3))
+    gq, ge = ctx.attention(0, pos, q, k, v)
+    oq, oe = oracle.attention(kv, 2, 4096, 0, pos, oracle.rope(q, rope_tables, pos),
+                              oracle.rope(k, rope_tables, pos), v)
+    assert np.array_equal(gq, oq) and np.array_equal(ge, oe)
+
+
+@pytest.mark.parametrize("pos", [150, 300, 700])
+def test_attention_events_across_warps(ctx, oracle, rope_tables, pos):
+    """A moderate number of events per window (the shift steps up every few
+    tokens, with one-token bumps between): the windows take the summed path
+    with runs that start in one worker warp's 16 tokens and end in a later
+    one, and events inside a warp's tokens."""
+    rng = np.random.default_rng(20 + pos)
+    ctx.kv_reset()
+    q = rng.integers(-1024, 1024, 4096).astype(np.int32)
+    qr = oracle.rope(q, rope_tables, pos)
+    kv = oracle.kv_store(2, 4096)
+    recs = {}
+    for head in (3, 18, 29):
+        k8 = np.where(qr[head * 128:(head + 1) * 128] >= 0, 40, -40)
+        recs[head] = [_record(k8, [2 + (t * 12) // pos + (t % 11 == 5)] * 4, rng.integers(-127, 128, 128),
+                              [int(rng.integers(0, 10))] * 4) for t in range(pos)]
+    _write_records(ctx, kv, 1, recs)
+    k, v = (_rand_q17(rng, 4096, 0.5) for _ in range(2))
+    gq, ge = ctx.attention(1, pos, q, k, v)
+    oq, oe = oracle.attention(kv, 2, 4096, 1, pos, qr, oracle.rope(k, rope_tables, pos), v)
+    assert np.array_equal(gq, oq) and np.array_equal(ge, oe)
+
+
+def test_attention_saturation_in_a_later_window(ctx, oracle, rope_tables):
+    """Small values in the first 256-token window, then values near the int32
+    limit from token 300 on: the second window's magnitude sum does not fit,
+    so it takes the reference's saturating recurrence after a summed first
+    window."""
+    rng = np.random.default_rng(13)
+    ctx.kv_reset()
+    pos = 420
+    kv = oracle.kv_store(2, 4096)
+    recs = {}
+    for head in (6, 25):
+        k8 = rng.integers(-5, 6, 128)
+        recs[head] = [_record(k8, [2] * 4, rng.integers(-127, 128, 128), [24 if t >= 300 else 6] * 4)
                       for t in range(pos)]
     _write_records(ctx, kv, 0, recs)
     q, k, v = (_rand_q17(rng, 4096, 0.01) for _ in range(3))
