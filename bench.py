@@ -11,9 +11,17 @@ positions, then 128 decode steps).
 value  tokens/s over K steps with inputs resident in HBM (embedding rows
        already on the device), CUDA events on the library's stream, max over
        ranks.
-e2e    the same K steps through the public C ABI i4d_decode_token with host
-       buffers (residual in, logits out copied every step).
+e2e    the same K steps through the public C ABI with host data:
+       i4d_decode_greedy (token id in, next token id out, 8 B / 12 B copied
+       per step); e2e_logits through i4d_decode_token (embedding row in,
+       logits, residual and status out every step).
 Weights (3.46 GB per token) exceed the 126 MB L2, so no flush is needed.
+Further keys: the decode roofline of k_token, a per-stage breakdown from an
+instrumented copy, long-context steps (positions 143/1023/2047), config 1
+(one Q-shape GEMV), config 2 (one layer at position 511), config 4 (the
+attention sweep L = 512..4096), batched prefill and perplexity evaluation,
+the reference emulator on the host cores, and the SM clocks sampled during
+the timed region.
 
 `--impl reference` times the reference's own CPU implementation (the
 emulator compiled from its source into oracle/_ref) on the host cores.
