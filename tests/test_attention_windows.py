@@ -14,8 +14,10 @@ This file checks that transformation on its own, against the recurrence
 (restated from the oracle's attention_head, which is pinned to the compiled
 reference emulator), on coefficient and value sequences built to hit every
 branch: sparse and dense events, events on warp and window boundaries,
-ragged window ends, and values that saturate the int32 state.  The GPU parity
-tests (tests/test_gpu_ops.py) check the kernel itself against the oracle.
+ragged window ends, and values that saturate the int32 state; and that the
+coefficient phase, which carries the running maximum from window to window,
+gives the reference's coefficients and events.  The GPU parity tests
+(tests/test_gpu_ops.py) check the kernel itself against the oracle.
 """
 import numpy as np
 import pytest
@@ -220,3 +222,49 @@ def test_cases_reach_both_paths():
             paths.add(("summed" if summed else "sequential", bool(ev.sum() > 0)))
             st, _ = reference_chain(coef[:t0 + cnt], event[:t0 + cnt], vals[:t0 + cnt])
     assert ("summed", True) in paths and ("sequential", True) in paths
+
+
+def window_coefficients(scores, orc):
+    """The item's coefficient phase (one warp per 32-token word of a
+    window): the running maximum before a token is the largest of the carry
+    into the window, the window's earlier words and the prefix of its own
+    word; the last word's warp hands max(carry, its prefix) on as the next
+    window's carry."""
+    n = len(scores)
+    coef, event = np.zeros(n, np.int64), np.zeros(n, bool)
+    carry = I32_MIN
+    for k in range((n + WIN - 1) // WIN):
+        t0, cnt = k * WIN, min(WIN, n - k * WIN)
+        sc = [int(s) for s in scores[t0:t0 + cnt]]
+        nxt = carry
+        for w in range((cnt + 31) // 32):
+            word = sc[w * 32:(w + 1) * 32]
+            c_in = max([carry] + sc[:w * 32])
+            pm = I32_MIN
+            for i, s in enumerate(word):
+                prev = max(c_in, pm)
+                t = t0 + w * 32 + i
+                ev = t == 0 or s > prev
+                if t == 0:
+                    c = 1 << 17
+                elif not ev:
+                    c = orc.L.i4o_exp_negative_q17(max(s - prev, I32_MIN))
+                else:
+                    c = orc.L.i4o_exp_negative_q17(max(prev - s, I32_MIN))
+                coef[t], event[t] = c, ev
+                pm = max(pm, s)
+            if (w + 1) * 32 >= cnt:
+                nxt = max(c_in, pm)
+        carry = nxt
+    return coef, event
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_window_coefficients_carry_the_running_maximum(name):
+    n, scores_of, _ = CASES[name]
+    rng = np.random.default_rng(sum(map(ord, name)))
+    orc = Oracle()
+    scores = scores_of(rng, n)
+    want = coefficients(scores, orc)
+    got = window_coefficients(scores, orc)
+    assert np.array_equal(got[0], want[0]) and np.array_equal(got[1], want[1])
