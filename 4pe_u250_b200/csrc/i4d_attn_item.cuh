@@ -148,7 +148,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs a, const AttnItemSmem S
     const uint8_t* head_base = kv_record(a, h, 0);
     if (tid == 0) misc[2] = INT32_MIN;  // running maximum before window k: misc[2 + (k & 1)]
     if (tid < 33) S.lut[tid] = a.exp2_q30[tid];
-    if (tid < 16) reinterpret_cast<uint32_t*>(S.cur)[tid] = 0u;  // record word 0
+    if (tid < 16) reinterpret_cast<uint32_t*>(S.cur)[tid] = 0u;  // record bytes 0..63: shift word (ORed in below), padding
     // RoPE factors of this position: independent of the projections.
     long long rope_c = 0, rope_s = 0;
     if (tid < 128) {
