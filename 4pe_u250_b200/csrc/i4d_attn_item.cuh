@@ -77,6 +77,18 @@ struct AttnItemSmem {
 constexpr size_t kZsBytes = ((kMaxEv + 1) * 4 + 15) / 16 * 16;
 constexpr size_t kAttnItemBytes = 320 + kWin * 4 + kWin * 4 + kWin * 32 + kWin + (kMaxEv + 1) * 128 +
                                   kMaxEv * 128 + kMaxEv * 4 + kZsBytes + sizeof(WinInfo) + 144 + 128 * 4 + 16 * 4;
+// Offsets of the carve's 16-byte accessed arrays (the carve starts 16-byte
+// aligned): coef (four-word loads), vbuf (cp.async and 16-byte stores), vsh
+// (16-byte loads), the window summary (64-bit atomics) and qrot (16-byte loads).
+constexpr size_t kOffCoef = 320 + kWin * 4;
+constexpr size_t kOffVbuf = kOffCoef + kWin * 4;
+constexpr size_t kOffVsh = kOffVbuf + kWin * 32;
+constexpr size_t kOffInfo = kOffVsh + kWin + (kMaxEv + 1) * 128 + kMaxEv * 128 + kMaxEv * 4 + kZsBytes;
+constexpr size_t kOffQrot = kOffInfo + sizeof(WinInfo) + 144;
+static_assert(kOffCoef % 16 == 0 && kOffVbuf % 16 == 0 && kOffVsh % 16 == 0 && kOffInfo % 16 == 0 &&
+                  kOffQrot % 16 == 0,
+              "16-byte alignment of the attention item's vector-accessed arrays");
+static_assert(kOffQrot + 128 * 4 + 16 * 4 == kAttnItemBytes, "the carve and its size agree");
 
 __device__ __forceinline__ AttnItemSmem attn_item_carve(uint8_t* p) {
     AttnItemSmem s;
