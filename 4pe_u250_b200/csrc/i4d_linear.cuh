@@ -78,7 +78,7 @@ struct LinearSmem {
     int* issued;        // [ns]: chunk index last issued into each ring slot
 };
 
-__host__ __device__ inline size_t align16(size_t b) { return (b + 15) & ~static_cast<size_t>(15); }
+__host__ __device__ constexpr size_t align16(size_t b) { return (b + 15) & ~static_cast<size_t>(15); }
 
 __host__ __device__ inline size_t linear_smem_bytes(int ns, int chunks, int nu) {
     const size_t groups = static_cast<size_t>(chunks) * 8;

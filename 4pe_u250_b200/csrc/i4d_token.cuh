@@ -160,10 +160,15 @@ struct TokSmem {
     double* expf_tab;    // [64]: the expf core's 2^(j/64) table
 };
 
-__host__ __device__ inline size_t tok_smem_bytes() {
+__host__ __device__ constexpr size_t tok_smem_bytes() {
     return static_cast<size_t>(kTokRing) * kChunkBytes + 2 * kTokSlots * 8 + kTokUnion + 16 +
            align16(kTokSlots * 4) + 64 * 8;
 }
+// One CTA per SM: the carve must fit the 227 KB a block may opt into, and the
+// union region (GEMV activations, attention scratch) must start 16-byte aligned.
+static_assert(tok_smem_bytes() <= 227 * 1024, "token kernel shared memory exceeds the per-block maximum");
+static_assert((static_cast<size_t>(kTokRing) * kChunkBytes + 2 * kTokSlots * 8) % 16 == 0,
+              "union region alignment");
 
 __device__ __forceinline__ TokSmem tok_carve(uint8_t* p) {
     TokSmem s;
